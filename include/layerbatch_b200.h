@@ -1,0 +1,165 @@
+/* layerbatch_b200: C ABI of the B200-native (sm_100a) LayerBatch hot path.
+ *
+ * Every entry point takes plain device pointers, element counts / strides and a CUDA
+ * stream (as `void*`, a cudaStream_t; NULL = legacy default stream).  Calls are
+ * stream-ordered, perform no host synchronisation and no device allocation: scratch comes
+ * from a caller-provided workspace whose size the matching *_workspace_size() returns.
+ * All tensors are owned by the caller.  bf16 tensors are row-major with the innermost
+ * dimension contiguous.  Errors are returned as status codes (never thrown or trapped);
+ * lb_get_last_error_string() describes the last failure of the calling thread.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   lb_moe_forward          <- Qwen3_5SparseMoeBlock.forward   nanovllm/models/qwen3_5.py:899-905
+ *                              (router :767-774, experts :802-874, shared expert :903,916-917)
+ *   lb_router_topk          <- Qwen3_5TopKRouter.forward tail  nanovllm/models/qwen3_5.py:770-774
+ *   lb_moe_permute          <- expert dispatch of _forward_sparse nanovllm/models/qwen3_5.py:821-831
+ *   lb_gemm_bf16            <- F.linear / RowParallelLinear.forward nanovllm/layers/linear.py:149-159
+ *   lb_store_kvcache        <- store_kvcache                    nanovllm/layers/attention.py:71-80
+ *   lb_pod_attn_oproj       <- pod_fused_attn_gemm / pod_attn_only nanovllm/layers/pod_kernels.py:237-354
+ *                              + Attention.forward decode/prefill nanovllm/layers/attention.py:99-226
+ *                              + output gate and o_proj         nanovllm/models/qwen3_5.py:739-746
+ */
+#ifndef LAYERBATCH_B200_H_
+#define LAYERBATCH_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status codes */
+#define LB_OK 0
+#define LB_ERR_INVALID_ARG 1 /* shape, stride, alignment or pointer check failed */
+#define LB_ERR_UNSUPPORTED 2 /* valid but not implemented shape (message says which) */
+#define LB_ERR_WORKSPACE 3   /* workspace missing or smaller than *_workspace_size() */
+#define LB_ERR_CUDA 4        /* a CUDA runtime call failed (launch, attribute, ...) */
+#define LB_ERR_DEVICE 5      /* a kernel recorded a device status (lb_read_device_status) */
+
+/* Device status values a kernel may record in the workspace status word. */
+#define LB_DEV_OK 0
+#define LB_DEV_TIMEOUT 1   /* a bounded pipeline wait gave up */
+#define LB_DEV_BAD_INDEX 2 /* an out-of-range page / expert index was skipped */
+
+const char* lb_get_last_error_string(void);
+int lb_version(void);
+/* Number of SMs and the sm_XY of the current device (for host-side planning). */
+int lb_device_info(int* num_sms, int* sm_version);
+
+/* Synchronously read (and optionally clear) the device status word that kernels of the
+ * call using `workspace` report into.  This is the only entry point that synchronises. */
+int lb_read_device_status(const void* workspace, int clear, int* status_out);
+
+/* ---------------------------------------------------------------- dense GEMM
+ * C[M,N] = A[M,K] . B[N,K]^T   (bf16 in, fp32 accumulate on tcgen05 tensor cores).
+ * c_is_fp32 = 0: C is bf16 and written;   splits must be 1.
+ * c_is_fp32 = 1: C is fp32 and ACCUMULATED into (C += A.B^T), K split `splits` ways; the
+ *                caller zeroes C first when a plain product is wanted.
+ * Requirements: K % 64 == 0, N % 32 == 0, lda/ldb/ldc multiples of 8 elements,
+ * pointers 16-byte aligned.  `workspace` needs lb_gemm_workspace_size() bytes. */
+size_t lb_gemm_workspace_size(void);
+int lb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                 int64_t M, int64_t N, int64_t K, int c_is_fp32, int splits, void* workspace,
+                 void* stream);
+
+/* ---------------------------------------------------------------- router top-k
+ * From bf16 router logits [T, E] (row stride ld): softmax in fp32, top-k with ties broken
+ * towards the lowest expert index, renormalise over the selected k.
+ * Outputs ids [T,k] int32 (descending probability), weights_f32 [T,k] (may be NULL),
+ * weights_bf16 [T,k] (may be NULL).  E <= 1024, k <= 32, k <= E. */
+int lb_router_topk(const void* logits, int64_t ld, int64_t T, int64_t E, int64_t k,
+                   int32_t* ids, float* weights_f32, void* weights_bf16, void* stream);
+
+/* ---------------------------------------------------------------- permutation
+ * Expert-major permutation of the (token, slot) pairs of ids [T,k] (global expert ids).
+ * Groups: group 0 is the shared expert (rows [0,T), token order); group 1+e is local
+ * expert e = id - expert_base for 0 <= e < num_local_experts; other ids are dropped.
+ * Inside a group, pairs are ordered slot-major then token (the reference's
+ * torch.where(expert_mask[e]) order).
+ * Outputs: row_start [G+1] (G = num_local_experts + 1), perm_token [T + T*k] (token of
+ * each packed row; rows past row_start[G] are untouched), row_of [T*k] (packed row of
+ * pair (t,j) or -1).  workspace: lb_moe_permute_workspace_size(). */
+size_t lb_moe_permute_workspace_size(int64_t T, int64_t k, int64_t num_local_experts);
+int lb_moe_permute(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base,
+                   int64_t num_local_experts, int32_t* row_start, int32_t* perm_token,
+                   int32_t* row_of, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- MoE block */
+typedef struct LbMoeArgs {
+  int64_t num_tokens;        /* T */
+  int64_t hidden;            /* H (multiple of 64) */
+  int64_t num_experts;       /* E, global routed experts (router width) */
+  int64_t top_k;             /* k */
+  int64_t inter;             /* I, routed expert intermediate (multiple of 128) */
+  int64_t shared_inter;      /* Is, shared expert intermediate (must equal I) */
+  int64_t expert_base;       /* first global expert id held in w_gate_up / w_down */
+  int64_t num_local_experts; /* experts held locally (E on one GPU) */
+  const void* x;             /* [T, H] bf16, row stride H */
+  const void* w_router;      /* [E, H] bf16           mlp.gate.weight */
+  const void* w_gate_up;     /* [nl, 2I, H] bf16      mlp.experts.gate_up_proj */
+  const void* w_down;        /* [nl, H, I] bf16       mlp.experts.down_proj */
+  const void* w_shared_gate; /* [Is, H] bf16          mlp.shared_expert.gate_proj.weight */
+  const void* w_shared_up;   /* [Is, H] bf16          mlp.shared_expert.up_proj.weight */
+  const void* w_shared_down; /* [H, Is] bf16          mlp.shared_expert.down_proj.weight */
+  const void* w_shared_expert_gate; /* [1, H] bf16    mlp.shared_expert_gate.weight */
+  void* out;                 /* [T, H] bf16 output */
+  void* router_logits;       /* optional out [T, E] bf16 */
+  int32_t* topk_ids;         /* optional out [T, k] int32 */
+  void* topk_weights;        /* optional out [T, k] bf16 */
+  void* workspace;
+  size_t workspace_bytes;
+} LbMoeArgs;
+
+int lb_moe_workspace_size(const LbMoeArgs* args, size_t* bytes);
+int lb_moe_forward(const LbMoeArgs* args, void* stream);
+
+/* ---------------------------------------------------------------- KV cache store
+ * k_cache/v_cache[slot] = k/v[i] for slot_mapping[i] != -1, rows of Hkv*D bf16.
+ * k, v: [N, Hkv, D] with token stride k_stride / v_stride (elements), heads packed. */
+int lb_store_kvcache(const void* k, int64_t k_stride, const void* v, int64_t v_stride,
+                     void* k_cache, void* v_cache, const int32_t* slot_mapping, int64_t N,
+                     int64_t num_slots, int64_t row_elems, void* stream);
+
+/* ---------------------------------------------------------------- POD attention + o_proj
+ * One batch of sequences, prefill chunks and decode steps mixed in any order.
+ * Sequence b owns query rows [cu_seqlens_q[b], cu_seqlens_q[b+1]) which are its last
+ * positions out of context_lens[b] tokens already in the paged cache (bottom-right
+ * causal).  Output: out[N, hidden] = (attn(q) * sigmoid(gate)).flatten() . W_o^T. */
+typedef struct LbPodArgs {
+  int64_t num_seqs;           /* B */
+  int64_t num_tokens;         /* N = cu_seqlens_q[B] */
+  int64_t max_q_len;          /* upper bound on any sequence's query length */
+  int64_t num_q_heads;        /* Hq */
+  int64_t num_kv_heads;       /* Hkv (Hq % Hkv == 0, Hq/Hkv <= 16) */
+  int64_t head_dim;           /* D (256) */
+  int64_t page_size;          /* tokens per KV block (256) */
+  int64_t num_pages;          /* blocks in the cache pool */
+  int64_t max_pages_per_seq;  /* block_tables row length */
+  int64_t hidden;             /* o_proj output width */
+  float sm_scale;
+  int32_t kv_split_pages;     /* decode split length in pages (0 = automatic) */
+  const void* q;              /* [N, Hq, D] bf16 */
+  int64_t q_stride_tok, q_stride_head;
+  const void* gate;           /* [N, Hq, D] bf16 (pre-sigmoid output gate) */
+  int64_t gate_stride_tok, gate_stride_head;
+  const void* k_cache;        /* [num_pages, page_size, Hkv, D] bf16 */
+  const void* v_cache;
+  const int32_t* block_tables;/* [B, max_pages_per_seq] int32 */
+  const int32_t* context_lens;/* [B] int32 */
+  const int32_t* cu_seqlens_q;/* [B+1] int32 */
+  const void* w_o;            /* [hidden, Hq*D] bf16 */
+  void* attn_out;             /* optional out: [N, Hq*D] bf16 attention output (pre-gate) */
+  void* out;                  /* [N, hidden] bf16, or fp32 when out_fp32 */
+  int32_t out_fp32;           /* 1: write fp32 o_proj partials (tensor-parallel reduce) */
+  void* workspace;
+  size_t workspace_bytes;
+} LbPodArgs;
+
+int lb_pod_workspace_size(const LbPodArgs* args, size_t* bytes);
+int lb_pod_attn_oproj(const LbPodArgs* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LAYERBATCH_B200_H_ */

@@ -1,0 +1,182 @@
+// C-ABI plumbing: error strings, device info, TMA descriptor encoding, the generic GEMM
+// entry point and the device status word.
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+
+#include "lb_gemm_launch.cuh"
+#include "lb_host.h"
+
+namespace lb {
+
+static thread_local char g_err[1024] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+static int encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
+                  const cuuint64_t* strides, const cuuint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(LB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  if (!aligned16(base)) return fail(LB_ERR_INVALID_ARG, "TMA base %p not 16-byte aligned", base);
+  for (int i = 0; i < rank - 1; ++i)
+    if (strides[i] % 16 != 0)
+      return fail(LB_ERR_INVALID_ARG, "TMA stride %llu not a multiple of 16 bytes",
+                  (unsigned long long)strides[i]);
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims,
+                  strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LB_ERR_INVALID_ARG, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return LB_OK;
+}
+
+int make_tmap_bf16_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
+                      uint64_t row_pitch_elems, uint32_t box_rows, uint32_t box_cols) {
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_pitch_elems * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  return encode(m, base, 2, dims, strides, box);
+}
+
+int make_tmap_bf16_3d(CUtensorMap* m, const void* base, uint64_t depth, uint64_t rows,
+                      uint64_t cols, uint64_t row_pitch_elems, uint64_t depth_pitch_elems,
+                      uint32_t box_rows, uint32_t box_cols) {
+  cuuint64_t dims[3] = {cols, rows, depth};
+  cuuint64_t strides[2] = {row_pitch_elems * 2, depth_pitch_elems * 2};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
+  return encode(m, base, 3, dims, strides, box);
+}
+
+int num_sms() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+int max_smem_optin() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  return n > 0 ? n : 232448;
+}
+
+}  // namespace lb
+
+using namespace lb;
+
+extern "C" {
+
+const char* lb_get_last_error_string(void) { return g_err; }
+
+int lb_version(void) { return 100; }
+
+int lb_device_info(int* n_sms, int* sm_version) {
+  int dev = 0;
+  LB_CUDA_CHECK(cudaGetDevice(&dev));
+  int major = 0, minor = 0, n = 0;
+  LB_CUDA_CHECK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+  LB_CUDA_CHECK(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+  LB_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  if (n_sms) *n_sms = n;
+  if (sm_version) *sm_version = major * 10 + minor;
+  return LB_OK;
+}
+
+int lb_read_device_status(const void* workspace, int clear, int* status_out) {
+  LB_REQUIRE(workspace != nullptr && status_out != nullptr, "null workspace/status pointer");
+  LB_CUDA_CHECK(cudaDeviceSynchronize());
+  int v = 0;
+  LB_CUDA_CHECK(cudaMemcpy(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost));
+  *status_out = v;
+  if (clear && v != 0) LB_CUDA_CHECK(cudaMemset(const_cast<void*>(workspace), 0, sizeof(int)));
+  return LB_OK;
+}
+
+size_t lb_gemm_workspace_size(void) { return 256; }
+
+int lb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                 int64_t M, int64_t N, int64_t K, int c_is_fp32, int splits, void* workspace,
+                 void* stream) {
+  LB_REQUIRE(A && B && C && workspace, "lb_gemm_bf16: null pointer");
+  LB_REQUIRE(M >= 0 && N > 0 && K > 0, "lb_gemm_bf16: bad shape M=%lld N=%lld K=%lld",
+             (long long)M, (long long)N, (long long)K);
+  LB_REQUIRE(K % 64 == 0, "lb_gemm_bf16: K=%lld must be a multiple of 64", (long long)K);
+  LB_REQUIRE(N % 32 == 0, "lb_gemm_bf16: N=%lld must be a multiple of 32", (long long)N);
+  LB_REQUIRE(lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0 && lda >= K && ldb >= K && ldc >= N,
+             "lb_gemm_bf16: leading dimensions must be >= the row length and multiples of 8");
+  LB_REQUIRE(aligned16(A) && aligned16(B) && aligned16(C), "lb_gemm_bf16: unaligned pointer");
+  LB_REQUIRE(M <= (1ll << 30) && N <= (1ll << 30), "lb_gemm_bf16: shape too large");
+  if (splits < 1) splits = 1;
+  LB_REQUIRE(c_is_fp32 || splits == 1, "lb_gemm_bf16: split-K needs an fp32 accumulator");
+  LB_REQUIRE((K / 64) % splits == 0, "lb_gemm_bf16: K/64 must divide by splits");
+  if (M == 0) return LB_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  const int BN = (N % 256 == 0 && M > 512) ? 256 : (N % 128 == 0 ? 128 : (N % 64 == 0 ? 64 : 32));
+  CUtensorMap tA, tB;
+  int rc = make_tmap_bf16_2d(&tA, A, M, K, lda, GEMM_BM, 64);
+  if (rc) return rc;
+  rc = make_tmap_bf16_3d(&tB, B, 1, N, K, ldb, ldb * N, BN, 64);
+  if (rc) return rc;
+  GemmArgs a = gemm_args_default(static_cast<int*>(workspace));
+  a.single_m = (int)M;
+  a.single_row_base = 0;
+  a.n_tiles = (int)(N / BN);
+  a.splits = splits;
+  a.k_blocks = (int)(K / 64) / splits;
+  a.out = C;
+  a.ldo = ldc;
+  a.out_rows = (int)M;
+  a.out_cols = (int)N;
+  const long long tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (long long)a.n_tiles * splits;
+  const int grid = (int)std::min<long long>(tiles, num_sms());
+  if (c_is_fp32) {
+    switch (BN) {
+      case 256: return launch_gemm<256, 4, EPI_F32_RED, false>(tA, tA, tB, tB, tB, a, grid, st);
+      case 128: return launch_gemm<128, 6, EPI_F32_RED, false>(tA, tA, tB, tB, tB, a, grid, st);
+      case 64: return launch_gemm<64, 8, EPI_F32_RED, false>(tA, tA, tB, tB, tB, a, grid, st);
+      default: return launch_gemm<32, 8, EPI_F32_RED, false>(tA, tA, tB, tB, tB, a, grid, st);
+    }
+  }
+  switch (BN) {
+    case 256: return launch_gemm<256, 4, EPI_BF16, false>(tA, tA, tB, tB, tB, a, grid, st);
+    case 128: return launch_gemm<128, 6, EPI_BF16, false>(tA, tA, tB, tB, tB, a, grid, st);
+    case 64: return launch_gemm<64, 8, EPI_BF16, false>(tA, tA, tB, tB, tB, a, grid, st);
+    default: return launch_gemm<32, 8, EPI_BF16, false>(tA, tA, tB, tB, tB, a, grid, st);
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,369 @@
+// Persistent grouped GEMM on sm_100a tensor cores: C[g] = A[g] . B[g]^T, bf16 in, f32
+// accumulate in TMEM, with fused epilogues for the MoE and o_proj hot path.
+//
+// Layout: A rows are packed per group (rows [row_start[g], row_start[g+1])), K contiguous.
+// B is a 3-D tensor [G, N, K] (K contiguous), i.e. nn.Linear / expert weight layout.
+// Tiles are 128 x BN x 64 (M x N x K); one CTA per SM walks a static tile sequence:
+//   warp 0      : TMA producer (one elected lane)
+//   warp 1      : TMEM allocator + tcgen05.mma issuer (one elected lane)
+//   warps 2..5  : epilogue (TMEM -> registers -> global), 1 thread per accumulator row
+// Accumulators are double-buffered in TMEM so the epilogue of tile i overlaps the
+// mainloop of tile i+1.  Stages of A/B tiles are 128B-swizzled, K-major.
+#pragma once
+
+#include <cuda.h>
+#include "lb_common.cuh"
+
+namespace lb {
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+enum EpiKind : int {
+  EPI_BF16 = 0,        // C = bf16(acc)
+  EPI_SWIGLU = 1,      // act = bf16(silu(acc[:, :BN/2]) * acc[:, BN/2:])
+  EPI_SCALE_BF16 = 2,  // C = bf16(acc * row_scale[row])
+  EPI_COMBINE = 3,     // out[t] = bf16(tok_scale[t] * acc + sum_j yw[row_of[t, j]])
+  EPI_F32_RED = 4,     // out32 += acc (split-K partials, vector reductions)
+};
+
+struct GemmArgs {
+  int* status;
+  const int* mtile_start;  // [G+1] cumulative 128-row tiles per group; null => one group
+  const int* row_start;    // [G+1] first packed row per group; null => 0
+  int num_groups;          // G
+  int single_m;            // rows of the single group (mtile_start == null)
+  int single_row_base;     // first A row of the single group
+  int n_tiles;             // N / BN
+  int k_blocks;            // K / 64 handled by one split
+  int splits;              // split-K factor
+  int shared_group;        // group whose A/B come from the *_sh tensor maps (-1: none)
+  int b_group_base;        // routed B depth coordinate = g - b_group_base
+  int b_half_offset;       // two-half B tiles: row offset of the second half in tmB
+  // epilogue
+  void* out;
+  long long ldo;
+  const float* row_scale;      // EPI_SCALE_BF16
+  const float* tok_scale;      // EPI_COMBINE
+  const __nv_bfloat16* yw;     // EPI_COMBINE
+  long long ldyw;
+  const int* row_of;           // EPI_COMBINE: [T, top_k] permuted row or -1
+  int top_k;
+  int out_rows;                // rows of `out` (bounds check)
+  int out_cols;                // columns of `out` (bounds check)
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static size_t bytes(int num_groups) {
+    return 1024 + (size_t)STAGES * STAGE_BYTES + BAR_BYTES + 4 * (size_t)(num_groups + 2);
+  }
+};
+
+struct TileCoord {
+  int g, m, n, ks;
+};
+
+__device__ __forceinline__ void decode_tile(int t, const GemmArgs& p, const int* s_mt,
+                                            TileCoord& c) {
+  const int per = p.n_tiles * p.splits;
+  int g = 0, mt = 0, base = 0;
+  if (p.mtile_start == nullptr) {
+    mt = (p.single_m + GEMM_BM - 1) / GEMM_BM;
+  } else {
+    // The table may be a window of a larger one, so s_mt[0] need not be 0.
+    const int q = t / per + s_mt[0];
+    int lo = 0, hi = p.num_groups - 1;  // largest g with s_mt[g] <= q
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_mt[mid] <= q) lo = mid; else hi = mid - 1;
+    }
+    g = lo;
+    mt = s_mt[g + 1] - s_mt[g];
+    base = (s_mt[g] - s_mt[0]) * per;
+  }
+  const int l = t - base;
+  c.g = g;
+  c.m = l % mt;
+  const int rest = l / mt;
+  c.ks = rest % p.splits;
+  c.n = rest / p.splits;
+}
+
+template <int BN, int STAGES, int EPI, bool TWO_HALVES>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA_sh,
+           const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmB_sh0,
+           const __grid_constant__ CUtensorMap tmB_sh1, const GemmArgs p) {
+  using S = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * S::B_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* s_mt = reinterpret_cast<int*>(bars) + S::BAR_BYTES / 4;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(drain, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (p.mtile_start != nullptr) {
+    for (int i = threadIdx.x; i <= p.num_groups; i += blockDim.x) s_mt[i] = p.mtile_start[i];
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  int total;
+  if (p.mtile_start == nullptr)
+    total = ((p.single_m + GEMM_BM - 1) / GEMM_BM) * p.n_tiles * p.splits;
+  else
+    total = (s_mt[p.num_groups] - s_mt[0]) * p.n_tiles * p.splits;
+  if (p.single_m <= 0 && p.mtile_start == nullptr) total = 0;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (elect_one_sync()) {
+      prefetch_tmap(&tmA);
+      prefetch_tmap(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int t = blockIdx.x; t < total && !*s_abort; t += gridDim.x) {
+        TileCoord c;
+        decode_tile(t, p, s_mt, c);
+        const bool sh = (c.g == p.shared_group);
+        int a_row;
+        if (p.mtile_start == nullptr)
+          a_row = p.single_row_base + c.m * GEMM_BM;
+        else
+          a_row = (sh ? 0 : p.row_start[c.g]) + c.m * GEMM_BM;
+        const void* mapA = sh ? (const void*)&tmA_sh : (const void*)&tmA;
+        const int bdepth = c.g - p.b_group_base;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.status)) { *s_abort = 1; break; }
+          mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
+          const int kc = (c.ks * p.k_blocks + kb) * GEMM_BK;
+          tma_load_2d(sA + stage * S::A_BYTES, mapA, &full[stage], kc, a_row);
+          uint8_t* dB = sB + stage * S::B_BYTES;
+          if (TWO_HALVES) {
+            const int r0 = c.n * (BN / 2);
+            if (sh) {
+              tma_load_3d(dB, &tmB_sh0, &full[stage], kc, r0, 0);
+              tma_load_3d(dB + S::B_BYTES / 2, &tmB_sh1, &full[stage], kc, r0, 0);
+            } else {
+              tma_load_3d(dB, &tmB, &full[stage], kc, r0, bdepth);
+              tma_load_3d(dB + S::B_BYTES / 2, &tmB, &full[stage], kc, r0 + p.b_half_offset,
+                          bdepth);
+            }
+          } else {
+            if (sh)
+              tma_load_3d(dB, &tmB_sh0, &full[stage], kc, c.n * BN, 0);
+            else
+              tma_load_3d(dB, &tmB, &full[stage], kc, c.n * BN, bdepth);
+          }
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (*s_abort) {
+        // Let copies already in flight land before the CTA can exit (bounded).
+        int st = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--st < 0) { st = STAGES - 1; ph ^= 1; }
+          mbar_wait(&full[st], ph, nullptr);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t IDESC = umma_idesc_bf16(GEMM_BM, BN, false, false);
+    if (elect_one_sync()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int buf = 0;
+      uint32_t aphase = 0;
+      bool issued_any = false;
+      for (int t = blockIdx.x; t < total && !*s_abort; t += gridDim.x) {
+        if (!mbar_wait(&tempty[buf], aphase ^ 1, p.status)) { *s_abort = 1; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status)) { *s_abort = 1; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * S::A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * S::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 16; ++k) {
+            const uint64_t ad = umma_desc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = umma_desc_sw128(b0 + k * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (*s_abort) break;
+        umma_commit(&tfull[buf]);
+        buf ^= 1;
+        if (buf == 0) aphase ^= 1;
+      }
+      if (*s_abort && issued_any) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, nullptr);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int quad = warp & 3;             // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    int buf = 0;
+    uint32_t aphase = 0;
+    for (int t = blockIdx.x; t < total && !*s_abort; t += gridDim.x) {
+      TileCoord c;
+      decode_tile(t, p, s_mt, c);
+      if (!mbar_wait(&tfull[buf], aphase, p.status)) { *s_abort = 1; break; }
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * BN;
+
+      // row bookkeeping
+      int valid_rows, out_row;
+      if (p.mtile_start == nullptr) {
+        valid_rows = p.single_m - c.m * GEMM_BM;
+        out_row = c.m * GEMM_BM + row_in_tile;
+      } else {
+        valid_rows = (p.row_start[c.g + 1] - p.row_start[c.g]) - c.m * GEMM_BM;
+        out_row = p.row_start[c.g] + c.m * GEMM_BM + row_in_tile;
+      }
+      const bool row_ok = row_in_tile < valid_rows && out_row < p.out_rows;
+
+      if constexpr (EPI == EPI_SWIGLU) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+        for (int ch = 0; ch < BN / 64; ++ch) {
+          uint32_t g[32], u[32];
+          __syncwarp();
+          tmem_ld32(tbase + ch * 32, g);
+          tmem_ld32(tbase + BN / 2 + ch * 32, u);
+          tmem_wait_ld();
+          const int col = c.n * (BN / 2) + ch * 32;
+          if (row_ok && col + 32 <= p.out_cols) {
+            uint32_t o[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float a0 = silu_f(__uint_as_float(g[2 * i])) * __uint_as_float(u[2 * i]);
+              const float a1 =
+                  silu_f(__uint_as_float(g[2 * i + 1])) * __uint_as_float(u[2 * i + 1]);
+              o[i] = pack_bf16x2(a0, a1);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(out + (long long)out_row * p.ldo + col);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int ch = 0; ch < BN / 32; ++ch) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld32(tbase + ch * 32, v);
+          tmem_wait_ld();
+          const int col = c.n * BN + ch * 32;
+          if (!row_ok || col + 32 > p.out_cols) {
+            // nothing to store for this row / chunk
+          } else if constexpr (EPI == EPI_F32_RED) {
+            float* out = reinterpret_cast<float*>(p.out) + (long long)out_row * p.ldo + col;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              red_add_v4_f32(out + 4 * i, __uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                             __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+          } else {
+            float f[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+            if constexpr (EPI == EPI_SCALE_BF16) {
+              const float s = p.row_scale[out_row];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) f[i] *= s;
+            }
+            if constexpr (EPI == EPI_COMBINE) {
+              const float s = p.tok_scale[out_row];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) f[i] *= s;
+              for (int j = 0; j < p.top_k; ++j) {
+                const int r = p.row_of[(long long)out_row * p.top_k + j];
+                if (r < 0) continue;
+                const uint4* src =
+                    reinterpret_cast<const uint4*>(p.yw + (long long)r * p.ldyw + col);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const uint4 w = src[q];
+                  f[8 * q + 0] += bf16_lo(w.x);
+                  f[8 * q + 1] += bf16_hi(w.x);
+                  f[8 * q + 2] += bf16_lo(w.y);
+                  f[8 * q + 3] += bf16_hi(w.y);
+                  f[8 * q + 4] += bf16_lo(w.z);
+                  f[8 * q + 5] += bf16_hi(w.z);
+                  f[8 * q + 6] += bf16_lo(w.w);
+                  f[8 * q + 7] += bf16_hi(w.w);
+                }
+              }
+            }
+            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+            uint4* dst = reinterpret_cast<uint4*>(out + (long long)out_row * p.ldo + col);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(pack_bf16x2(f[8 * i], f[8 * i + 1]),
+                                  pack_bf16x2(f[8 * i + 2], f[8 * i + 3]),
+                                  pack_bf16x2(f[8 * i + 4], f[8 * i + 5]),
+                                  pack_bf16x2(f[8 * i + 6], f[8 * i + 7]));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+      buf ^= 1;
+      if (buf == 0) aphase ^= 1;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+}
+
+}  // namespace lb

@@ -1,0 +1,64 @@
+// Host-side helpers shared by the C-ABI entry points: error reporting, TMA tensor-map
+// encoding (through the driver entry point, so the library does not link libcuda), and
+// workspace carving.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/layerbatch_b200.h"
+
+namespace lb {
+
+void set_error(const char* fmt, ...);
+int fail(int code, const char* fmt, ...);
+
+// Check a CUDA runtime call; on failure record the error and return LB_ERR_CUDA.
+#define LB_CUDA_CHECK(expr)                                                        \
+  do {                                                                             \
+    cudaError_t _e = (expr);                                                       \
+    if (_e != cudaSuccess)                                                         \
+      return ::lb::fail(LB_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,               \
+                        cudaGetErrorString(_e), __FILE__, __LINE__);               \
+  } while (0)
+
+#define LB_REQUIRE(cond, ...)                                                      \
+  do {                                                                             \
+    if (!(cond)) return ::lb::fail(LB_ERR_INVALID_ARG, __VA_ARGS__);               \
+  } while (0)
+
+// 2-D bf16 tensor map: `rows` x `cols` (cols contiguous), row pitch in elements.
+int make_tmap_bf16_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
+                      uint64_t row_pitch_elems, uint32_t box_rows, uint32_t box_cols);
+// 3-D bf16 tensor map: depth x rows x cols (cols contiguous).
+int make_tmap_bf16_3d(CUtensorMap* m, const void* base, uint64_t depth, uint64_t rows,
+                      uint64_t cols, uint64_t row_pitch_elems, uint64_t depth_pitch_elems,
+                      uint32_t box_rows, uint32_t box_cols);
+
+int num_sms();
+int max_smem_optin();
+
+// Bump allocator over a caller-provided workspace (256-byte aligned sub-buffers).
+struct Carve {
+  uint8_t* base;
+  size_t cap;
+  size_t off = 0;
+  Carve(void* b, size_t c) : base(static_cast<uint8_t*>(b)), cap(c) {}
+  template <class T>
+  T* take(size_t count) {
+    off = (off + 255) & ~size_t(255);
+    T* p = reinterpret_cast<T*>(base ? base + off : nullptr);
+    off += count * sizeof(T);
+    return p;
+  }
+  bool ok() const { return off <= cap; }
+};
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace lb

@@ -1,0 +1,514 @@
+// MoE block on sm_100a: router GEMM -> top-k -> permutation -> grouped SwiGLU GEMM
+// (routed experts + shared expert in one persistent launch) -> grouped down GEMM with the
+// routing weight fused -> shared-expert down GEMM with the sigmoid gate and the weighted
+// combine of the routed rows fused into its epilogue.
+//
+// Packed row layout used by every stage (G = num_local_experts + 1 groups):
+//   rows [0, T)                          group 0: shared expert, token order
+//   rows [row_start[g], row_start[g+1])  group g >= 1: local expert g-1, pairs ordered
+//                                        slot-major then token (torch.where order of
+//                                        nanovllm/models/qwen3_5.py:823-831)
+#include <algorithm>
+#include <cfloat>
+
+#include "lb_gemm_launch.cuh"
+#include "lb_host.h"
+
+namespace lb {
+
+// ------------------------------------------------------------------------------ top-k
+// One warp per token.  Softmax in fp32 over E logits, top-k by (value desc, index asc),
+// renormalisation over the selected k (qwen3_5.py:770-773).  Optionally the shared-expert
+// gate sigmoid(x . w_sg) (qwen3_5.py:903) in fp32.
+template <int VPL>
+__global__ void k_router_topk(const __nv_bfloat16* __restrict__ logits, long long ld, int T,
+                              int E, int k, int32_t* __restrict__ ids, float* __restrict__ wf,
+                              __nv_bfloat16* __restrict__ wb, const __nv_bfloat16* __restrict__ x,
+                              const __nv_bfloat16* __restrict__ wsg, int H,
+                              float* __restrict__ sg) {
+  const int warps_per_block = blockDim.x / 32;
+  const int t = blockIdx.x * warps_per_block + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  const __nv_bfloat16* row = logits + (long long)t * ld;
+  float v[VPL];
+  float m = -FLT_MAX;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? __bfloat162float(row[e]) : -FLT_MAX;
+    m = fmaxf(m, v[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float z = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i)
+    if (lane + 32 * i < E) z += expf(v[i] - m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+
+  unsigned taken = 0;
+  float my_p = 0.f, psum = 0.f;
+  int my_id = 0;
+  for (int j = 0; j < k; ++j) {
+    float best = -FLT_MAX;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && !((taken >> i) & 1u) && v[i] > best) {  // ascending e within a lane
+        best = v[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    const float p = expf(best - m) / z;
+    psum += p;
+    if (lane == j) {
+      my_p = p;
+      my_id = bi;
+    }
+  }
+  if (lane < k) {
+    const float w = my_p / psum;
+    const long long o = (long long)t * k + lane;
+    ids[o] = my_id;
+    if (wf) wf[o] = w;
+    if (wb) wb[o] = __float2bfloat16_rn(w);
+  }
+  if (sg != nullptr) {
+    const __nv_bfloat16* xr = x + (long long)t * H;
+    float acc = 0.f;
+    for (int h = lane * 8; h < H; h += 256) {
+      const uint4 a = *reinterpret_cast<const uint4*>(xr + h);
+      const uint4 b = *reinterpret_cast<const uint4*>(wsg + h);
+      acc += bf16_lo(a.x) * bf16_lo(b.x) + bf16_hi(a.x) * bf16_hi(b.x);
+      acc += bf16_lo(a.y) * bf16_lo(b.y) + bf16_hi(a.y) * bf16_hi(b.y);
+      acc += bf16_lo(a.z) * bf16_lo(b.z) + bf16_hi(a.z) * bf16_hi(b.z);
+      acc += bf16_lo(a.w) * bf16_lo(b.w) + bf16_hi(a.w) * bf16_hi(b.w);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) sg[t] = 1.0f / (1.0f + expf(-acc));
+  }
+}
+
+// ------------------------------------------------------------------------------ permute
+// counts[1+e] += #pairs routed to local expert e (block-local histogram first).
+__global__ void k_moe_count(const int32_t* __restrict__ ids, int n, int expert_base, int nl,
+                            int* __restrict__ counts) {
+  extern __shared__ int hist[];
+  for (int i = threadIdx.x; i < nl; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < n; f += gridDim.x * blockDim.x) {
+    const int e = ids[f] - expert_base;
+    if (e >= 0 && e < nl) atomicAdd(&hist[e], 1);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nl; i += blockDim.x)
+    if (hist[i]) atomicAdd(&counts[1 + i], hist[i]);
+}
+
+// Exclusive scans: row_start[g] and mtile_start[g] (128-row tiles) over G groups, with
+// group 0 (shared expert) holding T rows.  One block of 1024 threads, G <= 2047.
+__global__ void k_moe_scan(const int* __restrict__ counts, int G, int T,
+                           int* __restrict__ row_start, int* __restrict__ mtile_start) {
+  __shared__ int s_rows[1024], s_tiles[1024];
+  const int tid = threadIdx.x;
+  int r[2], tl[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int g = 2 * tid + i;
+    int c = 0;
+    if (g < G) c = (g == 0) ? T : counts[g];
+    r[i] = c;
+    tl[i] = (c + GEMM_BM - 1) / GEMM_BM;
+  }
+  s_rows[tid] = r[0] + r[1];
+  s_tiles[tid] = tl[0] + tl[1];
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    int a = 0, b = 0;
+    if (tid >= off) {
+      a = s_rows[tid - off];
+      b = s_tiles[tid - off];
+    }
+    __syncthreads();
+    s_rows[tid] += a;
+    s_tiles[tid] += b;
+    __syncthreads();
+  }
+  const int ex_r = tid ? s_rows[tid - 1] : 0;
+  const int ex_t = tid ? s_tiles[tid - 1] : 0;
+  if (2 * tid <= G) {
+    row_start[2 * tid] = ex_r;
+    mtile_start[2 * tid] = ex_t;
+  }
+  if (2 * tid + 1 <= G) {
+    row_start[2 * tid + 1] = ex_r + r[0];
+    mtile_start[2 * tid + 1] = ex_t + tl[0];
+  }
+}
+
+// One block per local expert: scan all pairs in (slot, token) order and assign packed
+// rows with a block-wide ballot prefix, so the order is deterministic.
+__global__ void k_moe_scatter(const int32_t* __restrict__ ids, const float* __restrict__ w,
+                              int T, int k, int expert_base, const int* __restrict__ row_start,
+                              int32_t* __restrict__ perm_token, float* __restrict__ perm_w,
+                              int32_t* __restrict__ row_of) {
+  __shared__ int warp_cnt[32];
+  const int g = blockIdx.x + 1;
+  const int e_global = expert_base + blockIdx.x;
+  const int base = row_start[g];
+  const int cnt = row_start[g + 1] - base;
+  if (cnt == 0) return;
+  const int n = T * k;
+  const int lane = threadIdx.x % 32, wid = threadIdx.x / 32, nw = blockDim.x / 32;
+  int running = 0;
+  for (int f0 = 0; f0 < n; f0 += blockDim.x) {
+    const int f = f0 + threadIdx.x;
+    int t = 0, j = 0;
+    bool match = false;
+    if (f < n) {
+      j = f / T;
+      t = f - j * T;
+      match = ids[(long long)t * k + j] == e_global;
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, match);
+    if (lane == 0) warp_cnt[wid] = __popc(bal);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int i = 0; i < nw; ++i) {
+      const int c = warp_cnt[i];
+      if (i < wid) before += c;
+      total += c;
+    }
+    if (match) {
+      const int r = base + running + before + __popc(bal & ((1u << lane) - 1u));
+      perm_token[r] = t;
+      if (perm_w) perm_w[r] = w[(long long)t * k + j];
+      row_of[(long long)t * k + j] = r;
+    }
+    running += total;
+    __syncthreads();
+  }
+}
+
+// Identity map of the shared-expert rows [0, T).
+__global__ void k_iota(int32_t* __restrict__ p, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = i;
+}
+
+// a_packed[r] = x[perm_token[r]] for packed rows r in [T, row_start[G]); 16-byte vectors.
+__global__ void k_gather_rows(const __nv_bfloat16* __restrict__ x, int H,
+                              const int32_t* __restrict__ perm_token,
+                              const int* __restrict__ row_end_ptr, int row_begin,
+                              __nv_bfloat16* __restrict__ a_packed) {
+  const int row_end = *row_end_ptr;
+  const int vec_per_row = H / 8;
+  const long long n = (long long)(row_end - row_begin) * vec_per_row;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int r = row_begin + (int)(i / vec_per_row);
+    const int c = (int)(i % vec_per_row);
+    const int t = perm_token[r];
+    reinterpret_cast<uint4*>(a_packed + (long long)r * H)[c] =
+        reinterpret_cast<const uint4*>(x + (long long)t * H)[c];
+  }
+}
+
+// ------------------------------------------------------------------------------ host
+struct MoeWs {
+  int* status;
+  __nv_bfloat16* logits;
+  int32_t* ids;
+  float* wf;
+  __nv_bfloat16* wb;
+  float* sg;
+  int* counts;
+  int* row_start;
+  int* mtile_start;
+  int32_t* perm_token;
+  float* perm_w;
+  int32_t* row_of;
+  __nv_bfloat16* a_packed;
+  __nv_bfloat16* act;
+  __nv_bfloat16* yw;
+};
+
+static size_t carve_moe(const LbMoeArgs& a, void* base, MoeWs& w) {
+  const size_t T = a.num_tokens, k = a.top_k, H = a.hidden, E = a.num_experts;
+  const size_t nl = a.num_local_experts, I = a.inter;
+  const size_t rows = T + T * k;
+  Carve c(base, ~size_t(0));
+  w.status = c.take<int>(64);
+  w.logits = c.take<__nv_bfloat16>(T * E);
+  w.ids = c.take<int32_t>(T * k);
+  w.wf = c.take<float>(T * k);
+  w.wb = c.take<__nv_bfloat16>(T * k);
+  w.sg = c.take<float>(T);
+  w.counts = c.take<int>(nl + 2);
+  w.row_start = c.take<int>(nl + 2);
+  w.mtile_start = c.take<int>(nl + 2);
+  w.perm_token = c.take<int32_t>(rows);
+  w.perm_w = c.take<float>(rows);
+  w.row_of = c.take<int32_t>(T * k);
+  w.a_packed = c.take<__nv_bfloat16>(rows * H);
+  w.act = c.take<__nv_bfloat16>(rows * I);
+  w.yw = c.take<__nv_bfloat16>(rows * H);
+  return c.off + 256;
+}
+
+static int check_moe(const LbMoeArgs* a) {
+  LB_REQUIRE(a != nullptr, "lb_moe: null args");
+  LB_REQUIRE(a->num_tokens >= 0 && a->num_tokens <= (1 << 20), "lb_moe: num_tokens out of range");
+  LB_REQUIRE(a->hidden > 0 && a->hidden % 64 == 0 && a->hidden <= 16384,
+             "lb_moe: hidden must be a positive multiple of 64 (<= 16384)");
+  LB_REQUIRE(a->num_experts > 0 && a->num_experts <= 1024, "lb_moe: num_experts in [1, 1024]");
+  LB_REQUIRE(a->top_k > 0 && a->top_k <= 32 && a->top_k <= a->num_experts,
+             "lb_moe: top_k in [1, min(32, E)]");
+  LB_REQUIRE(a->inter > 0 && a->inter % 128 == 0, "lb_moe: inter must be a multiple of 128");
+  LB_REQUIRE(a->shared_inter == a->inter,
+             "lb_moe: shared_inter must equal inter (fused shared-expert group)");
+  LB_REQUIRE(a->num_local_experts > 0 && a->num_local_experts <= a->num_experts &&
+                 a->expert_base >= 0 && a->expert_base + a->num_local_experts <= a->num_experts,
+             "lb_moe: local expert range outside [0, E)");
+  LB_REQUIRE(a->num_experts % 32 == 0 || a->num_experts < 32,
+             "lb_moe: num_experts must be a multiple of 32");
+  LB_REQUIRE(a->x && a->w_router && a->w_gate_up && a->w_down && a->w_shared_gate &&
+                 a->w_shared_up && a->w_shared_down && a->w_shared_expert_gate && a->out,
+             "lb_moe: null tensor pointer");
+  LB_REQUIRE(aligned16(a->x) && aligned16(a->w_router) && aligned16(a->w_gate_up) &&
+                 aligned16(a->w_down) && aligned16(a->w_shared_gate) && aligned16(a->w_shared_up) &&
+                 aligned16(a->w_shared_down) && aligned16(a->w_shared_expert_gate) &&
+                 aligned16(a->out),
+             "lb_moe: tensors must be 16-byte aligned");
+  return LB_OK;
+}
+
+static int launch_topk(const __nv_bfloat16* logits, long long ld, int T, int E, int k,
+                       int32_t* ids, float* wf, __nv_bfloat16* wb, const __nv_bfloat16* x,
+                       const __nv_bfloat16* wsg, int H, float* sg, cudaStream_t st) {
+  if (T == 0) return LB_OK;
+  const int threads = 256, wpb = threads / 32;
+  const int grid = (T + wpb - 1) / wpb;
+  const int vpl = (E + 31) / 32;
+#define LB_TOPK_CASE(V)                                                                   \
+  if (vpl <= V) {                                                                         \
+    k_router_topk<V><<<grid, threads, 0, st>>>(logits, ld, T, E, k, ids, wf, wb, x, wsg, H, \
+                                               sg);                                       \
+    LB_CUDA_CHECK(cudaGetLastError());                                                    \
+    return LB_OK;                                                                         \
+  }
+  LB_TOPK_CASE(2)
+  LB_TOPK_CASE(4)
+  LB_TOPK_CASE(8)
+  LB_TOPK_CASE(16)
+  LB_TOPK_CASE(32)
+#undef LB_TOPK_CASE
+  return fail(LB_ERR_UNSUPPORTED, "router top-k: E=%d too large", E);
+}
+
+// Permutation stages shared by lb_moe_permute and lb_moe_forward.
+static int run_permute(const int32_t* ids, const float* wf, int T, int k, int expert_base,
+                       int nl, int* counts, int* row_start, int* mtile_start, int32_t* perm_token,
+                       float* perm_w, int32_t* row_of, cudaStream_t st) {
+  const int G = nl + 1;
+  LB_CUDA_CHECK(cudaMemsetAsync(counts, 0, sizeof(int) * (G + 1), st));
+  LB_CUDA_CHECK(cudaMemsetAsync(row_of, 0xff, sizeof(int32_t) * (size_t)T * k, st));
+  const int n = T * k;
+  if (n > 0) {
+    const int grid = std::min(num_sms() * 2, (n + 1023) / 1024);
+    k_moe_count<<<std::max(grid, 1), 1024, sizeof(int) * nl, st>>>(ids, n, expert_base, nl, counts);
+    LB_CUDA_CHECK(cudaGetLastError());
+  }
+  k_moe_scan<<<1, 1024, 0, st>>>(counts, G, T, row_start, mtile_start);
+  LB_CUDA_CHECK(cudaGetLastError());
+  if (T > 0) {
+    k_iota<<<std::min(1024, (T + 255) / 256), 256, 0, st>>>(perm_token, T);
+    LB_CUDA_CHECK(cudaGetLastError());
+  }
+  if (n > 0) {
+    k_moe_scatter<<<nl, 256, 0, st>>>(ids, wf, T, k, expert_base, row_start, perm_token, perm_w,
+                                      row_of);
+    LB_CUDA_CHECK(cudaGetLastError());
+  }
+  return LB_OK;
+}
+
+}  // namespace lb
+
+using namespace lb;
+
+extern "C" {
+
+int lb_router_topk(const void* logits, int64_t ld, int64_t T, int64_t E, int64_t k, int32_t* ids,
+                   float* weights_f32, void* weights_bf16, void* stream) {
+  LB_REQUIRE(logits && ids, "lb_router_topk: null pointer");
+  LB_REQUIRE(T >= 0 && E > 0 && E <= 1024 && k > 0 && k <= 32 && k <= E && ld >= E,
+             "lb_router_topk: need 0<k<=min(32,E), E<=1024, ld>=E");
+  return launch_topk(static_cast<const __nv_bfloat16*>(logits), ld, (int)T, (int)E, (int)k, ids,
+                     weights_f32, static_cast<__nv_bfloat16*>(weights_bf16), nullptr, nullptr, 0,
+                     nullptr, static_cast<cudaStream_t>(stream));
+}
+
+size_t lb_moe_permute_workspace_size(int64_t T, int64_t k, int64_t nl) {
+  (void)T;
+  (void)k;
+  return 256 + 2 * 256 + sizeof(int) * (size_t)(2 * (nl + 2));
+}
+
+int lb_moe_permute(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base,
+                   int64_t nl, int32_t* row_start, int32_t* perm_token, int32_t* row_of,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  LB_REQUIRE(ids && row_start && perm_token && row_of, "lb_moe_permute: null pointer");
+  LB_REQUIRE(T >= 0 && k > 0 && k <= 32 && nl > 0 && nl <= 2046 && expert_base >= 0,
+             "lb_moe_permute: bad sizes");
+  LB_REQUIRE(T * k < (1ll << 30), "lb_moe_permute: too many pairs");
+  if (!workspace || workspace_bytes < lb_moe_permute_workspace_size(T, k, nl))
+    return fail(LB_ERR_WORKSPACE, "lb_moe_permute: workspace too small");
+  Carve c(workspace, workspace_bytes);
+  c.take<int>(64);  // status word
+  int* counts = c.take<int>(nl + 2);
+  int* mt = c.take<int>(nl + 2);
+  return run_permute(ids, nullptr, (int)T, (int)k, (int)expert_base, (int)nl, counts, row_start,
+                     mt, perm_token, nullptr, row_of, static_cast<cudaStream_t>(stream));
+}
+
+int lb_moe_workspace_size(const LbMoeArgs* a, size_t* bytes) {
+  int rc = check_moe(a);
+  if (rc) return rc;
+  LB_REQUIRE(bytes != nullptr, "lb_moe_workspace_size: null output");
+  MoeWs w;
+  *bytes = carve_moe(*a, nullptr, w);
+  return LB_OK;
+}
+
+int lb_moe_forward(const LbMoeArgs* a, void* stream) {
+  int rc = check_moe(a);
+  if (rc) return rc;
+  MoeWs w;
+  const size_t need = carve_moe(*a, a->workspace, w);
+  if (!a->workspace || a->workspace_bytes < need)
+    return fail(LB_ERR_WORKSPACE, "lb_moe_forward: workspace %zu < %zu bytes",
+                (size_t)a->workspace_bytes, need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int T = (int)a->num_tokens, H = (int)a->hidden, E = (int)a->num_experts;
+  const int k = (int)a->top_k, I = (int)a->inter, nl = (int)a->num_local_experts;
+  const int G = nl + 1;
+  if (T == 0) return LB_OK;
+  const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(a->x);
+  __nv_bfloat16* logits =
+      a->router_logits ? static_cast<__nv_bfloat16*>(a->router_logits) : w.logits;
+  int32_t* ids = a->topk_ids ? a->topk_ids : w.ids;
+  __nv_bfloat16* wb = a->topk_weights ? static_cast<__nv_bfloat16*>(a->topk_weights) : w.wb;
+
+  // 1. router logits [T, E] = x . W_router^T (bf16 out, fp32 accumulate)
+  rc = lb_gemm_bf16(a->x, H, a->w_router, H, logits, E, T, E, H, 0, 1, w.status, stream);
+  if (rc) return rc;
+  // 2. top-k + shared-expert gate
+  rc = launch_topk(logits, E, T, E, k, ids, w.wf, wb, x,
+                   static_cast<const __nv_bfloat16*>(a->w_shared_expert_gate), H, w.sg, st);
+  if (rc) return rc;
+  // 3. permutation
+  rc = run_permute(ids, w.wf, T, k, (int)a->expert_base, nl, w.counts, w.row_start,
+                   w.mtile_start, w.perm_token, w.perm_w, w.row_of, st);
+  if (rc) return rc;
+  {
+    const long long vec = (long long)T * k * (H / 8);
+    const int grid = (int)std::max<long long>(1, std::min<long long>(num_sms() * 8, (vec + 255) / 256));
+    k_gather_rows<<<grid, 256, 0, st>>>(x, H, w.perm_token, w.row_start + G, T, w.a_packed);
+    LB_CUDA_CHECK(cudaGetLastError());
+  }
+  const long long rows = (long long)T + (long long)T * k;
+  const long long max_mtiles = ((long long)T * k) / GEMM_BM + nl + (T + GEMM_BM - 1) / GEMM_BM;
+
+  // 4. grouped gate/up GEMM with SwiGLU: act[rows, I]
+  {
+    constexpr int BN = 256;
+    CUtensorMap tA, tAsh, tB, tB0, tB1;
+    if ((rc = make_tmap_bf16_2d(&tA, w.a_packed, rows, H, H, GEMM_BM, 64))) return rc;
+    if ((rc = make_tmap_bf16_2d(&tAsh, x, T, H, H, GEMM_BM, 64))) return rc;
+    if ((rc = make_tmap_bf16_3d(&tB, a->w_gate_up, nl, 2 * I, H, H, (uint64_t)2 * I * H, BN / 2, 64)))
+      return rc;
+    if ((rc = make_tmap_bf16_3d(&tB0, a->w_shared_gate, 1, I, H, H, (uint64_t)I * H, BN / 2, 64)))
+      return rc;
+    if ((rc = make_tmap_bf16_3d(&tB1, a->w_shared_up, 1, I, H, H, (uint64_t)I * H, BN / 2, 64)))
+      return rc;
+    GemmArgs g = gemm_args_default(w.status);
+    g.mtile_start = w.mtile_start;
+    g.row_start = w.row_start;
+    g.num_groups = G;
+    g.n_tiles = (2 * I) / BN;
+    g.k_blocks = H / 64;
+    g.shared_group = 0;
+    g.b_group_base = 1;
+    g.b_half_offset = I;
+    g.out = w.act;
+    g.ldo = I;
+    g.out_rows = (int)rows;
+    g.out_cols = I;
+    const int grid = (int)std::min<long long>(num_sms(), max_mtiles * g.n_tiles);
+    if ((rc = launch_gemm<BN, 4, EPI_SWIGLU, true>(tA, tAsh, tB, tB0, tB1, g, grid, st))) return rc;
+  }
+  // 5. grouped down GEMM of the routed experts, scaled by the routing weight: yw[rows, H]
+  {
+    constexpr int BN = 256;
+    CUtensorMap tA, tB;
+    if ((rc = make_tmap_bf16_2d(&tA, w.act, rows, I, I, GEMM_BM, 64))) return rc;
+    if ((rc = make_tmap_bf16_3d(&tB, a->w_down, nl, H, I, I, (uint64_t)H * I, BN, 64))) return rc;
+    GemmArgs g = gemm_args_default(w.status);
+    g.mtile_start = w.mtile_start + 1;  // window: groups 1..G-1
+    g.row_start = w.row_start + 1;
+    g.num_groups = nl;
+    g.n_tiles = H / BN;
+    g.k_blocks = I / 64;
+    g.b_group_base = 0;
+    g.row_scale = w.perm_w;
+    g.out = w.yw;
+    g.ldo = H;
+    g.out_rows = (int)rows;
+    g.out_cols = H;
+    const int grid = (int)std::min<long long>(num_sms(), max_mtiles * g.n_tiles);
+    if ((rc = launch_gemm<BN, 4, EPI_SCALE_BF16, false>(tA, tA, tB, tB, tB, g, grid, st))) return rc;
+  }
+  // 6. shared-expert down GEMM; epilogue: out = sigmoid_gate * shared + sum_j yw[row_of]
+  {
+    constexpr int BN = 128;
+    CUtensorMap tA, tB;
+    if ((rc = make_tmap_bf16_2d(&tA, w.act, rows, I, I, GEMM_BM, 64))) return rc;
+    if ((rc = make_tmap_bf16_3d(&tB, a->w_shared_down, 1, H, I, I, (uint64_t)H * I, BN, 64)))
+      return rc;
+    GemmArgs g = gemm_args_default(w.status);
+    g.single_m = T;
+    g.single_row_base = 0;
+    g.n_tiles = H / BN;
+    g.k_blocks = I / 64;
+    g.tok_scale = w.sg;
+    g.yw = w.yw;
+    g.ldyw = H;
+    g.row_of = w.row_of;
+    g.top_k = k;
+    g.out = a->out;
+    g.ldo = H;
+    g.out_rows = T;
+    g.out_cols = H;
+    const long long tiles = (long long)((T + GEMM_BM - 1) / GEMM_BM) * g.n_tiles;
+    const int grid = (int)std::min<long long>(num_sms(), tiles);
+    if ((rc = launch_gemm<BN, 6, EPI_COMBINE, false>(tA, tA, tB, tB, tB, g, grid, st))) return rc;
+  }
+  (void)E;
+  return LB_OK;
+}
+
+}  // extern "C"

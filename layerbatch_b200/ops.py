@@ -1,0 +1,174 @@
+"""Thin torch-facing wrappers over the C ABI (``include/layerbatch_b200.h``).
+
+Tensors are passed by pointer; every call is stream-ordered on the current torch stream,
+allocates nothing inside the library and is CUDA-graph capturable once its workspace has
+been sized (workspaces are cached per device and grown on demand outside capture).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from ._lib import LbMoeArgs, LbPodArgs, check, lib, ptr, stream_ptr
+
+_WS: dict = {}
+
+
+def workspace(nbytes: int, device, tag: str = "default") -> torch.Tensor:
+    """A cached uint8 workspace of at least ``nbytes`` bytes (256-byte header zeroed)."""
+    dev = torch.device(device)
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(), tag)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("workspace must be sized before CUDA-graph capture")
+        buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        _WS[key] = buf
+    return buf
+
+
+def device_status(ws: torch.Tensor, clear: bool = True) -> int:
+    v = C.c_int(0)
+    check(lib().lb_read_device_status(ws.data_ptr(), int(clear), C.byref(v)),
+          "lb_read_device_status")
+    return v.value
+
+
+def _bf16_2d(t, name):
+    if t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a 2-D bf16 tensor with a contiguous last dim")
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
+         accumulate_fp32: bool = False, splits: int = 1) -> torch.Tensor:
+    """``out = a @ b.T`` (bf16) or ``out += a @ b.T`` (fp32 ``out``, split-K allowed)."""
+    _bf16_2d(a, "a")
+    _bf16_2d(b, "b")
+    M, K = a.shape
+    N = b.shape[0]
+    if out is None:
+        out = (torch.zeros if accumulate_fp32 else torch.empty)(
+            M, N, dtype=torch.float32 if accumulate_fp32 else torch.bfloat16, device=a.device)
+    ws = workspace(256, a.device, "gemm")
+    rc = lib().lb_gemm_bf16(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), out.data_ptr(),
+                            out.stride(0), M, N, K, int(accumulate_fp32), splits, ws.data_ptr(),
+                            stream_ptr())
+    check(rc, "lb_gemm_bf16")
+    return out
+
+
+def router_topk(logits: torch.Tensor, k: int):
+    """Top-k of softmax(logits) with lowest-index ties; returns (ids i32, w f32, w bf16)."""
+    _bf16_2d(logits, "logits")
+    T, E = logits.shape
+    ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+    wf = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+    wb = torch.empty(T, k, dtype=torch.bfloat16, device=logits.device)
+    check(lib().lb_router_topk(logits.data_ptr(), logits.stride(0), T, E, k, ids.data_ptr(),
+                               wf.data_ptr(), wb.data_ptr(), stream_ptr()), "lb_router_topk")
+    return ids, wf, wb
+
+
+def moe_permute(ids: torch.Tensor, expert_base: int, num_local_experts: int):
+    """Expert-major permutation; returns (row_start [G+1], perm_token [T+T*k], row_of [T,k])."""
+    T, k = ids.shape
+    ids = ids.to(torch.int32).contiguous()
+    G = num_local_experts + 1
+    dev = ids.device
+    row_start = torch.empty(G + 1, dtype=torch.int32, device=dev)
+    perm_token = torch.full((T + T * k,), -1, dtype=torch.int32, device=dev)
+    row_of = torch.empty(T, k, dtype=torch.int32, device=dev)
+    nbytes = lib().lb_moe_permute_workspace_size(T, k, num_local_experts)
+    ws = workspace(nbytes, dev, "permute")
+    check(lib().lb_moe_permute(ids.data_ptr(), T, k, expert_base, num_local_experts,
+                               row_start.data_ptr(), perm_token.data_ptr(), row_of.data_ptr(),
+                               ws.data_ptr(), ws.numel(), stream_ptr()), "lb_moe_permute")
+    return row_start, perm_token, row_of
+
+
+def moe_forward(x, router, gate_up, down, sh_gate, sh_up, sh_down, sh_gate_w, top_k,
+                out=None, expert_base=0, return_routing=False, ws_tag="moe"):
+    """The full MoE block (router -> experts -> shared expert -> combine) on the GPU."""
+    T, H = x.shape
+    E = router.shape[0]
+    nl, I2, _ = gate_up.shape
+    I = I2 // 2
+    if out is None:
+        out = torch.empty_like(x)
+    for name, t in (("x", x), ("router", router), ("gate_up", gate_up), ("down", down),
+                    ("sh_gate", sh_gate), ("sh_up", sh_up), ("sh_down", sh_down),
+                    ("sh_gate_w", sh_gate_w), ("out", out)):
+        if t.dtype != torch.bfloat16 or not t.is_contiguous() or not t.is_cuda:
+            raise ValueError(f"{name} must be a contiguous CUDA bf16 tensor")
+    logits = ids = wb = None
+    if return_routing:
+        logits = torch.empty(T, E, dtype=torch.bfloat16, device=x.device)
+        ids = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
+        wb = torch.empty(T, top_k, dtype=torch.bfloat16, device=x.device)
+    a = LbMoeArgs(num_tokens=T, hidden=H, num_experts=E, top_k=top_k, inter=I,
+                  shared_inter=sh_gate.shape[0], expert_base=expert_base, num_local_experts=nl,
+                  x=x.data_ptr(), w_router=router.data_ptr(), w_gate_up=gate_up.data_ptr(),
+                  w_down=down.data_ptr(), w_shared_gate=sh_gate.data_ptr(),
+                  w_shared_up=sh_up.data_ptr(), w_shared_down=sh_down.data_ptr(),
+                  w_shared_expert_gate=sh_gate_w.data_ptr(), out=out.data_ptr(),
+                  router_logits=ptr(logits), topk_ids=ptr(ids), topk_weights=ptr(wb))
+    need = C.c_size_t(0)
+    check(lib().lb_moe_workspace_size(C.byref(a), C.byref(need)), "lb_moe_workspace_size")
+    ws = workspace(need.value, x.device, ws_tag)
+    a.workspace = ws.data_ptr()
+    a.workspace_bytes = ws.numel()
+    check(lib().lb_moe_forward(C.byref(a), stream_ptr()), "lb_moe_forward")
+    if return_routing:
+        return out, logits, ids, wb
+    return out
+
+
+def store_kvcache(k, v, k_cache, v_cache, slot_mapping):
+    """``k_cache/v_cache[slot] = k/v`` for slot != -1 (reference attention.py:71-80)."""
+    N = k.shape[0]
+    row = k_cache.shape[-2] * k_cache.shape[-1]
+    if k.stride(-1) != 1 or k.stride(-2) != k.shape[-1] or v.stride(-2) != v.shape[-1]:
+        raise ValueError("k/v heads must be packed ([N, Hkv, D] with D contiguous)")
+    slots = k_cache.numel() // row
+    sm = slot_mapping.to(torch.int32)
+    check(lib().lb_store_kvcache(k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+                                 k_cache.data_ptr(), v_cache.data_ptr(), sm.data_ptr(), N, slots,
+                                 row, stream_ptr()), "lb_store_kvcache")
+
+
+def pod_args(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o, scale,
+             out, attn_out=None, max_q_len=None, kv_split_pages=0) -> LbPodArgs:
+    N, Hq, D = q.shape
+    B = context_lens.numel()
+    nb, ps, Hkv, _ = k_cache.shape
+    if max_q_len is None:
+        max_q_len = N
+    return LbPodArgs(
+        num_seqs=B, num_tokens=N, max_q_len=max_q_len, num_q_heads=Hq, num_kv_heads=Hkv,
+        head_dim=D, page_size=ps, num_pages=nb, max_pages_per_seq=block_tables.shape[1],
+        hidden=w_o.shape[0], sm_scale=float(scale), kv_split_pages=kv_split_pages,
+        q=q.data_ptr(), q_stride_tok=q.stride(0), q_stride_head=q.stride(1),
+        gate=gate.data_ptr(), gate_stride_tok=gate.stride(0), gate_stride_head=gate.stride(1),
+        k_cache=k_cache.data_ptr(), v_cache=v_cache.data_ptr(),
+        block_tables=block_tables.data_ptr(), context_lens=context_lens.data_ptr(),
+        cu_seqlens_q=cu_seqlens_q.data_ptr(), w_o=w_o.data_ptr(), attn_out=ptr(attn_out),
+        out=out.data_ptr(), out_fp32=int(out.dtype == torch.float32))
+
+
+def pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o,
+                   scale, out=None, attn_out=None, max_q_len=None, kv_split_pages=0,
+                   ws_tag="pod"):
+    """Fused paged attention (prefill + decode mixed) -> sigmoid gate -> o_proj."""
+    N = q.shape[0]
+    if out is None:
+        out = torch.empty(N, w_o.shape[0], dtype=torch.bfloat16, device=q.device)
+    a = pod_args(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o, scale,
+                 out, attn_out, max_q_len, kv_split_pages)
+    need = C.c_size_t(0)
+    check(lib().lb_pod_workspace_size(C.byref(a), C.byref(need)), "lb_pod_workspace_size")
+    ws = workspace(need.value, q.device, ws_tag)
+    a.workspace = ws.data_ptr()
+    a.workspace_bytes = ws.numel()
+    check(lib().lb_pod_attn_oproj(C.byref(a), stream_ptr()), "lb_pod_attn_oproj")
+    return out

@@ -1,0 +1,165 @@
+"""CPU oracle of the paged attention + output gate + o_proj tail.
+
+TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``).  Restates:
+
+* ``store_kvcache`` (nanovllm/layers/attention.py:50-80): scatter of new K/V rows into
+  ``[num_blocks, 256, Hkv, D]`` by ``slot_mapping``, skipping slot -1;
+* ``sdpa_decode_paged`` (nanovllm/layers/sdpa_fallback.py:121-159): one query per sequence
+  over its pages;
+* prefill over a cached prefix (attention.py:104-141): causal attention where query i of
+  a chunk of length L on a sequence of context C sits at absolute position C-L+i and sees
+  keys [0, C-L+i].  This is flash-attn's bottom-right causal alignment, the reference's
+  default GPU path (attention.py:124-127).  The reference's SDPA fallback
+  (sdpa_fallback.py:108 via ``_sdpa_one_seq``) passes ``is_causal=True`` to
+  ``F.scaled_dot_product_attention``, which aligns top-left when Sq != Sk; for Sq == Sk
+  (no prefix) both agree, and the golden vectors pin that case;
+* the split-KV online softmax with LSE merge of the POD kernel
+  (nanovllm/layers/pod_kernels.py:102-159 and 205-231), in fp32;
+* ``o * sigmoid(gate)`` then o_proj (nanovllm/models/qwen3_5.py:742-746).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+
+def store_kvcache(k, v, k_cache, v_cache, slot_mapping):
+    """attention.py:50-80: ``cache.flat[slot] = row`` for slot != -1."""
+    nb, bs, hkv, d = k_cache.shape
+    kc = k_cache.view(nb * bs, hkv, d)
+    vc = v_cache.view(nb * bs, hkv, d)
+    for i, s in enumerate(slot_mapping.tolist()):
+        if s == -1:
+            continue
+        kc[s] = k[i]
+        vc[s] = v[i]
+
+
+def gather_pages(cache, table_row, n):
+    """Concatenate the first ``n`` token rows of a sequence's pages -> [n, Hkv, D]."""
+    bs = cache.shape[1]
+    pieces, rem = [], n
+    for blk in table_row[: (n + bs - 1) // bs]:
+        take = min(bs, rem)
+        pieces.append(cache[int(blk), :take])
+        rem -= take
+    return torch.cat(pieces, 0)
+
+
+def _sdpa_one_seq(q, k, v, scale, causal):
+    """sdpa_fallback.py:34-58 restated: [Sq,Hq,D] x [Sk,Hkv,D] -> [Sq,Hq,D]."""
+    hq, hkv = q.shape[1], k.shape[1]
+    qq = q.transpose(0, 1).unsqueeze(0)
+    kk = k.transpose(0, 1).unsqueeze(0)
+    vv = v.transpose(0, 1).unsqueeze(0)
+    if hkv != hq:
+        kk = kk.repeat_interleave(hq // hkv, dim=1)
+        vv = vv.repeat_interleave(hq // hkv, dim=1)
+    o = F.scaled_dot_product_attention(qq, kk, vv, is_causal=causal, scale=scale)
+    return o.squeeze(0).transpose(0, 1)
+
+
+def paged_decode_bf16(q, k_cache, v_cache, block_tables, context_lens, scale):
+    """sdpa_decode_paged restated (sdpa_fallback.py:121-159); returns [B, 1, Hq, D]."""
+    outs = []
+    for i, n in enumerate(context_lens.tolist()):
+        row = block_tables[i].tolist()
+        k = gather_pages(k_cache, row, n)
+        v = gather_pages(v_cache, row, n)
+        outs.append(_sdpa_one_seq(q[i].unsqueeze(0), k, v, scale, causal=False))
+    return torch.stack(outs, 0)
+
+
+def paged_attention(q, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, scale,
+                    dtype=torch.float32):
+    """Mixed prefill + decode attention over paged KV, bottom-right causal.
+
+    ``q`` is ``[N, Hq, D]`` packed by ``cu_seqlens_q``; sequence b owns query rows
+    ``cu[b]:cu[b+1]`` which are its last ``L_b`` positions of ``context_lens[b]``.
+    Computed in ``dtype`` (fp32 by default) with an explicit mask.  Returns ``[N, Hq, D]``.
+    """
+    cu = cu_seqlens_q.tolist()
+    out = torch.empty(q.shape, dtype=dtype)
+    hq = q.shape[1]
+    for b, c in enumerate(context_lens.tolist()):
+        s, e = cu[b], cu[b + 1]
+        L = e - s
+        if L == 0:
+            continue
+        row = block_tables[b].tolist()
+        k = gather_pages(k_cache, row, c).to(dtype)
+        v = gather_pages(v_cache, row, c).to(dtype)
+        hkv = k.shape[1]
+        k = k.repeat_interleave(hq // hkv, dim=1)       # [C, Hq, D]
+        v = v.repeat_interleave(hq // hkv, dim=1)
+        qq = q[s:e].to(dtype)                            # [L, Hq, D]
+        sc = torch.einsum("lhd,chd->hlc", qq, k) * scale
+        qpos = torch.arange(c - L, c).view(L, 1)
+        kpos = torch.arange(c).view(1, c)
+        sc = sc.masked_fill((kpos > qpos).unsqueeze(0), float("-inf"))
+        p = torch.softmax(sc, dim=-1)
+        out[s:e] = torch.einsum("hlc,chd->lhd", p, v)
+    return out
+
+
+def split_kv_decode_fp32(q, k_cache, v_cache, block_tables, context_lens, scale, num_splits):
+    """POD split-KV decode + LSE merge restated in fp32 (pod_kernels.py:102-159, 205-231).
+
+    Split s of a sequence of length n covers ``[s*ceil(n/S), min((s+1)*ceil(n/S), n))``.
+    Returns ``[B, Hq, D]`` fp32.
+    """
+    B, hq, d = q.shape
+    out = torch.zeros(B, hq, d)
+    for b, n in enumerate(context_lens.tolist()):
+        row = block_tables[b].tolist()
+        k = gather_pages(k_cache, row, n).float()
+        v = gather_pages(v_cache, row, n).float()
+        hkv = k.shape[1]
+        k = k.repeat_interleave(hq // hkv, dim=1)
+        v = v.repeat_interleave(hq // hkv, dim=1)
+        per = -(-n // num_splits)
+        acc = torch.zeros(hq, d)
+        e_sum = torch.zeros(hq)
+        e_max = torch.full((hq,), float("-inf"))
+        for s in range(num_splits):
+            lo, hi = per * s, min(per * (s + 1), n)
+            if hi <= lo:
+                continue
+            qk = torch.einsum("hd,chd->hc", q[b].float(), k[lo:hi]) * scale
+            m = qk.max(-1).values
+            p = torch.exp(qk - m[:, None])
+            l = p.sum(-1)
+            o = torch.einsum("hc,chd->hd", p, v[lo:hi]) / l[:, None]
+            lse = m + torch.log(l)
+            n_max = torch.maximum(lse, e_max)
+            old = torch.exp(e_max - n_max)
+            new = torch.exp(lse - n_max)
+            acc = acc * old[:, None] + new[:, None] * o
+            e_sum = e_sum * old + new
+            e_max = n_max
+        out[b] = acc / e_sum[:, None]
+    return out
+
+
+def gate_oproj_bf16(o_flat, gate_flat, w_o):
+    """qwen3_5.py:742-746 at tp=1: ``F.linear(o * sigmoid(gate), W_o)`` in bf16."""
+    return F.linear(o_flat * torch.sigmoid(gate_flat), w_o)
+
+
+def gate_oproj_fp32(o_flat, gate_flat, w_o):
+    return (o_flat.float() * torch.sigmoid(gate_flat.float())) @ w_o.float().t()
+
+
+def attn_oproj_fp32(batch):
+    """The full fused op in fp32 on an ``AttnBatch``: attention -> gate -> o_proj."""
+    o = paged_attention(batch.q, batch.k_cache, batch.v_cache, batch.block_tables,
+                        batch.context_lens, batch.cu_seqlens_q, batch.scale)
+    N = o.shape[0]
+    return gate_oproj_fp32(o.reshape(N, -1), batch.gate.reshape(N, -1), batch.w_o), o
+
+
+def default_scale(head_dim):
+    """qwen3_5.py:638: ``head_dim ** -0.5``."""
+    return head_dim ** -0.5 if head_dim else math.nan
