@@ -1,6 +1,10 @@
-// Paged attention hot path: KV-cache store, POD attention + gated o_proj.
+// Paged attention hot path: KV-cache store, POD attention (prefill + decode in one
+// persistent launch), split merge with the sigmoid output gate, and the o_proj GEMM.
+#include <algorithm>
+
 #include "lb_gemm_launch.cuh"
 #include "lb_host.h"
+#include "lb_pod.cuh"
 
 namespace lb {
 
@@ -26,6 +30,331 @@ __global__ void k_store_kvcache(const __nv_bfloat16* __restrict__ k, long long k
   }
 }
 
+
+// ------------------------------------------------------------------------------ plan
+// One block: per-sequence item counts, block-wide exclusive scans, item lists.
+// Prefill items are emitted latest query tile first (longest causal range first).
+__global__ void k_pod_plan(const int32_t* __restrict__ ctx_lens, const int32_t* __restrict__ cu,
+                           int B, int Hq, int Hkv, int split_tokens, int max_splits,
+                           int max_ctx, int pf_cap, int dec_cap, int4* __restrict__ pf_items,
+                           int* __restrict__ counters, int4* __restrict__ dec_items,
+                           int* __restrict__ status) {
+  __shared__ int s_pf[1024], s_dec[1024];
+  const int tid = threadIdx.x;
+  const int per = (B + 1023) / 1024;
+  const int b0 = min(B, tid * per), b1 = min(B, b0 + per);
+  int npf = 0, ndec = 0;
+  for (int b = b0; b < b1; ++b) {
+    const int qlen = cu[b + 1] - cu[b];
+    const int ctx = ctx_lens[b];
+    if (qlen <= 0 || ctx < qlen || ctx > max_ctx) {
+      if (qlen != 0) report(status, LB_DEV_BAD_INDEX);
+      continue;
+    }
+    if (qlen == 1)
+      ndec += Hkv * min(max_splits, (ctx + split_tokens - 1) / split_tokens);
+    else
+      npf += Hq * ((qlen + POD_KV - 1) / POD_KV);
+  }
+  s_pf[tid] = npf;
+  s_dec[tid] = ndec;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    int a = 0, c = 0;
+    if (tid >= off) {
+      a = s_pf[tid - off];
+      c = s_dec[tid - off];
+    }
+    __syncthreads();
+    s_pf[tid] += a;
+    s_dec[tid] += c;
+    __syncthreads();
+  }
+  int opf = s_pf[tid] - npf, odec = s_dec[tid] - ndec;
+  for (int b = b0; b < b1; ++b) {
+    const int qlen = cu[b + 1] - cu[b];
+    const int ctx = ctx_lens[b];
+    if (qlen <= 0 || ctx < qlen || ctx > max_ctx) continue;
+    if (qlen == 1) {
+      const int ns = min(max_splits, (ctx + split_tokens - 1) / split_tokens);
+      for (int sp = 0; sp < ns; ++sp)
+        for (int h = 0; h < Hkv; ++h) {
+          if (odec < dec_cap) dec_items[odec] = make_int4(b, h, sp, 0);
+          ++odec;
+        }
+    } else {
+      const int nqt = (qlen + POD_KV - 1) / POD_KV;
+      for (int qt = nqt - 1; qt >= 0; --qt)
+        for (int h = 0; h < Hq; ++h) {
+          if (opf < pf_cap) pf_items[opf] = make_int4(b, h, qt, 0);
+          ++opf;
+        }
+    }
+  }
+  if (tid == 1023) {
+    int tp = s_pf[1023], td = s_dec[1023];
+    if (tp > pf_cap || td > dec_cap) report(status, LB_DEV_BAD_INDEX);
+    counters[0] = min(tp, pf_cap);
+    counters[1] = 0;
+    counters[2] = min(td, dec_cap);
+    counters[3] = 0;
+  }
+}
+
+// ------------------------------------------------------------------------------ merge
+// Decode sequences: combine the split partials by their log2-sum-exp, apply
+// sigmoid(gate) and write the bf16 o_proj input row (and optionally the raw output).
+__global__ void k_pod_merge(const int32_t* __restrict__ ctx_lens, const int32_t* __restrict__ cu,
+                            int Hq, int split_tokens, int max_splits, int max_ctx,
+                            const float* __restrict__ part_o, const float* __restrict__ part_lse,
+                            const __nv_bfloat16* __restrict__ gate, long long gst, long long gsh,
+                            __nv_bfloat16* __restrict__ ogated, __nv_bfloat16* __restrict__ attn_out) {
+  extern __shared__ float wts[];  // [max_splits][Hq]
+  const int b = blockIdx.x;
+  const int q0 = cu[b];
+  if (cu[b + 1] - q0 != 1) return;
+  const int ctx = ctx_lens[b];
+  const int ns = (ctx >= 1 && ctx <= max_ctx) ? min(max_splits, (ctx + split_tokens - 1) / split_tokens) : 0;
+  const long long pb = (long long)b * max_splits;
+  for (int h = threadIdx.x; h < Hq; h += blockDim.x) {
+    float m = -INFINITY;
+    for (int s = 0; s < ns; ++s) m = fmaxf(m, part_lse[(pb + s) * Hq + h]);
+    float sum = 0.f;
+    for (int s = 0; s < ns; ++s) {
+      const float w = exp2f(part_lse[(pb + s) * Hq + h] - m);
+      wts[s * Hq + h] = w;
+      sum += w;
+    }
+    const float inv = sum > 0.f ? 1.f / sum : 0.f;
+    for (int s = 0; s < ns; ++s) wts[s * Hq + h] *= inv;
+  }
+  __syncthreads();
+  const int HD = Hq * POD_D;
+  for (int i = threadIdx.x * 8; i < HD; i += blockDim.x * 8) {
+    const int h = i / POD_D, d = i % POD_D;
+    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < ns; ++s) {
+      const float w = wts[s * Hq + h];
+      const float4* src = reinterpret_cast<const float4*>(part_o + ((pb + s) * Hq + h) * POD_D + d);
+      const float4 x0 = src[0], x1 = src[1];
+      o[0] += w * x0.x; o[1] += w * x0.y; o[2] += w * x0.z; o[3] += w * x0.w;
+      o[4] += w * x1.x; o[5] += w * x1.y; o[6] += w * x1.z; o[7] += w * x1.w;
+    }
+    const uint4 g = *reinterpret_cast<const uint4*>(gate + (long long)q0 * gst + (long long)h * gsh + d);
+    const float gv[8] = {bf16_lo(g.x), bf16_hi(g.x), bf16_lo(g.y), bf16_hi(g.y),
+                         bf16_lo(g.z), bf16_hi(g.z), bf16_lo(g.w), bf16_hi(g.w)};
+    uint4 outv;
+    outv.x = pack_bf16x2(o[0] * sigmoid_f(gv[0]), o[1] * sigmoid_f(gv[1]));
+    outv.y = pack_bf16x2(o[2] * sigmoid_f(gv[2]), o[3] * sigmoid_f(gv[3]));
+    outv.z = pack_bf16x2(o[4] * sigmoid_f(gv[4]), o[5] * sigmoid_f(gv[5]));
+    outv.w = pack_bf16x2(o[6] * sigmoid_f(gv[6]), o[7] * sigmoid_f(gv[7]));
+    *reinterpret_cast<uint4*>(ogated + (long long)q0 * HD + i) = outv;
+    if (attn_out) {
+      uint4 r;
+      r.x = pack_bf16x2(o[0], o[1]);
+      r.y = pack_bf16x2(o[2], o[3]);
+      r.z = pack_bf16x2(o[4], o[5]);
+      r.w = pack_bf16x2(o[6], o[7]);
+      *reinterpret_cast<uint4*>(attn_out + (long long)q0 * HD + i) = r;
+    }
+  }
+}
+
+__global__ void k_f32_to_bf16(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst,
+                              long long rows, int cols, long long ld_dst) {
+  const long long n = rows * (cols / 4);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / (cols / 4);
+    const int c = (int)(i % (cols / 4)) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(src + r * cols + c);
+    uint2 o;
+    o.x = pack_bf16x2(v.x, v.y);
+    o.y = pack_bf16x2(v.z, v.w);
+    *reinterpret_cast<uint2*>(dst + r * ld_dst + c) = o;
+  }
+}
+
+// ------------------------------------------------------------------------------ host
+struct PodPlan {
+  int split_tokens, max_splits, max_ctx, pf_cap, dec_cap, gqa, grid, n_pf_ctas;
+};
+
+struct PodWs {
+  int* status;
+  int* counters;
+  int4* pf_items;
+  int4* dec_items;
+  float* part_o;
+  float* part_lse;
+  __nv_bfloat16* ogated;
+  float* o32;
+};
+
+static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
+  LB_REQUIRE(a != nullptr, "lb_pod: null args");
+  LB_REQUIRE(a->head_dim == POD_D, "lb_pod: head_dim must be 256 (got %lld)", (long long)a->head_dim);
+  LB_REQUIRE(a->num_seqs >= 0 && a->num_seqs <= (1 << 20) && a->num_tokens >= 0 &&
+                 a->num_tokens <= (1 << 24),
+             "lb_pod: num_seqs/num_tokens out of range");
+  LB_REQUIRE(a->num_q_heads > 0 && a->num_kv_heads > 0 && a->num_q_heads % a->num_kv_heads == 0 &&
+                 a->num_q_heads / a->num_kv_heads <= 16,
+             "lb_pod: need Hq %% Hkv == 0 and Hq/Hkv <= 16");
+  LB_REQUIRE(a->page_size > 0 && a->page_size % POD_KV == 0,
+             "lb_pod: page_size must be a multiple of 128");
+  LB_REQUIRE(a->num_pages > 0 && a->max_pages_per_seq > 0, "lb_pod: empty KV pool / tables");
+  LB_REQUIRE(a->num_pages * a->page_size < (1ll << 31), "lb_pod: KV pool too large for 32-bit slots");
+  LB_REQUIRE(a->hidden > 0 && a->hidden % 32 == 0, "lb_pod: hidden must be a multiple of 32");
+  LB_REQUIRE(a->q && a->gate && a->k_cache && a->v_cache && a->block_tables && a->context_lens &&
+                 a->cu_seqlens_q && a->w_o && a->out,
+             "lb_pod: null pointer");
+  LB_REQUIRE(aligned16(a->q) && aligned16(a->gate) && aligned16(a->k_cache) &&
+                 aligned16(a->v_cache) && aligned16(a->w_o) && aligned16(a->out) &&
+                 (a->attn_out == nullptr || aligned16(a->attn_out)),
+             "lb_pod: tensors must be 16-byte aligned");
+  LB_REQUIRE(a->q_stride_head % 8 == 0 && a->q_stride_tok % 8 == 0 && a->gate_stride_head % 8 == 0 &&
+                 a->gate_stride_tok % 8 == 0 && a->q_stride_head >= POD_D && a->gate_stride_head >= POD_D,
+             "lb_pod: q/gate strides must be multiples of 8 elements with contiguous heads");
+  const long long HD = a->num_q_heads * POD_D;
+  LB_REQUIRE(HD % 64 == 0, "lb_pod: Hq*D must be a multiple of 64");
+  pl.gqa = (int)(a->num_q_heads / a->num_kv_heads);
+  pl.max_ctx = (int)std::min<long long>(a->max_pages_per_seq * a->page_size, 1ll << 30);
+  const int nsm = num_sms();
+  long long split = a->kv_split_pages > 0 ? (long long)a->kv_split_pages * a->page_size : 0;
+  if (split == 0) {
+    // largest power-of-two page count whose item count (assuming half-full tables)
+    // still gives every SM a few items to balance the tail
+    const long long est_ctx = std::max<long long>(1, pl.max_ctx / 2);
+    long long pages = 1;
+    for (long long pg = 16; pg >= 1; pg >>= 1) {
+      const long long st = pg * a->page_size;
+      const long long items = a->num_seqs * a->num_kv_heads * ((est_ctx + st - 1) / st);
+      if (items >= 4ll * nsm) { pages = pg; break; }
+    }
+    split = pages * a->page_size;
+  }
+  pl.split_tokens = (int)split;
+  pl.max_splits = (int)((pl.max_ctx + split - 1) / split);
+  pl.dec_cap = (int)std::min<long long>(a->num_seqs * a->num_kv_heads * pl.max_splits, 1ll << 30);
+  pl.pf_cap = (int)std::min<long long>(a->num_q_heads * ((a->num_tokens + POD_KV - 1) / POD_KV + a->num_seqs),
+                                       1ll << 30);
+  pl.grid = nsm;
+  pl.n_pf_ctas = a->max_q_len > 1 ? nsm / 2 : 0;
+  if (a->max_q_len > 1 && a->num_tokens >= a->num_seqs) {
+    // estimate the tensor-bound share: prefill rows ~ N - B, each seeing about max_ctx/2 keys
+    const double pf_rows = (double)(a->num_tokens - (a->num_seqs - 1));
+    const double pf_flops = pf_rows * (pl.max_ctx / 2.0) * a->num_q_heads * POD_D * 4.0;
+    const double dec_bytes = (double)(a->num_seqs - 1) * (pl.max_ctx / 2.0) * a->num_kv_heads * POD_D * 4.0;
+    const double t_pf = pf_flops / 1.0e15, t_dec = dec_bytes / 6.0e12;
+    pl.n_pf_ctas = std::max(1, std::min(nsm, (int)(nsm * t_pf / (t_pf + t_dec + 1e-30) + 0.5)));
+  }
+  return LB_OK;
+}
+
+static size_t carve_pod(const LbPodArgs& a, const PodPlan& pl, void* base, PodWs& w) {
+  Carve c(base, ~size_t(0));
+  w.status = c.take<int>(64);
+  w.counters = c.take<int>(4);
+  w.pf_items = c.take<int4>(pl.pf_cap);
+  w.dec_items = c.take<int4>(pl.dec_cap);
+  w.part_o = c.take<float>((size_t)a.num_seqs * pl.max_splits * a.num_q_heads * POD_D);
+  w.part_lse = c.take<float>((size_t)a.num_seqs * pl.max_splits * a.num_q_heads);
+  w.ogated = c.take<__nv_bfloat16>((size_t)a.num_tokens * a.num_q_heads * POD_D);
+  w.o32 = c.take<float>((size_t)a.num_tokens * a.hidden);
+  return c.off + 256;
+}
+
+static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaStream_t st) {
+  const int B = (int)a.num_seqs, N = (int)a.num_tokens;
+  if (B == 0 || N == 0) return LB_OK;
+  int rc;
+  // TMA maps.  K/V: [slots, Hkv, D] boxes of 128 slots x 1 head x 64 dims.  Q: [N, Hq, D];
+  // decode box = 16 heads x 64 dims of one token, prefill box = 128 tokens of one head.
+  CUtensorMap tmK, tmV, tmQd, tmQp;
+  const int qd_rows = (int)std::min<long long>(16, a.num_q_heads);
+  {
+    const uint64_t slots = (uint64_t)(a.num_pages * a.page_size);
+    if ((rc = make_tmap_bf16_3d_box(&tmK, a.k_cache, slots, a.num_kv_heads, POD_D,
+                                    (uint64_t)a.num_kv_heads * POD_D, POD_D, POD_KV, 1, 64)))
+      return rc;
+    if ((rc = make_tmap_bf16_3d_box(&tmV, a.v_cache, slots, a.num_kv_heads, POD_D,
+                                    (uint64_t)a.num_kv_heads * POD_D, POD_D, POD_KV, 1, 64)))
+      return rc;
+    if ((rc = make_tmap_bf16_3d_box(&tmQd, a.q, N, a.num_q_heads, POD_D, a.q_stride_tok,
+                                    a.q_stride_head, 1, qd_rows, 64)))
+      return rc;
+    if ((rc = make_tmap_bf16_3d_box(&tmQp, a.q, N, a.num_q_heads, POD_D, a.q_stride_tok,
+                                    a.q_stride_head, POD_KV, 1, 64)))
+      return rc;
+  }
+  k_pod_plan<<<1, 1024, 0, st>>>(a.context_lens, a.cu_seqlens_q, B, (int)a.num_q_heads,
+                                 (int)a.num_kv_heads, pl.split_tokens, pl.max_splits, pl.max_ctx,
+                                 pl.pf_cap, pl.dec_cap, w.pf_items, w.counters, w.dec_items, w.status);
+  LB_CUDA_CHECK(cudaGetLastError());
+
+  PodParams p{};
+  p.status = w.status;
+  p.pf_items = w.pf_items;
+  p.pf_count = w.counters + 0;
+  p.pf_next = w.counters + 1;
+  p.dec_items = w.dec_items;
+  p.dec_count = w.counters + 2;
+  p.dec_next = w.counters + 3;
+  p.block_tables = a.block_tables;
+  p.bt_stride = a.max_pages_per_seq;
+  p.context_lens = a.context_lens;
+  p.cu_seqlens_q = a.cu_seqlens_q;
+  p.gate = static_cast<const __nv_bfloat16*>(a.gate);
+  p.gate_st = a.gate_stride_tok;
+  p.gate_sh = a.gate_stride_head;
+  p.ogated = w.ogated;
+  p.attn_out = static_cast<__nv_bfloat16*>(a.attn_out);
+  p.part_o = w.part_o;
+  p.part_lse = w.part_lse;
+  p.max_splits = pl.max_splits;
+  p.Hq = (int)a.num_q_heads;
+  p.Hkv = (int)a.num_kv_heads;
+  p.gqa = pl.gqa;
+  p.page_size = (int)a.page_size;
+  p.num_pages = (int)a.num_pages;
+  p.split_tokens = pl.split_tokens;
+  p.n_prefill_ctas = pl.n_pf_ctas;
+  p.scale_log2 = a.sm_scale * 1.4426950408889634f;
+  p.qd_bytes = 4 * qd_rows * 128;
+  LB_CUDA_CHECK(cudaFuncSetAttribute(k_pod_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, POD_SMEM));
+  k_pod_attn<<<pl.grid, POD_THREADS, POD_SMEM, st>>>(tmK, tmV, tmQd, tmQp, p);
+  LB_CUDA_CHECK(cudaGetLastError());
+
+  const size_t merge_smem = sizeof(float) * (size_t)pl.max_splits * a.num_q_heads;
+  LB_REQUIRE(merge_smem <= 48 * 1024, "lb_pod: too many decode splits (%d)", pl.max_splits);
+  k_pod_merge<<<B, 256, merge_smem, st>>>(a.context_lens, a.cu_seqlens_q, (int)a.num_q_heads,
+                                          pl.split_tokens, pl.max_splits, pl.max_ctx, w.part_o,
+                                          w.part_lse, p.gate, a.gate_stride_tok, a.gate_stride_head,
+                                          w.ogated, p.attn_out);
+  LB_CUDA_CHECK(cudaGetLastError());
+
+  // o_proj: out[N, hidden] = ogated[N, Hq*D] . W_o^T
+  const int K = (int)(a.num_q_heads * POD_D), Hd = (int)a.hidden;
+  const int nsm = num_sms();
+  const int mt = (N + GEMM_BM - 1) / GEMM_BM;
+  const int BN = (Hd % 128 == 0) ? 128 : 32;
+  const long long tiles = (long long)mt * (Hd / BN);
+  if (!a.out_fp32 && tiles * 2 >= nsm) {
+    return lb_gemm_bf16(w.ogated, K, a.w_o, K, a.out, Hd, N, Hd, K, 0, 1, w.status, st);
+  }
+  int splits = 1;
+  const int kb = K / 64;
+  while (splits * 2 <= kb && kb % (splits * 2) == 0 && tiles * splits * 2 <= nsm) splits *= 2;
+  float* acc = a.out_fp32 ? static_cast<float*>(a.out) : w.o32;
+  LB_CUDA_CHECK(cudaMemsetAsync(acc, 0, sizeof(float) * (size_t)N * Hd, st));
+  rc = lb_gemm_bf16(w.ogated, K, a.w_o, K, acc, Hd, N, Hd, K, 1, splits, w.status, st);
+  if (rc || a.out_fp32) return rc;
+  const long long n4 = (long long)N * (Hd / 4);
+  const int g = (int)std::max<long long>(1, std::min<long long>(nsm * 4, (n4 + 255) / 256));
+  k_f32_to_bf16<<<g, 256, 0, st>>>(w.o32, static_cast<__nv_bfloat16*>(a.out), N, Hd, Hd);
+  LB_CUDA_CHECK(cudaGetLastError());
+  return LB_OK;
+}
 }  // namespace lb
 
 using namespace lb;
@@ -53,15 +382,25 @@ int lb_store_kvcache(const void* k, int64_t k_stride, const void* v, int64_t v_s
 }
 
 int lb_pod_workspace_size(const LbPodArgs* a, size_t* bytes) {
-  (void)a;
-  (void)bytes;
-  return fail(LB_ERR_UNSUPPORTED, "lb_pod_workspace_size: not built yet");
+  PodPlan pl;
+  int rc = pod_plan_host(a, pl);
+  if (rc) return rc;
+  LB_REQUIRE(bytes != nullptr, "lb_pod_workspace_size: null output");
+  PodWs w;
+  *bytes = carve_pod(*a, pl, nullptr, w);
+  return LB_OK;
 }
 
 int lb_pod_attn_oproj(const LbPodArgs* a, void* stream) {
-  (void)a;
-  (void)stream;
-  return fail(LB_ERR_UNSUPPORTED, "lb_pod_attn_oproj: not built yet");
+  PodPlan pl;
+  int rc = pod_plan_host(a, pl);
+  if (rc) return rc;
+  PodWs w;
+  const size_t need = carve_pod(*a, pl, a->workspace, w);
+  if (!a->workspace || a->workspace_bytes < need)
+    return fail(LB_ERR_WORKSPACE, "lb_pod_attn_oproj: workspace %zu < %zu bytes",
+                (size_t)a->workspace_bytes, need);
+  return pod_run(*a, pl, w, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

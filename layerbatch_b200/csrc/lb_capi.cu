@@ -79,6 +79,15 @@ int make_tmap_bf16_3d(CUtensorMap* m, const void* base, uint64_t depth, uint64_t
   return encode(m, base, 3, dims, strides, box);
 }
 
+int make_tmap_bf16_3d_box(CUtensorMap* m, const void* base, uint64_t d2, uint64_t d1,
+                          uint64_t d0, uint64_t s2_elems, uint64_t s1_elems, uint32_t b2,
+                          uint32_t b1, uint32_t b0) {
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1_elems * 2, s2_elems * 2};
+  cuuint32_t box[3] = {b0, b1, b2};
+  return encode(m, base, 3, dims, strides, box);
+}
+
 int num_sms() {
   int dev = 0, n = 0;
   cudaGetDevice(&dev);

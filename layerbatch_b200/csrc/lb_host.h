@@ -40,6 +40,12 @@ int make_tmap_bf16_3d(CUtensorMap* m, const void* base, uint64_t depth, uint64_t
                       uint64_t cols, uint64_t row_pitch_elems, uint64_t depth_pitch_elems,
                       uint32_t box_rows, uint32_t box_cols);
 
+// General 3-D bf16 tensor map: dims (d2, d1, d0) outermost first, d0 contiguous, strides
+// of dims 2 and 1 in elements, box (b2, b1, b0).
+int make_tmap_bf16_3d_box(CUtensorMap* m, const void* base, uint64_t d2, uint64_t d1,
+                          uint64_t d0, uint64_t s2_elems, uint64_t s1_elems, uint32_t b2,
+                          uint32_t b1, uint32_t b0);
+
 int num_sms();
 int max_smem_optin();
 

@@ -1,0 +1,660 @@
+// POD attention for sm_100a: one persistent launch that runs causal prefill tiles and
+// split-KV decode items over a paged KV cache, side by side on different SMs.
+//
+// Work items come from two device-built queues (k_pod_plan).  A CTA starts in the mode
+// the host assigned to it (prefill for blockIdx < n_prefill_ctas, decode otherwise),
+// drains that queue, then switches once to the other queue, so prefill (tensor-bound)
+// and decode (HBM-bound) items overlap across SMs and the tail is balanced.
+//
+// Roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + tcgen05.mma issuer,
+// warps 2..5 = softmax / epilogue (one thread per TMEM lane).
+//
+// KV tiles are 128 tokens x 256 dims, loaded by TMA as four 64-dim chunks of
+// [128 rows x 128 B] (128B swizzle), the same layout for K and V.  A 128-token tile never
+// crosses a 256-token page, so one page-table lookup addresses a whole tile.
+//
+// Decode item (b, kv_head, split): S^T = K . Q^T (M = 128 tokens, N = 16 q-heads of the
+// GQA group, K = 256) and O^T = V^T . P^T (M = 128 dims x 2, N = 16, K = 128 tokens,
+// V^T read MN-major straight from the V tile).  Online softmax keeps per-head state in
+// the 128 softmax threads; partial O and the log2-sum-exp of each split go to the
+// workspace and k_pod_merge combines them.
+// Prefill item (b, q_head, q_tile): S = Q . K^T (M = 128 queries, N = 128 keys) and
+// O += P . V (N = 256 dims, V MN-major), O accumulating in TMEM with per-row rescaling;
+// bottom-right causal mask; the epilogue applies sigmoid(gate) and writes bf16 rows of
+// the o_proj input.
+#pragma once
+
+#include <cuda.h>
+#include "lb_common.cuh"
+
+namespace lb {
+
+constexpr int POD_THREADS = 192;
+constexpr int POD_KV = 128;          // tokens per K or V tile
+constexpr int POD_D = 256;           // head_dim
+constexpr int POD_CHUNK = POD_KV * 128;          // 16 KB: one 64-dim chunk of a tile
+constexpr int POD_TILE = 4 * POD_CHUNK;          // 64 KB
+constexpr int POD_QD_BYTES = 16 * POD_D * 2;     // 8 KB decode Q (16 head rows)
+constexpr int POD_PD_BYTES = 16 * POD_KV * 2;    // 4 KB decode P^T
+constexpr int POD_QP_BYTES = POD_KV * POD_D * 2; // 64 KB prefill Q
+constexpr int POD_PP_BYTES = POD_KV * POD_KV * 2;// 32 KB prefill P
+constexpr int POD_DATA = 224 * 1024;
+constexpr int POD_MISC = 2048;
+constexpr int POD_SMEM = 1024 + POD_DATA + POD_MISC;
+constexpr int POD_TMEM_COLS = 512;
+constexpr int DEC_SLOTS = 3;
+constexpr int PF_SLOTS = 2;
+
+struct PodParams {
+  int* status;
+  const int4* pf_items;
+  const int* pf_count;
+  int* pf_next;
+  const int4* dec_items;
+  const int* dec_count;
+  int* dec_next;
+  const int32_t* block_tables;
+  long long bt_stride;
+  const int32_t* context_lens;
+  const int32_t* cu_seqlens_q;
+  const __nv_bfloat16* gate;
+  long long gate_st, gate_sh;
+  __nv_bfloat16* ogated;       // [N, Hq*D] gated attention output (o_proj input)
+  __nv_bfloat16* attn_out;     // optional [N, Hq*D] pre-gate attention output
+  float* part_o;               // [B, max_splits, Hq, D]
+  float* part_lse;             // [B, max_splits, Hq]
+  int max_splits;
+  int Hq, Hkv, gqa;
+  int page_size, num_pages;
+  int split_tokens;
+  int n_prefill_ctas;
+  int qd_bytes;                // bytes of one decode Q tile (4 chunks x rows x 128 B)
+  float scale_log2;
+};
+
+struct PodBars {
+  uint64_t kv_full[3], kv_empty[3];
+  uint64_t item_full[2], item_empty[2];
+  uint64_t s_full[2], s_empty[2];
+  uint64_t p_full[2], o_full[2];
+  uint64_t q_empty;
+  uint64_t drain;
+  int4 items[2];
+  uint32_t tmem_base;
+  int abort;
+  float red[2][4][16];
+  float lred[4][16];
+};
+
+struct PodCounters {  // per-role running positions, kept across items and modes
+  uint32_t kv, item, s, o, qp;
+};
+
+__device__ __forceinline__ int kv_page_row(const PodParams& p, int b, int tok) {
+  const int pi = tok / p.page_size;
+  int blk = p.block_tables[(long long)b * p.bt_stride + pi];
+  if (blk < 0 || blk >= p.num_pages) {
+    report(p.status, LB_DEV_BAD_INDEX);
+    blk = 0;
+  }
+  return blk * p.page_size + (tok - pi * p.page_size);
+}
+
+// Load a 128-token K or V tile (4 chunks) for kv head `kvh` starting at token `tok`.
+__device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* map,
+                                             uint64_t* bar, int kvh, int row) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) tma_load_3d(dst + c * POD_CHUNK, map, bar, c * 64, kvh, row);
+}
+
+// Byte offset of element (r, c) in a K-major SW128 tile of 64-element (128 B) rows.
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+  return (uint32_t)(r * 128 + ((((c >> 3) ^ (r & 7)) & 7) << 4) + ((c & 7) << 1));
+}
+
+__global__ void __launch_bounds__(POD_THREADS, 1)
+    k_pod_attn(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+               const __grid_constant__ CUtensorMap tmQd, const __grid_constant__ CUtensorMap tmQp,
+               const PodParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  PodBars* bars = reinterpret_cast<PodBars*>(smem + POD_DATA);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  volatile int* abortp = &bars->abort;
+
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, POD_TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 0) bars->abort = 0;
+  PodCounters cnt = {0, 0, 0, 0, 0};
+
+  const bool pf_first = (int)blockIdx.x < p.n_prefill_ctas;
+  for (int pass = 0; pass < 2; ++pass) {
+    const bool prefill = (pass == 0) ? pf_first : !pf_first;
+    const int nslots = prefill ? PF_SLOTS : DEC_SLOTS;
+    if (threadIdx.x == 0) {
+      for (int i = 0; i < 3; ++i) {
+        mbar_init(&bars->kv_full[i], 1);
+        mbar_init(&bars->kv_empty[i], 1);
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&bars->item_full[i], 1);
+        mbar_init(&bars->item_empty[i], 1);
+        mbar_init(&bars->s_full[i], 1);
+        mbar_init(&bars->s_empty[i], 128);
+        mbar_init(&bars->p_full[i], 128);
+        mbar_init(&bars->o_full[i], 1);
+      }
+      mbar_init(&bars->q_empty, 1);
+      mbar_init(&bars->drain, 1);
+      fence_barrier_init();
+    }
+    cnt = {0, 0, 0, 0, 0};
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    uint8_t* kv_base = smem;  // ring of `nslots` 64 KB tiles
+
+    if (warp == 0) {
+      // ============================================================ producer
+      if (elect_one_sync()) {
+        const int4* items = prefill ? p.pf_items : p.dec_items;
+        const int n_items = *(prefill ? p.pf_count : p.dec_count);
+        int* next = prefill ? p.pf_next : p.dec_next;
+        while (!*abortp) {
+          const int islot = cnt.item & 1;
+          const uint32_t iph = (cnt.item >> 1) & 1;
+          if (!mbar_wait(&bars->item_empty[islot], iph ^ 1, p.status)) { *abortp = 1; break; }
+          const int idx = atomicAdd(next, 1);
+          if (idx >= n_items) {
+            bars->items[islot] = make_int4(-1, 0, 0, 0);
+            mbar_arrive(&bars->item_full[islot]);
+            ++cnt.item;
+            break;
+          }
+          const int4 it = items[idx];
+          bars->items[islot] = it;
+          const int b = it.x;
+          const int ctx = p.context_lens[b];
+          int kvh, t_begin, ntiles;
+          if (prefill) {
+            const int qlen = p.cu_seqlens_q[b + 1] - p.cu_seqlens_q[b];
+            const int h = it.y, qt = it.z;
+            kvh = h / p.gqa;
+            const int kv_end = min(ctx, ctx - qlen + (qt + 1) * POD_KV);
+            t_begin = 0;
+            ntiles = (kv_end + POD_KV - 1) / POD_KV;
+            // the single prefill Q buffer is free once the previous item's S MMAs finish
+            if (!mbar_wait(&bars->q_empty, (cnt.qp & 1) ^ 1, p.status)) { *abortp = 1; break; }
+            ++cnt.qp;
+            uint8_t* qbuf = smem + PF_SLOTS * POD_TILE;
+            const int row0 = p.cu_seqlens_q[b] + qt * POD_KV;
+            mbar_arrive_expect_tx(&bars->item_full[islot], POD_QP_BYTES);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              tma_load_3d(qbuf + c * POD_CHUNK, &tmQp, &bars->item_full[islot], c * 64, h, row0);
+          } else {
+            kvh = it.y;
+            const int split = it.z;
+            t_begin = split * p.split_tokens;
+            const int t_end = min(ctx, t_begin + p.split_tokens);
+            ntiles = (t_end - t_begin + POD_KV - 1) / POD_KV;
+            uint8_t* qbuf = smem + DEC_SLOTS * POD_TILE + islot * POD_QD_BYTES;
+            const int tok = p.cu_seqlens_q[b];
+            mbar_arrive_expect_tx(&bars->item_full[islot], p.qd_bytes);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              tma_load_3d(qbuf + c * 2048, &tmQd, &bars->item_full[islot], c * 64,
+                          kvh * p.gqa, tok);
+          }
+          ++cnt.item;
+          for (int j = 0; j < 2 * ntiles && !*abortp; ++j) {
+            const int slot = cnt.kv % nslots;
+            const uint32_t ph = (cnt.kv / nslots) & 1;
+            if (!mbar_wait(&bars->kv_empty[slot], ph ^ 1, p.status)) { *abortp = 1; break; }
+            const int row = kv_page_row(p, b, t_begin + (j >> 1) * POD_KV);
+            mbar_arrive_expect_tx(&bars->kv_full[slot], POD_TILE);
+            load_kv_tile(kv_base + slot * POD_TILE, (j & 1) ? &tmV : &tmK, &bars->kv_full[slot],
+                         kvh, row);
+            ++cnt.kv;
+          }
+        }
+      }
+    } else if (warp == 1) {
+      // ============================================================ MMA issuer
+      if (elect_one_sync()) {
+        const uint32_t idesc_s = prefill ? umma_idesc_bf16(128, 128, false, false)
+                                         : umma_idesc_bf16(128, 16, false, false);
+        const uint32_t idesc_o = prefill ? umma_idesc_bf16(128, 256, false, true)
+                                         : umma_idesc_bf16(128, 16, true, false);
+        while (!*abortp) {
+          const int islot = cnt.item & 1;
+          const uint32_t iph = (cnt.item >> 1) & 1;
+          if (!mbar_wait(&bars->item_full[islot], iph, p.status)) { *abortp = 1; break; }
+          const int4 it = bars->items[islot];
+          ++cnt.item;
+          if (it.x < 0) break;
+          const int b = it.x;
+          const int ctx = p.context_lens[b];
+          int ntiles;
+          if (prefill) {
+            const int qlen = p.cu_seqlens_q[b + 1] - p.cu_seqlens_q[b];
+            const int kv_end = min(ctx, ctx - qlen + (it.z + 1) * POD_KV);
+            ntiles = (kv_end + POD_KV - 1) / POD_KV;
+          } else {
+            const int t_begin = it.z * p.split_tokens;
+            const int t_end = min(ctx, t_begin + p.split_tokens);
+            ntiles = (t_end - t_begin + POD_KV - 1) / POD_KV;
+          }
+          const uint32_t base = cnt.kv;
+          const uint32_t qaddr = prefill ? smem_u32(smem + PF_SLOTS * POD_TILE)
+                                         : smem_u32(smem + DEC_SLOTS * POD_TILE + islot * POD_QD_BYTES);
+          bool ok = true;
+          for (int j = 0; j <= ntiles && ok; ++j) {
+            if (j < ntiles) {
+              // ---- S_j
+              const uint32_t kp = base + 2 * j;
+              const int ks = kp % nslots;
+              const int sb = cnt.s & 1;
+              if (!mbar_wait(&bars->s_empty[sb], ((cnt.s >> 1) & 1) ^ 1, p.status) ||
+                  !mbar_wait(&bars->kv_full[ks], (kp / nslots) & 1, p.status)) { ok = false; break; }
+              tc_fence_after();
+              const uint32_t kaddr = smem_u32(kv_base + ks * POD_TILE);
+              if (prefill) {
+                const uint32_t d = tmem + sb * 128;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                  for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16(d, umma_desc_sw128(qaddr + c * POD_CHUNK + kk * 32, 16, 1024),
+                              umma_desc_sw128(kaddr + c * POD_CHUNK + kk * 32, 16, 1024), idesc_s,
+                              (c | kk) != 0);
+              } else {
+                const uint32_t d = tmem + sb * 16;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                  for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16(d, umma_desc_sw128(kaddr + c * POD_CHUNK + kk * 32, 16, 1024),
+                              umma_desc_sw128(qaddr + c * 2048 + kk * 32, 16, 1024), idesc_s,
+                              (c | kk) != 0);
+              }
+              umma_commit(&bars->s_full[sb]);
+              umma_commit(&bars->kv_empty[ks]);
+              if (prefill && j == ntiles - 1) umma_commit(&bars->q_empty);
+              ++cnt.s;
+            }
+            if (j > 0) {
+              // ---- PV_{j-1}
+              const int jj = j - 1;
+              const uint32_t vp = base + 2 * jj + 1;
+              const int vs = vp % nslots;
+              const int ob = cnt.o & 1;
+              if (!mbar_wait(&bars->p_full[ob], (cnt.o >> 1) & 1, p.status) ||
+                  !mbar_wait(&bars->kv_full[vs], (vp / nslots) & 1, p.status)) { ok = false; break; }
+              tc_fence_after();
+              const uint32_t vaddr = smem_u32(kv_base + vs * POD_TILE);
+              if (prefill) {
+                const uint32_t paddr = smem_u32(smem + PF_SLOTS * POD_TILE + POD_QP_BYTES);
+                const uint32_t d = tmem + 256;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                  umma_bf16(d,
+                            umma_desc_sw128(paddr + (kk >> 2) * (POD_KV * 128) + (kk & 3) * 32, 16,
+                                            1024),
+                            umma_desc_sw128(vaddr + kk * 2048, POD_CHUNK, 1024), idesc_o,
+                            (jj | kk) != 0);
+              } else {
+                const uint32_t paddr =
+                    smem_u32(smem + DEC_SLOTS * POD_TILE + 2 * POD_QD_BYTES + ob * POD_PD_BYTES);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const uint32_t d = tmem + 32 + ob * 32 + h * 16;
+#pragma unroll
+                  for (int kk = 0; kk < 8; ++kk)
+                    umma_bf16(d, umma_desc_sw128(vaddr + h * 2 * POD_CHUNK + kk * 2048, POD_CHUNK, 1024),
+                              umma_desc_sw128(paddr + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024),
+                              idesc_o, kk != 0);
+                }
+              }
+              umma_commit(&bars->o_full[ob]);
+              umma_commit(&bars->kv_empty[vs]);
+              ++cnt.o;
+            }
+          }
+          cnt.kv = base + 2 * ntiles;
+          if (!ok) { *abortp = 1; break; }
+        }
+        // every commit issued above has arrived once this one has: the barriers can be
+        // re-initialised for the next pass without a late arrive landing on them
+        umma_commit(&bars->drain);
+        mbar_wait(&bars->drain, 0, p.status);
+      }
+    } else {
+      // ============================================================ softmax / epilogue
+      const int quad = warp & 3;
+      const int row = quad * 32 + lane;
+      const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
+      const int tid = threadIdx.x - 64;
+      while (true) {
+        const int islot = cnt.item & 1;
+        const uint32_t iph = (cnt.item >> 1) & 1;
+        if (!mbar_wait(&bars->item_full[islot], iph, p.status)) { *abortp = 1; break; }
+        const int4 it = bars->items[islot];
+        ++cnt.item;
+        if (it.x < 0 || *abortp) break;
+        const int b = it.x;
+        const int ctx = p.context_lens[b];
+        const int q0 = p.cu_seqlens_q[b];
+        const int qlen = p.cu_seqlens_q[b + 1] - q0;
+        bool ok = true;
+        if (prefill) {
+          // ---------------------------------------------------- prefill item
+          const int h = it.y, qt = it.z;
+          const int qrow = qt * POD_KV + row;
+          const bool rvalid = qrow < qlen;
+          const int pos = rvalid ? ctx - qlen + qrow : -1;   // last visible key
+          const int kv_end = min(ctx, ctx - qlen + (qt + 1) * POD_KV);
+          const int ntiles = (kv_end + POD_KV - 1) / POD_KV;
+          float m = -INFINITY, l = 0.f;
+          const uint32_t paddr = smem_u32(smem + PF_SLOTS * POD_TILE + POD_QP_BYTES);
+          const uint32_t kvbase = cnt.kv;
+          cnt.kv += 2 * ntiles;
+          for (int j = 0; j < ntiles; ++j) {
+            const int sb = cnt.s & 1;
+            if (!mbar_wait(&bars->s_full[sb], (cnt.s >> 1) & 1, p.status)) { ok = false; break; }
+            tc_fence_after();
+            float s[128];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+              tmem_ld32(tl + sb * 128 + c * 32, r);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+            }
+            tc_fence_before();
+            mbar_arrive(&bars->s_empty[sb]);
+            ++cnt.s;
+            float mt = -INFINITY;
+            const int k0 = j * POD_KV;
+#pragma unroll
+            for (int i = 0; i < 128; ++i) {
+              const float v = (k0 + i <= pos) ? s[i] * p.scale_log2 : -INFINITY;
+              s[i] = v;
+              mt = fmaxf(mt, v);
+            }
+            const float m_new = fmaxf(m, mt);
+            const float alpha = (m == -INFINITY) ? 1.f : exp2_approx(m - m_new);
+            const float msub = (m_new == -INFINITY) ? 0.f : m_new;
+            float rs = 0.f;
+#pragma unroll
+            for (int i = 0; i < 128; ++i) {
+              s[i] = exp2_approx(s[i] - msub);
+              rs += s[i];
+            }
+            l = l * alpha + rs;
+            m = m_new;
+            // PV_{j-1} must be done before P is overwritten and O rescaled
+            if (j > 0) {
+              const int ob = cnt.o & 1;
+              if (!mbar_wait(&bars->o_full[ob], (cnt.o >> 1) & 1, p.status)) { ok = false; break; }
+              ++cnt.o;
+              tc_fence_after();
+            }
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const uint32_t a = paddr + (c >> 3) * (POD_KV * 128) + sw128_off(row, (c & 7) * 8);
+              st_shared_v4(a, pack_bf16x2(s[c * 8], s[c * 8 + 1]),
+                           pack_bf16x2(s[c * 8 + 2], s[c * 8 + 3]),
+                           pack_bf16x2(s[c * 8 + 4], s[c * 8 + 5]),
+                           pack_bf16x2(s[c * 8 + 6], s[c * 8 + 7]));
+            }
+            // rescale O rows in TMEM (warp-uniform decision: tcgen05.ld/st are collective)
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+              for (int c = 0; c < 8; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tl + 256 + c * 32, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                tmem_st32(tl + 256 + c * 32, r);
+              }
+              tmem_wait_st();
+            }
+            // keys past the context in the last tile may hold stale (even NaN) cache
+            // bytes; P is 0 there, but 0 * NaN would poison O, so zero those V rows
+            if (k0 + POD_KV > ctx) {
+              const uint32_t vp = kvbase + 2 * j + 1;
+              if (!mbar_wait(&bars->kv_full[vp % nslots], (vp / nslots) & 1, p.status)) { ok = false; break; }
+              if (k0 + row >= ctx) {
+                const uint32_t v = smem_u32(kv_base + (vp % nslots) * POD_TILE) + row * 128;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                  for (int u = 0; u < 8; ++u) st_shared_v4(v + c * POD_CHUNK + u * 16, 0, 0, 0, 0);
+              }
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(&bars->p_full[cnt.o & 1]);
+          }
+          if (!ok) { *abortp = 1; break; }
+          // last PV
+          {
+            const int ob = cnt.o & 1;
+            if (!mbar_wait(&bars->o_full[ob], (cnt.o >> 1) & 1, p.status)) { *abortp = 1; break; }
+            ++cnt.o;
+            tc_fence_after();
+          }
+          const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+          const long long tok = (long long)q0 + qrow;
+          const __nv_bfloat16* grow = p.gate + tok * p.gate_st + (long long)h * p.gate_sh;
+          __nv_bfloat16* orow = p.ogated + tok * (long long)(p.Hq * POD_D) + h * POD_D;
+#pragma unroll 1
+          for (int c = 0; c < 8; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tl + 256 + c * 32, r);
+            tmem_wait_ld();
+            if (rvalid) {
+              float o[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(r[i]) * inv_l;
+              if (p.attn_out) {
+                uint4* dst = reinterpret_cast<uint4*>(p.attn_out + tok * (long long)(p.Hq * POD_D) +
+                                                      h * POD_D + c * 32);
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                  dst[q] = make_uint4(pack_bf16x2(o[8 * q], o[8 * q + 1]),
+                                      pack_bf16x2(o[8 * q + 2], o[8 * q + 3]),
+                                      pack_bf16x2(o[8 * q + 4], o[8 * q + 5]),
+                                      pack_bf16x2(o[8 * q + 6], o[8 * q + 7]));
+              }
+              const uint4* gsrc = reinterpret_cast<const uint4*>(grow + c * 32);
+              uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint4 g = gsrc[q];
+                dst[q] = make_uint4(pack_bf16x2(o[8 * q] * sigmoid_f(bf16_lo(g.x)),
+                                                o[8 * q + 1] * sigmoid_f(bf16_hi(g.x))),
+                                    pack_bf16x2(o[8 * q + 2] * sigmoid_f(bf16_lo(g.y)),
+                                                o[8 * q + 3] * sigmoid_f(bf16_hi(g.y))),
+                                    pack_bf16x2(o[8 * q + 4] * sigmoid_f(bf16_lo(g.z)),
+                                                o[8 * q + 5] * sigmoid_f(bf16_hi(g.z))),
+                                    pack_bf16x2(o[8 * q + 6] * sigmoid_f(bf16_lo(g.w)),
+                                                o[8 * q + 7] * sigmoid_f(bf16_hi(g.w))));
+              }
+            }
+          }
+          tc_fence_before();
+        } else {
+          // ---------------------------------------------------- decode item
+          const int kvh = it.y, split = it.z;
+          const int t_begin = split * p.split_tokens;
+          const int t_end = min(ctx, t_begin + p.split_tokens);
+          const int ntiles = (t_end - t_begin + POD_KV - 1) / POD_KV;
+          const uint32_t kvbase = cnt.kv;
+          cnt.kv += 2 * ntiles;
+          float m[16], l[16], a0[16], a1[16], ap[16];
+#pragma unroll
+          for (int h = 0; h < 16; ++h) {
+            m[h] = -INFINITY;
+            l[h] = 0.f;
+            a0[h] = 0.f;
+            a1[h] = 0.f;
+            ap[h] = 1.f;
+          }
+          for (int j = 0; j <= ntiles && ok; ++j) {
+            if (j < ntiles) {
+              const int sb = cnt.s & 1;
+              if (!mbar_wait(&bars->s_full[sb], (cnt.s >> 1) & 1, p.status)) { ok = false; break; }
+              tc_fence_after();
+              uint32_t r[16];
+              tmem_ld16(tl + sb * 16, r);
+              tmem_wait_ld();
+              tc_fence_before();
+              mbar_arrive(&bars->s_empty[sb]);
+              ++cnt.s;
+              const bool valid = t_begin + j * POD_KV + row < t_end;
+              float s[16];
+#pragma unroll
+              for (int h = 0; h < 16; ++h)
+                s[h] = (valid && h < p.gqa) ? __uint_as_float(r[h]) * p.scale_log2 : -INFINITY;
+              // tile max per head across the 128 token rows
+              const int par = j & 1;
+#pragma unroll
+              for (int h = 0; h < 16; ++h) {
+                float v = s[h];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+                if (lane == 0) bars->red[par][quad][h] = v;
+              }
+              named_bar_sync(1, 128);
+              const int ob = cnt.o & 1;
+              const uint32_t pt = smem_u32(smem + DEC_SLOTS * POD_TILE + 2 * POD_QD_BYTES +
+                                           ob * POD_PD_BYTES);
+              float al[16];
+#pragma unroll
+              for (int h = 0; h < 16; ++h) {
+                const float mt = fmaxf(fmaxf(bars->red[par][0][h], bars->red[par][1][h]),
+                                       fmaxf(bars->red[par][2][h], bars->red[par][3][h]));
+                const float mn = fmaxf(m[h], mt);
+                al[h] = (m[h] == -INFINITY) ? 1.f : exp2_approx(m[h] - mn);
+                const float e = (mn == -INFINITY) ? 0.f : exp2_approx(s[h] - mn);
+                l[h] = l[h] * al[h] + e;
+                m[h] = mn;
+                // P^T[h][token]: K-major rows of 128 tokens, two 64-token chunks
+                st_shared_u16(pt + (row >> 6) * 2048 + sw128_off(h, row & 63),
+                              __bfloat16_as_ushort(__float2bfloat16_rn(e)));
+              }
+              // tokens past the end of the last tile: zero their V rows (stale cache bytes
+              // could be NaN, and 0 * NaN would poison O^T)
+              if (t_begin + (j + 1) * POD_KV > t_end) {
+                const uint32_t vp = kvbase + 2 * j + 1;
+                if (!mbar_wait(&bars->kv_full[vp % nslots], (vp / nslots) & 1, p.status)) { ok = false; break; }
+                if (!valid) {
+                  const uint32_t v = smem_u32(kv_base + (vp % nslots) * POD_TILE) + row * 128;
+#pragma unroll
+                  for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) st_shared_v4(v + c * POD_CHUNK + u * 16, 0, 0, 0, 0);
+                }
+              }
+              fence_proxy_async_smem();
+              tc_fence_before();
+              mbar_arrive(&bars->p_full[ob]);
+              if (j > 0) {
+                // accumulate O_{j-1} (scale of tile j-1), deferred behind P_j
+                const int pb = ob ^ 1;
+                if (!mbar_wait(&bars->o_full[pb], ((cnt.o - 1) >> 1) & 1, p.status)) { ok = false; break; }
+                tc_fence_after();
+                uint32_t o0[16], o1[16];
+                tmem_ld16(tl + 32 + pb * 32, o0);
+                tmem_ld16(tl + 32 + pb * 32 + 16, o1);
+                tmem_wait_ld();
+#pragma unroll
+                for (int h = 0; h < 16; ++h) {
+                  a0[h] = a0[h] * ap[h] + __uint_as_float(o0[h]);
+                  a1[h] = a1[h] * ap[h] + __uint_as_float(o1[h]);
+                }
+                tc_fence_before();
+              }
+#pragma unroll
+              for (int h = 0; h < 16; ++h) ap[h] = al[h];
+              ++cnt.o;
+            } else {
+              // final O
+              const int pb = (cnt.o - 1) & 1;
+              if (!mbar_wait(&bars->o_full[pb], ((cnt.o - 1) >> 1) & 1, p.status)) { ok = false; break; }
+              tc_fence_after();
+              uint32_t o0[16], o1[16];
+              tmem_ld16(tl + 32 + pb * 32, o0);
+              tmem_ld16(tl + 32 + pb * 32 + 16, o1);
+              tmem_wait_ld();
+#pragma unroll
+              for (int h = 0; h < 16; ++h) {
+                a0[h] = a0[h] * ap[h] + __uint_as_float(o0[h]);
+                a1[h] = a1[h] * ap[h] + __uint_as_float(o1[h]);
+              }
+              tc_fence_before();
+            }
+          }
+          if (!ok) { *abortp = 1; break; }
+          // row sums across the 128 threads
+#pragma unroll
+          for (int h = 0; h < 16; ++h) {
+            float v = l[h];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) bars->lred[quad][h] = v;
+          }
+          named_bar_sync(1, 128);
+          const long long pbase = ((long long)b * p.max_splits + split) * p.Hq;
+#pragma unroll
+          for (int h = 0; h < 16; ++h) {
+            if (h < p.gqa) {
+              const float ls = bars->lred[0][h] + bars->lred[1][h] + bars->lred[2][h] + bars->lred[3][h];
+              const float inv = ls > 0.f ? 1.f / ls : 0.f;
+              const int hq = kvh * p.gqa + h;
+              float* dst = p.part_o + (pbase + hq) * POD_D;
+              dst[row] = a0[h] * inv;
+              dst[row + 128] = a1[h] * inv;
+              if (tid == h) p.part_lse[pbase + hq] = m[h] + log2f(ls);
+            }
+          }
+        }
+        // item done: release its descriptor / Q slot (all softmax threads are past it)
+        named_bar_sync(1, 128);
+        if (tid == 0) mbar_arrive(&bars->item_empty[islot]);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int i = 0; i < 3; ++i) {
+        mbar_inval(&bars->kv_full[i]);
+        mbar_inval(&bars->kv_empty[i]);
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_inval(&bars->item_full[i]);
+        mbar_inval(&bars->item_empty[i]);
+        mbar_inval(&bars->s_full[i]);
+        mbar_inval(&bars->s_empty[i]);
+        mbar_inval(&bars->p_full[i]);
+        mbar_inval(&bars->o_full[i]);
+      }
+      mbar_inval(&bars->q_empty);
+      mbar_inval(&bars->drain);
+    }
+    __syncthreads();
+    if (*abortp) break;
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(bars->tmem_base, POD_TMEM_COLS);
+  }
+}
+
+}  // namespace lb
