@@ -1,0 +1,453 @@
+#!/usr/bin/env python
+"""Benchmark of the LayerBatch hot path on B200: gated full-attention layer (POD paged
+attention over prefill + decode, sigmoid gate, o_proj) followed by the Qwen3.5 MoE layer.
+
+Default workload (``--config c4``): 512 decode sequences with contexts ~U[1024,16384] plus
+one 4096-token prefill chunk through the attention layer (Hq=16, Hkv=2, D=256, H=2048,
+256-token pages, shuffled block tables), then the MoE layer (E=512 top-10, I=512, one
+shared expert, Zipf(1.1) routing skew) on the step's 4608 tokens.  One step = both layers
+on one batch.  Inputs exceed L2 (the KV cache and expert weights are gigabytes), so no L2
+flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1|c2|c3s|c3l|c4]
+    python bench.py --impl reference ...   # the reference's CPU path (restated) only
+
+Under torchrun every rank runs its own batch (attention data parallel, experts
+replicated): weak scaling, no cross-GPU exchange on the data path.  Rank 0 prints one JSON
+line; the time is the max over ranks of CUDA-event time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "source": "measured"}
+    except Exception:
+        return dict(PEAKS_FALLBACK, source="fallback")
+
+
+# ---------------------------------------------------------------------------- workloads
+CONFIGS = {
+    "c1": "c1: 64 decode seqs ctx~U[512,4096] -> gated paged attention + o_proj 4096->2048",
+    "c2": "c2: 2048-token prefill chunk on a 2048 prefix + 128 decode seqs ctx~U[256,8192] "
+          "-> POD attention + gate + o_proj",
+    "c3s": "c3: MoE E=512 top-10 I=512 +shared, H=2048, T=256 (decode batch), Zipf(1.1)",
+    "c3l": "c3: MoE E=512 top-10 I=512 +shared, H=2048, T=8192 (prefill batch), Zipf(1.1)",
+    "c4": "c4: 512 decode seqs ctx~U[1024,16384] + 4096-token prefill chunk -> gated attention"
+          " + o_proj (Hq16/Hkv2/D256/H2048), then MoE E=512 top-10 I=512 +shared at T=4608, "
+          "Zipf(1.1)",
+}
+
+
+def attn_batch_for(cfg, seed, device):
+    from layerbatch_b200 import workloads as W
+    if cfg == "c1":
+        return W.c1_batch(seed=seed, device=device)
+    if cfg == "c2":
+        return W.c2_batch(seed=seed, device=device)
+    if cfg == "c4":
+        return W.c4_attn_batch(seed=seed, device=device)
+    return None
+
+
+def moe_tokens_for(cfg, attn):
+    if cfg == "c3s":
+        return 256
+    if cfg == "c3l":
+        return 8192
+    if cfg == "c4":
+        return attn.num_tokens
+    return 0
+
+
+def attn_work(b):
+    """Algorithmic FLOPs and bytes of the attention kernel for one batch."""
+    Hq, D = b.q.shape[1], b.q.shape[2]
+    Hkv = b.k_cache.shape[2]
+    kv_tokens = sum(b.ctx_list)
+    pairs = 0
+    for c, L in zip(b.ctx_list, b.qlen_list):
+        # query i of the chunk sees c - L + i + 1 keys
+        pairs += L * (c - L) + L * (L + 1) // 2
+    flops = 4.0 * pairs * Hq * D
+    bytes_ = kv_tokens * Hkv * D * 2 * 2 + 3 * b.num_tokens * Hq * D * 2
+    return flops, bytes_
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running (read-only)."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, index, period=0.01):
+        self.index, self.period = index, period
+        self.samples, self.reasons = [], 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        except Exception:
+            self.ok = False
+        return self
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        rs = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": rs, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------- CPU side
+_CPU_INPUTS: dict = {}
+
+
+def _cached(key, fn):
+    if key not in _CPU_INPUTS:
+        _CPU_INPUTS[key] = fn()
+    return _CPU_INPUTS[key]
+
+
+def cpu_reference_sample(cfg, seed=1):
+    """Time the reference's CPU path (restated in ``oracle/``) on a bounded sample and
+    extrapolate it to one full step of ``cfg``.  Returns (tokens/s, cores, description)."""
+    from layerbatch_b200 import workloads as W
+    from oracle import attention as OA
+    from oracle import moe as OM
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    t_total = 0.0
+    parts = []
+    full_tokens = 0
+    with torch.no_grad():
+        if cfg in ("c1", "c2", "c4"):
+            full = {"c1": (64, (512, 4096), None), "c2": (128, (256, 8192), (2048, 2048)),
+                    "c4": (512, (1024, 16384), (0, 4096))}[cfg]
+            n_dec, (lo, hi), pf = full
+            ns = min(16, n_dec)
+            dec = W.uniform_ctx(ns, lo, hi, seed)
+            b = _cached(("dec", cfg), lambda: W.make_attn_batch(dec, (), seed=seed))
+            t0 = time.perf_counter()
+            o = OA.paged_decode_bf16(b.q, b.k_cache, b.v_cache, b.block_tables, b.context_lens,
+                                     b.scale)
+            OA.gate_oproj_bf16(o.flatten(1, -1), b.gate.reshape(ns, -1), b.w_o)
+            t_dec = (time.perf_counter() - t0) * n_dec / ns
+            parts.append(f"{ns}/{n_dec} decode seqs (x{n_dec / ns:.0f})")
+            t_total += t_dec
+            full_tokens += n_dec
+            if pf is not None:
+                prefix, chunk = pf
+                sc = 512
+                bp = _cached(("pf", cfg), lambda: W.make_attn_batch(
+                    [], [(min(prefix, sc), sc)], seed=seed))
+                t0 = time.perf_counter()
+                o = OA.paged_prefill_bf16(bp.q, bp.k_cache, bp.v_cache, bp.block_tables,
+                                          bp.context_lens, bp.cu_seqlens_q, bp.scale)
+                OA.gate_oproj_bf16(o.reshape(sc, -1), bp.gate.reshape(sc, -1), bp.w_o)
+                dt = time.perf_counter() - t0
+                pairs_s = sc * min(prefix, sc) + sc * (sc + 1) / 2
+                pairs_f = chunk * prefix + chunk * (chunk + 1) / 2
+                t_total += dt * pairs_f / pairs_s
+                parts.append(f"{sc}-token prefill chunk (x{pairs_f / pairs_s:.0f} by causal pairs)")
+                full_tokens += chunk
+        if cfg in ("c3s", "c3l", "c4"):
+            T_full = {"c3s": 256, "c3l": 8192, "c4": 4608}[cfg]
+            Ts = min(256, T_full)
+            def mk():
+                p = W.make_moe_params(2048, 512, 512, 512, 10, seed=0)
+                x = W.make_moe_input(Ts, 2048, seed=seed)
+                W.apply_zipf_bias(p, x)
+                return p, x
+            p, x = _cached(("moe", Ts), mk)
+            t0 = time.perf_counter()
+            OM.moe_block_bf16(x, p, "sparse")
+            dt = time.perf_counter() - t0
+            t_total += dt * T_full / Ts
+            parts.append(f"MoE sparse path at T={Ts} (x{T_full / Ts:.0f})")
+            if cfg != "c4":
+                full_tokens = T_full
+    return full_tokens / t_total, cores, "; ".join(parts) + f"; {cores} threads"
+
+
+# ---------------------------------------------------------------------------- GPU side
+def run_ours(args, rank, world, device):
+    from layerbatch_b200 import ops
+    from layerbatch_b200 import workloads as W
+    cfg = args.config
+    seed = 1 + rank
+    attn = attn_batch_for(cfg, seed, device)
+    T_moe = moe_tokens_for(cfg, attn)
+    moe = None
+    if T_moe:
+        p = W.make_moe_params(2048, 512, 512, 512, 10, seed=0, device=device)
+        x = W.make_moe_input(T_moe, 2048, seed=seed, device=device)
+        W.apply_zipf_bias(p, x)
+        moe = (p, x)
+    tokens = attn.num_tokens if attn is not None else T_moe
+    max_q = max(attn.qlen_list) if attn is not None else 0
+
+    a_out = torch.empty(attn.num_tokens, attn.w_o.shape[0], dtype=torch.bfloat16,
+                        device=device) if attn is not None else None
+    m_out = torch.empty_like(moe[1]) if moe else None
+
+    def step(ev_a=None, ev_m=None, q=None, gate=None, x=None):
+        if attn is not None:
+            ops.pod_attn_oproj(q if q is not None else attn.q, gate if gate is not None else attn.gate,
+                               attn.k_cache, attn.v_cache, attn.block_tables, attn.context_lens,
+                               attn.cu_seqlens_q, attn.w_o, attn.scale, out=a_out,
+                               max_q_len=max_q, events=ev_a)
+        if moe:
+            pm, xm = moe
+            ops.moe_forward(x if x is not None else xm, pm.router, pm.gate_up, pm.down,
+                            pm.sh_gate, pm.sh_up, pm.sh_down, pm.sh_gate_w, 10, out=m_out,
+                            events=ev_m)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    K, Wu = args.steps, args.warmup
+    for _ in range(Wu):
+        step()
+    torch.cuda.synchronize()
+    ev_attn = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K)]
+    ev_moe = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = ops.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        st.record()
+        for i in range(K):
+            step(ev_attn[i] if attn is not None else None, ev_moe[i] if moe else None)
+        en.record()
+        torch.cuda.synchronize()
+    barrier()
+    launches = ops.launch_count() - n0
+    ms = st.elapsed_time(en) / K
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(ms_t)
+    ws_status = 0
+    for tag in ("pod", "moe"):
+        if (torch.cuda.current_device(), tag) in ops._WS:
+            ws_status |= ops.device_status(ops._WS[(torch.cuda.current_device(), tag)])
+
+    res = {"ms": ms, "tokens": tokens, "launches": launches, "clocks": clk.summary(),
+           "device_status": ws_status}
+    peaks = load_peaks()
+    if attn is not None:
+        t_attn = statistics.mean(e[0].elapsed_time(e[1]) for e in ev_attn) * 1e-3
+        flops, byts = attn_work(attn)
+        res["attn"] = {"ms": t_attn * 1e3, "flops": flops, "bytes": byts,
+                       "gbs": byts / t_attn / 1e9, "tflops": flops / t_attn / 1e12}
+    if moe:
+        pm, xm = moe
+        t_g1 = statistics.mean(e[0].elapsed_time(e[1]) for e in ev_moe) * 1e-3
+        t_g2 = statistics.mean(e[2].elapsed_time(e[3]) for e in ev_moe) * 1e-3
+        res["moe_gemm"] = {"gate_up_ms": t_g1 * 1e3, "down_ms": t_g2 * 1e3}
+    res["peaks"] = peaks
+
+    # ---------------- end-to-end through the public API with host buffers
+    if not args.no_e2e:
+        pin = {}
+        if attn is not None:
+            pin["q"] = attn.q.cpu().pin_memory()
+            pin["gate"] = attn.gate.cpu().pin_memory()
+            pin["meta"] = [t.cpu().pin_memory() for t in
+                           (attn.block_tables, attn.context_lens, attn.cu_seqlens_q)]
+            out_a_h = torch.empty(a_out.shape, dtype=a_out.dtype).pin_memory()
+        if moe:
+            pin["x"] = moe[1].cpu().pin_memory()
+            out_m_h = torch.empty(m_out.shape, dtype=m_out.dtype).pin_memory()
+        qd = torch.empty_like(attn.q) if attn is not None else None
+        gd = torch.empty_like(attn.gate) if attn is not None else None
+        xd = torch.empty_like(moe[1]) if moe else None
+        h2d = d2h = 0
+        for v in pin.values():
+            h2d += sum(t.numel() * t.element_size() for t in (v if isinstance(v, list) else [v]))
+        if attn is not None:
+            d2h += out_a_h.numel() * out_a_h.element_size()
+        if moe:
+            d2h += out_m_h.numel() * out_m_h.element_size()
+
+        def e2e_step():
+            if attn is not None:
+                qd.copy_(pin["q"], non_blocking=True)
+                gd.copy_(pin["gate"], non_blocking=True)
+                for dst, src in zip((attn.block_tables, attn.context_lens, attn.cu_seqlens_q),
+                                    pin["meta"]):
+                    dst.copy_(src, non_blocking=True)
+            if moe:
+                xd.copy_(pin["x"], non_blocking=True)
+            step(q=qd, gate=gd, x=xd)
+            if attn is not None:
+                out_a_h.copy_(a_out, non_blocking=True)
+            if moe:
+                out_m_h.copy_(m_out, non_blocking=True)
+
+        for _ in range(max(1, Wu)):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        Ke = max(3, K // 2)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(Ke):
+            e2e_step()
+        e2.record()
+        torch.cuda.synchronize()
+        ms_e = s2.elapsed_time(e2) / Ke
+        mt = torch.tensor([ms_e], dtype=torch.float64, device=device)
+        if world > 1:
+            torch.distributed.all_reduce(mt, op=torch.distributed.ReduceOp.MAX)
+        res["e2e"] = {"ms": float(mt), "h2d": h2d, "d2h": d2h}
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=list(CONFIGS), default="c4")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg_desc = {"workload": CONFIGS[args.config]}
+
+    if args.impl == "reference":
+        # The reference path is CPU code: rank 0 alone times it on the host cores.
+        if rank != 0:
+            return
+        vals = []
+        for i in range(args.warmup + args.steps):
+            v, cores, sample = cpu_reference_sample(args.config)
+            if i >= args.warmup:
+                vals.append(v)
+        v = statistics.median(vals)
+        line = {"metric": "hot-path tokens/s", "value": v, "unit": "tokens/s",
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+                "config": dict(cfg_desc, parallelism="host CPU"), "impl": "reference",
+                "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores,
+                                 "kind": "port", "sample": sample},
+                "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    res = run_ours(args, rank, world, device)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_reference_sample(args.config)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        peaks = res["peaks"]
+        value = res["tokens"] * world / (res["ms"] * 1e-3)
+        roof = None
+        if "attn" in res:
+            a = res["attn"]
+            t_hbm = a["bytes"] / (peaks["hbm_gbs"] * 1e9)
+            t_tc = a["flops"] / (peaks["bf16_tflops"] * 1e12)
+            if t_hbm >= t_tc:
+                roof = {"bound": "hbm", "achieved": a["gbs"], "peak": peaks["hbm_gbs"],
+                        "unit": "GB/s", "frac": a["gbs"] / peaks["hbm_gbs"]}
+            else:
+                roof = {"bound": "tensor", "achieved": a["tflops"], "peak": peaks["bf16_tflops"],
+                        "unit": "TFLOP/s", "frac": a["tflops"] / peaks["bf16_tflops"]}
+            roof.update({"kernel": "k_pod_attn", "traffic": None,
+                         "peak_source": peaks["source"], "kernel_ms": a["ms"],
+                         "algorithmic_bytes": a["bytes"], "algorithmic_flops": a["flops"]})
+        line = {
+            "metric": "hot-path tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["ms"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": dict(cfg_desc, tokens_per_step_per_gpu=res["tokens"],
+                           l2="inputs larger than L2 (KV cache and expert weights are GBs)",
+                           parallelism=(f"dp{world}: per-rank batches, experts replicated"
+                                        if world > 1 else "single GPU")),
+            "roofline": roof, "cpu_baseline": cpu, "clocks": res["clocks"],
+            "gpu_launches": res["launches"],
+        }
+        if "moe_gemm" in res:
+            line["moe_gemm_ms"] = res["moe_gemm"]
+        if "e2e" in res:
+            e = res["e2e"]
+            line["e2e"] = {"value": res["tokens"] * world / (e["ms"] * 1e-3), "unit": "tokens/s",
+                           "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"]}
+        if res["device_status"]:
+            line["device_status"] = res["device_status"]
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -44,6 +44,8 @@ extern "C" {
 
 const char* lb_get_last_error_string(void);
 int lb_version(void);
+/* Total kernels this library has launched in the process (all threads, all devices). */
+unsigned long long lb_kernel_launch_count(void);
 /* Number of SMs and the sm_XY of the current device (for host-side planning). */
 int lb_device_info(int* num_sms, int* sm_version);
 
@@ -109,6 +111,9 @@ typedef struct LbMoeArgs {
   void* topk_weights;        /* optional out [T, k] bf16 */
   void* workspace;
   size_t workspace_bytes;
+  /* optional cudaEvent_t handles recorded on the stream around the grouped gate/up GEMM
+   * ([0], [1]) and the grouped down GEMM ([2], [3]); NULL entries are skipped */
+  void* timing_events[4];
 } LbMoeArgs;
 
 int lb_moe_workspace_size(const LbMoeArgs* args, size_t* bytes);
@@ -154,6 +159,9 @@ typedef struct LbPodArgs {
   int32_t out_fp32;           /* 1: write fp32 o_proj partials (tensor-parallel reduce) */
   void* workspace;
   size_t workspace_bytes;
+  /* optional cudaEvent_t handles recorded around the attention kernel ([0], [1]) and the
+   * o_proj GEMM ([2], [3]); NULL entries are skipped */
+  void* timing_events[4];
 } LbPodArgs;
 
 int lb_pod_workspace_size(const LbPodArgs* args, size_t* bytes);

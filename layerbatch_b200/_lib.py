@@ -18,7 +18,8 @@ ERRORS = {1: "invalid argument", 2: "unsupported", 3: "workspace", 4: "CUDA erro
 
 # Every symbol the header declares (checked by the CPU test suite).
 EXPORTS = [
-    "lb_get_last_error_string", "lb_version", "lb_device_info", "lb_read_device_status",
+    "lb_get_last_error_string", "lb_version", "lb_kernel_launch_count", "lb_device_info",
+    "lb_read_device_status",
     "lb_gemm_workspace_size", "lb_gemm_bf16", "lb_router_topk",
     "lb_moe_permute_workspace_size", "lb_moe_permute", "lb_moe_workspace_size",
     "lb_moe_forward", "lb_store_kvcache", "lb_pod_workspace_size", "lb_pod_attn_oproj",
@@ -38,7 +39,7 @@ class LbMoeArgs(C.Structure):
         ("w_shared_gate", vp), ("w_shared_up", vp), ("w_shared_down", vp),
         ("w_shared_expert_gate", vp), ("out", vp), ("router_logits", vp),
         ("topk_ids", vp), ("topk_weights", vp), ("workspace", vp),
-        ("workspace_bytes", C.c_size_t),
+        ("workspace_bytes", C.c_size_t), ("timing_events", vp * 4),
     ]
 
 
@@ -53,6 +54,7 @@ class LbPodArgs(C.Structure):
         ("k_cache", vp), ("v_cache", vp), ("block_tables", vp), ("context_lens", vp),
         ("cu_seqlens_q", vp), ("w_o", vp), ("attn_out", vp), ("out", vp),
         ("out_fp32", i32), ("workspace", vp), ("workspace_bytes", C.c_size_t),
+        ("timing_events", vp * 4),
     ]
 
 
@@ -68,6 +70,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L = C.CDLL(path)
     L.lb_get_last_error_string.restype = C.c_char_p
     L.lb_gemm_workspace_size.restype = C.c_size_t
+    L.lb_kernel_launch_count.restype = C.c_ulonglong
     L.lb_moe_permute_workspace_size.restype = C.c_size_t
     L.lb_moe_permute_workspace_size.argtypes = [i64, i64, i64]
     L.lb_gemm_bf16.argtypes = [vp, i64, vp, i64, vp, i64, i64, i64, i64, C.c_int, C.c_int, vp, vp]

@@ -290,7 +290,7 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
   k_pod_plan<<<1, 1024, 0, st>>>(a.context_lens, a.cu_seqlens_q, B, (int)a.num_q_heads,
                                  (int)a.num_kv_heads, pl.split_tokens, pl.max_splits, pl.max_ctx,
                                  pl.pf_cap, pl.dec_cap, w.pf_items, w.counters, w.dec_items, w.status);
-  LB_CUDA_CHECK(cudaGetLastError());
+  { int _rc = launched("k_pod_plan"); if (_rc) return _rc; }
 
   PodParams p{};
   p.status = w.status;
@@ -322,8 +322,10 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
   p.scale_log2 = a.sm_scale * 1.4426950408889634f;
   p.qd_bytes = 4 * qd_rows * 128;
   LB_CUDA_CHECK(cudaFuncSetAttribute(k_pod_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, POD_SMEM));
+  record_event(a.timing_events[0], st);
   k_pod_attn<<<pl.grid, POD_THREADS, POD_SMEM, st>>>(tmK, tmV, tmQd, tmQp, p);
-  LB_CUDA_CHECK(cudaGetLastError());
+  { int _rc = launched("k_pod_attn"); if (_rc) return _rc; }
+  record_event(a.timing_events[1], st);
 
   const size_t merge_smem = sizeof(float) * (size_t)pl.max_splits * a.num_q_heads;
   LB_REQUIRE(merge_smem <= 48 * 1024, "lb_pod: too many decode splits (%d)", pl.max_splits);
@@ -331,7 +333,7 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
                                           pl.split_tokens, pl.max_splits, pl.max_ctx, w.part_o,
                                           w.part_lse, p.gate, a.gate_stride_tok, a.gate_stride_head,
                                           w.ogated, p.attn_out);
-  LB_CUDA_CHECK(cudaGetLastError());
+  { int _rc = launched("k_pod_merge"); if (_rc) return _rc; }
 
   // o_proj: out[N, hidden] = ogated[N, Hq*D] . W_o^T
   const int K = (int)(a.num_q_heads * POD_D), Hd = (int)a.hidden;
@@ -339,8 +341,11 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
   const int mt = (N + GEMM_BM - 1) / GEMM_BM;
   const int BN = (Hd % 128 == 0) ? 128 : 32;
   const long long tiles = (long long)mt * (Hd / BN);
+  record_event(a.timing_events[2], st);
   if (!a.out_fp32 && tiles * 2 >= nsm) {
-    return lb_gemm_bf16(w.ogated, K, a.w_o, K, a.out, Hd, N, Hd, K, 0, 1, w.status, st);
+    rc = lb_gemm_bf16(w.ogated, K, a.w_o, K, a.out, Hd, N, Hd, K, 0, 1, w.status, st);
+    record_event(a.timing_events[3], st);
+    return rc;
   }
   int splits = 1;
   const int kb = K / 64;
@@ -348,11 +353,15 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
   float* acc = a.out_fp32 ? static_cast<float*>(a.out) : w.o32;
   LB_CUDA_CHECK(cudaMemsetAsync(acc, 0, sizeof(float) * (size_t)N * Hd, st));
   rc = lb_gemm_bf16(w.ogated, K, a.w_o, K, acc, Hd, N, Hd, K, 1, splits, w.status, st);
-  if (rc || a.out_fp32) return rc;
+  if (rc || a.out_fp32) {
+    record_event(a.timing_events[3], st);
+    return rc;
+  }
   const long long n4 = (long long)N * (Hd / 4);
   const int g = (int)std::max<long long>(1, std::min<long long>(nsm * 4, (n4 + 255) / 256));
   k_f32_to_bf16<<<g, 256, 0, st>>>(w.o32, static_cast<__nv_bfloat16*>(a.out), N, Hd, Hd);
-  LB_CUDA_CHECK(cudaGetLastError());
+  { int _rc = launched("k_f32_to_bf16"); if (_rc) return _rc; }
+  record_event(a.timing_events[3], st);
   return LB_OK;
 }
 }  // namespace lb
@@ -377,7 +386,7 @@ int lb_store_kvcache(const void* k, int64_t k_stride, const void* v, int64_t v_s
       static_cast<const __nv_bfloat16*>(k), k_stride, static_cast<const __nv_bfloat16*>(v),
       v_stride, static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),
       slot_mapping, (int)N, num_slots, (int)row_elems);
-  LB_CUDA_CHECK(cudaGetLastError());
+  { int _rc = launched("k_store_kvcache"); if (_rc) return _rc; }
   return LB_OK;
 }
 

@@ -1,5 +1,6 @@
 // C-ABI plumbing: error strings, device info, TMA descriptor encoding, the generic GEMM
 // entry point and the device status word.
+#include <atomic>
 #include <cstdarg>
 #include <cstring>
 #include <mutex>
@@ -88,6 +89,19 @@ int make_tmap_bf16_3d_box(CUtensorMap* m, const void* base, uint64_t d2, uint64_
   return encode(m, base, 3, dims, strides, box);
 }
 
+static std::atomic<unsigned long long> g_launches{0};
+
+int launched(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(LB_ERR_CUDA, "launch of %s failed: %s", what, cudaGetErrorString(e));
+  return LB_OK;
+}
+
+void record_event(void* ev, cudaStream_t st) {
+  if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev), st);
+}
+
 int num_sms() {
   int dev = 0, n = 0;
   cudaGetDevice(&dev);
@@ -111,6 +125,8 @@ extern "C" {
 const char* lb_get_last_error_string(void) { return g_err; }
 
 int lb_version(void) { return 100; }
+
+unsigned long long lb_kernel_launch_count(void) { return g_launches.load(); }
 
 int lb_device_info(int* n_sms, int* sm_version) {
   int dev = 0;

@@ -18,7 +18,7 @@ int launch_gemm(const CUtensorMap& tA, const CUtensorMap& tAsh, const CUtensorMa
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   if (grid <= 0) return LB_OK;
   kern<<<grid, GEMM_THREADS, smem, st>>>(tA, tAsh, tB, tBsh0, tBsh1, a);
-  LB_CUDA_CHECK(cudaGetLastError());
+  { int _rc = launched("kern"); if (_rc) return _rc; }
   return LB_OK;
 }
 

@@ -46,6 +46,10 @@ int make_tmap_bf16_3d_box(CUtensorMap* m, const void* base, uint64_t d2, uint64_
                           uint64_t d0, uint64_t s2_elems, uint64_t s1_elems, uint32_t b2,
                           uint32_t b1, uint32_t b0);
 
+// Count one kernel launch of this library and check the launch error.
+int launched(const char* what);
+void record_event(void* ev, cudaStream_t st);
+
 int num_sms();
 int max_smem_optin();
 

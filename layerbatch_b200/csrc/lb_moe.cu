@@ -307,7 +307,7 @@ static int launch_topk(const __nv_bfloat16* logits, long long ld, int T, int E, 
   if (vpl <= V) {                                                                         \
     k_router_topk<V><<<grid, threads, 0, st>>>(logits, ld, T, E, k, ids, wf, wb, x, wsg, H, \
                                                sg);                                       \
-    LB_CUDA_CHECK(cudaGetLastError());                                                    \
+    { int _rc = launched("k_router_topk"); if (_rc) return _rc; }                                          \
     return LB_OK;                                                                         \
   }
   LB_TOPK_CASE(2)
@@ -330,18 +330,18 @@ static int run_permute(const int32_t* ids, const float* wf, int T, int k, int ex
   if (n > 0) {
     const int grid = std::min(num_sms() * 2, (n + 1023) / 1024);
     k_moe_count<<<std::max(grid, 1), 1024, sizeof(int) * nl, st>>>(ids, n, expert_base, nl, counts);
-    LB_CUDA_CHECK(cudaGetLastError());
+    { int _rc = launched("k_moe_count"); if (_rc) return _rc; }
   }
   k_moe_scan<<<1, 1024, 0, st>>>(counts, G, T, row_start, mtile_start);
-  LB_CUDA_CHECK(cudaGetLastError());
+  { int _rc = launched("k_moe_scan"); if (_rc) return _rc; }
   if (T > 0) {
     k_iota<<<std::min(1024, (T + 255) / 256), 256, 0, st>>>(perm_token, T);
-    LB_CUDA_CHECK(cudaGetLastError());
+    { int _rc = launched("k_iota"); if (_rc) return _rc; }
   }
   if (n > 0) {
     k_moe_scatter<<<nl, 256, 0, st>>>(ids, wf, T, k, expert_base, row_start, perm_token, perm_w,
                                       row_of);
-    LB_CUDA_CHECK(cudaGetLastError());
+    { int _rc = launched("k_moe_scatter"); if (_rc) return _rc; }
   }
   return LB_OK;
 }
@@ -428,7 +428,7 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
     const long long vec = (long long)T * k * (H / 8);
     const int grid = (int)std::max<long long>(1, std::min<long long>(num_sms() * 8, (vec + 255) / 256));
     k_gather_rows<<<grid, 256, 0, st>>>(x, H, w.perm_token, w.row_start + G, T, w.a_packed);
-    LB_CUDA_CHECK(cudaGetLastError());
+    { int _rc = launched("k_gather_rows"); if (_rc) return _rc; }
   }
   const long long rows = (long long)T + (long long)T * k;
   const long long max_mtiles = ((long long)T * k) / GEMM_BM + nl + (T + GEMM_BM - 1) / GEMM_BM;
@@ -459,7 +459,9 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
     g.out_rows = (int)rows;
     g.out_cols = I;
     const int grid = (int)std::min<long long>(num_sms(), max_mtiles * g.n_tiles);
+    record_event(a->timing_events[0], st);
     if ((rc = launch_gemm<BN, 4, EPI_SWIGLU, true>(tA, tAsh, tB, tB0, tB1, g, grid, st))) return rc;
+    record_event(a->timing_events[1], st);
   }
   // 5. grouped down GEMM of the routed experts, scaled by the routing weight: yw[rows, H]
   {
@@ -480,7 +482,9 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
     g.out_rows = (int)rows;
     g.out_cols = H;
     const int grid = (int)std::min<long long>(num_sms(), max_mtiles * g.n_tiles);
+    record_event(a->timing_events[2], st);
     if ((rc = launch_gemm<BN, 4, EPI_SCALE_BF16, false>(tA, tA, tB, tB, tB, g, grid, st))) return rc;
+    record_event(a->timing_events[3], st);
   }
   // 6. shared-expert down GEMM; epilogue: out = sigmoid_gate * shared + sum_j yw[row_of]
   {

@@ -28,6 +28,21 @@ def workspace(nbytes: int, device, tag: str = "default") -> torch.Tensor:
     return buf
 
 
+def launch_count() -> int:
+    """Kernels launched by the CUDA library so far in this process."""
+    return int(lib().lb_kernel_launch_count())
+
+
+def _events(a, events):
+    """Attach up to four recorded torch.cuda.Event handles to an args struct."""
+    if events:
+        for i, e in enumerate(events[:4]):
+            if e is not None:
+                if not e.cuda_event:
+                    e.record()  # creates the underlying CUDA event
+                a.timing_events[i] = e.cuda_event
+
+
 def device_status(ws: torch.Tensor, clear: bool = True) -> int:
     v = C.c_int(0)
     check(lib().lb_read_device_status(ws.data_ptr(), int(clear), C.byref(v)),
@@ -88,7 +103,7 @@ def moe_permute(ids: torch.Tensor, expert_base: int, num_local_experts: int):
 
 
 def moe_forward(x, router, gate_up, down, sh_gate, sh_up, sh_down, sh_gate_w, top_k,
-                out=None, expert_base=0, return_routing=False, ws_tag="moe"):
+                out=None, expert_base=0, return_routing=False, ws_tag="moe", events=None):
     """The full MoE block (router -> experts -> shared expert -> combine) on the GPU."""
     T, H = x.shape
     E = router.shape[0]
@@ -113,6 +128,7 @@ def moe_forward(x, router, gate_up, down, sh_gate, sh_up, sh_down, sh_gate_w, to
                   w_shared_up=sh_up.data_ptr(), w_shared_down=sh_down.data_ptr(),
                   w_shared_expert_gate=sh_gate_w.data_ptr(), out=out.data_ptr(),
                   router_logits=ptr(logits), topk_ids=ptr(ids), topk_weights=ptr(wb))
+    _events(a, events)
     need = C.c_size_t(0)
     check(lib().lb_moe_workspace_size(C.byref(a), C.byref(need)), "lb_moe_workspace_size")
     ws = workspace(need.value, x.device, ws_tag)
@@ -158,13 +174,14 @@ def pod_args(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q
 
 def pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o,
                    scale, out=None, attn_out=None, max_q_len=None, kv_split_pages=0,
-                   ws_tag="pod"):
+                   ws_tag="pod", events=None):
     """Fused paged attention (prefill + decode mixed) -> sigmoid gate -> o_proj."""
     N = q.shape[0]
     if out is None:
         out = torch.empty(N, w_o.shape[0], dtype=torch.bfloat16, device=q.device)
     a = pod_args(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o, scale,
                  out, attn_out, max_q_len, kv_split_pages)
+    _events(a, events)
     need = C.c_size_t(0)
     check(lib().lb_pod_workspace_size(C.byref(a), C.byref(need)), "lb_pod_workspace_size")
     ws = workspace(need.value, q.device, ws_tag)

@@ -72,6 +72,33 @@ def paged_decode_bf16(q, k_cache, v_cache, block_tables, context_lens, scale):
     return torch.stack(outs, 0)
 
 
+def paged_prefill_bf16(q, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, scale):
+    """``sdpa_prefill_varlen`` with block tables restated (sdpa_fallback.py:61-118), bf16.
+
+    The reference gathers each sequence's pages and calls SDPA with ``is_causal=True``;
+    here the mask is given explicitly in bottom-right form so that a chunk on a cached
+    prefix sees the prefix (identical to the reference when there is no prefix).
+    """
+    cu = cu_seqlens_q.tolist()
+    out = torch.empty_like(q)
+    for b, c in enumerate(context_lens.tolist()):
+        s, e = cu[b], cu[b + 1]
+        L = e - s
+        if L == 0:
+            continue
+        row = block_tables[b].tolist()
+        k = gather_pages(k_cache, row, c)
+        v = gather_pages(v_cache, row, c)
+        hq, hkv = q.shape[1], k.shape[1]
+        qq = q[s:e].transpose(0, 1).unsqueeze(0)
+        kk = k.transpose(0, 1).unsqueeze(0).repeat_interleave(hq // hkv, dim=1)
+        vv = v.transpose(0, 1).unsqueeze(0).repeat_interleave(hq // hkv, dim=1)
+        mask = torch.arange(c).view(1, c) <= torch.arange(c - L, c).view(L, 1)
+        o = F.scaled_dot_product_attention(qq, kk, vv, attn_mask=mask, scale=scale)
+        out[s:e] = o.squeeze(0).transpose(0, 1)
+    return out
+
+
 def paged_attention(q, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, scale,
                     dtype=torch.float32):
     """Mixed prefill + decode attention over paged KV, bottom-right causal.
