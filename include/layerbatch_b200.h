@@ -87,6 +87,20 @@ int lb_moe_permute(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base
                    int64_t num_local_experts, int32_t* row_start, int32_t* perm_token,
                    int32_t* row_of, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same permutation for callers that cannot allocate device memory (no workspace):
+ * a plugin host whose enqueue hook forbids allocation, code that runs while a stream is
+ * being captured into a CUDA graph under a no-allocation policy, or a foreign-language
+ * binding without a device allocator.  No counterpart in the reference (which allocates
+ * with torch inside the MoE module).  Scratch is a fixed 8,464-byte array in the
+ * library's static device memory, held by every GPU that loads the library until exit.
+ * Limit: num_local_experts <= 1024 (larger returns LB_ERR_UNSUPPORTED).  The first call
+ * on each device looks up that array's address (cudaGetSymbolAddress) and caches it; make
+ * that first call before any stream capture.  All calls on a device share the array, so
+ * calls that overlap on the GPU (different streams, no ordering between them) race. */
+int lb_moe_permute_noalloc(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base,
+                           int64_t num_local_experts, int32_t* row_start, int32_t* perm_token,
+                           int32_t* row_of, void* stream);
+
 /* ---------------------------------------------------------------- MoE block */
 typedef struct LbMoeArgs {
   int64_t num_tokens;        /* T */

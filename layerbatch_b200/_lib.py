@@ -21,7 +21,8 @@ EXPORTS = [
     "lb_get_last_error_string", "lb_version", "lb_kernel_launch_count", "lb_device_info",
     "lb_read_device_status",
     "lb_gemm_workspace_size", "lb_gemm_bf16", "lb_router_topk",
-    "lb_moe_permute_workspace_size", "lb_moe_permute", "lb_moe_workspace_size",
+    "lb_moe_permute_workspace_size", "lb_moe_permute", "lb_moe_permute_noalloc",
+    "lb_moe_workspace_size",
     "lb_moe_forward", "lb_store_kvcache", "lb_pod_workspace_size", "lb_pod_attn_oproj",
 ]
 
@@ -76,6 +77,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.lb_gemm_bf16.argtypes = [vp, i64, vp, i64, vp, i64, i64, i64, i64, C.c_int, C.c_int, vp, vp]
     L.lb_router_topk.argtypes = [vp, i64, i64, i64, i64, vp, vp, vp, vp]
     L.lb_moe_permute.argtypes = [vp, i64, i64, i64, i64, vp, vp, vp, vp, C.c_size_t, vp]
+    L.lb_moe_permute_noalloc.argtypes = [vp, i64, i64, i64, i64, vp, vp, vp, vp]
     L.lb_moe_workspace_size.argtypes = [C.POINTER(LbMoeArgs), C.POINTER(C.c_size_t)]
     L.lb_moe_forward.argtypes = [C.POINTER(LbMoeArgs), vp]
     L.lb_store_kvcache.argtypes = [vp, i64, vp, i64, vp, vp, vp, i64, i64, i64, vp]

@@ -10,6 +10,7 @@
 //                                        nanovllm/models/qwen3_5.py:823-831)
 #include <algorithm>
 #include <cfloat>
+#include <mutex>
 
 #include "lb_gemm_launch.cuh"
 #include "lb_host.h"
@@ -346,6 +347,41 @@ static int run_permute(const int32_t* ids, const float* wf, int T, int k, int ex
   return LB_OK;
 }
 
+// ------------------------------------------------------------------------------ no-alloc
+// Fixed scratch for lb_moe_permute_noalloc, for callers that may not allocate device
+// memory.  It lives in this module's static device memory: every GPU that loads the
+// library holds LB_NOALLOC_SCRATCH_INTS * 4 bytes (8,464 bytes) of it until the process
+// exits, and every call on a device shares it.
+constexpr int LB_NOALLOC_MAX_LOCAL_EXPERTS = 1024;
+constexpr int LB_NOALLOC_SCRATCH_INTS = 64 + 2 * (LB_NOALLOC_MAX_LOCAL_EXPERTS + 2);
+static __device__ __align__(256) int g_permute_scratch[LB_NOALLOC_SCRATCH_INTS];
+
+constexpr int LB_NOALLOC_MAX_DEVICES = 64;
+static std::mutex g_noalloc_mu;
+static int* g_noalloc_addr[LB_NOALLOC_MAX_DEVICES] = {};
+
+// Device address of g_permute_scratch on the current device.  In host code the array's
+// name only stands in for the symbol; the address a kernel may use comes from
+// cudaGetSymbolAddress, looked up once per device (with that device current) and cached.
+static int noalloc_scratch(int** out) {
+  int dev = -1;
+  LB_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= LB_NOALLOC_MAX_DEVICES)
+    return fail(LB_ERR_UNSUPPORTED, "lb_moe_permute_noalloc: device %d beyond the %d cached",
+                dev, LB_NOALLOC_MAX_DEVICES);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_permute_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(LB_ERR_CUDA, "lb_moe_permute_noalloc: cudaGetSymbolAddress failed: %s",
+                  cudaGetErrorString(e));
+    g_noalloc_addr[dev] = static_cast<int*>(p);
+  }
+  *out = g_noalloc_addr[dev];
+  return LB_OK;
+}
+
 }  // namespace lb
 
 using namespace lb;
@@ -381,6 +417,29 @@ int lb_moe_permute(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base
   c.take<int>(64);  // status word
   int* counts = c.take<int>(nl + 2);
   int* mt = c.take<int>(nl + 2);
+  return run_permute(ids, nullptr, (int)T, (int)k, (int)expert_base, (int)nl, counts, row_start,
+                     mt, perm_token, nullptr, row_of, static_cast<cudaStream_t>(stream));
+}
+
+int lb_moe_permute_noalloc(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base,
+                           int64_t nl, int32_t* row_start, int32_t* perm_token, int32_t* row_of,
+                           void* stream) {
+  LB_REQUIRE(ids && row_start && perm_token && row_of, "lb_moe_permute_noalloc: null pointer");
+  LB_REQUIRE(T >= 0 && k > 0 && k <= 32 && expert_base >= 0 && nl > 0,
+             "lb_moe_permute_noalloc: bad sizes");
+  LB_REQUIRE(T * k < (1ll << 30), "lb_moe_permute_noalloc: too many pairs");
+  if (nl > LB_NOALLOC_MAX_LOCAL_EXPERTS)
+    return fail(LB_ERR_UNSUPPORTED,
+                "lb_moe_permute_noalloc: %lld local experts exceed the fixed scratch limit of %d "
+                "(use lb_moe_permute with a workspace)",
+                (long long)nl, LB_NOALLOC_MAX_LOCAL_EXPERTS);
+  int* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  // layout: [status x64][counts: nl+2][mtile_start: nl+2]; run_permute zeroes the counts
+  // (and presets row_of) on the stream before use, so a previous call's contents are harmless
+  int* counts = scratch + 64;
+  int* mt = counts + (nl + 2);
   return run_permute(ids, nullptr, (int)T, (int)k, (int)expert_base, (int)nl, counts, row_start,
                      mt, perm_token, nullptr, row_of, static_cast<cudaStream_t>(stream));
 }
