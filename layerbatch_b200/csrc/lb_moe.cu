@@ -17,6 +17,10 @@
 
 namespace lb {
 
+// pairs per chunk of the chunked permutation (k_perm_chunk_*)
+constexpr int PERM_CHUNK = 256;
+static int perm_chunks(int T, int k) { return (T * k + PERM_CHUNK - 1) / PERM_CHUNK; }
+
 // ------------------------------------------------------------------------------ top-k
 // One warp per token.  Softmax in fp32 over E logits, top-k by (value desc, index asc),
 // renormalisation over the selected k (qwen3_5.py:770-773).  Optionally the shared-expert
@@ -235,8 +239,7 @@ struct MoeWs {
   int32_t* ids;
   float* wf;
   __nv_bfloat16* wb;
-  float* sg;
-  int* counts;
+  int* chunk_hist;
   int* row_start;
   int* mtile_start;
   int32_t* perm_token;
@@ -257,8 +260,7 @@ static size_t carve_moe(const LbMoeArgs& a, void* base, MoeWs& w) {
   w.ids = c.take<int32_t>(T * k);
   w.wf = c.take<float>(T * k);
   w.wb = c.take<__nv_bfloat16>(T * k);
-  w.sg = c.take<float>(T);
-  w.counts = c.take<int>(nl + 2);
+  w.chunk_hist = c.take<int>((size_t)perm_chunks((int)T, (int)k) * nl);
   w.row_start = c.take<int>(nl + 2);
   w.mtile_start = c.take<int>(nl + 2);
   w.perm_token = c.take<int32_t>(rows);
@@ -273,8 +275,8 @@ static size_t carve_moe(const LbMoeArgs& a, void* base, MoeWs& w) {
 static int check_moe(const LbMoeArgs* a) {
   LB_REQUIRE(a != nullptr, "lb_moe: null args");
   LB_REQUIRE(a->num_tokens >= 0 && a->num_tokens <= (1 << 20), "lb_moe: num_tokens out of range");
-  LB_REQUIRE(a->hidden > 0 && a->hidden % 64 == 0 && a->hidden <= 16384,
-             "lb_moe: hidden must be a positive multiple of 64 (<= 16384)");
+  LB_REQUIRE(a->hidden > 0 && a->hidden % 256 == 0 && a->hidden <= 8192,
+             "lb_moe: hidden must be a positive multiple of 256 (<= 8192)");
   LB_REQUIRE(a->num_experts > 0 && a->num_experts <= 1024, "lb_moe: num_experts in [1, 1024]");
   LB_REQUIRE(a->top_k > 0 && a->top_k <= 32 && a->top_k <= a->num_experts,
              "lb_moe: top_k in [1, min(32, E)]");
@@ -347,6 +349,198 @@ static int run_permute(const int32_t* ids, const float* wf, int T, int k, int ex
   return LB_OK;
 }
 
+// ------------------------------------------------------------------------------ chunked permute
+// The (slot, token)-ordered pairs f = j*T + t are cut into chunks of PERM_CHUNK pairs.
+// k_perm_chunk_hist counts every local expert per chunk; k_perm_chunk_scan turns the
+// counts into each chunk's first packed row per expert (plus row_start / mtile_start);
+// k_perm_chunk_scatter walks each chunk in order with one warp and assigns rows, so the
+// result equals the sequential definition bit for bit.
+__global__ void k_perm_chunk_hist(const int32_t* __restrict__ ids, int T, int k, int expert_base,
+                                  int nl, int* __restrict__ chunk_hist) {
+  extern __shared__ int hist[];
+  for (int i = threadIdx.x; i < nl; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int n = T * k;
+  const int f = blockIdx.x * PERM_CHUNK + threadIdx.x;
+  if (threadIdx.x < PERM_CHUNK && f < n) {
+    const int j = f / T, t = f - (f / T) * T;
+    const int e = ids[(long long)t * k + j] - expert_base;
+    if (e >= 0 && e < nl) atomicAdd(&hist[e], 1);
+  }
+  __syncthreads();
+  int* dst = chunk_hist + (long long)blockIdx.x * nl;
+  for (int i = threadIdx.x; i < nl; i += blockDim.x) dst[i] = hist[i];
+}
+
+// One block.  For expert e: chunk_hist[c][e] <- first packed row of expert e's pairs in
+// chunk c; row_start / mtile_start as in k_moe_scan (group 0 = shared expert, T rows).
+__global__ void k_perm_chunk_scan(int* __restrict__ chunk_hist, int n_chunks, int nl, int T,
+                                  int* __restrict__ row_start, int* __restrict__ mtile_start) {
+  __shared__ int s_rows[1024], s_tiles[1024];
+  __shared__ int s_tot[2048];
+  const int tid = threadIdx.x;
+  const int G = nl + 1;
+  for (int e = tid; e < nl; e += blockDim.x) {
+    int run = 0;
+    for (int c = 0; c < n_chunks; ++c) {
+      int* h = chunk_hist + (long long)c * nl + e;
+      const int v = *h;
+      *h = run;
+      run += v;
+    }
+    s_tot[1 + e] = run;
+  }
+  if (tid == 0) s_tot[0] = T;
+  __syncthreads();
+  int r[2], tl[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int g = 2 * tid + i;
+    const int c = g < G ? s_tot[g] : 0;
+    r[i] = c;
+    tl[i] = (c + GEMM_BM - 1) / GEMM_BM;
+  }
+  s_rows[tid] = r[0] + r[1];
+  s_tiles[tid] = tl[0] + tl[1];
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    int a = 0, b = 0;
+    if (tid >= off) {
+      a = s_rows[tid - off];
+      b = s_tiles[tid - off];
+    }
+    __syncthreads();
+    s_rows[tid] += a;
+    s_tiles[tid] += b;
+    __syncthreads();
+  }
+  const int ex_r = tid ? s_rows[tid - 1] : 0;
+  const int ex_t = tid ? s_tiles[tid - 1] : 0;
+  __syncthreads();
+  // exclusive row start of every group, kept in s_tot for the per-chunk bases below
+  if (2 * tid <= G) {
+    row_start[2 * tid] = ex_r;
+    mtile_start[2 * tid] = ex_t;
+  }
+  if (2 * tid + 1 <= G) {
+    row_start[2 * tid + 1] = ex_r + r[0];
+    mtile_start[2 * tid + 1] = ex_t + tl[0];
+  }
+  __syncthreads();
+  if (2 * tid < G) s_tot[2 * tid] = ex_r;
+  if (2 * tid + 1 < G) s_tot[2 * tid + 1] = ex_r + r[0];
+  __syncthreads();
+  for (int e = tid; e < nl; e += blockDim.x) {
+    const int base = s_tot[1 + e];
+    for (int c = 0; c < n_chunks; ++c) chunk_hist[(long long)c * nl + e] += base;
+  }
+}
+
+// One warp per chunk, pairs in order; equal experts inside a 32-pair step are ranked with
+// __match_any_sync, and a per-expert running count in shared memory carries the order
+// across steps.
+__global__ void k_perm_chunk_scatter(const int32_t* __restrict__ ids, const float* __restrict__ w,
+                                     int T, int k, int expert_base, int nl,
+                                     const int* __restrict__ chunk_base,
+                                     int32_t* __restrict__ perm_token, float* __restrict__ perm_w,
+                                     int32_t* __restrict__ row_of) {
+  extern __shared__ int cnt[];
+  const int lane = threadIdx.x;
+  for (int i = lane; i < nl; i += 32) cnt[i] = 0;
+  __syncwarp();
+  const int n = T * k;
+  const int* base = chunk_base + (long long)blockIdx.x * nl;
+  const int f0 = blockIdx.x * PERM_CHUNK;
+  for (int s = 0; s < PERM_CHUNK; s += 32) {
+    const int f = f0 + s + lane;
+    int e = -1, t = 0, j = 0;
+    if (f < n) {
+      j = f / T;
+      t = f - j * T;
+      e = ids[(long long)t * k + j] - expert_base;
+      if (e < 0 || e >= nl) e = -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int before = __popc(peers & ((1u << lane) - 1u));
+    int r = 0;
+    if (e >= 0) r = base[e] + cnt[e] + before;
+    __syncwarp();
+    if (e >= 0 && before == 0) cnt[e] += __popc(peers);
+    __syncwarp();
+    if (e >= 0) {
+      perm_token[r] = t;
+      if (perm_w) perm_w[r] = w[(long long)t * k + j];
+      row_of[(long long)t * k + j] = r;
+    }
+  }
+}
+
+// out[t] = bf16( sum over the shared row t and the routed rows row_of[t, :] of yw ),
+// one warp per token, fp32 accumulation, 16-byte loads.
+template <int MAXS>  // H <= MAXS * 256, H % 256 == 0
+__global__ void k_moe_combine(const __nv_bfloat16* __restrict__ yw, const int32_t* __restrict__ row_of,
+                              int T, int k, int H, __nv_bfloat16* __restrict__ out) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  float acc[MAXS][8];
+#pragma unroll
+  for (int s = 0; s < MAXS; ++s)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[s][i] = 0.f;
+  const int stripes = H / 256;
+  for (int j = -1; j < k; ++j) {
+    const int r = (j < 0) ? t : row_of[(long long)t * k + j];
+    if (r < 0) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(yw + (long long)r * H) + lane;
+    uint4 v[MAXS];
+#pragma unroll
+    for (int s = 0; s < MAXS; ++s)
+      if (s < stripes) v[s] = src[s * 32];
+#pragma unroll
+    for (int s = 0; s < MAXS; ++s)
+      if (s < stripes) {
+        acc[s][0] += bf16_lo(v[s].x); acc[s][1] += bf16_hi(v[s].x);
+        acc[s][2] += bf16_lo(v[s].y); acc[s][3] += bf16_hi(v[s].y);
+        acc[s][4] += bf16_lo(v[s].z); acc[s][5] += bf16_hi(v[s].z);
+        acc[s][6] += bf16_lo(v[s].w); acc[s][7] += bf16_hi(v[s].w);
+      }
+  }
+  uint4* dst = reinterpret_cast<uint4*>(out + (long long)t * H) + lane;
+#pragma unroll
+  for (int s = 0; s < MAXS; ++s)
+    if (s < stripes)
+      dst[s * 32] = make_uint4(pack_bf16x2(acc[s][0], acc[s][1]), pack_bf16x2(acc[s][2], acc[s][3]),
+                               pack_bf16x2(acc[s][4], acc[s][5]), pack_bf16x2(acc[s][6], acc[s][7]));
+}
+
+// Chunked permutation used by lb_moe_permute and lb_moe_forward.  chunk_hist needs
+// perm_chunks(T, k) * nl ints of scratch.
+static int run_permute_chunked(const int32_t* ids, const float* wf, int T, int k, int expert_base,
+                               int nl, int* chunk_hist, int* row_start, int* mtile_start,
+                               int32_t* perm_token, float* perm_w, int32_t* row_of,
+                               cudaStream_t st) {
+  const int n = T * k;
+  const int nc = perm_chunks(T, k);
+  LB_CUDA_CHECK(cudaMemsetAsync(row_of, 0xff, sizeof(int32_t) * (size_t)n, st));
+  if (nc > 0) {
+    k_perm_chunk_hist<<<nc, PERM_CHUNK, sizeof(int) * nl, st>>>(ids, T, k, expert_base, nl, chunk_hist);
+    { int _rc = launched("k_perm_chunk_hist"); if (_rc) return _rc; }
+  }
+  k_perm_chunk_scan<<<1, 1024, 0, st>>>(chunk_hist, nc, nl, T, row_start, mtile_start);
+  { int _rc = launched("k_perm_chunk_scan"); if (_rc) return _rc; }
+  if (T > 0) {
+    k_iota<<<std::min(1024, (T + 255) / 256), 256, 0, st>>>(perm_token, T);
+    { int _rc = launched("k_iota"); if (_rc) return _rc; }
+  }
+  if (nc > 0) {
+    k_perm_chunk_scatter<<<nc, 32, sizeof(int) * nl, st>>>(ids, wf, T, k, expert_base, nl, chunk_hist,
+                                                           perm_token, perm_w, row_of);
+    { int _rc = launched("k_perm_chunk_scatter"); if (_rc) return _rc; }
+  }
+  return LB_OK;
+}
+
 // ------------------------------------------------------------------------------ no-alloc
 // Fixed scratch for lb_moe_permute_noalloc, for callers that may not allocate device
 // memory.  It lives in this module's static device memory: every GPU that loads the
@@ -399,9 +593,8 @@ int lb_router_topk(const void* logits, int64_t ld, int64_t T, int64_t E, int64_t
 }
 
 size_t lb_moe_permute_workspace_size(int64_t T, int64_t k, int64_t nl) {
-  (void)T;
-  (void)k;
-  return 256 + 2 * 256 + sizeof(int) * (size_t)(2 * (nl + 2));
+  const size_t nc = (size_t)((T * k + PERM_CHUNK - 1) / PERM_CHUNK);
+  return 256 + 3 * 256 + sizeof(int) * (size_t)(nl + 2) + sizeof(int) * nc * (size_t)nl;
 }
 
 int lb_moe_permute(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base,
@@ -415,10 +608,11 @@ int lb_moe_permute(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base
     return fail(LB_ERR_WORKSPACE, "lb_moe_permute: workspace too small");
   Carve c(workspace, workspace_bytes);
   c.take<int>(64);  // status word
-  int* counts = c.take<int>(nl + 2);
   int* mt = c.take<int>(nl + 2);
-  return run_permute(ids, nullptr, (int)T, (int)k, (int)expert_base, (int)nl, counts, row_start,
-                     mt, perm_token, nullptr, row_of, static_cast<cudaStream_t>(stream));
+  int* chunk_hist = c.take<int>((size_t)perm_chunks((int)T, (int)k) * nl);
+  return run_permute_chunked(ids, nullptr, (int)T, (int)k, (int)expert_base, (int)nl, chunk_hist,
+                             row_start, mt, perm_token, nullptr, row_of,
+                             static_cast<cudaStream_t>(stream));
 }
 
 int lb_moe_permute_noalloc(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base,
@@ -476,12 +670,14 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
   rc = lb_gemm_bf16(a->x, H, a->w_router, H, logits, E, T, E, H, 0, 1, w.status, stream);
   if (rc) return rc;
   // 2. top-k + shared-expert gate
+  // the shared-expert gate lands in perm_w[0:T): rows [0,T) of every packed buffer are the
+  // shared expert's, so the down GEMM scales them by it like routed rows by their weight
   rc = launch_topk(logits, E, T, E, k, ids, w.wf, wb, x,
-                   static_cast<const __nv_bfloat16*>(a->w_shared_expert_gate), H, w.sg, st);
+                   static_cast<const __nv_bfloat16*>(a->w_shared_expert_gate), H, w.perm_w, st);
   if (rc) return rc;
   // 3. permutation
-  rc = run_permute(ids, w.wf, T, k, (int)a->expert_base, nl, w.counts, w.row_start,
-                   w.mtile_start, w.perm_token, w.perm_w, w.row_of, st);
+  rc = run_permute_chunked(ids, w.wf, T, k, (int)a->expert_base, nl, w.chunk_hist, w.row_start,
+                           w.mtile_start, w.perm_token, w.perm_w, w.row_of, st);
   if (rc) return rc;
   {
     const long long vec = (long long)T * k * (H / 8);
@@ -522,19 +718,23 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
     if ((rc = launch_gemm<BN, 4, EPI_SWIGLU, true>(tA, tAsh, tB, tB0, tB1, g, grid, st))) return rc;
     record_event(a->timing_events[1], st);
   }
-  // 5. grouped down GEMM of the routed experts, scaled by the routing weight: yw[rows, H]
+  // 5. grouped down GEMM of every group (shared expert = group 0), each row scaled by its
+  //    routing weight (shared rows: sigmoid gate): yw[rows, H]
   {
     constexpr int BN = 256;
-    CUtensorMap tA, tB;
+    CUtensorMap tA, tB, tBs;
     if ((rc = make_tmap_bf16_2d(&tA, w.act, rows, I, I, GEMM_BM, 64))) return rc;
     if ((rc = make_tmap_bf16_3d(&tB, a->w_down, nl, H, I, I, (uint64_t)H * I, BN, 64))) return rc;
+    if ((rc = make_tmap_bf16_3d(&tBs, a->w_shared_down, 1, H, I, I, (uint64_t)H * I, BN, 64)))
+      return rc;
     GemmArgs g = gemm_args_default(w.status);
-    g.mtile_start = w.mtile_start + 1;  // window: groups 1..G-1
-    g.row_start = w.row_start + 1;
-    g.num_groups = nl;
+    g.mtile_start = w.mtile_start;
+    g.row_start = w.row_start;
+    g.num_groups = G;
     g.n_tiles = H / BN;
     g.k_blocks = I / 64;
-    g.b_group_base = 0;
+    g.shared_group = 0;
+    g.b_group_base = 1;
     g.row_scale = w.perm_w;
     g.out = w.yw;
     g.ldo = H;
@@ -542,33 +742,20 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
     g.out_cols = H;
     const int grid = (int)std::min<long long>(num_sms(), max_mtiles * g.n_tiles);
     record_event(a->timing_events[2], st);
-    if ((rc = launch_gemm<BN, 4, EPI_SCALE_BF16, false>(tA, tA, tB, tB, tB, g, grid, st))) return rc;
+    if ((rc = launch_gemm<BN, 4, EPI_SCALE_BF16, false>(tA, tA, tB, tBs, tBs, g, grid, st))) return rc;
     record_event(a->timing_events[3], st);
   }
-  // 6. shared-expert down GEMM; epilogue: out = sigmoid_gate * shared + sum_j yw[row_of]
+  // 6. combine: out[t] = yw[t] + sum_j yw[row_of[t, j]]
   {
-    constexpr int BN = 128;
-    CUtensorMap tA, tB;
-    if ((rc = make_tmap_bf16_2d(&tA, w.act, rows, I, I, GEMM_BM, 64))) return rc;
-    if ((rc = make_tmap_bf16_3d(&tB, a->w_shared_down, 1, H, I, I, (uint64_t)H * I, BN, 64)))
-      return rc;
-    GemmArgs g = gemm_args_default(w.status);
-    g.single_m = T;
-    g.single_row_base = 0;
-    g.n_tiles = H / BN;
-    g.k_blocks = I / 64;
-    g.tok_scale = w.sg;
-    g.yw = w.yw;
-    g.ldyw = H;
-    g.row_of = w.row_of;
-    g.top_k = k;
-    g.out = a->out;
-    g.ldo = H;
-    g.out_rows = T;
-    g.out_cols = H;
-    const long long tiles = (long long)((T + GEMM_BM - 1) / GEMM_BM) * g.n_tiles;
-    const int grid = (int)std::min<long long>(num_sms(), tiles);
-    if ((rc = launch_gemm<BN, 6, EPI_COMBINE, false>(tA, tA, tB, tB, tB, g, grid, st))) return rc;
+    const int blocks = (T * 32 + 255) / 256;
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a->out);
+    if (H <= 2048)
+      k_moe_combine<8><<<blocks, 256, 0, st>>>(w.yw, w.row_of, T, k, H, out);
+    else if (H <= 4096)
+      k_moe_combine<16><<<blocks, 256, 0, st>>>(w.yw, w.row_of, T, k, H, out);
+    else
+      k_moe_combine<32><<<blocks, 256, 0, st>>>(w.yw, w.row_of, T, k, H, out);
+    { int _rc = launched("k_moe_combine"); if (_rc) return _rc; }
   }
   (void)E;
   return LB_OK;

@@ -110,19 +110,46 @@ def make_moe_input(T, H, seed=1, device="cpu") -> torch.Tensor:
     return _randn(g, (T, H), 1.0, device)
 
 
-def apply_zipf_bias(params: MoEParams, x: torch.Tensor, s: float = 1.1, seed: int = 2):
-    """Bias the router so that expert load follows Zipf(s).
+def zipf_targets(E: int, total: int, cap: int, s: float = 1.1) -> torch.Tensor:
+    """Expert loads proportional to rank^-s summing to ``total``, none above ``cap``
+    (one expert can take each token at most once)."""
+    w = torch.arange(1, E + 1, dtype=torch.float64) ** (-s)
+    lo, hi = 0.0, float(total) / float(w.min())
+    for _ in range(100):
+        c = 0.5 * (lo + hi)
+        if torch.clamp(c * w, max=cap).sum() > total:
+            hi = c
+        else:
+            lo = c
+    return torch.clamp(lo * w, max=cap)
+
+
+def apply_zipf_bias(params: MoEParams, x: torch.Tensor, s: float = 1.1, seed: int = 2,
+                    calib_tokens: int = 2048, iters: int = 60):
+    """Bias the router so that the expert LOAD (selections per expert) follows Zipf(s).
 
     Hidden dimension 0 of every token is set to 1 and router column 0 of expert e is set
-    to ``-s * ln(rank_e)``, where ``rank`` is a seeded permutation of 1..E.  The softmax
-    then weighs expert e by ``rank_e^-s`` on top of the N(0, 0.02*sqrt(H)) logit noise.
-    The router operator itself is unchanged.
+    to a bias b_e, so the router operator itself is unchanged.  Experts get Zipf ranks
+    from a seeded permutation; the biases are calibrated by a fixed-point iteration on a
+    seeded calibration batch (``calib_tokens`` N(0,1) tokens) so that the top-k selection
+    counts match ``zipf_targets`` (rank^-s, capped at one selection per token).
+    Returns the rank of every expert (1 = most loaded).
     """
-    E = params.num_experts
+    E, H = params.router.shape
+    k = params.top_k
     g = torch.Generator().manual_seed(seed)
     rank = torch.randperm(E, generator=g) + 1
-    bias = (-s * torch.log(rank.double())).to(torch.bfloat16)
-    params.router[:, 0] = bias.to(params.router.device)
+    xc = torch.randn(calib_tokens, H, generator=g).to(torch.bfloat16).float()
+    w = params.router.detach().float().cpu()
+    noise = xc[:, 1:] @ w[:, 1:].t()                     # [Tc, E] logit part without bias
+    target = zipf_targets(E, calib_tokens * k, calib_tokens, s)[rank - 1]
+    b = -s * torch.log(rank.double()).float()
+    for _ in range(iters):
+        top = torch.topk(noise + b, k, dim=-1).indices
+        cnt = torch.bincount(top.reshape(-1), minlength=E).float()
+        b = b + 0.5 * (torch.log(target.float() + 1.0) - torch.log(cnt + 1.0))
+        b = b - b.max()
+    params.router[:, 0] = b.to(torch.bfloat16).to(params.router.device)
     x[:, 0] = 1.0
     return rank
 
