@@ -110,7 +110,8 @@ typedef struct LbMoeArgs {
   int64_t inter;             /* I, routed expert intermediate (multiple of 128) */
   int64_t shared_inter;      /* Is, shared expert intermediate (must equal I) */
   int64_t expert_base;       /* first global expert id held in w_gate_up / w_down */
-  int64_t num_local_experts; /* experts held locally (E on one GPU) */
+  int64_t num_local_experts; /* experts held locally (E on one GPU; 0 allowed only with
+                              * routing_given, e.g. a combine-only call) */
   const void* x;             /* [T, H] bf16, row stride H */
   const void* w_router;      /* [E, H] bf16           mlp.gate.weight */
   const void* w_gate_up;     /* [nl, 2I, H] bf16      mlp.experts.gate_up_proj */
@@ -128,6 +129,13 @@ typedef struct LbMoeArgs {
   /* optional cudaEvent_t handles recorded on the stream around the grouped gate/up GEMM
    * ([0], [1]) and the grouped down GEMM ([2], [3]); NULL entries are skipped */
   void* timing_events[4];
+  /* ---- expert-parallel building blocks (all zero/NULL for the plain block) */
+  int32_t routing_given;     /* 1: topk_ids [T,k] (global ids) and topk_weights_f32 are
+                              * INPUTS; the router is skipped and w_router may be NULL */
+  const float* topk_weights_f32; /* [T, k] fp32 routing weights when routing_given */
+  int32_t no_shared;         /* 1: no shared expert (its weights may be NULL) */
+  const void* pair_rows;     /* optional [*, H] bf16 rows computed elsewhere (other ranks) */
+  const int32_t* pair_index; /* [T, k]: row of pair_rows added into out[t], or -1 */
 } LbMoeArgs;
 
 int lb_moe_workspace_size(const LbMoeArgs* args, size_t* bytes);
@@ -160,14 +168,15 @@ typedef struct LbPodArgs {
   int32_t kv_split_pages;     /* decode split length in pages (0 = automatic) */
   const void* q;              /* [N, Hq, D] bf16 */
   int64_t q_stride_tok, q_stride_head;
-  const void* gate;           /* [N, Hq, D] bf16 (pre-sigmoid output gate) */
+  const void* gate;           /* [N, Hq, D] bf16 (pre-sigmoid output gate), NULL = no gate */
   int64_t gate_stride_tok, gate_stride_head;
   const void* k_cache;        /* [num_pages, page_size, Hkv, D] bf16 */
   const void* v_cache;
   const int32_t* block_tables;/* [B, max_pages_per_seq] int32 */
   const int32_t* context_lens;/* [B] int32 */
   const int32_t* cu_seqlens_q;/* [B+1] int32 */
-  const void* w_o;            /* [hidden, Hq*D] bf16 */
+  const void* w_o;            /* [hidden, Hq*D] bf16; NULL = attention only (then attn_out
+                               * is required and out / hidden are ignored) */
   void* attn_out;             /* optional out: [N, Hq*D] bf16 attention output (pre-gate) */
   void* out;                  /* [N, hidden] bf16, or fp32 when out_fp32 */
   int32_t out_fp32;           /* 1: write fp32 o_proj partials (tensor-parallel reduce) */

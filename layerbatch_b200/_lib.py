@@ -41,6 +41,8 @@ class LbMoeArgs(C.Structure):
         ("w_shared_expert_gate", vp), ("out", vp), ("router_logits", vp),
         ("topk_ids", vp), ("topk_weights", vp), ("workspace", vp),
         ("workspace_bytes", C.c_size_t), ("timing_events", vp * 4),
+        ("routing_given", i32), ("topk_weights_f32", vp), ("no_shared", i32),
+        ("pair_rows", vp), ("pair_index", vp),
     ]
 
 

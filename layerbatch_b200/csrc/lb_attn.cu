@@ -140,15 +140,22 @@ __global__ void k_pod_merge(const int32_t* __restrict__ ctx_lens, const int32_t*
       o[0] += w * x0.x; o[1] += w * x0.y; o[2] += w * x0.z; o[3] += w * x0.w;
       o[4] += w * x1.x; o[5] += w * x1.y; o[6] += w * x1.z; o[7] += w * x1.w;
     }
-    const uint4 g = *reinterpret_cast<const uint4*>(gate + (long long)q0 * gst + (long long)h * gsh + d);
-    const float gv[8] = {bf16_lo(g.x), bf16_hi(g.x), bf16_lo(g.y), bf16_hi(g.y),
-                         bf16_lo(g.z), bf16_hi(g.z), bf16_lo(g.w), bf16_hi(g.w)};
-    uint4 outv;
-    outv.x = pack_bf16x2(o[0] * sigmoid_f(gv[0]), o[1] * sigmoid_f(gv[1]));
-    outv.y = pack_bf16x2(o[2] * sigmoid_f(gv[2]), o[3] * sigmoid_f(gv[3]));
-    outv.z = pack_bf16x2(o[4] * sigmoid_f(gv[4]), o[5] * sigmoid_f(gv[5]));
-    outv.w = pack_bf16x2(o[6] * sigmoid_f(gv[6]), o[7] * sigmoid_f(gv[7]));
-    *reinterpret_cast<uint4*>(ogated + (long long)q0 * HD + i) = outv;
+    if (ogated) {
+      float gv[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+      if (gate) {
+        const uint4 g = *reinterpret_cast<const uint4*>(gate + (long long)q0 * gst + (long long)h * gsh + d);
+        gv[0] = sigmoid_f(bf16_lo(g.x)); gv[1] = sigmoid_f(bf16_hi(g.x));
+        gv[2] = sigmoid_f(bf16_lo(g.y)); gv[3] = sigmoid_f(bf16_hi(g.y));
+        gv[4] = sigmoid_f(bf16_lo(g.z)); gv[5] = sigmoid_f(bf16_hi(g.z));
+        gv[6] = sigmoid_f(bf16_lo(g.w)); gv[7] = sigmoid_f(bf16_hi(g.w));
+      }
+      uint4 outv;
+      outv.x = pack_bf16x2(o[0] * gv[0], o[1] * gv[1]);
+      outv.y = pack_bf16x2(o[2] * gv[2], o[3] * gv[3]);
+      outv.z = pack_bf16x2(o[4] * gv[4], o[5] * gv[5]);
+      outv.w = pack_bf16x2(o[6] * gv[6], o[7] * gv[7]);
+      *reinterpret_cast<uint4*>(ogated + (long long)q0 * HD + i) = outv;
+    }
     if (attn_out) {
       uint4 r;
       r.x = pack_bf16x2(o[0], o[1]);
@@ -204,17 +211,23 @@ static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
              "lb_pod: page_size must be a multiple of 128");
   LB_REQUIRE(a->num_pages > 0 && a->max_pages_per_seq > 0, "lb_pod: empty KV pool / tables");
   LB_REQUIRE(a->num_pages * a->page_size < (1ll << 31), "lb_pod: KV pool too large for 32-bit slots");
-  LB_REQUIRE(a->hidden > 0 && a->hidden % 32 == 0, "lb_pod: hidden must be a multiple of 32");
-  LB_REQUIRE(a->q && a->gate && a->k_cache && a->v_cache && a->block_tables && a->context_lens &&
-                 a->cu_seqlens_q && a->w_o && a->out,
+  LB_REQUIRE(a->w_o == nullptr || (a->hidden > 0 && a->hidden % 32 == 0),
+             "lb_pod: hidden must be a multiple of 32");
+  LB_REQUIRE(a->q && a->k_cache && a->v_cache && a->block_tables && a->context_lens &&
+                 a->cu_seqlens_q,
              "lb_pod: null pointer");
-  LB_REQUIRE(aligned16(a->q) && aligned16(a->gate) && aligned16(a->k_cache) &&
-                 aligned16(a->v_cache) && aligned16(a->w_o) && aligned16(a->out) &&
+  LB_REQUIRE((a->w_o && a->out) || (!a->w_o && a->attn_out),
+             "lb_pod: need w_o and out, or (attention only) attn_out without w_o");
+  LB_REQUIRE(aligned16(a->q) && (a->gate == nullptr || aligned16(a->gate)) &&
+                 aligned16(a->k_cache) && aligned16(a->v_cache) &&
+                 (a->w_o == nullptr || aligned16(a->w_o)) && (a->out == nullptr || aligned16(a->out)) &&
                  (a->attn_out == nullptr || aligned16(a->attn_out)),
              "lb_pod: tensors must be 16-byte aligned");
-  LB_REQUIRE(a->q_stride_head % 8 == 0 && a->q_stride_tok % 8 == 0 && a->gate_stride_head % 8 == 0 &&
-                 a->gate_stride_tok % 8 == 0 && a->q_stride_head >= POD_D && a->gate_stride_head >= POD_D,
-             "lb_pod: q/gate strides must be multiples of 8 elements with contiguous heads");
+  LB_REQUIRE(a->q_stride_head % 8 == 0 && a->q_stride_tok % 8 == 0 && a->q_stride_head >= POD_D,
+             "lb_pod: q strides must be multiples of 8 elements with contiguous heads");
+  LB_REQUIRE(a->gate == nullptr || (a->gate_stride_head % 8 == 0 && a->gate_stride_tok % 8 == 0 &&
+                                    a->gate_stride_head >= POD_D),
+             "lb_pod: gate strides must be multiples of 8 elements with contiguous heads");
   const long long HD = a->num_q_heads * POD_D;
   LB_REQUIRE(HD % 64 == 0, "lb_pod: Hq*D must be a multiple of 64");
   pl.gqa = (int)(a->num_q_heads / a->num_kv_heads);
@@ -260,7 +273,7 @@ static size_t carve_pod(const LbPodArgs& a, const PodPlan& pl, void* base, PodWs
   w.part_o = c.take<float>((size_t)a.num_seqs * pl.max_splits * a.num_q_heads * POD_D);
   w.part_lse = c.take<float>((size_t)a.num_seqs * pl.max_splits * a.num_q_heads);
   w.ogated = c.take<__nv_bfloat16>((size_t)a.num_tokens * a.num_q_heads * POD_D);
-  w.o32 = c.take<float>((size_t)a.num_tokens * a.hidden);
+  w.o32 = c.take<float>(a.w_o ? (size_t)a.num_tokens * a.hidden : 0);
   return c.off + 256;
 }
 
@@ -307,7 +320,7 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
   p.gate = static_cast<const __nv_bfloat16*>(a.gate);
   p.gate_st = a.gate_stride_tok;
   p.gate_sh = a.gate_stride_head;
-  p.ogated = w.ogated;
+  p.ogated = a.w_o ? w.ogated : nullptr;
   p.attn_out = static_cast<__nv_bfloat16*>(a.attn_out);
   p.part_o = w.part_o;
   p.part_lse = w.part_lse;
@@ -332,9 +345,10 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
   k_pod_merge<<<B, 256, merge_smem, st>>>(a.context_lens, a.cu_seqlens_q, (int)a.num_q_heads,
                                           pl.split_tokens, pl.max_splits, pl.max_ctx, w.part_o,
                                           w.part_lse, p.gate, a.gate_stride_tok, a.gate_stride_head,
-                                          w.ogated, p.attn_out);
+                                          p.ogated, p.attn_out);
   { int _rc = launched("k_pod_merge"); if (_rc) return _rc; }
 
+  if (a.w_o == nullptr) return LB_OK;  // attention only
   // o_proj: out[N, hidden] = ogated[N, Hq*D] . W_o^T
   const int K = (int)(a.num_q_heads * POD_D), Hd = (int)a.hidden;
   const int nsm = num_sms();

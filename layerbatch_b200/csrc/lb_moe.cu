@@ -108,6 +108,28 @@ __global__ void k_router_topk(const __nv_bfloat16* __restrict__ logits, long lon
   }
 }
 
+// sg[t] = sigmoid(x[t] . w_sg) in fp32, one warp per token (qwen3_5.py:903); used when the
+// routing is given and the top-k kernel (which also computes it) does not run.
+__global__ void k_shared_gate(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wsg,
+                              int T, int H, float* __restrict__ sg) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  const __nv_bfloat16* xr = x + (long long)t * H;
+  float acc = 0.f;
+  for (int h = lane * 8; h < H; h += 256) {
+    const uint4 a = *reinterpret_cast<const uint4*>(xr + h);
+    const uint4 b = *reinterpret_cast<const uint4*>(wsg + h);
+    acc += bf16_lo(a.x) * bf16_lo(b.x) + bf16_hi(a.x) * bf16_hi(b.x);
+    acc += bf16_lo(a.y) * bf16_lo(b.y) + bf16_hi(a.y) * bf16_hi(b.y);
+    acc += bf16_lo(a.z) * bf16_lo(b.z) + bf16_hi(a.z) * bf16_hi(b.z);
+    acc += bf16_lo(a.w) * bf16_lo(b.w) + bf16_hi(a.w) * bf16_hi(b.w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) sg[t] = 1.0f / (1.0f + expf(-acc));
+}
+
 // ------------------------------------------------------------------------------ permute
 // counts[1+e] += #pairs routed to local expert e (block-local histogram first).
 __global__ void k_moe_count(const int32_t* __restrict__ ids, int n, int expert_base, int nl,
@@ -253,12 +275,12 @@ struct MoeWs {
 static size_t carve_moe(const LbMoeArgs& a, void* base, MoeWs& w) {
   const size_t T = a.num_tokens, k = a.top_k, H = a.hidden, E = a.num_experts;
   const size_t nl = a.num_local_experts, I = a.inter;
-  const size_t rows = T + T * k;
+  const size_t rows = (a.no_shared ? 0 : T) + T * k;
   Carve c(base, ~size_t(0));
   w.status = c.take<int>(64);
-  w.logits = c.take<__nv_bfloat16>(T * E);
+  w.logits = c.take<__nv_bfloat16>(a.routing_given ? 0 : T * E);
   w.ids = c.take<int32_t>(T * k);
-  w.wf = c.take<float>(T * k);
+  w.wf = c.take<float>(a.routing_given ? 0 : T * k);
   w.wb = c.take<__nv_bfloat16>(T * k);
   w.chunk_hist = c.take<int>((size_t)perm_chunks((int)T, (int)k) * nl);
   w.row_start = c.take<int>(nl + 2);
@@ -281,21 +303,25 @@ static int check_moe(const LbMoeArgs* a) {
   LB_REQUIRE(a->top_k > 0 && a->top_k <= 32 && a->top_k <= a->num_experts,
              "lb_moe: top_k in [1, min(32, E)]");
   LB_REQUIRE(a->inter > 0 && a->inter % 128 == 0, "lb_moe: inter must be a multiple of 128");
-  LB_REQUIRE(a->shared_inter == a->inter,
+  LB_REQUIRE(a->no_shared || a->shared_inter == a->inter,
              "lb_moe: shared_inter must equal inter (fused shared-expert group)");
-  LB_REQUIRE(a->num_local_experts > 0 && a->num_local_experts <= a->num_experts &&
-                 a->expert_base >= 0 && a->expert_base + a->num_local_experts <= a->num_experts,
+  LB_REQUIRE(a->num_local_experts >= (a->routing_given ? 0 : 1) &&
+                 a->num_local_experts <= a->num_experts && a->expert_base >= 0 &&
+                 a->expert_base + a->num_local_experts <= a->num_experts,
              "lb_moe: local expert range outside [0, E)");
-  LB_REQUIRE(a->num_experts % 32 == 0 || a->num_experts < 32,
+  LB_REQUIRE(a->routing_given || a->num_experts % 32 == 0,
              "lb_moe: num_experts must be a multiple of 32");
-  LB_REQUIRE(a->x && a->w_router && a->w_gate_up && a->w_down && a->w_shared_gate &&
-                 a->w_shared_up && a->w_shared_down && a->w_shared_expert_gate && a->out,
-             "lb_moe: null tensor pointer");
-  LB_REQUIRE(aligned16(a->x) && aligned16(a->w_router) && aligned16(a->w_gate_up) &&
-                 aligned16(a->w_down) && aligned16(a->w_shared_gate) && aligned16(a->w_shared_up) &&
-                 aligned16(a->w_shared_down) && aligned16(a->w_shared_expert_gate) &&
-                 aligned16(a->out),
-             "lb_moe: tensors must be 16-byte aligned");
+  LB_REQUIRE(a->x && a->out, "lb_moe: null x/out");
+  LB_REQUIRE(a->routing_given ? (a->topk_ids && a->topk_weights_f32) : (a->w_router != nullptr),
+             "lb_moe: need w_router, or topk_ids + topk_weights_f32 with routing_given");
+  LB_REQUIRE(a->num_local_experts == 0 || (a->w_gate_up && a->w_down), "lb_moe: null expert weights");
+  LB_REQUIRE(a->no_shared || (a->w_shared_gate && a->w_shared_up && a->w_shared_down &&
+                              a->w_shared_expert_gate),
+             "lb_moe: null shared-expert weights");
+  LB_REQUIRE(!a->pair_rows == !a->pair_index, "lb_moe: pair_rows and pair_index go together");
+  const void* ptrs[] = {a->x, a->out, a->w_router, a->w_gate_up, a->w_down, a->w_shared_gate,
+                        a->w_shared_up, a->w_shared_down, a->w_shared_expert_gate, a->pair_rows};
+  for (const void* q : ptrs) LB_REQUIRE(q == nullptr || aligned16(q), "lb_moe: tensors must be 16-byte aligned");
   return LB_OK;
 }
 
@@ -374,7 +400,7 @@ __global__ void k_perm_chunk_hist(const int32_t* __restrict__ ids, int T, int k,
 
 // One block.  For expert e: chunk_hist[c][e] <- first packed row of expert e's pairs in
 // chunk c; row_start / mtile_start as in k_moe_scan (group 0 = shared expert, T rows).
-__global__ void k_perm_chunk_scan(int* __restrict__ chunk_hist, int n_chunks, int nl, int T,
+__global__ void k_perm_chunk_scan(int* __restrict__ chunk_hist, int n_chunks, int nl, int T0,
                                   int* __restrict__ row_start, int* __restrict__ mtile_start) {
   __shared__ int s_rows[1024], s_tiles[1024];
   __shared__ int s_tot[2048];
@@ -390,7 +416,7 @@ __global__ void k_perm_chunk_scan(int* __restrict__ chunk_hist, int n_chunks, in
     }
     s_tot[1 + e] = run;
   }
-  if (tid == 0) s_tot[0] = T;
+  if (tid == 0) s_tot[0] = T0;
   __syncthreads();
   int r[2], tl[2];
 #pragma unroll
@@ -479,7 +505,10 @@ __global__ void k_perm_chunk_scatter(const int32_t* __restrict__ ids, const floa
 // one warp per token, fp32 accumulation, 16-byte loads.
 template <int MAXS>  // H <= MAXS * 256, H % 256 == 0
 __global__ void k_moe_combine(const __nv_bfloat16* __restrict__ yw, const int32_t* __restrict__ row_of,
-                              int T, int k, int H, __nv_bfloat16* __restrict__ out) {
+                              int T, int k, int H, int has_shared,
+                              const __nv_bfloat16* __restrict__ pair_rows,
+                              const int32_t* __restrict__ pair_index,
+                              __nv_bfloat16* __restrict__ out) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (t >= T) return;
@@ -489,10 +518,21 @@ __global__ void k_moe_combine(const __nv_bfloat16* __restrict__ yw, const int32_
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[s][i] = 0.f;
   const int stripes = H / 256;
-  for (int j = -1; j < k; ++j) {
-    const int r = (j < 0) ? t : row_of[(long long)t * k + j];
-    if (r < 0) continue;
-    const uint4* src = reinterpret_cast<const uint4*>(yw + (long long)r * H) + lane;
+  const int nsrc = pair_index ? 2 * k : k;
+  for (int j = has_shared ? -1 : 0; j < nsrc; ++j) {
+    const __nv_bfloat16* base;
+    if (j < 0) {
+      base = yw + (long long)t * H;                       // shared expert row
+    } else if (j < k) {
+      const int r = row_of[(long long)t * k + j];         // routed row computed here
+      if (r < 0) continue;
+      base = yw + (long long)r * H;
+    } else {
+      const int r = pair_index[(long long)t * k + (j - k)];  // routed row computed elsewhere
+      if (r < 0) continue;
+      base = pair_rows + (long long)r * H;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(base) + lane;
     uint4 v[MAXS];
 #pragma unroll
     for (int s = 0; s < MAXS; ++s)
@@ -519,7 +559,8 @@ __global__ void k_moe_combine(const __nv_bfloat16* __restrict__ yw, const int32_
 static int run_permute_chunked(const int32_t* ids, const float* wf, int T, int k, int expert_base,
                                int nl, int* chunk_hist, int* row_start, int* mtile_start,
                                int32_t* perm_token, float* perm_w, int32_t* row_of,
-                               cudaStream_t st) {
+                               cudaStream_t st, bool has_shared = true) {
+  const int T0 = has_shared ? T : 0;
   const int n = T * k;
   const int nc = perm_chunks(T, k);
   LB_CUDA_CHECK(cudaMemsetAsync(row_of, 0xff, sizeof(int32_t) * (size_t)n, st));
@@ -527,9 +568,9 @@ static int run_permute_chunked(const int32_t* ids, const float* wf, int T, int k
     k_perm_chunk_hist<<<nc, PERM_CHUNK, sizeof(int) * nl, st>>>(ids, T, k, expert_base, nl, chunk_hist);
     { int _rc = launched("k_perm_chunk_hist"); if (_rc) return _rc; }
   }
-  k_perm_chunk_scan<<<1, 1024, 0, st>>>(chunk_hist, nc, nl, T, row_start, mtile_start);
+  k_perm_chunk_scan<<<1, 1024, 0, st>>>(chunk_hist, nc, nl, T0, row_start, mtile_start);
   { int _rc = launched("k_perm_chunk_scan"); if (_rc) return _rc; }
-  if (T > 0) {
+  if (T0 > 0) {
     k_iota<<<std::min(1024, (T + 255) / 256), 256, 0, st>>>(perm_token, T);
     { int _rc = launched("k_iota"); if (_rc) return _rc; }
   }
@@ -659,54 +700,77 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
   const int T = (int)a->num_tokens, H = (int)a->hidden, E = (int)a->num_experts;
   const int k = (int)a->top_k, I = (int)a->inter, nl = (int)a->num_local_experts;
   const int G = nl + 1;
+  const bool shared = !a->no_shared;
+  const int T0 = shared ? T : 0;  // rows of group 0 (the shared expert)
   if (T == 0) return LB_OK;
   const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(a->x);
-  __nv_bfloat16* logits =
-      a->router_logits ? static_cast<__nv_bfloat16*>(a->router_logits) : w.logits;
-  int32_t* ids = a->topk_ids ? a->topk_ids : w.ids;
-  __nv_bfloat16* wb = a->topk_weights ? static_cast<__nv_bfloat16*>(a->topk_weights) : w.wb;
-
-  // 1. router logits [T, E] = x . W_router^T (bf16 out, fp32 accumulate)
-  rc = lb_gemm_bf16(a->x, H, a->w_router, H, logits, E, T, E, H, 0, 1, w.status, stream);
+  const int32_t* ids;
+  const float* wf;
+  if (a->routing_given) {
+    ids = a->topk_ids;
+    wf = a->topk_weights_f32;
+    if (shared) {
+      // the shared-expert gate lands in perm_w[0:T) (see below)
+      k_shared_gate<<<(T * 32 + 255) / 256, 256, 0, st>>>(
+          x, static_cast<const __nv_bfloat16*>(a->w_shared_expert_gate), T, H, w.perm_w);
+      { int _rc = launched("k_shared_gate"); if (_rc) return _rc; }
+    }
+  } else {
+    __nv_bfloat16* logits =
+        a->router_logits ? static_cast<__nv_bfloat16*>(a->router_logits) : w.logits;
+    int32_t* ids_out = a->topk_ids ? a->topk_ids : w.ids;
+    __nv_bfloat16* wb = a->topk_weights ? static_cast<__nv_bfloat16*>(a->topk_weights) : w.wb;
+    // 1. router logits [T, E] = x . W_router^T (bf16 out, fp32 accumulate)
+    rc = lb_gemm_bf16(a->x, H, a->w_router, H, logits, E, T, E, H, 0, 1, w.status, stream);
+    if (rc) return rc;
+    // 2. top-k + shared-expert gate.  The gate lands in perm_w[0:T): rows [0,T) of every
+    //    packed buffer are the shared expert's, so the down GEMM scales them by it exactly
+    //    as it scales routed rows by their routing weight.
+    rc = launch_topk(logits, E, T, E, k, ids_out, w.wf, wb, x,
+                     static_cast<const __nv_bfloat16*>(a->w_shared_expert_gate), H,
+                     shared ? w.perm_w : nullptr, st);
+    if (rc) return rc;
+    ids = ids_out;
+    wf = w.wf;
+  }
+  // 3. permutation (routed pairs of the local experts) and gather of their input rows
+  rc = run_permute_chunked(ids, wf, T, k, (int)a->expert_base, nl, w.chunk_hist, w.row_start,
+                           w.mtile_start, w.perm_token, w.perm_w, w.row_of, st, shared);
   if (rc) return rc;
-  // 2. top-k + shared-expert gate
-  // the shared-expert gate lands in perm_w[0:T): rows [0,T) of every packed buffer are the
-  // shared expert's, so the down GEMM scales them by it like routed rows by their weight
-  rc = launch_topk(logits, E, T, E, k, ids, w.wf, wb, x,
-                   static_cast<const __nv_bfloat16*>(a->w_shared_expert_gate), H, w.perm_w, st);
-  if (rc) return rc;
-  // 3. permutation
-  rc = run_permute_chunked(ids, w.wf, T, k, (int)a->expert_base, nl, w.chunk_hist, w.row_start,
-                           w.mtile_start, w.perm_token, w.perm_w, w.row_of, st);
-  if (rc) return rc;
-  {
+  if (nl > 0) {
     const long long vec = (long long)T * k * (H / 8);
     const int grid = (int)std::max<long long>(1, std::min<long long>(num_sms() * 8, (vec + 255) / 256));
-    k_gather_rows<<<grid, 256, 0, st>>>(x, H, w.perm_token, w.row_start + G, T, w.a_packed);
+    k_gather_rows<<<grid, 256, 0, st>>>(x, H, w.perm_token, w.row_start + G, T0, w.a_packed);
     { int _rc = launched("k_gather_rows"); if (_rc) return _rc; }
   }
-  const long long rows = (long long)T + (long long)T * k;
-  const long long max_mtiles = ((long long)T * k) / GEMM_BM + nl + (T + GEMM_BM - 1) / GEMM_BM;
+  const long long rows = (long long)T0 + (long long)T * k;
+  const long long max_mtiles = ((long long)T * k) / GEMM_BM + nl + (T0 + GEMM_BM - 1) / GEMM_BM;
+  const bool any_gemm = shared || nl > 0;
 
   // 4. grouped gate/up GEMM with SwiGLU: act[rows, I]
-  {
+  if (any_gemm) {
     constexpr int BN = 256;
     CUtensorMap tA, tAsh, tB, tB0, tB1;
     if ((rc = make_tmap_bf16_2d(&tA, w.a_packed, rows, H, H, GEMM_BM, 64))) return rc;
     if ((rc = make_tmap_bf16_2d(&tAsh, x, T, H, H, GEMM_BM, 64))) return rc;
-    if ((rc = make_tmap_bf16_3d(&tB, a->w_gate_up, nl, 2 * I, H, H, (uint64_t)2 * I * H, BN / 2, 64)))
+    if (nl > 0 && (rc = make_tmap_bf16_3d(&tB, a->w_gate_up, nl, 2 * I, H, H, (uint64_t)2 * I * H,
+                                          BN / 2, 64)))
       return rc;
-    if ((rc = make_tmap_bf16_3d(&tB0, a->w_shared_gate, 1, I, H, H, (uint64_t)I * H, BN / 2, 64)))
-      return rc;
-    if ((rc = make_tmap_bf16_3d(&tB1, a->w_shared_up, 1, I, H, H, (uint64_t)I * H, BN / 2, 64)))
-      return rc;
+    if (shared) {
+      if ((rc = make_tmap_bf16_3d(&tB0, a->w_shared_gate, 1, I, H, H, (uint64_t)I * H, BN / 2, 64)))
+        return rc;
+      if ((rc = make_tmap_bf16_3d(&tB1, a->w_shared_up, 1, I, H, H, (uint64_t)I * H, BN / 2, 64)))
+        return rc;
+    }
+    if (nl == 0) tB = tB0;
+    if (!shared) tB0 = tB1 = tB;
     GemmArgs g = gemm_args_default(w.status);
     g.mtile_start = w.mtile_start;
     g.row_start = w.row_start;
     g.num_groups = G;
     g.n_tiles = (2 * I) / BN;
     g.k_blocks = H / 64;
-    g.shared_group = 0;
+    g.shared_group = shared ? 0 : -1;
     g.b_group_base = 1;
     g.b_half_offset = I;
     g.out = w.act;
@@ -720,20 +784,23 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
   }
   // 5. grouped down GEMM of every group (shared expert = group 0), each row scaled by its
   //    routing weight (shared rows: sigmoid gate): yw[rows, H]
-  {
+  if (any_gemm) {
     constexpr int BN = 256;
     CUtensorMap tA, tB, tBs;
     if ((rc = make_tmap_bf16_2d(&tA, w.act, rows, I, I, GEMM_BM, 64))) return rc;
-    if ((rc = make_tmap_bf16_3d(&tB, a->w_down, nl, H, I, I, (uint64_t)H * I, BN, 64))) return rc;
-    if ((rc = make_tmap_bf16_3d(&tBs, a->w_shared_down, 1, H, I, I, (uint64_t)H * I, BN, 64)))
+    if (nl > 0 && (rc = make_tmap_bf16_3d(&tB, a->w_down, nl, H, I, I, (uint64_t)H * I, BN, 64)))
       return rc;
+    if (shared && (rc = make_tmap_bf16_3d(&tBs, a->w_shared_down, 1, H, I, I, (uint64_t)H * I, BN, 64)))
+      return rc;
+    if (nl == 0) tB = tBs;
+    if (!shared) tBs = tB;
     GemmArgs g = gemm_args_default(w.status);
     g.mtile_start = w.mtile_start;
     g.row_start = w.row_start;
     g.num_groups = G;
     g.n_tiles = H / BN;
     g.k_blocks = I / 64;
-    g.shared_group = 0;
+    g.shared_group = shared ? 0 : -1;
     g.b_group_base = 1;
     g.row_scale = w.perm_w;
     g.out = w.yw;
@@ -745,16 +812,17 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
     if ((rc = launch_gemm<BN, 4, EPI_SCALE_BF16, false>(tA, tA, tB, tBs, tBs, g, grid, st))) return rc;
     record_event(a->timing_events[3], st);
   }
-  // 6. combine: out[t] = yw[t] + sum_j yw[row_of[t, j]]
+  // 6. combine: out[t] = yw[t] (shared) + sum_j yw[row_of[t, j]] + sum_j pair_rows[pair_index[t, j]]
   {
     const int blocks = (T * 32 + 255) / 256;
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a->out);
+    const __nv_bfloat16* pr = static_cast<const __nv_bfloat16*>(a->pair_rows);
     if (H <= 2048)
-      k_moe_combine<8><<<blocks, 256, 0, st>>>(w.yw, w.row_of, T, k, H, out);
+      k_moe_combine<8><<<blocks, 256, 0, st>>>(w.yw, w.row_of, T, k, H, shared, pr, a->pair_index, out);
     else if (H <= 4096)
-      k_moe_combine<16><<<blocks, 256, 0, st>>>(w.yw, w.row_of, T, k, H, out);
+      k_moe_combine<16><<<blocks, 256, 0, st>>>(w.yw, w.row_of, T, k, H, shared, pr, a->pair_index, out);
     else
-      k_moe_combine<32><<<blocks, 256, 0, st>>>(w.yw, w.row_of, T, k, H, out);
+      k_moe_combine<32><<<blocks, 256, 0, st>>>(w.yw, w.row_of, T, k, H, shared, pr, a->pair_index, out);
     { int _rc = launched("k_moe_combine"); if (_rc) return _rc; }
   }
   (void)E;

@@ -57,9 +57,9 @@ struct PodParams {
   long long bt_stride;
   const int32_t* context_lens;
   const int32_t* cu_seqlens_q;
-  const __nv_bfloat16* gate;
+  const __nv_bfloat16* gate;   // output gate (pre-sigmoid) or null for no gate
   long long gate_st, gate_sh;
-  __nv_bfloat16* ogated;       // [N, Hq*D] gated attention output (o_proj input)
+  __nv_bfloat16* ogated;       // [N, Hq*D] gated attention output (o_proj input) or null
   __nv_bfloat16* attn_out;     // optional [N, Hq*D] pre-gate attention output
   float* part_o;               // [B, max_splits, Hq, D]
   float* part_lse;             // [B, max_splits, Hq]
@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
           const long long tok = (long long)q0 + qrow;
           const __nv_bfloat16* grow = p.gate + tok * p.gate_st + (long long)h * p.gate_sh;
-          __nv_bfloat16* orow = p.ogated + tok * (long long)(p.Hq * POD_D) + h * POD_D;
+          __nv_bfloat16* orow = p.ogated ? p.ogated + tok * (long long)(p.Hq * POD_D) + h * POD_D : nullptr;
 #pragma unroll 1
           for (int c = 0; c < 8; ++c) {
             uint32_t r[32];
@@ -473,19 +473,34 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
                                       pack_bf16x2(o[8 * q + 4], o[8 * q + 5]),
                                       pack_bf16x2(o[8 * q + 6], o[8 * q + 7]));
               }
-              const uint4* gsrc = reinterpret_cast<const uint4*>(grow + c * 32);
-              uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+              if (p.ogated) {
+                // o_proj input: o * sigmoid(gate), or o itself when there is no gate
+                float gs[32];
+                if (p.gate) {
+                  const uint4* gsrc = reinterpret_cast<const uint4*>(grow + c * 32);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const uint4 g = gsrc[q];
-                dst[q] = make_uint4(pack_bf16x2(o[8 * q] * sigmoid_f(bf16_lo(g.x)),
-                                                o[8 * q + 1] * sigmoid_f(bf16_hi(g.x))),
-                                    pack_bf16x2(o[8 * q + 2] * sigmoid_f(bf16_lo(g.y)),
-                                                o[8 * q + 3] * sigmoid_f(bf16_hi(g.y))),
-                                    pack_bf16x2(o[8 * q + 4] * sigmoid_f(bf16_lo(g.z)),
-                                                o[8 * q + 5] * sigmoid_f(bf16_hi(g.z))),
-                                    pack_bf16x2(o[8 * q + 6] * sigmoid_f(bf16_lo(g.w)),
-                                                o[8 * q + 7] * sigmoid_f(bf16_hi(g.w))));
+                  for (int q = 0; q < 4; ++q) {
+                    const uint4 g = gsrc[q];
+                    gs[8 * q] = sigmoid_f(bf16_lo(g.x));
+                    gs[8 * q + 1] = sigmoid_f(bf16_hi(g.x));
+                    gs[8 * q + 2] = sigmoid_f(bf16_lo(g.y));
+                    gs[8 * q + 3] = sigmoid_f(bf16_hi(g.y));
+                    gs[8 * q + 4] = sigmoid_f(bf16_lo(g.z));
+                    gs[8 * q + 5] = sigmoid_f(bf16_hi(g.z));
+                    gs[8 * q + 6] = sigmoid_f(bf16_lo(g.w));
+                    gs[8 * q + 7] = sigmoid_f(bf16_hi(g.w));
+                  }
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) gs[i] = 1.f;
+                }
+                uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                  dst[q] = make_uint4(pack_bf16x2(o[8 * q] * gs[8 * q], o[8 * q + 1] * gs[8 * q + 1]),
+                                      pack_bf16x2(o[8 * q + 2] * gs[8 * q + 2], o[8 * q + 3] * gs[8 * q + 3]),
+                                      pack_bf16x2(o[8 * q + 4] * gs[8 * q + 4], o[8 * q + 5] * gs[8 * q + 5]),
+                                      pack_bf16x2(o[8 * q + 6] * gs[8 * q + 6], o[8 * q + 7] * gs[8 * q + 7]));
               }
             }
           }

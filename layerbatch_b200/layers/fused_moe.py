@@ -1,0 +1,100 @@
+"""Drop-in MoE modules with the reference's constructor signatures and parameter names
+(nanovllm/models/qwen3_5.py:754-917), computed by the sm_100a library.
+
+* ``Qwen3_5TopKRouter`` (qwen3_5.py:754-774): router GEMM on tensor cores, then the
+  top-k kernel (softmax fp32, lowest-index ties, renormalised, cast to the input dtype).
+* ``Qwen3_5SparseMoeBlock`` (qwen3_5.py:881-905): the whole block in one library call,
+  ``lb_moe_forward``: router, top-k, permutation, grouped SwiGLU GEMM of the routed and
+  shared experts, grouped down GEMM with the routing weight and the sigmoid shared gate
+  fused, and the combine.  The prefill/decode split of ``Qwen3_5Experts.forward``
+  (qwen3_5.py:802-813) disappears: one path serves both.
+* ``fused_moe`` is the functional form over borrowed parameter tensors.
+
+Parameters are registered exactly as the reference loader expects (``gate.weight``,
+``experts.gate_up_proj``, ``experts.down_proj``, ``shared_expert.{gate,up,down}_proj.weight``,
+``shared_expert_gate.weight``), so a reference state dict loads unchanged.  With an
+expert-parallel shard (``ep_rank``/``ep_size``) the module holds only its slice of the
+expert tensors and ``layerbatch_b200.engine.sharding`` routes tokens between ranks.
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from .. import ops
+
+
+def fused_moe(x, router_w, gate_up, down, sh_gate, sh_up, sh_down, sh_gate_w, top_k,
+              out=None, expert_base=0):
+    return ops.moe_forward(x.contiguous(), router_w, gate_up, down, sh_gate, sh_up, sh_down,
+                           sh_gate_w, top_k, out=out, expert_base=expert_base)
+
+
+class Qwen3_5TopKRouter(nn.Module):
+
+    def __init__(self, num_experts: int, hidden_size: int, top_k: int):
+        super().__init__()
+        self.top_k = top_k
+        self.num_experts = num_experts
+        self.weight = nn.Parameter(torch.zeros(num_experts, hidden_size))
+
+    def forward(self, hidden_states: torch.Tensor):
+        logits = ops.gemm(hidden_states.contiguous(), self.weight)
+        ids, _, wb = ops.router_topk(logits, self.top_k)
+        return wb.to(hidden_states.dtype), ids.long()
+
+
+class Qwen3_5Experts(nn.Module):
+
+    def __init__(self, num_experts: int, hidden_size: int, moe_intermediate_size: int):
+        super().__init__()
+        self.num_experts = num_experts
+        self.hidden_size = hidden_size
+        self.intermediate_size = moe_intermediate_size
+        self.gate_up_proj = nn.Parameter(
+            torch.empty(num_experts, 2 * moe_intermediate_size, hidden_size))
+        self.down_proj = nn.Parameter(torch.empty(num_experts, hidden_size, moe_intermediate_size))
+
+
+class Qwen3_5SharedExpertMLP(nn.Module):
+
+    def __init__(self, hidden_size: int, intermediate_size: int):
+        super().__init__()
+        self.gate_proj = nn.Linear(hidden_size, intermediate_size, bias=False)
+        self.up_proj = nn.Linear(hidden_size, intermediate_size, bias=False)
+        self.down_proj = nn.Linear(intermediate_size, hidden_size, bias=False)
+
+
+class Qwen3_5SparseMoeBlock(nn.Module):
+
+    def __init__(self, hidden_size: int, num_experts: int, num_experts_per_tok: int,
+                 moe_intermediate_size: int, shared_expert_intermediate_size: int,
+                 ep_rank: int = 0, ep_size: int = 1):
+        super().__init__()
+        if num_experts % ep_size:
+            raise ValueError("num_experts must divide by ep_size")
+        self.num_experts = num_experts
+        self.top_k = num_experts_per_tok
+        self.ep_rank, self.ep_size = ep_rank, ep_size
+        self.local_experts = num_experts // ep_size
+        self.expert_base = ep_rank * self.local_experts
+        self.gate = Qwen3_5TopKRouter(num_experts, hidden_size, num_experts_per_tok)
+        self.experts = Qwen3_5Experts(self.local_experts, hidden_size, moe_intermediate_size)
+        self.shared_expert = Qwen3_5SharedExpertMLP(hidden_size, shared_expert_intermediate_size)
+        self.shared_expert_gate = nn.Linear(hidden_size, 1, bias=False)
+
+    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        if self.ep_size > 1:
+            from ..engine.sharding import ep_moe_forward
+            return ep_moe_forward(self, hidden_states)
+        return fused_moe(hidden_states, self.gate.weight, self.experts.gate_up_proj,
+                         self.experts.down_proj, self.shared_expert.gate_proj.weight,
+                         self.shared_expert.up_proj.weight, self.shared_expert.down_proj.weight,
+                         self.shared_expert_gate.weight, self.top_k)
+
+    def load_expert_shard(self, gate_up_full: torch.Tensor, down_full: torch.Tensor):
+        """Copy this rank's slice of full ``[E, ...]`` expert tensors (expert parallel)."""
+        s, e = self.expert_base, self.expert_base + self.local_experts
+        with torch.no_grad():
+            self.experts.gate_up_proj.copy_(gate_up_full[s:e])
+            self.experts.down_proj.copy_(down_full[s:e])

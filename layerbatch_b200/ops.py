@@ -103,31 +103,53 @@ def moe_permute(ids: torch.Tensor, expert_base: int, num_local_experts: int):
 
 
 def moe_forward(x, router, gate_up, down, sh_gate, sh_up, sh_down, sh_gate_w, top_k,
-                out=None, expert_base=0, return_routing=False, ws_tag="moe", events=None):
-    """The full MoE block (router -> experts -> shared expert -> combine) on the GPU."""
+                out=None, expert_base=0, return_routing=False, ws_tag="moe", events=None,
+                topk_ids=None, topk_weights=None, pair_rows=None, pair_index=None,
+                num_experts=None):
+    """The MoE block (router -> experts -> shared expert -> combine) on the GPU.
+
+    Expert-parallel building blocks (all optional):
+    * ``topk_ids`` [T,k] int32 global expert ids and ``topk_weights`` [T,k] fp32 given:
+      the router is skipped (``router`` may be None; pass ``num_experts``);
+    * ``sh_gate=None``: no shared expert;
+    * ``gate_up``/``down`` with 0 local experts (shape [0, ...]) or None: no routed compute;
+    * ``pair_rows`` [*, H] bf16 + ``pair_index`` [T, k] int32: rows computed elsewhere that
+      the combine adds into ``out[t]`` (-1 = none).
+    """
     T, H = x.shape
-    E = router.shape[0]
-    nl, I2, _ = gate_up.shape
-    I = I2 // 2
+    given = topk_ids is not None
+    E = num_experts if num_experts is not None else router.shape[0]
+    nl = 0 if gate_up is None else gate_up.shape[0]
+    I = (down.shape[2] if down is not None and nl else sh_down.shape[1])
+    shared = sh_gate is not None
     if out is None:
         out = torch.empty_like(x)
     for name, t in (("x", x), ("router", router), ("gate_up", gate_up), ("down", down),
                     ("sh_gate", sh_gate), ("sh_up", sh_up), ("sh_down", sh_down),
-                    ("sh_gate_w", sh_gate_w), ("out", out)):
+                    ("sh_gate_w", sh_gate_w), ("out", out), ("pair_rows", pair_rows)):
+        if t is None:
+            continue
         if t.dtype != torch.bfloat16 or not t.is_contiguous() or not t.is_cuda:
             raise ValueError(f"{name} must be a contiguous CUDA bf16 tensor")
     logits = ids = wb = None
-    if return_routing:
+    if return_routing and not given:
         logits = torch.empty(T, E, dtype=torch.bfloat16, device=x.device)
         ids = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
         wb = torch.empty(T, top_k, dtype=torch.bfloat16, device=x.device)
+    if given:
+        ids = topk_ids.to(torch.int32).contiguous()
+        topk_weights = topk_weights.to(torch.float32).contiguous()
+    if pair_index is not None:
+        pair_index = pair_index.to(torch.int32).contiguous()
     a = LbMoeArgs(num_tokens=T, hidden=H, num_experts=E, top_k=top_k, inter=I,
-                  shared_inter=sh_gate.shape[0], expert_base=expert_base, num_local_experts=nl,
-                  x=x.data_ptr(), w_router=router.data_ptr(), w_gate_up=gate_up.data_ptr(),
-                  w_down=down.data_ptr(), w_shared_gate=sh_gate.data_ptr(),
-                  w_shared_up=sh_up.data_ptr(), w_shared_down=sh_down.data_ptr(),
-                  w_shared_expert_gate=sh_gate_w.data_ptr(), out=out.data_ptr(),
-                  router_logits=ptr(logits), topk_ids=ptr(ids), topk_weights=ptr(wb))
+                  shared_inter=sh_gate.shape[0] if shared else 0, expert_base=expert_base,
+                  num_local_experts=nl, x=x.data_ptr(), w_router=ptr(router),
+                  w_gate_up=ptr(gate_up) if nl else None, w_down=ptr(down) if nl else None,
+                  w_shared_gate=ptr(sh_gate), w_shared_up=ptr(sh_up), w_shared_down=ptr(sh_down),
+                  w_shared_expert_gate=ptr(sh_gate_w), out=out.data_ptr(),
+                  router_logits=ptr(logits), topk_ids=ptr(ids), topk_weights=ptr(wb),
+                  routing_given=int(given), topk_weights_f32=ptr(topk_weights),
+                  no_shared=int(not shared), pair_rows=ptr(pair_rows), pair_index=ptr(pair_index))
     _events(a, events)
     need = C.c_size_t(0)
     check(lib().lb_moe_workspace_size(C.byref(a), C.byref(need)), "lb_moe_workspace_size")
@@ -135,7 +157,7 @@ def moe_forward(x, router, gate_up, down, sh_gate, sh_up, sh_down, sh_gate_w, to
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws.numel()
     check(lib().lb_moe_forward(C.byref(a), stream_ptr()), "lb_moe_forward")
-    if return_routing:
+    if return_routing and not given:
         return out, logits, ids, wb
     return out
 
@@ -163,24 +185,40 @@ def pod_args(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q
     return LbPodArgs(
         num_seqs=B, num_tokens=N, max_q_len=max_q_len, num_q_heads=Hq, num_kv_heads=Hkv,
         head_dim=D, page_size=ps, num_pages=nb, max_pages_per_seq=block_tables.shape[1],
-        hidden=w_o.shape[0], sm_scale=float(scale), kv_split_pages=kv_split_pages,
+        hidden=w_o.shape[0] if w_o is not None else 0, sm_scale=float(scale),
+        kv_split_pages=kv_split_pages,
         q=q.data_ptr(), q_stride_tok=q.stride(0), q_stride_head=q.stride(1),
-        gate=gate.data_ptr(), gate_stride_tok=gate.stride(0), gate_stride_head=gate.stride(1),
+        gate=ptr(gate), gate_stride_tok=gate.stride(0) if gate is not None else 0,
+        gate_stride_head=gate.stride(1) if gate is not None else 0,
         k_cache=k_cache.data_ptr(), v_cache=v_cache.data_ptr(),
         block_tables=block_tables.data_ptr(), context_lens=context_lens.data_ptr(),
-        cu_seqlens_q=cu_seqlens_q.data_ptr(), w_o=w_o.data_ptr(), attn_out=ptr(attn_out),
-        out=out.data_ptr(), out_fp32=int(out.dtype == torch.float32))
+        cu_seqlens_q=cu_seqlens_q.data_ptr(), w_o=ptr(w_o), attn_out=ptr(attn_out),
+        out=ptr(out), out_fp32=int(out is not None and out.dtype == torch.float32))
 
 
 def pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o,
                    scale, out=None, attn_out=None, max_q_len=None, kv_split_pages=0,
                    ws_tag="pod", events=None):
-    """Fused paged attention (prefill + decode mixed) -> sigmoid gate -> o_proj."""
-    N = q.shape[0]
-    if out is None:
+    """Fused paged attention (prefill + decode mixed) -> sigmoid gate -> o_proj.
+
+    ``gate`` may be None (no output gate).  With ``w_o=None`` only the attention runs and
+    ``attn_out`` [N, Hq*D] receives it; the function then returns ``attn_out``.
+    ``out`` may be fp32 to receive the o_proj partial sums unrounded (tensor parallel).
+    """
+    N, Hq, D = q.shape
+    for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache)):
+        if t.dtype != torch.bfloat16 or not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA bf16 tensor")
+    if w_o is None:
+        if attn_out is None:
+            attn_out = torch.empty(N, Hq * D, dtype=torch.bfloat16, device=q.device)
+    elif out is None:
         out = torch.empty(N, w_o.shape[0], dtype=torch.bfloat16, device=q.device)
-    a = pod_args(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o, scale,
-                 out, attn_out, max_q_len, kv_split_pages)
+    bt = block_tables.to(torch.int32)
+    cl = context_lens.to(torch.int32)
+    cu = cu_seqlens_q.to(torch.int32)
+    a = pod_args(q, gate, k_cache, v_cache, bt, cl, cu, w_o, scale, out, attn_out, max_q_len,
+                 kv_split_pages)
     _events(a, events)
     need = C.c_size_t(0)
     check(lib().lb_pod_workspace_size(C.byref(a), C.byref(need)), "lb_pod_workspace_size")
@@ -188,4 +226,4 @@ def pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seq
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws.numel()
     check(lib().lb_pod_attn_oproj(C.byref(a), stream_ptr()), "lb_pod_attn_oproj")
-    return out
+    return out if w_o is not None else attn_out

@@ -126,3 +126,44 @@ def test_moe_block_vs_reference_golden(cuda, golden):
     same = OM.same_up_to_ties(ids, g["topk_ids"], g["logits"])
     assert float(same.float().mean()) >= 0.95
     assert OM.rel_err(out[same], g["y_sparse"][same]) <= TOL
+
+
+def test_expert_parallel_building_blocks_emulated(cuda):
+    """Routing given / no shared expert / rows added from elsewhere: splitting the experts
+    over P virtual ranks in one process reproduces the single-call block bit for bit in
+    routing and within tolerance in value."""
+    T, H, E, I, k, P = 200, 2048, 64, 512, 8, 4
+    p = W.make_moe_params(H, E, I, I, k, seed=3)
+    x = W.make_moe_input(T, H, seed=4)
+    pd, xd = p.to(cuda), x.to(cuda)
+    ref, logits, ids, _ = ops.moe_forward(xd, pd.router, pd.gate_up, pd.down, pd.sh_gate,
+                                          pd.sh_up, pd.sh_down, pd.sh_gate_w, k,
+                                          return_routing=True)
+    _, wf, _ = ops.router_topk(logits, k)
+    nl = E // P
+    dest = ids.long() // nl
+    order = torch.argsort(dest.reshape(-1), stable=True)
+    counts = torch.bincount(dest.reshape(-1), minlength=P).tolist()
+    flat_ids, flat_w = ids.reshape(-1)[order], wf.reshape(-1)[order]
+    rows_x = xd[(order // k)]
+    y_parts, s0 = [], 0
+    for r in range(P):
+        n = counts[r]
+        if n == 0:
+            continue
+        y_parts.append(ops.moe_forward(
+            rows_x[s0:s0 + n].contiguous(), None, pd.gate_up[r * nl:(r + 1) * nl],
+            pd.down[r * nl:(r + 1) * nl], None, None, None, None, 1, expert_base=r * nl,
+            topk_ids=flat_ids[s0:s0 + n].view(n, 1), topk_weights=flat_w[s0:s0 + n].view(n, 1),
+            num_experts=E, ws_tag=f"ep{r}"))
+        s0 += n
+    y_send = torch.cat(y_parts, 0)
+    pair_pos = torch.empty(T * k, dtype=torch.int32, device=cuda)
+    pair_pos[order] = torch.arange(T * k, dtype=torch.int32, device=cuda)
+    out = ops.moe_forward(xd, None, None, None, pd.sh_gate, pd.sh_up, pd.sh_down, pd.sh_gate_w,
+                          k, topk_ids=ids, topk_weights=wf, num_experts=E,
+                          pair_rows=y_send, pair_index=pair_pos.view(T, k), ws_tag="ep_src")
+    torch.cuda.synchronize()
+    y32 = OM.moe_block_fp32(x, p, ids.cpu().long(), wf.cpu())
+    assert OM.rel_err(out.cpu(), y32) <= TOL
+    assert OM.rel_err(out.cpu(), ref.cpu()) <= TOL
