@@ -224,15 +224,46 @@ def run_ours(args, rank, world, device):
     from layerbatch_b200 import workloads as W
     cfg = args.config
     seed = 1 + rank
-    attn = attn_batch_for(cfg, seed, device)
-    T_moe = moe_tokens_for(cfg, attn)
+    sharded = world > 1 and cfg == "c4"
+    tp = 2 if (sharded and world % 2 == 0) else 1
+    tp_group, shard, ep_block = None, None, None
+    if sharded:
+        # TP pairs by KV head, data parallel across pairs, experts split over all ranks.
+        # Per-GPU work stays that of one c4 batch: a TP pair runs tp batches.
+        from layerbatch_b200.engine import sharding as S
+        from layerbatch_b200.layers.fused_moe import Qwen3_5SparseMoeBlock
+        groups = [torch.distributed.new_group(list(range(g * tp, (g + 1) * tp)))
+                  for g in range(world // tp)] if tp > 1 else []
+        gid, tp_rank = rank // tp, rank % tp
+        tp_group = groups[gid] if tp > 1 else None
+        shard = S.attention_shard(16, 2, tp_rank, tp)
+        dec = W.uniform_ctx(512 * tp, 1024, 16384, seed=100 + gid)
+        attn = W.make_attn_batch(dec, [(0, 4096)] * tp, Hq=16 // tp, Hkv=2 // tp, H=2048,
+                                 seed=1000 + rank, device=device)
+        attn.scale = 256 ** -0.5
+    else:
+        attn = attn_batch_for(cfg, seed, device)
+    T_moe = moe_tokens_for(cfg, attn) if not sharded else 4608
     moe = None
     if T_moe:
         p = W.make_moe_params(2048, 512, 512, 512, 10, seed=0, device=device)
         x = W.make_moe_input(T_moe, 2048, seed=seed, device=device)
         W.apply_zipf_bias(p, x)
         moe = (p, x)
-    tokens = attn.num_tokens if attn is not None else T_moe
+        if sharded:
+            ep_block = Qwen3_5SparseMoeBlock(2048, 512, 10, 512, 512, ep_rank=rank,
+                                             ep_size=world).to(torch.bfloat16).to(device)
+            with torch.no_grad():
+                ep_block.gate.weight.copy_(p.router)
+                ep_block.load_expert_shard(p.gate_up, p.down)
+                ep_block.shared_expert.gate_proj.weight.copy_(p.sh_gate)
+                ep_block.shared_expert.up_proj.weight.copy_(p.sh_up)
+                ep_block.shared_expert.down_proj.weight.copy_(p.sh_down)
+                ep_block.shared_expert_gate.weight.copy_(p.sh_gate_w)
+            del p
+            moe = (None, x)
+            torch.cuda.empty_cache()
+    tokens = (attn.num_tokens // tp) if attn is not None else T_moe
     max_q = max(attn.qlen_list) if attn is not None else 0
 
     a_out = torch.empty(attn.num_tokens, attn.w_o.shape[0], dtype=torch.bfloat16,
@@ -241,15 +272,24 @@ def run_ours(args, rank, world, device):
 
     def step(ev_a=None, ev_m=None, q=None, gate=None, x=None):
         if attn is not None:
-            ops.pod_attn_oproj(q if q is not None else attn.q, gate if gate is not None else attn.gate,
-                               attn.k_cache, attn.v_cache, attn.block_tables, attn.context_lens,
-                               attn.cu_seqlens_q, attn.w_o, attn.scale, out=a_out,
-                               max_q_len=max_q, events=ev_a)
+            qq = q if q is not None else attn.q
+            gg = gate if gate is not None else attn.gate
+            if sharded:
+                S.tp_attention_oproj(shard, qq, gg, attn.k_cache, attn.v_cache, attn.block_tables,
+                                     attn.context_lens, attn.cu_seqlens_q, attn.w_o, attn.scale,
+                                     group=tp_group, max_q_len=max_q, events=ev_a, out=a_out)
+            else:
+                ops.pod_attn_oproj(qq, gg, attn.k_cache, attn.v_cache, attn.block_tables,
+                                   attn.context_lens, attn.cu_seqlens_q, attn.w_o, attn.scale,
+                                   out=a_out, max_q_len=max_q, events=ev_a)
         if moe:
             pm, xm = moe
-            ops.moe_forward(x if x is not None else xm, pm.router, pm.gate_up, pm.down,
-                            pm.sh_gate, pm.sh_up, pm.sh_down, pm.sh_gate_w, 10, out=m_out,
-                            events=ev_m)
+            xx = x if x is not None else xm
+            if sharded:
+                m_out.copy_(ep_block(xx))
+            else:
+                ops.moe_forward(xx, pm.router, pm.gate_up, pm.down, pm.sh_gate, pm.sh_up,
+                                pm.sh_down, pm.sh_gate_w, 10, out=m_out, events=ev_m)
 
     def barrier():
         if world > 1:
@@ -268,7 +308,8 @@ def run_ours(args, rank, world, device):
     with ClockSampler(torch.cuda.current_device()) as clk:
         st.record()
         for i in range(K):
-            step(ev_attn[i] if attn is not None else None, ev_moe[i] if moe else None)
+            step(ev_attn[i] if attn is not None else None,
+                 ev_moe[i] if (moe and not sharded) else None)
         en.record()
         torch.cuda.synchronize()
     barrier()
@@ -279,7 +320,7 @@ def run_ours(args, rank, world, device):
         torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
     ms = float(ms_t)
     ws_status = 0
-    for tag in ("pod", "moe"):
+    for tag in ("pod", "moe", "tp_attn", "ep_owner", "ep_source"):
         if (torch.cuda.current_device(), tag) in ops._WS:
             ws_status |= ops.device_status(ops._WS[(torch.cuda.current_device(), tag)])
 
@@ -291,11 +332,14 @@ def run_ours(args, rank, world, device):
         flops, byts = attn_work(attn)
         res["attn"] = {"ms": t_attn * 1e3, "flops": flops, "bytes": byts,
                        "gbs": byts / t_attn / 1e9, "tflops": flops / t_attn / 1e12}
-    if moe:
-        pm, xm = moe
+    if moe and not sharded:
         t_g1 = statistics.mean(e[0].elapsed_time(e[1]) for e in ev_moe) * 1e-3
         t_g2 = statistics.mean(e[2].elapsed_time(e[3]) for e in ev_moe) * 1e-3
         res["moe_gemm"] = {"gate_up_ms": t_g1 * 1e3, "down_ms": t_g2 * 1e3}
+    res["parallelism"] = (f"tp{tp} x dp{world // tp} attention (KV-head shards, fp32 o_proj "
+                          f"all-reduce), ep{world} MoE (NCCL all-to-all)" if sharded else
+                          ("single GPU" if world == 1 else
+                           f"dp{world}: per-rank batches, experts replicated"))
     res["peaks"] = peaks
 
     # ---------------- end-to-end through the public API with host buffers
@@ -431,8 +475,7 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
             "config": dict(cfg_desc, tokens_per_step_per_gpu=res["tokens"],
                            l2="inputs larger than L2 (KV cache and expert weights are GBs)",
-                           parallelism=(f"dp{world}: per-rank batches, experts replicated"
-                                        if world > 1 else "single GPU")),
+                           parallelism=res["parallelism"]),
             "roofline": roof, "cpu_baseline": cpu, "clocks": res["clocks"],
             "gpu_launches": res["launches"],
         }

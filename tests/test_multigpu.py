@@ -1,0 +1,96 @@
+"""Tensor / expert parallel on 2 GPUs with NCCL (skipped with fewer than 2 GPUs).
+
+Each rank compares the sharded result with the single-GPU library call on the same
+inputs: attention TP by KV head with the fp32 o_proj all-reduce, and the MoE block with
+experts split over the ranks and the all-to-all exchange.  NVLS is off (plain NCCL
+transport) and the process group has a short timeout.
+"""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    try:
+        import sys
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        import torch.distributed as dist
+        from layerbatch_b200 import ops
+        from layerbatch_b200 import workloads as W
+        from layerbatch_b200.engine import sharding as S
+        from layerbatch_b200.layers.fused_moe import Qwen3_5SparseMoeBlock
+        from oracle import moe as OM
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        errs = {}
+        # ---- attention, TP by KV head
+        b = W.make_attn_batch([900, 2000, 64], [(128, 300)], seed=31).to(dev)
+        full = ops.pod_attn_oproj(b.q, b.gate, b.k_cache, b.v_cache, b.block_tables,
+                                  b.context_lens, b.cu_seqlens_q, b.w_o, b.scale, max_q_len=300,
+                                  ws_tag="full")
+        shard = S.attention_shard(16, 2, rank, world)
+        qs, gs, kc, vc, wo = S.shard_attention_tensors(shard, b.q, b.gate, b.k_cache, b.v_cache,
+                                                       b.w_o, 256)
+        tp = S.tp_attention_oproj(shard, qs, gs, kc, vc, b.block_tables, b.context_lens,
+                                  b.cu_seqlens_q, wo, b.scale, max_q_len=300)
+        errs["tp"] = OM.rel_err(tp.float(), full.float())
+        # ---- MoE, expert parallel with all-to-all
+        H, E, I, k, T = 2048, 64, 512, 8, 96 + 32 * rank
+        p = W.make_moe_params(H, E, I, I, k, seed=0).to(dev)
+        x = W.make_moe_input(T, H, seed=40 + rank).to(dev)
+        blk = Qwen3_5SparseMoeBlock(H, E, k, I, I, ep_rank=rank, ep_size=world).to(torch.bfloat16).to(dev)
+        with torch.no_grad():
+            blk.gate.weight.copy_(p.router)
+            blk.load_expert_shard(p.gate_up, p.down)
+            blk.shared_expert.gate_proj.weight.copy_(p.sh_gate)
+            blk.shared_expert.up_proj.weight.copy_(p.sh_up)
+            blk.shared_expert.down_proj.weight.copy_(p.sh_down)
+            blk.shared_expert_gate.weight.copy_(p.sh_gate_w)
+            y_ep = blk(x)
+        y_1 = ops.moe_forward(x, p.router, p.gate_up, p.down, p.sh_gate, p.sh_up, p.sh_down,
+                              p.sh_gate_w, k, ws_tag="moe_full")
+        torch.cuda.synchronize()
+        errs["ep"] = OM.rel_err(y_ep.float(), y_1.float())
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok", errs))
+    except Exception as e:
+        q.put((rank, "fail", repr(e)))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_tp_attention_and_ep_moe_on_two_gpus():
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    res = sorted(q.get(timeout=300) for _ in range(2))
+    for pr in procs:
+        pr.join(timeout=60)
+        if pr.is_alive():
+            pr.kill()
+    assert all(r[1] == "ok" for r in res), res
+    for _, _, errs in res:
+        assert errs["tp"] <= 2e-2 and errs["ep"] <= 2e-2, errs
