@@ -265,6 +265,7 @@ def run_ours(args, rank, world, device):
             torch.cuda.empty_cache()
     tokens = (attn.num_tokens // tp) if attn is not None else T_moe
     max_q = max(attn.qlen_list) if attn is not None else 0
+    hint = ops.pod_work_hint(attn.ctx_list, attn.qlen_list) if attn is not None else None
 
     a_out = torch.empty(attn.num_tokens, attn.w_o.shape[0], dtype=torch.bfloat16,
                         device=device) if attn is not None else None
@@ -277,11 +278,12 @@ def run_ours(args, rank, world, device):
             if sharded:
                 S.tp_attention_oproj(shard, qq, gg, attn.k_cache, attn.v_cache, attn.block_tables,
                                      attn.context_lens, attn.cu_seqlens_q, attn.w_o, attn.scale,
-                                     group=tp_group, max_q_len=max_q, events=ev_a, out=a_out)
+                                     group=tp_group, max_q_len=max_q, events=ev_a, out=a_out,
+                                     work_hint=hint)
             else:
                 ops.pod_attn_oproj(qq, gg, attn.k_cache, attn.v_cache, attn.block_tables,
                                    attn.context_lens, attn.cu_seqlens_q, attn.w_o, attn.scale,
-                                   out=a_out, max_q_len=max_q, events=ev_a)
+                                   out=a_out, max_q_len=max_q, events=ev_a, work_hint=hint)
         if moe:
             pm, xm = moe
             xx = x if x is not None else xm

@@ -154,7 +154,7 @@ int lb_store_kvcache(const void* k, int64_t k_stride, const void* v, int64_t v_s
  * positions out of context_lens[b] tokens already in the paged cache (bottom-right
  * causal).  Output: out[N, hidden] = (attn(q) * sigmoid(gate)).flatten() . W_o^T. */
 typedef struct LbPodArgs {
-  int64_t num_seqs;           /* B */
+  int64_t num_seqs;           /* B (<= 16000) */
   int64_t num_tokens;         /* N = cu_seqlens_q[B] */
   int64_t max_q_len;          /* upper bound on any sequence's query length */
   int64_t num_q_heads;        /* Hq */
@@ -185,6 +185,11 @@ typedef struct LbPodArgs {
   /* optional cudaEvent_t handles recorded around the attention kernel ([0], [1]) and the
    * o_proj GEMM ([2], [3]); NULL entries are skipped */
   void* timing_events[4];
+  /* optional host-side work hints (0 = estimate from the shapes): query-key pairs of the
+   * prefill rows (sum over prefill sequences of L*(C-L) + L*(L+1)/2) and context tokens
+   * of the decode sequences; they set how many SMs start on prefill tiles */
+  int64_t prefill_pairs_hint;
+  int64_t decode_tokens_hint;
 } LbPodArgs;
 
 int lb_pod_workspace_size(const LbPodArgs* args, size_t* bytes);

@@ -57,7 +57,7 @@ class LbPodArgs(C.Structure):
         ("k_cache", vp), ("v_cache", vp), ("block_tables", vp), ("context_lens", vp),
         ("cu_seqlens_q", vp), ("w_o", vp), ("attn_out", vp), ("out", vp),
         ("out_fp32", i32), ("workspace", vp), ("workspace_bytes", C.c_size_t),
-        ("timing_events", vp * 4),
+        ("timing_events", vp * 4), ("prefill_pairs_hint", i64), ("decode_tokens_hint", i64),
     ]
 
 

@@ -32,18 +32,22 @@ __global__ void k_store_kvcache(const __nv_bfloat16* __restrict__ k, long long k
 
 
 // ------------------------------------------------------------------------------ plan
-// One block: per-sequence item counts, block-wide exclusive scans, item lists.
-// Prefill items are emitted latest query tile first (longest causal range first).
+// One block.  Phase 1: per-sequence item counts and block-wide exclusive scans give every
+// sequence its first item slots (kept in shared memory).  Phase 2: one warp per sequence
+// writes its items with the lanes in parallel.  Queue order is longest first, so the
+// dynamic scheduler ends on short items: prefill tiles latest query tile first; decode
+// items all full-length splits first, then every sequence's shorter last split.
 __global__ void k_pod_plan(const int32_t* __restrict__ ctx_lens, const int32_t* __restrict__ cu,
                            int B, int Hq, int Hkv, int split_tokens, int max_splits,
                            int max_ctx, int pf_cap, int dec_cap, int4* __restrict__ pf_items,
                            int* __restrict__ counters, int4* __restrict__ dec_items,
                            int* __restrict__ status) {
-  __shared__ int s_pf[1024], s_dec[1024];
+  __shared__ int s_pf[1024], s_full[1024], s_rem[1024];
+  extern __shared__ int s_off[];  // [3 * B]: first prefill / full-split / last-split item
   const int tid = threadIdx.x;
   const int per = (B + 1023) / 1024;
   const int b0 = min(B, tid * per), b1 = min(B, b0 + per);
-  int npf = 0, ndec = 0;
+  int npf = 0, nfull = 0, nrem = 0;
   for (int b = b0; b < b1; ++b) {
     const int qlen = cu[b + 1] - cu[b];
     const int ctx = ctx_lens[b];
@@ -51,48 +55,73 @@ __global__ void k_pod_plan(const int32_t* __restrict__ ctx_lens, const int32_t* 
       if (qlen != 0) report(status, LB_DEV_BAD_INDEX);
       continue;
     }
-    if (qlen == 1)
-      ndec += Hkv * min(max_splits, (ctx + split_tokens - 1) / split_tokens);
-    else
+    if (qlen == 1) {
+      nfull += Hkv * (ctx / split_tokens);
+      nrem += (ctx % split_tokens) ? Hkv : 0;
+    } else {
       npf += Hq * ((qlen + POD_KV - 1) / POD_KV);
+    }
   }
   s_pf[tid] = npf;
-  s_dec[tid] = ndec;
+  s_full[tid] = nfull;
+  s_rem[tid] = nrem;
   __syncthreads();
   for (int off = 1; off < 1024; off <<= 1) {
-    int a = 0, c = 0;
+    int a = 0, c = 0, d = 0;
     if (tid >= off) {
       a = s_pf[tid - off];
-      c = s_dec[tid - off];
+      c = s_full[tid - off];
+      d = s_rem[tid - off];
     }
     __syncthreads();
     s_pf[tid] += a;
-    s_dec[tid] += c;
+    s_full[tid] += c;
+    s_rem[tid] += d;
     __syncthreads();
   }
-  int opf = s_pf[tid] - npf, odec = s_dec[tid] - ndec;
+  const int total_full = s_full[1023];
+  int opf = s_pf[tid] - npf, ofull = s_full[tid] - nfull, orem = total_full + s_rem[tid] - nrem;
   for (int b = b0; b < b1; ++b) {
+    s_off[b] = opf;
+    s_off[B + b] = ofull;
+    s_off[2 * B + b] = orem;
     const int qlen = cu[b + 1] - cu[b];
     const int ctx = ctx_lens[b];
     if (qlen <= 0 || ctx < qlen || ctx > max_ctx) continue;
     if (qlen == 1) {
-      const int ns = min(max_splits, (ctx + split_tokens - 1) / split_tokens);
-      for (int sp = 0; sp < ns; ++sp)
-        for (int h = 0; h < Hkv; ++h) {
-          if (odec < dec_cap) dec_items[odec] = make_int4(b, h, sp, 0);
-          ++odec;
-        }
+      ofull += Hkv * (ctx / split_tokens);
+      orem += (ctx % split_tokens) ? Hkv : 0;
+    } else {
+      opf += Hq * ((qlen + POD_KV - 1) / POD_KV);
+    }
+  }
+  __syncthreads();
+  const int warp = tid / 32, lane = tid % 32;
+  for (int b = warp; b < B; b += 32) {
+    const int qlen = cu[b + 1] - cu[b];
+    const int ctx = ctx_lens[b];
+    if (qlen <= 0 || ctx < qlen || ctx > max_ctx) continue;
+    if (qlen == 1) {
+      const int nf = ctx / split_tokens;
+      const int n = Hkv * nf;
+      const int o = s_off[B + b];
+      for (int i = lane; i < n; i += 32)
+        if (o + i < dec_cap) dec_items[o + i] = make_int4(b, i % Hkv, i / Hkv, 0);
+      if (ctx % split_tokens) {
+        const int orr = s_off[2 * B + b];
+        for (int i = lane; i < Hkv; i += 32)
+          if (orr + i < dec_cap) dec_items[orr + i] = make_int4(b, i, nf, 0);
+      }
     } else {
       const int nqt = (qlen + POD_KV - 1) / POD_KV;
-      for (int qt = nqt - 1; qt >= 0; --qt)
-        for (int h = 0; h < Hq; ++h) {
-          if (opf < pf_cap) pf_items[opf] = make_int4(b, h, qt, 0);
-          ++opf;
-        }
+      const int n = Hq * nqt;
+      const int o = s_off[b];
+      for (int i = lane; i < n; i += 32)
+        if (o + i < pf_cap) pf_items[o + i] = make_int4(b, i % Hq, nqt - 1 - i / Hq, 0);
     }
   }
   if (tid == 1023) {
-    int tp = s_pf[1023], td = s_dec[1023];
+    const int tp = s_pf[1023], td = total_full + s_rem[1023];
     if (tp > pf_cap || td > dec_cap) report(status, LB_DEV_BAD_INDEX);
     counters[0] = min(tp, pf_cap);
     counters[1] = 0;
@@ -201,7 +230,7 @@ struct PodWs {
 static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
   LB_REQUIRE(a != nullptr, "lb_pod: null args");
   LB_REQUIRE(a->head_dim == POD_D, "lb_pod: head_dim must be 256 (got %lld)", (long long)a->head_dim);
-  LB_REQUIRE(a->num_seqs >= 0 && a->num_seqs <= (1 << 20) && a->num_tokens >= 0 &&
+  LB_REQUIRE(a->num_seqs >= 0 && a->num_seqs <= 16000 && a->num_tokens >= 0 &&
                  a->num_tokens <= (1 << 24),
              "lb_pod: num_seqs/num_tokens out of range");
   LB_REQUIRE(a->num_q_heads > 0 && a->num_kv_heads > 0 && a->num_q_heads % a->num_kv_heads == 0 &&
@@ -235,14 +264,15 @@ static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
   const int nsm = num_sms();
   long long split = a->kv_split_pages > 0 ? (long long)a->kv_split_pages * a->page_size : 0;
   if (split == 0) {
-    // largest power-of-two page count whose item count (assuming half-full tables)
-    // still gives every SM a few items to balance the tail
+    // largest power-of-two page count (<= 16 pages) whose item count, assuming half-full
+    // tables, still gives every SM ~16 items: long items pipeline well, many items keep
+    // the dynamic tail short
     const long long est_ctx = std::max<long long>(1, pl.max_ctx / 2);
     long long pages = 1;
     for (long long pg = 16; pg >= 1; pg >>= 1) {
       const long long st = pg * a->page_size;
       const long long items = a->num_seqs * a->num_kv_heads * ((est_ctx + st - 1) / st);
-      if (items >= 4ll * nsm) { pages = pg; break; }
+      if (items >= 16ll * nsm) { pages = pg; break; }
     }
     split = pages * a->page_size;
   }
@@ -253,12 +283,18 @@ static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
                                        1ll << 30);
   pl.grid = nsm;
   pl.n_pf_ctas = a->max_q_len > 1 ? nsm / 2 : 0;
-  if (a->max_q_len > 1 && a->num_tokens >= a->num_seqs) {
-    // estimate the tensor-bound share: prefill rows ~ N - B, each seeing about max_ctx/2 keys
-    const double pf_rows = (double)(a->num_tokens - (a->num_seqs - 1));
-    const double pf_flops = pf_rows * (pl.max_ctx / 2.0) * a->num_q_heads * POD_D * 4.0;
-    const double dec_bytes = (double)(a->num_seqs - 1) * (pl.max_ctx / 2.0) * a->num_kv_heads * POD_D * 4.0;
-    const double t_pf = pf_flops / 1.0e15, t_dec = dec_bytes / 6.0e12;
+  if (a->max_q_len > 1) {
+    // tensor-bound share of the work: prefill FLOPs at ~1 PFLOP/s vs decode KV bytes at
+    // ~6 TB/s; CTAs that finish their queue switch to the other one, so this only sets
+    // the starting split
+    double pf_pairs = (double)a->prefill_pairs_hint, dec_tok = (double)a->decode_tokens_hint;
+    if (pf_pairs <= 0 && dec_tok <= 0) {
+      const double pf_rows = (double)std::max<long long>(0, a->num_tokens - (a->num_seqs - 1));
+      pf_pairs = pf_rows * (pl.max_ctx / 4.0);
+      dec_tok = (double)(a->num_seqs - 1) * (pl.max_ctx / 2.0);
+    }
+    const double t_pf = pf_pairs * a->num_q_heads * POD_D * 4.0 / 1.0e15;
+    const double t_dec = dec_tok * a->num_kv_heads * POD_D * 4.0 / 6.0e12;
     pl.n_pf_ctas = std::max(1, std::min(nsm, (int)(nsm * t_pf / (t_pf + t_dec + 1e-30) + 0.5)));
   }
   return LB_OK;
@@ -283,7 +319,7 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
   int rc;
   // TMA maps.  K/V: [slots, Hkv, D] boxes of 128 slots x 1 head x 64 dims.  Q: [N, Hq, D];
   // decode box = 16 heads x 64 dims of one token, prefill box = 128 tokens of one head.
-  CUtensorMap tmK, tmV, tmQd, tmQp;
+  CUtensorMap tmK, tmV, tmK64, tmV64, tmQd, tmQp;
   const int qd_rows = (int)std::min<long long>(16, a.num_q_heads);
   {
     const uint64_t slots = (uint64_t)(a.num_pages * a.page_size);
@@ -293,6 +329,12 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
     if ((rc = make_tmap_bf16_3d_box(&tmV, a.v_cache, slots, a.num_kv_heads, POD_D,
                                     (uint64_t)a.num_kv_heads * POD_D, POD_D, POD_KV, 1, 64)))
       return rc;
+    if ((rc = make_tmap_bf16_3d_box(&tmK64, a.k_cache, slots, a.num_kv_heads, POD_D,
+                                    (uint64_t)a.num_kv_heads * POD_D, POD_D, PF_KV, 1, 64)))
+      return rc;
+    if ((rc = make_tmap_bf16_3d_box(&tmV64, a.v_cache, slots, a.num_kv_heads, POD_D,
+                                    (uint64_t)a.num_kv_heads * POD_D, POD_D, PF_KV, 1, 64)))
+      return rc;
     if ((rc = make_tmap_bf16_3d_box(&tmQd, a.q, N, a.num_q_heads, POD_D, a.q_stride_tok,
                                     a.q_stride_head, 1, qd_rows, 64)))
       return rc;
@@ -300,7 +342,9 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
                                     a.q_stride_head, POD_KV, 1, 64)))
       return rc;
   }
-  k_pod_plan<<<1, 1024, 0, st>>>(a.context_lens, a.cu_seqlens_q, B, (int)a.num_q_heads,
+  LB_CUDA_CHECK(cudaFuncSetAttribute(k_pod_plan, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)(3 * sizeof(int) * B)));
+  k_pod_plan<<<1, 1024, 3 * sizeof(int) * B, st>>>(a.context_lens, a.cu_seqlens_q, B, (int)a.num_q_heads,
                                  (int)a.num_kv_heads, pl.split_tokens, pl.max_splits, pl.max_ctx,
                                  pl.pf_cap, pl.dec_cap, w.pf_items, w.counters, w.dec_items, w.status);
   { int _rc = launched("k_pod_plan"); if (_rc) return _rc; }
@@ -336,7 +380,7 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
   p.qd_bytes = 4 * qd_rows * 128;
   LB_CUDA_CHECK(cudaFuncSetAttribute(k_pod_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, POD_SMEM));
   record_event(a.timing_events[0], st);
-  k_pod_attn<<<pl.grid, POD_THREADS, POD_SMEM, st>>>(tmK, tmV, tmQd, tmQp, p);
+  k_pod_attn<<<pl.grid, POD_THREADS, POD_SMEM, st>>>(tmK, tmV, tmK64, tmV64, tmQd, tmQp, p);
   { int _rc = launched("k_pod_attn"); if (_rc) return _rc; }
   record_event(a.timing_events[1], st);
 

@@ -262,6 +262,7 @@ struct MoeWs {
   float* wf;
   __nv_bfloat16* wb;
   int* chunk_hist;
+  int* counts;
   int* row_start;
   int* mtile_start;
   int32_t* perm_token;
@@ -283,6 +284,7 @@ static size_t carve_moe(const LbMoeArgs& a, void* base, MoeWs& w) {
   w.wf = c.take<float>(a.routing_given ? 0 : T * k);
   w.wb = c.take<__nv_bfloat16>(T * k);
   w.chunk_hist = c.take<int>((size_t)perm_chunks((int)T, (int)k) * nl);
+  w.counts = c.take<int>(nl + 2);
   w.row_start = c.take<int>(nl + 2);
   w.mtile_start = c.take<int>(nl + 2);
   w.perm_token = c.take<int32_t>(rows);
@@ -394,72 +396,33 @@ __global__ void k_perm_chunk_hist(const int32_t* __restrict__ ids, int T, int k,
     if (e >= 0 && e < nl) atomicAdd(&hist[e], 1);
   }
   __syncthreads();
-  int* dst = chunk_hist + (long long)blockIdx.x * nl;
-  for (int i = threadIdx.x; i < nl; i += blockDim.x) dst[i] = hist[i];
+  // expert-major layout [nl][n_chunks]: each expert's chunk counts are contiguous
+  for (int i = threadIdx.x; i < nl; i += blockDim.x)
+    chunk_hist[(long long)i * gridDim.x + blockIdx.x] = hist[i];
 }
 
-// One block.  For expert e: chunk_hist[c][e] <- first packed row of expert e's pairs in
-// chunk c; row_start / mtile_start as in k_moe_scan (group 0 = shared expert, T rows).
-__global__ void k_perm_chunk_scan(int* __restrict__ chunk_hist, int n_chunks, int nl, int T0,
-                                  int* __restrict__ row_start, int* __restrict__ mtile_start) {
-  __shared__ int s_rows[1024], s_tiles[1024];
-  __shared__ int s_tot[2048];
-  const int tid = threadIdx.x;
-  const int G = nl + 1;
-  for (int e = tid; e < nl; e += blockDim.x) {
-    int run = 0;
-    for (int c = 0; c < n_chunks; ++c) {
-      int* h = chunk_hist + (long long)c * nl + e;
-      const int v = *h;
-      *h = run;
-      run += v;
-    }
-    s_tot[1 + e] = run;
-  }
-  if (tid == 0) s_tot[0] = T0;
-  __syncthreads();
-  int r[2], tl[2];
+// One warp per local expert: exclusive prefix of its chunk counts, in place, and the
+// expert's total into counts[1 + e].
+__global__ void k_perm_expert_scan(int* __restrict__ chunk_hist, int n_chunks, int nl,
+                                   int* __restrict__ counts) {
+  const int e = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (e >= nl) return;
+  int* h = chunk_hist + (long long)e * n_chunks;
+  int run = 0;
+  for (int c0 = 0; c0 < n_chunks; c0 += 32) {
+    const int c = c0 + lane;
+    const int v = c < n_chunks ? h[c] : 0;
+    int incl = v;
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int g = 2 * tid + i;
-    const int c = g < G ? s_tot[g] : 0;
-    r[i] = c;
-    tl[i] = (c + GEMM_BM - 1) / GEMM_BM;
-  }
-  s_rows[tid] = r[0] + r[1];
-  s_tiles[tid] = tl[0] + tl[1];
-  __syncthreads();
-  for (int off = 1; off < 1024; off <<= 1) {
-    int a = 0, b = 0;
-    if (tid >= off) {
-      a = s_rows[tid - off];
-      b = s_tiles[tid - off];
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
     }
-    __syncthreads();
-    s_rows[tid] += a;
-    s_tiles[tid] += b;
-    __syncthreads();
+    if (c < n_chunks) h[c] = run + incl - v;
+    run += __shfl_sync(0xffffffffu, incl, 31);
   }
-  const int ex_r = tid ? s_rows[tid - 1] : 0;
-  const int ex_t = tid ? s_tiles[tid - 1] : 0;
-  __syncthreads();
-  // exclusive row start of every group, kept in s_tot for the per-chunk bases below
-  if (2 * tid <= G) {
-    row_start[2 * tid] = ex_r;
-    mtile_start[2 * tid] = ex_t;
-  }
-  if (2 * tid + 1 <= G) {
-    row_start[2 * tid + 1] = ex_r + r[0];
-    mtile_start[2 * tid + 1] = ex_t + tl[0];
-  }
-  __syncthreads();
-  if (2 * tid < G) s_tot[2 * tid] = ex_r;
-  if (2 * tid + 1 < G) s_tot[2 * tid + 1] = ex_r + r[0];
-  __syncthreads();
-  for (int e = tid; e < nl; e += blockDim.x) {
-    const int base = s_tot[1 + e];
-    for (int c = 0; c < n_chunks; ++c) chunk_hist[(long long)c * nl + e] += base;
-  }
+  if (lane == 0) counts[1 + e] = run;
 }
 
 // One warp per chunk, pairs in order; equal experts inside a 32-pair step are ranked with
@@ -467,15 +430,18 @@ __global__ void k_perm_chunk_scan(int* __restrict__ chunk_hist, int n_chunks, in
 // across steps.
 __global__ void k_perm_chunk_scatter(const int32_t* __restrict__ ids, const float* __restrict__ w,
                                      int T, int k, int expert_base, int nl,
-                                     const int* __restrict__ chunk_base,
+                                     const int* __restrict__ chunk_prefix,
+                                     const int* __restrict__ row_start,
                                      int32_t* __restrict__ perm_token, float* __restrict__ perm_w,
                                      int32_t* __restrict__ row_of) {
   extern __shared__ int cnt[];
   const int lane = threadIdx.x;
-  for (int i = lane; i < nl; i += 32) cnt[i] = 0;
+  const int nc = gridDim.x;
+  // cnt[e] starts at the first packed row of expert e's pairs in this chunk
+  for (int i = lane; i < nl; i += 32)
+    cnt[i] = row_start[1 + i] + chunk_prefix[(long long)i * nc + blockIdx.x];
   __syncwarp();
   const int n = T * k;
-  const int* base = chunk_base + (long long)blockIdx.x * nl;
   const int f0 = blockIdx.x * PERM_CHUNK;
   for (int s = 0; s < PERM_CHUNK; s += 32) {
     const int f = f0 + s + lane;
@@ -489,7 +455,7 @@ __global__ void k_perm_chunk_scatter(const int32_t* __restrict__ ids, const floa
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int before = __popc(peers & ((1u << lane) - 1u));
     int r = 0;
-    if (e >= 0) r = base[e] + cnt[e] + before;
+    if (e >= 0) r = cnt[e] + before;
     __syncwarp();
     if (e >= 0 && before == 0) cnt[e] += __popc(peers);
     __syncwarp();
@@ -557,26 +523,30 @@ __global__ void k_moe_combine(const __nv_bfloat16* __restrict__ yw, const int32_
 // Chunked permutation used by lb_moe_permute and lb_moe_forward.  chunk_hist needs
 // perm_chunks(T, k) * nl ints of scratch.
 static int run_permute_chunked(const int32_t* ids, const float* wf, int T, int k, int expert_base,
-                               int nl, int* chunk_hist, int* row_start, int* mtile_start,
-                               int32_t* perm_token, float* perm_w, int32_t* row_of,
-                               cudaStream_t st, bool has_shared = true) {
+                               int nl, int* chunk_hist, int* counts, int* row_start,
+                               int* mtile_start, int32_t* perm_token, float* perm_w,
+                               int32_t* row_of, cudaStream_t st, bool has_shared = true) {
   const int T0 = has_shared ? T : 0;
   const int n = T * k;
   const int nc = perm_chunks(T, k);
   LB_CUDA_CHECK(cudaMemsetAsync(row_of, 0xff, sizeof(int32_t) * (size_t)n, st));
-  if (nc > 0) {
+  if (nc > 0 && nl > 0) {
     k_perm_chunk_hist<<<nc, PERM_CHUNK, sizeof(int) * nl, st>>>(ids, T, k, expert_base, nl, chunk_hist);
     { int _rc = launched("k_perm_chunk_hist"); if (_rc) return _rc; }
+    k_perm_expert_scan<<<(nl + 7) / 8, 256, 0, st>>>(chunk_hist, nc, nl, counts);
+    { int _rc = launched("k_perm_expert_scan"); if (_rc) return _rc; }
+  } else if (nl > 0) {
+    LB_CUDA_CHECK(cudaMemsetAsync(counts, 0, sizeof(int) * (nl + 2), st));
   }
-  k_perm_chunk_scan<<<1, 1024, 0, st>>>(chunk_hist, nc, nl, T0, row_start, mtile_start);
-  { int _rc = launched("k_perm_chunk_scan"); if (_rc) return _rc; }
+  k_moe_scan<<<1, 1024, 0, st>>>(counts, nl + 1, T0, row_start, mtile_start);
+  { int _rc = launched("k_moe_scan"); if (_rc) return _rc; }
   if (T0 > 0) {
-    k_iota<<<std::min(1024, (T + 255) / 256), 256, 0, st>>>(perm_token, T);
+    k_iota<<<std::min(1024, (T0 + 255) / 256), 256, 0, st>>>(perm_token, T0);
     { int _rc = launched("k_iota"); if (_rc) return _rc; }
   }
-  if (nc > 0) {
+  if (nc > 0 && nl > 0) {
     k_perm_chunk_scatter<<<nc, 32, sizeof(int) * nl, st>>>(ids, wf, T, k, expert_base, nl, chunk_hist,
-                                                           perm_token, perm_w, row_of);
+                                                           row_start, perm_token, perm_w, row_of);
     { int _rc = launched("k_perm_chunk_scatter"); if (_rc) return _rc; }
   }
   return LB_OK;
@@ -635,7 +605,7 @@ int lb_router_topk(const void* logits, int64_t ld, int64_t T, int64_t E, int64_t
 
 size_t lb_moe_permute_workspace_size(int64_t T, int64_t k, int64_t nl) {
   const size_t nc = (size_t)((T * k + PERM_CHUNK - 1) / PERM_CHUNK);
-  return 256 + 3 * 256 + sizeof(int) * (size_t)(nl + 2) + sizeof(int) * nc * (size_t)nl;
+  return 256 + 4 * 256 + 2 * sizeof(int) * (size_t)(nl + 2) + sizeof(int) * nc * (size_t)nl;
 }
 
 int lb_moe_permute(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base,
@@ -650,9 +620,10 @@ int lb_moe_permute(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base
   Carve c(workspace, workspace_bytes);
   c.take<int>(64);  // status word
   int* mt = c.take<int>(nl + 2);
+  int* counts = c.take<int>(nl + 2);
   int* chunk_hist = c.take<int>((size_t)perm_chunks((int)T, (int)k) * nl);
   return run_permute_chunked(ids, nullptr, (int)T, (int)k, (int)expert_base, (int)nl, chunk_hist,
-                             row_start, mt, perm_token, nullptr, row_of,
+                             counts, row_start, mt, perm_token, nullptr, row_of,
                              static_cast<cudaStream_t>(stream));
 }
 
@@ -734,8 +705,9 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
     wf = w.wf;
   }
   // 3. permutation (routed pairs of the local experts) and gather of their input rows
-  rc = run_permute_chunked(ids, wf, T, k, (int)a->expert_base, nl, w.chunk_hist, w.row_start,
-                           w.mtile_start, w.perm_token, w.perm_w, w.row_of, st, shared);
+  rc = run_permute_chunked(ids, wf, T, k, (int)a->expert_base, nl, w.chunk_hist, w.counts,
+                           w.row_start, w.mtile_start, w.perm_token, w.perm_w, w.row_of, st,
+                           shared);
   if (rc) return rc;
   if (nl > 0) {
     const long long vec = (long long)T * k * (H / 8);

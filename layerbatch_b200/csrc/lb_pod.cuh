@@ -43,7 +43,13 @@ constexpr int POD_MISC = 2048;
 constexpr int POD_SMEM = 1024 + POD_DATA + POD_MISC;
 constexpr int POD_TMEM_COLS = 512;
 constexpr int DEC_SLOTS = 3;
-constexpr int PF_SLOTS = 2;
+// prefill: 64-key K/V tiles (32 KB) in a 4-slot ring so loads run two tiles ahead
+constexpr int PF_KV = 64;
+constexpr int PF_CHUNK = PF_KV * 128;            // 8 KB: one 64-dim chunk of a prefill tile
+constexpr int PF_TILE = 4 * PF_CHUNK;            // 32 KB
+constexpr int PF_SLOTS = 4;
+constexpr int PF_RING = PF_SLOTS * PF_TILE;      // 128 KB
+constexpr int PF_P_BYTES = POD_KV * PF_KV * 2;   // 16 KB prefill P (128 queries x 64 keys)
 
 struct PodParams {
   int* status;
@@ -73,7 +79,7 @@ struct PodParams {
 };
 
 struct PodBars {
-  uint64_t kv_full[3], kv_empty[3];
+  uint64_t kv_full[4], kv_empty[4];
   uint64_t item_full[2], item_empty[2];
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full[2], o_full[2];
@@ -114,6 +120,7 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
 
 __global__ void __launch_bounds__(POD_THREADS, 1)
     k_pod_attn(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+               const __grid_constant__ CUtensorMap tmK64, const __grid_constant__ CUtensorMap tmV64,
                const __grid_constant__ CUtensorMap tmQd, const __grid_constant__ CUtensorMap tmQp,
                const PodParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -135,7 +142,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
     const bool prefill = (pass == 0) ? pf_first : !pf_first;
     const int nslots = prefill ? PF_SLOTS : DEC_SLOTS;
     if (threadIdx.x == 0) {
-      for (int i = 0; i < 3; ++i) {
+      for (int i = 0; i < 4; ++i) {
         mbar_init(&bars->kv_full[i], 1);
         mbar_init(&bars->kv_empty[i], 1);
       }
@@ -185,11 +192,11 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             kvh = h / p.gqa;
             const int kv_end = min(ctx, ctx - qlen + (qt + 1) * POD_KV);
             t_begin = 0;
-            ntiles = (kv_end + POD_KV - 1) / POD_KV;
+            ntiles = (kv_end + PF_KV - 1) / PF_KV;
             // the single prefill Q buffer is free once the previous item's S MMAs finish
             if (!mbar_wait(&bars->q_empty, (cnt.qp & 1) ^ 1, p.status)) { *abortp = 1; break; }
             ++cnt.qp;
-            uint8_t* qbuf = smem + PF_SLOTS * POD_TILE;
+            uint8_t* qbuf = smem + PF_RING;
             const int row0 = p.cu_seqlens_q[b] + qt * POD_KV;
             mbar_arrive_expect_tx(&bars->item_full[islot], POD_QP_BYTES);
 #pragma unroll
@@ -214,10 +221,20 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             const int slot = cnt.kv % nslots;
             const uint32_t ph = (cnt.kv / nslots) & 1;
             if (!mbar_wait(&bars->kv_empty[slot], ph ^ 1, p.status)) { *abortp = 1; break; }
-            const int row = kv_page_row(p, b, t_begin + (j >> 1) * POD_KV);
-            mbar_arrive_expect_tx(&bars->kv_full[slot], POD_TILE);
-            load_kv_tile(kv_base + slot * POD_TILE, (j & 1) ? &tmV : &tmK, &bars->kv_full[slot],
-                         kvh, row);
+            if (prefill) {
+              const int row = kv_page_row(p, b, (j >> 1) * PF_KV);
+              mbar_arrive_expect_tx(&bars->kv_full[slot], PF_TILE);
+              uint8_t* dst = kv_base + slot * PF_TILE;
+              const CUtensorMap* map = (j & 1) ? &tmV64 : &tmK64;
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                tma_load_3d(dst + c * PF_CHUNK, map, &bars->kv_full[slot], c * 64, kvh, row);
+            } else {
+              const int row = kv_page_row(p, b, t_begin + (j >> 1) * POD_KV);
+              mbar_arrive_expect_tx(&bars->kv_full[slot], POD_TILE);
+              load_kv_tile(kv_base + slot * POD_TILE, (j & 1) ? &tmV : &tmK, &bars->kv_full[slot],
+                           kvh, row);
+            }
             ++cnt.kv;
           }
         }
@@ -225,7 +242,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
     } else if (warp == 1) {
       // ============================================================ MMA issuer
       if (elect_one_sync()) {
-        const uint32_t idesc_s = prefill ? umma_idesc_bf16(128, 128, false, false)
+        const uint32_t idesc_s = prefill ? umma_idesc_bf16(128, PF_KV, false, false)
                                          : umma_idesc_bf16(128, 16, false, false);
         const uint32_t idesc_o = prefill ? umma_idesc_bf16(128, 256, false, true)
                                          : umma_idesc_bf16(128, 16, true, false);
@@ -242,14 +259,14 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           if (prefill) {
             const int qlen = p.cu_seqlens_q[b + 1] - p.cu_seqlens_q[b];
             const int kv_end = min(ctx, ctx - qlen + (it.z + 1) * POD_KV);
-            ntiles = (kv_end + POD_KV - 1) / POD_KV;
+            ntiles = (kv_end + PF_KV - 1) / PF_KV;
           } else {
             const int t_begin = it.z * p.split_tokens;
             const int t_end = min(ctx, t_begin + p.split_tokens);
             ntiles = (t_end - t_begin + POD_KV - 1) / POD_KV;
           }
           const uint32_t base = cnt.kv;
-          const uint32_t qaddr = prefill ? smem_u32(smem + PF_SLOTS * POD_TILE)
+          const uint32_t qaddr = prefill ? smem_u32(smem + PF_RING)
                                          : smem_u32(smem + DEC_SLOTS * POD_TILE + islot * POD_QD_BYTES);
           bool ok = true;
           for (int j = 0; j <= ntiles && ok; ++j) {
@@ -261,15 +278,15 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               if (!mbar_wait(&bars->s_empty[sb], ((cnt.s >> 1) & 1) ^ 1, p.status) ||
                   !mbar_wait(&bars->kv_full[ks], (kp / nslots) & 1, p.status)) { ok = false; break; }
               tc_fence_after();
-              const uint32_t kaddr = smem_u32(kv_base + ks * POD_TILE);
+              const uint32_t kaddr = smem_u32(kv_base + ks * (prefill ? PF_TILE : POD_TILE));
               if (prefill) {
-                const uint32_t d = tmem + sb * 128;
+                const uint32_t d = tmem + sb * PF_KV;
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
 #pragma unroll
                   for (int kk = 0; kk < 4; ++kk)
                     umma_bf16(d, umma_desc_sw128(qaddr + c * POD_CHUNK + kk * 32, 16, 1024),
-                              umma_desc_sw128(kaddr + c * POD_CHUNK + kk * 32, 16, 1024), idesc_s,
+                              umma_desc_sw128(kaddr + c * PF_CHUNK + kk * 32, 16, 1024), idesc_s,
                               (c | kk) != 0);
               } else {
                 const uint32_t d = tmem + sb * 16;
@@ -295,16 +312,14 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               if (!mbar_wait(&bars->p_full[ob], (cnt.o >> 1) & 1, p.status) ||
                   !mbar_wait(&bars->kv_full[vs], (vp / nslots) & 1, p.status)) { ok = false; break; }
               tc_fence_after();
-              const uint32_t vaddr = smem_u32(kv_base + vs * POD_TILE);
+              const uint32_t vaddr = smem_u32(kv_base + vs * (prefill ? PF_TILE : POD_TILE));
               if (prefill) {
-                const uint32_t paddr = smem_u32(smem + PF_SLOTS * POD_TILE + POD_QP_BYTES);
+                const uint32_t paddr = smem_u32(smem + PF_RING + POD_QP_BYTES + ob * PF_P_BYTES);
                 const uint32_t d = tmem + 256;
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                  umma_bf16(d,
-                            umma_desc_sw128(paddr + (kk >> 2) * (POD_KV * 128) + (kk & 3) * 32, 16,
-                                            1024),
-                            umma_desc_sw128(vaddr + kk * 2048, POD_CHUNK, 1024), idesc_o,
+                for (int kk = 0; kk < PF_KV / 16; ++kk)
+                  umma_bf16(d, umma_desc_sw128(paddr + kk * 32, 16, 1024),
+                            umma_desc_sw128(vaddr + kk * 2048, PF_CHUNK, 1024), idesc_o,
                             (jj | kk) != 0);
               } else {
                 const uint32_t paddr =
@@ -357,20 +372,22 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           const bool rvalid = qrow < qlen;
           const int pos = rvalid ? ctx - qlen + qrow : -1;   // last visible key
           const int kv_end = min(ctx, ctx - qlen + (qt + 1) * POD_KV);
-          const int ntiles = (kv_end + POD_KV - 1) / POD_KV;
+          const int ntiles = (kv_end + PF_KV - 1) / PF_KV;
           float m = -INFINITY, l = 0.f;
-          const uint32_t paddr = smem_u32(smem + PF_SLOTS * POD_TILE + POD_QP_BYTES);
           const uint32_t kvbase = cnt.kv;
           cnt.kv += 2 * ntiles;
+          const uint32_t pv0 = cnt.o;  // global index of this item's first PV
+          cnt.o += ntiles;
           for (int j = 0; j < ntiles; ++j) {
+            const uint32_t pv = pv0 + j;
             const int sb = cnt.s & 1;
             if (!mbar_wait(&bars->s_full[sb], (cnt.s >> 1) & 1, p.status)) { ok = false; break; }
             tc_fence_after();
-            float s[128];
+            float s[PF_KV];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < PF_KV / 32; ++c) {
               uint32_t r[32];
-              tmem_ld32(tl + sb * 128 + c * 32, r);
+              tmem_ld32(tl + sb * PF_KV + c * 32, r);
               tmem_wait_ld();
 #pragma unroll
               for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
@@ -378,42 +395,55 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             tc_fence_before();
             mbar_arrive(&bars->s_empty[sb]);
             ++cnt.s;
-            float mt = -INFINITY;
-            const int k0 = j * POD_KV;
+            const int k0 = j * PF_KV;
+            float mx[8];
 #pragma unroll
-            for (int i = 0; i < 128; ++i) {
+            for (int u = 0; u < 8; ++u) mx[u] = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < PF_KV; ++i) {
               const float v = (k0 + i <= pos) ? s[i] * p.scale_log2 : -INFINITY;
               s[i] = v;
-              mt = fmaxf(mt, v);
+              mx[i & 7] = fmaxf(mx[i & 7], v);
             }
-            const float m_new = fmaxf(m, mt);
-            const float alpha = (m == -INFINITY) ? 1.f : exp2_approx(m - m_new);
-            const float msub = (m_new == -INFINITY) ? 0.f : m_new;
-            float rs = 0.f;
+            const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                   fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            // Lazy rescaling: the exponent base m moves only when the row max exceeds it by
+            // more than 8 (log2 units), so p = 2^(s - m) <= 256 stays exact in fp32/bf16
+            // and O in TMEM is rescaled rarely.  The final O / l uses the same m, so the
+            // result is unchanged.
+            float alpha = 1.f;
+            if (mt > m + 8.f) {
+              alpha = (m == -INFINITY) ? 1.f : exp2_approx(m - mt);
+              m = mt;
+            }
+            const float msub = (m == -INFINITY) ? 0.f : m;
+            float sm[8];
 #pragma unroll
-            for (int i = 0; i < 128; ++i) {
+            for (int u = 0; u < 8; ++u) sm[u] = 0.f;
+#pragma unroll
+            for (int i = 0; i < PF_KV; ++i) {
               s[i] = exp2_approx(s[i] - msub);
-              rs += s[i];
+              sm[i & 7] += s[i];
             }
-            l = l * alpha + rs;
-            m = m_new;
-            // PV_{j-1} must be done before P is overwritten and O rescaled
-            if (j > 0) {
-              const int ob = cnt.o & 1;
-              if (!mbar_wait(&bars->o_full[ob], (cnt.o >> 1) & 1, p.status)) { ok = false; break; }
-              ++cnt.o;
+            l = l * alpha + (((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7])));
+            // P buffer (pv & 1) was last read by PV pv-2; O may be rescaled only once PV pv-1
+            // has finished accumulating into it
+            const bool rescale = (j > 0) && __any_sync(0xffffffffu, alpha != 1.f);
+            if (j >= 2 || (rescale && j >= 1)) {
+              const uint32_t need = rescale ? pv - 1 : pv - 2;
+              if (!mbar_wait(&bars->o_full[need & 1], (need >> 1) & 1, p.status)) { ok = false; break; }
               tc_fence_after();
             }
+            const uint32_t paddr = smem_u32(smem + PF_RING + POD_QP_BYTES + (pv & 1) * PF_P_BYTES);
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-              const uint32_t a = paddr + (c >> 3) * (POD_KV * 128) + sw128_off(row, (c & 7) * 8);
+            for (int c = 0; c < PF_KV / 8; ++c) {
+              const uint32_t a = paddr + sw128_off(row, c * 8);
               st_shared_v4(a, pack_bf16x2(s[c * 8], s[c * 8 + 1]),
                            pack_bf16x2(s[c * 8 + 2], s[c * 8 + 3]),
                            pack_bf16x2(s[c * 8 + 4], s[c * 8 + 5]),
                            pack_bf16x2(s[c * 8 + 6], s[c * 8 + 7]));
             }
-            // rescale O rows in TMEM (warp-uniform decision: tcgen05.ld/st are collective)
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+            if (rescale) {
 #pragma unroll 1
               for (int c = 0; c < 8; ++c) {
                 uint32_t r[32];
@@ -427,27 +457,26 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             }
             // keys past the context in the last tile may hold stale (even NaN) cache
             // bytes; P is 0 there, but 0 * NaN would poison O, so zero those V rows
-            if (k0 + POD_KV > ctx) {
+            if (k0 + PF_KV > ctx) {
               const uint32_t vp = kvbase + 2 * j + 1;
               if (!mbar_wait(&bars->kv_full[vp % nslots], (vp / nslots) & 1, p.status)) { ok = false; break; }
-              if (k0 + row >= ctx) {
-                const uint32_t v = smem_u32(kv_base + (vp % nslots) * POD_TILE) + row * 128;
+              if (row < PF_KV && k0 + row >= ctx) {
+                const uint32_t v = smem_u32(kv_base + (vp % nslots) * PF_TILE) + row * 128;
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
 #pragma unroll
-                  for (int u = 0; u < 8; ++u) st_shared_v4(v + c * POD_CHUNK + u * 16, 0, 0, 0, 0);
+                  for (int u = 0; u < 8; ++u) st_shared_v4(v + c * PF_CHUNK + u * 16, 0, 0, 0, 0);
               }
             }
             fence_proxy_async_smem();
             tc_fence_before();
-            mbar_arrive(&bars->p_full[cnt.o & 1]);
+            mbar_arrive(&bars->p_full[pv & 1]);
           }
           if (!ok) { *abortp = 1; break; }
-          // last PV
+          // last PV (completion implies all earlier ones)
           {
-            const int ob = cnt.o & 1;
-            if (!mbar_wait(&bars->o_full[ob], (cnt.o >> 1) & 1, p.status)) { *abortp = 1; break; }
-            ++cnt.o;
+            const uint32_t last = cnt.o - 1;
+            if (!mbar_wait(&bars->o_full[last & 1], (last >> 1) & 1, p.status)) { *abortp = 1; break; }
             tc_fence_after();
           }
           const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
@@ -648,7 +677,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-      for (int i = 0; i < 3; ++i) {
+      for (int i = 0; i < 4; ++i) {
         mbar_inval(&bars->kv_full[i]);
         mbar_inval(&bars->kv_empty[i]);
       }

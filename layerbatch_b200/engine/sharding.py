@@ -145,14 +145,14 @@ def shard_attention_tensors(shard: TPShard, q, gate, k_cache, v_cache, w_o, head
 
 def tp_attention_oproj(shard: TPShard, q, gate, k_cache, v_cache, block_tables, context_lens,
                        cu_seqlens_q, w_o, scale, group=None, max_q_len=None, events=None,
-                       out=None):
+                       out=None, work_hint=None):
     """This rank's heads -> fp32 o_proj partial -> fp32 all-reduce -> bf16 ``[N, H]``."""
     from .. import ops
     N = q.shape[0]
     partial = torch.empty(N, w_o.shape[0], dtype=torch.float32, device=q.device)
     ops.pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q,
                        w_o, scale, out=partial, max_q_len=max_q_len, ws_tag="tp_attn",
-                       events=events)
+                       events=events, work_hint=work_hint)
     if shard.tp_size > 1:
         dist.all_reduce(partial, group=group)
     if out is None:

@@ -196,9 +196,16 @@ def pod_args(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q
         out=ptr(out), out_fp32=int(out is not None and out.dtype == torch.float32))
 
 
+def pod_work_hint(ctx_list, qlen_list):
+    """(prefill query-key pairs, decode context tokens) of a batch, from host lists."""
+    pairs = sum(L * (c - L) + L * (L + 1) // 2 for c, L in zip(ctx_list, qlen_list) if L > 1)
+    dec = sum(c for c, L in zip(ctx_list, qlen_list) if L == 1)
+    return pairs, dec
+
+
 def pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o,
                    scale, out=None, attn_out=None, max_q_len=None, kv_split_pages=0,
-                   ws_tag="pod", events=None):
+                   ws_tag="pod", events=None, work_hint=None):
     """Fused paged attention (prefill + decode mixed) -> sigmoid gate -> o_proj.
 
     ``gate`` may be None (no output gate).  With ``w_o=None`` only the attention runs and
@@ -219,6 +226,8 @@ def pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seq
     cu = cu_seqlens_q.to(torch.int32)
     a = pod_args(q, gate, k_cache, v_cache, bt, cl, cu, w_o, scale, out, attn_out, max_q_len,
                  kv_split_pages)
+    if work_hint is not None:
+        a.prefill_pairs_hint, a.decode_tokens_hint = int(work_hint[0]), int(work_hint[1])
     _events(a, events)
     need = C.c_size_t(0)
     check(lib().lb_pod_workspace_size(C.byref(a), C.byref(need)), "lb_pod_workspace_size")
