@@ -7,7 +7,9 @@
 // and decode (HBM-bound) items overlap across SMs and the tail is balanced.
 //
 // Roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + tcgen05.mma issuer,
-// warps 2..5 = softmax / epilogue (one thread per TMEM lane).
+// warps 2..9 = softmax / epilogue: two warpgroups, one thread per TMEM lane each.  Decode
+// items use warpgroup 0 only; prefill items split every score row between the two
+// warpgroups (32 keys each) and each warpgroup owns half of the O columns.
 //
 // KV tiles are 128 tokens x 256 dims, loaded by TMA as four 64-dim chunks of
 // [128 rows x 128 B] (128B swizzle), the same layout for K and V.  A 128-token tile never
@@ -29,7 +31,7 @@
 
 namespace lb {
 
-constexpr int POD_THREADS = 192;
+constexpr int POD_THREADS = 320;
 constexpr int POD_KV = 128;          // tokens per K or V tile
 constexpr int POD_D = 256;           // head_dim
 constexpr int POD_CHUNK = POD_KV * 128;          // 16 KB: one 64-dim chunk of a tile
@@ -47,9 +49,17 @@ constexpr int DEC_SLOTS = 3;
 constexpr int PF_KV = 64;
 constexpr int PF_CHUNK = PF_KV * 128;            // 8 KB: one 64-dim chunk of a prefill tile
 constexpr int PF_TILE = 4 * PF_CHUNK;            // 32 KB
-constexpr int PF_SLOTS = 4;
-constexpr int PF_RING = PF_SLOTS * PF_TILE;      // 128 KB
+constexpr int PF_SLOTS = 2;                      // per ring: K and V have separate rings
 constexpr int PF_P_BYTES = POD_KV * PF_KV * 2;   // 16 KB prefill P (128 queries x 64 keys)
+// prefill shared-memory map: [K ring 2 x 32 KB][V ring 2 x 32 KB][Q 64 KB][P x2]
+constexpr int PF_K_OFF = 0;
+constexpr int PF_V_OFF = PF_SLOTS * PF_TILE;
+constexpr int PF_Q_OFF = PF_V_OFF + PF_SLOTS * PF_TILE;
+constexpr int PF_P_OFF = PF_Q_OFF + POD_QP_BYTES;
+static_assert(PF_P_OFF + 2 * PF_P_BYTES <= POD_DATA, "prefill shared-memory map exceeds the data region");
+// decode shared-memory map: [ring 3 x 64 KB][Q x2][P^T x2]
+static_assert(DEC_SLOTS * POD_TILE + 2 * POD_QD_BYTES + 2 * POD_PD_BYTES <= POD_DATA,
+              "decode shared-memory map exceeds the data region");
 
 struct PodParams {
   int* status;
@@ -90,10 +100,13 @@ struct PodBars {
   int abort;
   float red[2][4][16];
   float lred[4][16];
+  float psum[2][128];      // prefill: per-warpgroup partial row sums at the end of an item
 };
 
+static_assert(sizeof(PodBars) <= POD_MISC, "PodBars exceeds the reserved shared memory");
+
 struct PodCounters {  // per-role running positions, kept across items and modes
-  uint32_t kv, item, s, o, qp;
+  uint32_t kv, item, s, o, qp, kv2;  // kv2: prefill V tiles (K tiles use kv)
 };
 
 __device__ __forceinline__ int kv_page_row(const PodParams& p, int b, int tok) {
@@ -111,6 +124,34 @@ __device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* ma
                                              uint64_t* bar, int kvh, int row) {
 #pragma unroll
   for (int c = 0; c < 4; ++c) tma_load_3d(dst + c * POD_CHUNK, map, bar, c * 64, kvh, row);
+}
+
+// Decode TMEM columns: S^T [2 buffers][4 chunk partials][16 heads], O^T [2 buffers][2 dim
+// halves][4 token-quarter partials][16 heads].
+constexpr int DEC_S_COL = 0;
+constexpr int DEC_O_COL = 128;
+
+// Sum of the four token-quarter partials of each dim half of a decode O^T buffer.
+__device__ __forceinline__ void dec_load_o(uint32_t taddr, uint32_t (&o0)[16], uint32_t (&o1)[16]) {
+  uint32_t a[16], b[16], c[16];
+  tmem_ld16(taddr, o0);
+  tmem_ld16(taddr + 16, a);
+  tmem_ld16(taddr + 32, b);
+  tmem_ld16(taddr + 48, c);
+  tmem_wait_ld();
+#pragma unroll
+  for (int h = 0; h < 16; ++h)
+    o0[h] = __float_as_uint((__uint_as_float(o0[h]) + __uint_as_float(a[h])) +
+                            (__uint_as_float(b[h]) + __uint_as_float(c[h])));
+  tmem_ld16(taddr + 64, o1);
+  tmem_ld16(taddr + 80, a);
+  tmem_ld16(taddr + 96, b);
+  tmem_ld16(taddr + 112, c);
+  tmem_wait_ld();
+#pragma unroll
+  for (int h = 0; h < 16; ++h)
+    o1[h] = __float_as_uint((__uint_as_float(o1[h]) + __uint_as_float(a[h])) +
+                            (__uint_as_float(b[h]) + __uint_as_float(c[h])));
 }
 
 // Byte offset of element (r, c) in a K-major SW128 tile of 64-element (128 B) rows.
@@ -135,12 +176,12 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
     tmem_relinquish();
   }
   if (threadIdx.x == 0) bars->abort = 0;
-  PodCounters cnt = {0, 0, 0, 0, 0};
+  PodCounters cnt = {0, 0, 0, 0, 0, 0};
 
   const bool pf_first = (int)blockIdx.x < p.n_prefill_ctas;
   for (int pass = 0; pass < 2; ++pass) {
     const bool prefill = (pass == 0) ? pf_first : !pf_first;
-    const int nslots = prefill ? PF_SLOTS : DEC_SLOTS;
+    const int nslots = DEC_SLOTS;   // decode ring (prefill uses two PF_SLOTS rings)
     if (threadIdx.x == 0) {
       for (int i = 0; i < 4; ++i) {
         mbar_init(&bars->kv_full[i], 1);
@@ -150,15 +191,15 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
         mbar_init(&bars->item_full[i], 1);
         mbar_init(&bars->item_empty[i], 1);
         mbar_init(&bars->s_full[i], 1);
-        mbar_init(&bars->s_empty[i], 128);
-        mbar_init(&bars->p_full[i], 128);
+        mbar_init(&bars->s_empty[i], prefill ? 256 : 128);
+        mbar_init(&bars->p_full[i], prefill ? 256 : 128);
         mbar_init(&bars->o_full[i], 1);
       }
       mbar_init(&bars->q_empty, 1);
       mbar_init(&bars->drain, 1);
       fence_barrier_init();
     }
-    cnt = {0, 0, 0, 0, 0};
+    cnt = {0, 0, 0, 0, 0, 0};
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
@@ -166,7 +207,9 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
 
     if (warp == 0) {
       // ============================================================ producer
-      if (elect_one_sync()) {
+      // lane 0: items, Q, decode K/V tiles, prefill K tiles; lane 1: prefill V tiles, so
+      // K tiles never wait behind a V tile whose ring slot is still in use
+      if (lane == 0) {
         const int4* items = prefill ? p.pf_items : p.dec_items;
         const int n_items = *(prefill ? p.pf_count : p.dec_count);
         int* next = prefill ? p.pf_next : p.dec_next;
@@ -196,7 +239,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             // the single prefill Q buffer is free once the previous item's S MMAs finish
             if (!mbar_wait(&bars->q_empty, (cnt.qp & 1) ^ 1, p.status)) { *abortp = 1; break; }
             ++cnt.qp;
-            uint8_t* qbuf = smem + PF_RING;
+            uint8_t* qbuf = smem + PF_Q_OFF;
             const int row0 = p.cu_seqlens_q[b] + qt * POD_KV;
             mbar_arrive_expect_tx(&bars->item_full[islot], POD_QP_BYTES);
 #pragma unroll
@@ -217,25 +260,55 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
                           kvh * p.gqa, tok);
           }
           ++cnt.item;
-          for (int j = 0; j < 2 * ntiles && !*abortp; ++j) {
-            const int slot = cnt.kv % nslots;
-            const uint32_t ph = (cnt.kv / nslots) & 1;
-            if (!mbar_wait(&bars->kv_empty[slot], ph ^ 1, p.status)) { *abortp = 1; break; }
-            if (prefill) {
-              const int row = kv_page_row(p, b, (j >> 1) * PF_KV);
+          if (prefill) {
+            for (int j = 0; j < ntiles && !*abortp; ++j) {
+              const int slot = cnt.kv % PF_SLOTS;
+              if (!mbar_wait(&bars->kv_empty[slot], ((cnt.kv / PF_SLOTS) & 1) ^ 1, p.status)) { *abortp = 1; break; }
+              const int row = kv_page_row(p, b, j * PF_KV);
               mbar_arrive_expect_tx(&bars->kv_full[slot], PF_TILE);
-              uint8_t* dst = kv_base + slot * PF_TILE;
-              const CUtensorMap* map = (j & 1) ? &tmV64 : &tmK64;
+              uint8_t* dst = smem + PF_K_OFF + slot * PF_TILE;
 #pragma unroll
               for (int c = 0; c < 4; ++c)
-                tma_load_3d(dst + c * PF_CHUNK, map, &bars->kv_full[slot], c * 64, kvh, row);
-            } else {
+                tma_load_3d(dst + c * PF_CHUNK, &tmK64, &bars->kv_full[slot], c * 64, kvh, row);
+              ++cnt.kv;
+            }
+          } else {
+            for (int j = 0; j < 2 * ntiles && !*abortp; ++j) {
+              const int slot = cnt.kv % nslots;
+              const uint32_t ph = (cnt.kv / nslots) & 1;
+              if (!mbar_wait(&bars->kv_empty[slot], ph ^ 1, p.status)) { *abortp = 1; break; }
               const int row = kv_page_row(p, b, t_begin + (j >> 1) * POD_KV);
               mbar_arrive_expect_tx(&bars->kv_full[slot], POD_TILE);
               load_kv_tile(kv_base + slot * POD_TILE, (j & 1) ? &tmV : &tmK, &bars->kv_full[slot],
                            kvh, row);
+              ++cnt.kv;
             }
-            ++cnt.kv;
+          }
+        }
+      } else if (lane == 1 && prefill) {
+        // V loader: follows the item sequence through item_full
+        while (!*abortp) {
+          const int islot = cnt.item & 1;
+          if (!mbar_wait(&bars->item_full[islot], (cnt.item >> 1) & 1, p.status)) { *abortp = 1; break; }
+          const int4 it = bars->items[islot];
+          ++cnt.item;
+          if (it.x < 0) break;
+          const int b = it.x;
+          const int ctx = p.context_lens[b];
+          const int qlen = p.cu_seqlens_q[b + 1] - p.cu_seqlens_q[b];
+          const int kvh = it.y / p.gqa;
+          const int kv_end = min(ctx, ctx - qlen + (it.z + 1) * POD_KV);
+          const int ntiles = (kv_end + PF_KV - 1) / PF_KV;
+          for (int j = 0; j < ntiles && !*abortp; ++j) {
+            const int slot = cnt.kv2 % PF_SLOTS;
+            if (!mbar_wait(&bars->kv_empty[2 + slot], ((cnt.kv2 / PF_SLOTS) & 1) ^ 1, p.status)) { *abortp = 1; break; }
+            const int row = kv_page_row(p, b, j * PF_KV);
+            mbar_arrive_expect_tx(&bars->kv_full[2 + slot], PF_TILE);
+            uint8_t* dst = smem + PF_V_OFF + slot * PF_TILE;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              tma_load_3d(dst + c * PF_CHUNK, &tmV64, &bars->kv_full[2 + slot], c * 64, kvh, row);
+            ++cnt.kv2;
           }
         }
       }
@@ -265,20 +338,22 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             const int t_end = min(ctx, t_begin + p.split_tokens);
             ntiles = (t_end - t_begin + POD_KV - 1) / POD_KV;
           }
-          const uint32_t base = cnt.kv;
-          const uint32_t qaddr = prefill ? smem_u32(smem + PF_RING)
+          const uint32_t base = cnt.kv, vbase = cnt.kv2;
+          const uint32_t qaddr = prefill ? smem_u32(smem + PF_Q_OFF)
                                          : smem_u32(smem + DEC_SLOTS * POD_TILE + islot * POD_QD_BYTES);
           bool ok = true;
           for (int j = 0; j <= ntiles && ok; ++j) {
             if (j < ntiles) {
-              // ---- S_j
-              const uint32_t kp = base + 2 * j;
-              const int ks = kp % nslots;
+              // ---- S_j  (prefill: K ring slots 0-1; decode: unified ring)
+              const uint32_t kp = prefill ? base + j : base + 2 * j;
+              const int ring = prefill ? PF_SLOTS : nslots;
+              const int ks = kp % ring;
               const int sb = cnt.s & 1;
               if (!mbar_wait(&bars->s_empty[sb], ((cnt.s >> 1) & 1) ^ 1, p.status) ||
-                  !mbar_wait(&bars->kv_full[ks], (kp / nslots) & 1, p.status)) { ok = false; break; }
+                  !mbar_wait(&bars->kv_full[ks], (kp / ring) & 1, p.status)) { ok = false; break; }
               tc_fence_after();
-              const uint32_t kaddr = smem_u32(kv_base + ks * (prefill ? PF_TILE : POD_TILE));
+              const uint32_t kaddr = prefill ? smem_u32(smem + PF_K_OFF + ks * PF_TILE)
+                                             : smem_u32(kv_base + ks * POD_TILE);
               if (prefill) {
                 const uint32_t d = tmem + sb * PF_KV;
 #pragma unroll
@@ -289,14 +364,16 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
                               umma_desc_sw128(kaddr + c * PF_CHUNK + kk * 32, 16, 1024), idesc_s,
                               (c | kk) != 0);
               } else {
-                const uint32_t d = tmem + sb * 16;
+                // four independent accumulators (one per 64-dim chunk) keep the chain of
+                // dependent N=16 MMAs short; the softmax threads add them up
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
+                for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
-                  for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16(d, umma_desc_sw128(kaddr + c * POD_CHUNK + kk * 32, 16, 1024),
+                  for (int c = 0; c < 4; ++c)
+                    umma_bf16(tmem + DEC_S_COL + sb * 64 + c * 16,
+                              umma_desc_sw128(kaddr + c * POD_CHUNK + kk * 32, 16, 1024),
                               umma_desc_sw128(qaddr + c * 2048 + kk * 32, 16, 1024), idesc_s,
-                              (c | kk) != 0);
+                              kk != 0);
               }
               umma_commit(&bars->s_full[sb]);
               umma_commit(&bars->kv_empty[ks]);
@@ -304,17 +381,19 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               ++cnt.s;
             }
             if (j > 0) {
-              // ---- PV_{j-1}
+              // ---- PV_{j-1}  (prefill: V ring slots 2-3; decode: unified ring)
               const int jj = j - 1;
-              const uint32_t vp = base + 2 * jj + 1;
-              const int vs = vp % nslots;
+              const uint32_t vp = prefill ? vbase + jj : base + 2 * jj + 1;
+              const int ring = prefill ? PF_SLOTS : nslots;
+              const int vs = (prefill ? 2 : 0) + (int)(vp % ring);
               const int ob = cnt.o & 1;
               if (!mbar_wait(&bars->p_full[ob], (cnt.o >> 1) & 1, p.status) ||
-                  !mbar_wait(&bars->kv_full[vs], (vp / nslots) & 1, p.status)) { ok = false; break; }
+                  !mbar_wait(&bars->kv_full[vs], (vp / ring) & 1, p.status)) { ok = false; break; }
               tc_fence_after();
-              const uint32_t vaddr = smem_u32(kv_base + vs * (prefill ? PF_TILE : POD_TILE));
+              const uint32_t vaddr = prefill ? smem_u32(smem + PF_V_OFF + (vp % ring) * PF_TILE)
+                                             : smem_u32(kv_base + vs * POD_TILE);
               if (prefill) {
-                const uint32_t paddr = smem_u32(smem + PF_RING + POD_QP_BYTES + ob * PF_P_BYTES);
+                const uint32_t paddr = smem_u32(smem + PF_P_OFF + ob * PF_P_BYTES);
                 const uint32_t d = tmem + 256;
 #pragma unroll
                 for (int kk = 0; kk < PF_KV / 16; ++kk)
@@ -324,22 +403,32 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               } else {
                 const uint32_t paddr =
                     smem_u32(smem + DEC_SLOTS * POD_TILE + 2 * POD_QD_BYTES + ob * POD_PD_BYTES);
+                // per half of the dims, four token-quarter accumulators (independent chains
+                // of two MMAs); the softmax threads add them up with the running O
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const uint32_t d = tmem + 32 + ob * 32 + h * 16;
+                for (int k2 = 0; k2 < 2; ++k2)
 #pragma unroll
-                  for (int kk = 0; kk < 8; ++kk)
-                    umma_bf16(d, umma_desc_sw128(vaddr + h * 2 * POD_CHUNK + kk * 2048, POD_CHUNK, 1024),
-                              umma_desc_sw128(paddr + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024),
-                              idesc_o, kk != 0);
-                }
+                  for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                      const int kk = 2 * q + k2;
+                      umma_bf16(tmem + DEC_O_COL + ob * 128 + h * 64 + q * 16,
+                                umma_desc_sw128(vaddr + h * 2 * POD_CHUNK + kk * 2048, POD_CHUNK, 1024),
+                                umma_desc_sw128(paddr + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024),
+                                idesc_o, k2 != 0);
+                    }
               }
               umma_commit(&bars->o_full[ob]);
               umma_commit(&bars->kv_empty[vs]);
               ++cnt.o;
             }
           }
-          cnt.kv = base + 2 * ntiles;
+          if (prefill) {
+            cnt.kv = base + ntiles;
+            cnt.kv2 = vbase + ntiles;
+          } else {
+            cnt.kv = base + 2 * ntiles;
+          }
           if (!ok) { *abortp = 1; break; }
         }
         // every commit issued above has arrived once this one has: the barriers can be
@@ -349,11 +438,13 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
       }
     } else {
       // ============================================================ softmax / epilogue
+      const int wg = (warp - 2) >> 2;        // warpgroup 0 or 1
       const int quad = warp & 3;
       const int row = quad * 32 + lane;
       const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
-      const int tid = threadIdx.x - 64;
-      while (true) {
+      const int tid = threadIdx.x - 64 - 128 * wg;
+      const int nthr = prefill ? 256 : 128;   // threads taking part in this mode
+      while (prefill || wg == 0) {
         const int islot = cnt.item & 1;
         const uint32_t iph = (cnt.item >> 1) & 1;
         if (!mbar_wait(&bars->item_full[islot], iph, p.status)) { *abortp = 1; break; }
@@ -374,8 +465,9 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           const int kv_end = min(ctx, ctx - qlen + (qt + 1) * POD_KV);
           const int ntiles = (kv_end + PF_KV - 1) / PF_KV;
           float m = -INFINITY, l = 0.f;
-          const uint32_t kvbase = cnt.kv;
-          cnt.kv += 2 * ntiles;
+          const uint32_t vbase = cnt.kv2;
+          cnt.kv += ntiles;
+          cnt.kv2 += ntiles;
           const uint32_t pv0 = cnt.o;  // global index of this item's first PV
           cnt.o += ntiles;
           for (int j = 0; j < ntiles; ++j) {
@@ -383,30 +475,46 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             const int sb = cnt.s & 1;
             if (!mbar_wait(&bars->s_full[sb], (cnt.s >> 1) & 1, p.status)) { ok = false; break; }
             tc_fence_after();
-            float s[PF_KV];
-#pragma unroll
-            for (int c = 0; c < PF_KV / 32; ++c) {
-              uint32_t r[32];
-              tmem_ld32(tl + sb * PF_KV + c * 32, r);
+            // both warpgroups read the whole score row (for the row max); each then
+            // exponentiates and writes its own half of the keys
+            constexpr int HALF = PF_KV / 2;
+            float s[HALF], so[HALF];
+            {
+              uint32_t r[32], ro[32];
+              tmem_ld32(tl + sb * PF_KV + wg * HALF, r);
+              tmem_ld32(tl + sb * PF_KV + (wg ^ 1) * HALF, ro);
               tmem_wait_ld();
 #pragma unroll
-              for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+              for (int i = 0; i < 32; ++i) {
+                s[i] = __uint_as_float(r[i]);
+                so[i] = __uint_as_float(ro[i]);
+              }
             }
             tc_fence_before();
             mbar_arrive(&bars->s_empty[sb]);
             ++cnt.s;
-            const int k0 = j * PF_KV;
+            const int k0 = j * PF_KV + wg * HALF;
+            const int ko = j * PF_KV + (wg ^ 1) * HALF;
             float mx[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) mx[u] = -INFINITY;
+            if (j * PF_KV + PF_KV - 1 <= pos) {   // whole tile visible: no masking
 #pragma unroll
-            for (int i = 0; i < PF_KV; ++i) {
-              const float v = (k0 + i <= pos) ? s[i] * p.scale_log2 : -INFINITY;
-              s[i] = v;
-              mx[i & 7] = fmaxf(mx[i & 7], v);
+              for (int i = 0; i < HALF; ++i) {
+                mx[i & 7] = fmaxf(mx[i & 7], s[i]);
+                mx[(i + 4) & 7] = fmaxf(mx[(i + 4) & 7], so[i]);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < HALF; ++i) {
+                s[i] = (k0 + i <= pos) ? s[i] : -INFINITY;
+                mx[i & 7] = fmaxf(mx[i & 7], s[i]);
+                mx[(i + 4) & 7] = fmaxf(mx[(i + 4) & 7], (ko + i <= pos) ? so[i] : -INFINITY);
+              }
             }
-            const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                   fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            mt = (mt == -INFINITY) ? -INFINITY : mt * p.scale_log2;   // scale > 0 keeps order
             // Lazy rescaling: the exponent base m moves only when the row max exceeds it by
             // more than 8 (log2 units), so p = 2^(s - m) <= 256 stays exact in fp32/bf16
             // and O in TMEM is rescaled rarely.  The final O / l uses the same m, so the
@@ -421,8 +529,8 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
 #pragma unroll
             for (int u = 0; u < 8; ++u) sm[u] = 0.f;
 #pragma unroll
-            for (int i = 0; i < PF_KV; ++i) {
-              s[i] = exp2_approx(s[i] - msub);
+            for (int i = 0; i < HALF; ++i) {
+              s[i] = exp2_approx(fmaf(s[i], p.scale_log2, -msub));   // 2^(-inf) = 0 if masked
               sm[i & 7] += s[i];
             }
             l = l * alpha + (((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7])));
@@ -434,34 +542,34 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               if (!mbar_wait(&bars->o_full[need & 1], (need >> 1) & 1, p.status)) { ok = false; break; }
               tc_fence_after();
             }
-            const uint32_t paddr = smem_u32(smem + PF_RING + POD_QP_BYTES + (pv & 1) * PF_P_BYTES);
+            const uint32_t paddr = smem_u32(smem + PF_P_OFF + (pv & 1) * PF_P_BYTES);
 #pragma unroll
-            for (int c = 0; c < PF_KV / 8; ++c) {
-              const uint32_t a = paddr + sw128_off(row, c * 8);
+            for (int c = 0; c < HALF / 8; ++c) {
+              const uint32_t a = paddr + sw128_off(row, wg * HALF + c * 8);
               st_shared_v4(a, pack_bf16x2(s[c * 8], s[c * 8 + 1]),
                            pack_bf16x2(s[c * 8 + 2], s[c * 8 + 3]),
                            pack_bf16x2(s[c * 8 + 4], s[c * 8 + 5]),
                            pack_bf16x2(s[c * 8 + 6], s[c * 8 + 7]));
             }
-            if (rescale) {
+            if (rescale) {   // this warpgroup's half of the O columns
 #pragma unroll 1
-              for (int c = 0; c < 8; ++c) {
+              for (int c = 0; c < 4; ++c) {
                 uint32_t r[32];
-                tmem_ld32(tl + 256 + c * 32, r);
+                tmem_ld32(tl + 256 + wg * 128 + c * 32, r);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                tmem_st32(tl + 256 + c * 32, r);
+                tmem_st32(tl + 256 + wg * 128 + c * 32, r);
               }
               tmem_wait_st();
             }
             // keys past the context in the last tile may hold stale (even NaN) cache
             // bytes; P is 0 there, but 0 * NaN would poison O, so zero those V rows
-            if (k0 + PF_KV > ctx) {
-              const uint32_t vp = kvbase + 2 * j + 1;
-              if (!mbar_wait(&bars->kv_full[vp % nslots], (vp / nslots) & 1, p.status)) { ok = false; break; }
-              if (row < PF_KV && k0 + row >= ctx) {
-                const uint32_t v = smem_u32(kv_base + (vp % nslots) * PF_TILE) + row * 128;
+            if (j * PF_KV + PF_KV > ctx) {
+              const uint32_t vp = vbase + j;
+              if (!mbar_wait(&bars->kv_full[2 + vp % PF_SLOTS], (vp / PF_SLOTS) & 1, p.status)) { ok = false; break; }
+              if (wg == 0 && row < PF_KV && j * PF_KV + row >= ctx) {
+                const uint32_t v = smem_u32(smem + PF_V_OFF + (vp % PF_SLOTS) * PF_TILE) + row * 128;
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -479,12 +587,16 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             if (!mbar_wait(&bars->o_full[last & 1], (last >> 1) & 1, p.status)) { *abortp = 1; break; }
             tc_fence_after();
           }
+          bars->psum[wg][row] = l;
+          named_bar_sync(2, 256);
+          l += bars->psum[wg ^ 1][row];
           const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
           const long long tok = (long long)q0 + qrow;
           const __nv_bfloat16* grow = p.gate + tok * p.gate_st + (long long)h * p.gate_sh;
           __nv_bfloat16* orow = p.ogated ? p.ogated + tok * (long long)(p.Hq * POD_D) + h * POD_D : nullptr;
 #pragma unroll 1
-          for (int c = 0; c < 8; ++c) {
+          for (int cc = 0; cc < 4; ++cc) {
+            const int c = wg * 4 + cc;   // this warpgroup's 32-column chunks of O
             uint32_t r[32];
             tmem_ld32(tl + 256 + c * 32, r);
             tmem_wait_ld();
@@ -557,8 +669,18 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               if (!mbar_wait(&bars->s_full[sb], (cnt.s >> 1) & 1, p.status)) { ok = false; break; }
               tc_fence_after();
               uint32_t r[16];
-              tmem_ld16(tl + sb * 16, r);
-              tmem_wait_ld();
+              {
+                uint32_t r1[16], r2[16], r3[16];
+                tmem_ld16(tl + DEC_S_COL + sb * 64, r);
+                tmem_ld16(tl + DEC_S_COL + sb * 64 + 16, r1);
+                tmem_ld16(tl + DEC_S_COL + sb * 64 + 32, r2);
+                tmem_ld16(tl + DEC_S_COL + sb * 64 + 48, r3);
+                tmem_wait_ld();
+#pragma unroll
+                for (int h = 0; h < 16; ++h)
+                  r[h] = __float_as_uint((__uint_as_float(r[h]) + __uint_as_float(r1[h])) +
+                                         (__uint_as_float(r2[h]) + __uint_as_float(r3[h])));
+              }
               tc_fence_before();
               mbar_arrive(&bars->s_empty[sb]);
               ++cnt.s;
@@ -616,9 +738,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
                 if (!mbar_wait(&bars->o_full[pb], ((cnt.o - 1) >> 1) & 1, p.status)) { ok = false; break; }
                 tc_fence_after();
                 uint32_t o0[16], o1[16];
-                tmem_ld16(tl + 32 + pb * 32, o0);
-                tmem_ld16(tl + 32 + pb * 32 + 16, o1);
-                tmem_wait_ld();
+                dec_load_o(tl + DEC_O_COL + pb * 128, o0, o1);
 #pragma unroll
                 for (int h = 0; h < 16; ++h) {
                   a0[h] = a0[h] * ap[h] + __uint_as_float(o0[h]);
@@ -635,9 +755,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               if (!mbar_wait(&bars->o_full[pb], ((cnt.o - 1) >> 1) & 1, p.status)) { ok = false; break; }
               tc_fence_after();
               uint32_t o0[16], o1[16];
-              tmem_ld16(tl + 32 + pb * 32, o0);
-              tmem_ld16(tl + 32 + pb * 32 + 16, o1);
-              tmem_wait_ld();
+              dec_load_o(tl + DEC_O_COL + pb * 128, o0, o1);
 #pragma unroll
               for (int h = 0; h < 16; ++h) {
                 a0[h] = a0[h] * ap[h] + __uint_as_float(o0[h]);
@@ -671,8 +789,8 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           }
         }
         // item done: release its descriptor / Q slot (all softmax threads are past it)
-        named_bar_sync(1, 128);
-        if (tid == 0) mbar_arrive(&bars->item_empty[islot]);
+        named_bar_sync(3, nthr);
+        if (wg == 0 && tid == 0) mbar_arrive(&bars->item_empty[islot]);
       }
     }
     __syncthreads();
