@@ -12,9 +12,17 @@ flush is needed between steps.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1|c2|c3s|c3l|c4]
     python bench.py --impl reference ...   # the reference's CPU path (restated) only
 
-Under torchrun every rank runs its own batch (attention data parallel, experts
-replicated): weak scaling, no cross-GPU exchange on the data path.  Rank 0 prints one JSON
-line; the time is the max over ranks of CUDA-event time.
+Under torchrun (``--gpus N``, N even) the c4 step is sharded: ranks form tensor-parallel
+pairs that split the attention by KV head (fp32 o_proj partials all-reduced over NCCL),
+the pairs run different batches (data parallel), and the 512 experts are split over all N
+ranks with NCCL all-to-all dispatch and return.  Each GPU keeps one c4 batch of work, so
+scaling is weak.  Rank 0 prints one JSON line; the time is the max over ranks of
+CUDA-event time.
+
+``value`` is device throughput with inputs resident in HBM.  ``e2e`` is the same step
+through the same public calls in a serving loop: each step uploads its inputs from
+pinned host memory and downloads its outputs, on copy streams that overlap the previous
+and next steps' kernels (double-buffered device inputs and outputs).
 """
 from __future__ import annotations
 
@@ -271,27 +279,31 @@ def run_ours(args, rank, world, device):
                         device=device) if attn is not None else None
     m_out = torch.empty_like(moe[1]) if moe else None
 
-    def step(ev_a=None, ev_m=None, q=None, gate=None, x=None):
+    def step(ev_a=None, ev_m=None, q=None, gate=None, x=None, meta=None, out_a=None,
+             out_m=None):
         if attn is not None:
             qq = q if q is not None else attn.q
             gg = gate if gate is not None else attn.gate
+            bt, cl, cu = meta if meta is not None else (attn.block_tables, attn.context_lens,
+                                                        attn.cu_seqlens_q)
+            oa = out_a if out_a is not None else a_out
             if sharded:
-                S.tp_attention_oproj(shard, qq, gg, attn.k_cache, attn.v_cache, attn.block_tables,
-                                     attn.context_lens, attn.cu_seqlens_q, attn.w_o, attn.scale,
-                                     group=tp_group, max_q_len=max_q, events=ev_a, out=a_out,
-                                     work_hint=hint)
+                S.tp_attention_oproj(shard, qq, gg, attn.k_cache, attn.v_cache, bt, cl, cu,
+                                     attn.w_o, attn.scale, group=tp_group, max_q_len=max_q,
+                                     events=ev_a, out=oa, work_hint=hint)
             else:
-                ops.pod_attn_oproj(qq, gg, attn.k_cache, attn.v_cache, attn.block_tables,
-                                   attn.context_lens, attn.cu_seqlens_q, attn.w_o, attn.scale,
-                                   out=a_out, max_q_len=max_q, events=ev_a, work_hint=hint)
+                ops.pod_attn_oproj(qq, gg, attn.k_cache, attn.v_cache, bt, cl, cu, attn.w_o,
+                                   attn.scale, out=oa, max_q_len=max_q, events=ev_a,
+                                   work_hint=hint)
         if moe:
             pm, xm = moe
             xx = x if x is not None else xm
+            om = out_m if out_m is not None else m_out
             if sharded:
-                m_out.copy_(ep_block(xx))
+                om.copy_(ep_block(xx))
             else:
                 ops.moe_forward(xx, pm.router, pm.gate_up, pm.down, pm.sh_gate, pm.sh_up,
-                                pm.sh_down, pm.sh_gate_w, 10, out=m_out, events=ev_m)
+                                pm.sh_down, pm.sh_gate_w, 10, out=om, events=ev_m)
 
     def barrier():
         if world > 1:
@@ -345,6 +357,10 @@ def run_ours(args, rank, world, device):
     res["peaks"] = peaks
 
     # ---------------- end-to-end through the public API with host buffers
+    # A serving loop: every step copies its inputs from pinned host memory and reads its
+    # outputs back.  The copies run on their own streams into double-buffered device
+    # inputs/outputs, so step i+1's upload and step i-1's download overlap step i's
+    # kernels; events order each buffer's reuse.  All copies are inside the timed region.
     if not args.no_e2e:
         pin = {}
         if attn is not None:
@@ -352,46 +368,71 @@ def run_ours(args, rank, world, device):
             pin["gate"] = attn.gate.cpu().pin_memory()
             pin["meta"] = [t.cpu().pin_memory() for t in
                            (attn.block_tables, attn.context_lens, attn.cu_seqlens_q)]
-            out_a_h = torch.empty(a_out.shape, dtype=a_out.dtype).pin_memory()
         if moe:
             pin["x"] = moe[1].cpu().pin_memory()
-            out_m_h = torch.empty(m_out.shape, dtype=m_out.dtype).pin_memory()
-        qd = torch.empty_like(attn.q) if attn is not None else None
-        gd = torch.empty_like(attn.gate) if attn is not None else None
-        xd = torch.empty_like(moe[1]) if moe else None
+        bufs, host_out = [], []
+        for _ in range(2):
+            bd = {}
+            if attn is not None:
+                bd["q"] = torch.empty_like(attn.q)
+                bd["gate"] = torch.empty_like(attn.gate)
+                bd["meta"] = [torch.empty_like(t) for t in
+                              (attn.block_tables, attn.context_lens, attn.cu_seqlens_q)]
+                bd["out_a"] = torch.empty_like(a_out)
+            if moe:
+                bd["x"] = torch.empty_like(moe[1])
+                bd["out_m"] = torch.empty_like(m_out)
+            bufs.append(bd)
+            host_out.append({k: torch.empty(bd[k].shape, dtype=bd[k].dtype).pin_memory()
+                             for k in ("out_a", "out_m") if k in bd})
         h2d = d2h = 0
         for v in pin.values():
             h2d += sum(t.numel() * t.element_size() for t in (v if isinstance(v, list) else [v]))
-        if attn is not None:
-            d2h += out_a_h.numel() * out_a_h.element_size()
-        if moe:
-            d2h += out_m_h.numel() * out_m_h.element_size()
+        for v in host_out[0].values():
+            d2h += v.numel() * v.element_size()
+        comp = torch.cuda.current_stream()
+        s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_used = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
 
-        def e2e_step():
-            if attn is not None:
-                qd.copy_(pin["q"], non_blocking=True)
-                gd.copy_(pin["gate"], non_blocking=True)
-                for dst, src in zip((attn.block_tables, attn.context_lens, attn.cu_seqlens_q),
-                                    pin["meta"]):
-                    dst.copy_(src, non_blocking=True)
-            if moe:
-                xd.copy_(pin["x"], non_blocking=True)
-            step(q=qd, gate=gd, x=xd)
-            if attn is not None:
-                out_a_h.copy_(a_out, non_blocking=True)
-            if moe:
-                out_m_h.copy_(m_out, non_blocking=True)
+        def e2e_step(i):
+            k = i % 2
+            bd, ho = bufs[k], host_out[k]
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(ev_used[k])          # step i-2 is done reading buffer k
+                if attn is not None:
+                    bd["q"].copy_(pin["q"], non_blocking=True)
+                    bd["gate"].copy_(pin["gate"], non_blocking=True)
+                    for dst, src in zip(bd["meta"], pin["meta"]):
+                        dst.copy_(src, non_blocking=True)
+                if moe:
+                    bd["x"].copy_(pin["x"], non_blocking=True)
+                ev_in[k].record(s_in)
+            comp.wait_event(ev_in[k])
+            comp.wait_event(ev_out[k])                # step i-2's outputs have been read
+            step(q=bd.get("q"), gate=bd.get("gate"), x=bd.get("x"), meta=bd.get("meta"),
+                 out_a=bd.get("out_a"), out_m=bd.get("out_m"))
+            ev_used[k].record(comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_used[k])
+                for name, h in ho.items():
+                    h.copy_(bd[name], non_blocking=True)
+                ev_out[k].record(s_out)
 
-        for _ in range(max(1, Wu)):
-            e2e_step()
+        for i in range(max(2, Wu)):
+            e2e_step(i)
         torch.cuda.synchronize()
         barrier()
-        Ke = max(3, K // 2)
+        Ke = max(4, K // 2)
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s2.record()
-        for _ in range(Ke):
-            e2e_step()
-        e2.record()
+        s2.record(comp)
+        s_in.wait_event(s2)
+        for i in range(Ke):
+            e2e_step(i)
+        comp.wait_event(ev_out[0])
+        comp.wait_event(ev_out[1])
+        e2.record(comp)
         torch.cuda.synchronize()
         ms_e = s2.elapsed_time(e2) / Ke
         mt = torch.tensor([ms_e], dtype=torch.float64, device=device)

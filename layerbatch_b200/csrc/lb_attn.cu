@@ -264,15 +264,19 @@ static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
   const int nsm = num_sms();
   long long split = a->kv_split_pages > 0 ? (long long)a->kv_split_pages * a->page_size : 0;
   if (split == 0) {
-    // largest power-of-two page count (<= 16 pages) whose item count, assuming half-full
-    // tables, still gives every SM ~16 items: long items pipeline well, many items keep
-    // the dynamic tail short
-    const long long est_ctx = std::max<long long>(1, pl.max_ctx / 2);
+    // largest power-of-two page count (<= 16 pages) that still gives every SM about two
+    // items: each item pays a fixed start-up and epilogue cost (Q load, split flush),
+    // so items are made as long as the balance across SMs allows; the planner orders
+    // them longest first, which keeps the dynamic tail short.  The typical context is
+    // the caller's decode-token hint per sequence, else half the table width.
+    long long est_ctx = std::max<long long>(1, pl.max_ctx / 2);
+    if (a->decode_tokens_hint > 0 && a->num_seqs > 0)
+      est_ctx = std::max<long long>(1, a->decode_tokens_hint / a->num_seqs);
     long long pages = 1;
     for (long long pg = 16; pg >= 1; pg >>= 1) {
       const long long st = pg * a->page_size;
       const long long items = a->num_seqs * a->num_kv_heads * ((est_ctx + st - 1) / st);
-      if (items >= 16ll * nsm) { pages = pg; break; }
+      if (items >= 2ll * nsm) { pages = pg; break; }
     }
     split = pages * a->page_size;
   }
@@ -284,18 +288,24 @@ static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
   pl.grid = nsm;
   pl.n_pf_ctas = a->max_q_len > 1 ? nsm / 2 : 0;
   if (a->max_q_len > 1) {
-    // tensor-bound share of the work: prefill FLOPs at ~1 PFLOP/s vs decode KV bytes at
-    // ~6 TB/s; CTAs that finish their queue switch to the other one, so this only sets
-    // the starting split
+    // Starting split of the SMs between the queues (CTAs that finish their queue switch
+    // to the other, so this only sets where they start).  Work is counted in SM-seconds
+    // at the per-SM rates this kernel reaches on B200: prefill ~4.1 TFLOP/s per SM,
+    // decode ~60 GB/s of KV per SM, with decode as a whole capped at ~6.9 TB/s of HBM.
+    // The prefill CTAs get the share that finishes their queue when the decode queue is
+    // done, plus 10% so that decode CTAs, not the long prefill tiles, form the tail.
     double pf_pairs = (double)a->prefill_pairs_hint, dec_tok = (double)a->decode_tokens_hint;
     if (pf_pairs <= 0 && dec_tok <= 0) {
       const double pf_rows = (double)std::max<long long>(0, a->num_tokens - (a->num_seqs - 1));
       pf_pairs = pf_rows * (pl.max_ctx / 4.0);
       dec_tok = (double)(a->num_seqs - 1) * (pl.max_ctx / 2.0);
     }
-    const double t_pf = pf_pairs * a->num_q_heads * POD_D * 4.0 / 1.0e15;
-    const double t_dec = dec_tok * a->num_kv_heads * POD_D * 4.0 / 6.0e12;
-    pl.n_pf_ctas = std::max(1, std::min(nsm, (int)(nsm * t_pf / (t_pf + t_dec + 1e-30) + 0.5)));
+    const double w_pf = pf_pairs * a->num_q_heads * POD_D * 4.0 / 4.1e12;
+    const double dec_bytes = dec_tok * a->num_kv_heads * POD_D * 4.0;
+    const double w_dec = dec_bytes / 60.0e9;
+    const double t_end = std::max(dec_bytes / 6.9e12, (w_pf + w_dec) / nsm);
+    const int n = (int)(1.1 * w_pf / std::max(t_end, 1e-9) + 0.5);
+    pl.n_pf_ctas = std::max(1, std::min(nsm, n));
   }
   return LB_OK;
 }

@@ -126,6 +126,13 @@ __device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* ma
   for (int c = 0; c < 4; ++c) tma_load_3d(dst + c * POD_CHUNK, map, bar, c * 64, kvh, row);
 }
 
+// Decode ring order of one item of n tiles: K0, K1, V0, K2, V1, ..., K(n-1), V(n-2), V(n-1).
+// K runs one tile ahead of V, so the K tile of the next S MMA is never queued behind a V
+// tile that waits for the current softmax, and each V tile streams in while its scores are
+// being turned into P.
+__device__ __forceinline__ int dec_pos_k(int j) { return j ? 2 * j - 1 : 0; }
+__device__ __forceinline__ int dec_pos_v(int j, int n) { return min(2 * j + 2, 2 * n - 1); }
+
 // Decode TMEM columns: S^T [2 buffers][4 chunk partials][16 heads], O^T [2 buffers][2 dim
 // halves][4 token-quarter partials][16 heads].
 constexpr int DEC_S_COL = 0;
@@ -277,9 +284,17 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               const int slot = cnt.kv % nslots;
               const uint32_t ph = (cnt.kv / nslots) & 1;
               if (!mbar_wait(&bars->kv_empty[slot], ph ^ 1, p.status)) { *abortp = 1; break; }
-              const int row = kv_page_row(p, b, t_begin + (j >> 1) * POD_KV);
+              // ring position j -> (tile, K or V), the inverse of dec_pos_k / dec_pos_v
+              int tile = 0;
+              bool is_v = false;
+              if (j > 0) {
+                tile = (j - 1) >> 1;
+                is_v = ((j - 1) & 1) || tile + 1 >= ntiles;
+                if (!is_v) ++tile;
+              }
+              const int row = kv_page_row(p, b, t_begin + tile * POD_KV);
               mbar_arrive_expect_tx(&bars->kv_full[slot], POD_TILE);
-              load_kv_tile(kv_base + slot * POD_TILE, (j & 1) ? &tmV : &tmK, &bars->kv_full[slot],
+              load_kv_tile(kv_base + slot * POD_TILE, is_v ? &tmV : &tmK, &bars->kv_full[slot],
                            kvh, row);
               ++cnt.kv;
             }
@@ -345,7 +360,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           for (int j = 0; j <= ntiles && ok; ++j) {
             if (j < ntiles) {
               // ---- S_j  (prefill: K ring slots 0-1; decode: unified ring)
-              const uint32_t kp = prefill ? base + j : base + 2 * j;
+              const uint32_t kp = prefill ? base + j : base + dec_pos_k(j);
               const int ring = prefill ? PF_SLOTS : nslots;
               const int ks = kp % ring;
               const int sb = cnt.s & 1;
@@ -383,7 +398,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             if (j > 0) {
               // ---- PV_{j-1}  (prefill: V ring slots 2-3; decode: unified ring)
               const int jj = j - 1;
-              const uint32_t vp = prefill ? vbase + jj : base + 2 * jj + 1;
+              const uint32_t vp = prefill ? vbase + jj : base + dec_pos_v(jj, ntiles);
               const int ring = prefill ? PF_SLOTS : nslots;
               const int vs = (prefill ? 2 : 0) + (int)(vp % ring);
               const int ob = cnt.o & 1;
@@ -719,7 +734,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               // tokens past the end of the last tile: zero their V rows (stale cache bytes
               // could be NaN, and 0 * NaN would poison O^T)
               if (t_begin + (j + 1) * POD_KV > t_end) {
-                const uint32_t vp = kvbase + 2 * j + 1;
+                const uint32_t vp = kvbase + dec_pos_v(j, ntiles);
                 if (!mbar_wait(&bars->kv_full[vp % nslots], (vp / nslots) & 1, p.status)) { ok = false; break; }
                 if (!valid) {
                   const uint32_t v = smem_u32(kv_base + (vp % nslots) * POD_TILE) + row * 128;
