@@ -53,6 +53,12 @@ def load_peaks():
         return dict(PEAKS_FALLBACK, source="fallback")
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one k_pod_attn launch on the
+# single-GPU workload, from one ncu capture of the current kernel (summaries under
+# profiles/); re-captured whenever the kernel changes.
+NCU_POD_TRAFFIC = {"c1": 293285376 + 4167936, "c2": 1220580608 + 22867968,
+                   "c4": 9130017024 + 59481088}
+
 # ---------------------------------------------------------------------------- workloads
 CONFIGS = {
     "c1": "c1: 64 decode seqs ctx~U[512,4096] -> gated paged attention + o_proj 4096->2048",
@@ -508,7 +514,8 @@ def main():
             else:
                 roof = {"bound": "tensor", "achieved": a["tflops"], "peak": peaks["bf16_tflops"],
                         "unit": "TFLOP/s", "frac": a["tflops"] / peaks["bf16_tflops"]}
-            roof.update({"kernel": "k_pod_attn", "traffic": None,
+            traffic = NCU_POD_TRAFFIC.get(args.config) if world == 1 else None
+            roof.update({"kernel": "k_pod_attn", "traffic": traffic,
                          "peak_source": peaks["source"], "kernel_ms": a["ms"],
                          "algorithmic_bytes": a["bytes"], "algorithmic_flops": a["flops"]})
         line = {
