@@ -277,6 +277,8 @@ def run_ours(args, rank, world, device):
             del p
             moe = (None, x)
             torch.cuda.empty_cache()
+            from layerbatch_b200.engine.ep import EPExchange
+            ep_block.attach_exchange(EPExchange(T_moe, 2048, 10, device=device))
     tokens = (attn.num_tokens // tp) if attn is not None else T_moe
     max_q = max(attn.qlen_list) if attn is not None else 0
     hint = ops.pod_work_hint(attn.ctx_list, attn.qlen_list) if attn is not None else None
@@ -306,7 +308,8 @@ def run_ours(args, rank, world, device):
             xx = x if x is not None else xm
             om = out_m if out_m is not None else m_out
             if sharded:
-                om.copy_(ep_block(xx))
+                from layerbatch_b200.engine.ep import ep_moe_forward_nvlink
+                ep_moe_forward_nvlink(ep_block, xx, ep_block.ep_exchange, out=om)
             else:
                 ops.moe_forward(xx, pm.router, pm.gate_up, pm.down, pm.sh_gate, pm.sh_up,
                                 pm.sh_down, pm.sh_gate_w, 10, out=om, events=ev_m)
@@ -357,7 +360,8 @@ def run_ours(args, rank, world, device):
         t_g2 = statistics.mean(e[2].elapsed_time(e[3]) for e in ev_moe) * 1e-3
         res["moe_gemm"] = {"gate_up_ms": t_g1 * 1e3, "down_ms": t_g2 * 1e3}
     res["parallelism"] = (f"tp{tp} x dp{world // tp} attention (KV-head shards, fp32 o_proj "
-                          f"all-reduce), ep{world} MoE (NCCL all-to-all)" if sharded else
+                          f"all-reduce), ep{world} MoE (NVLink peer-memory dispatch/return)"
+                          if sharded else
                           ("single GPU" if world == 1 else
                            f"dp{world}: per-rank batches, experts replicated"))
     res["peaks"] = peaks

@@ -141,6 +141,69 @@ typedef struct LbMoeArgs {
 int lb_moe_workspace_size(const LbMoeArgs* args, size_t* bytes);
 int lb_moe_forward(const LbMoeArgs* args, void* stream);
 
+/* ---------------------------------------------------------------- expert parallel (NVLink)
+ * The MoE block with its experts split over the ranks of one node, exchanging token rows
+ * over NVLink through peer-mapped memory instead of a host-driven all-to-all.  The
+ * reference has no expert parallelism (every rank holds every expert,
+ * nanovllm/models/qwen3_5.py:795-800, and each forward runs the full MoE on its own
+ * tokens, qwen3_5.py:899-905); the result equals Qwen3_5SparseMoeBlock.forward on this
+ * rank's tokens.  Rank r holds experts [r*E/P, (r+1)*E/P) and one exchange buffer that
+ * every rank maps.  Per call: router + top-k on the rank's tokens; each token row is
+ * written ONCE to every rank owning at least one of its k experts (with its k ids and
+ * weights); the owner runs its experts on the rows it received plus the shared expert
+ * on its own tokens in one grouped GEMM pair, sums each received row over its local
+ * experts and writes that single row back to the source; the source adds the returned
+ * rows to its shared-expert row.  Ranks signal each other with epoch flags in the
+ * buffers; every wait is bounded (LB_DEV_TIMEOUT in the workspace status word). */
+#define LB_EP_MAX_RANKS 8
+#define LB_EP_IPC_HANDLE_BYTES 64
+
+/* Bytes of one rank's exchange buffer for `world` ranks, up to `capacity` tokens per rank
+ * and call, rows of `hidden` bf16 and `top_k` routed experts. */
+size_t lb_ep_buffer_size(int64_t world, int64_t capacity, int64_t hidden, int64_t top_k);
+/* cudaMalloc + zero a buffer on the current device and export its CUDA IPC handle
+ * (LB_EP_IPC_HANDLE_BYTES bytes written to ipc_handle). */
+int lb_ep_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+/* Map another rank's buffer (same node) into this process; lb_ep_buffer_close unmaps it. */
+int lb_ep_buffer_open(const void* ipc_handle, void** ptr);
+int lb_ep_buffer_close(void* ptr);
+int lb_ep_buffer_free(void* ptr);
+
+#define LB_EP_PHASE_DISPATCH 1 /* router, top-k, routing table, row dispatch + signal */
+#define LB_EP_PHASE_EXPERTS 2  /* wait, local experts (+ shared), per-row sums sent back */
+#define LB_EP_PHASE_COMBINE 4  /* wait, shared row + returned rows -> out */
+
+typedef struct LbEpArgs {
+  int64_t num_tokens;        /* T on this rank (<= capacity) */
+  int64_t capacity;          /* tokens per rank per call the buffers were sized for */
+  int64_t hidden;            /* H (multiple of 256) */
+  int64_t num_experts;       /* E (multiple of world and of 32) */
+  int64_t top_k;             /* k */
+  int64_t inter;             /* I = shared intermediate (multiple of 128) */
+  int32_t rank, world;       /* this rank and the EP group size (world <= LB_EP_MAX_RANKS) */
+  const void* x;             /* [T, H] bf16 */
+  const void* w_router;      /* [E, H] bf16, replicated */
+  const void* w_gate_up;     /* [E/P, 2I, H] bf16: this rank's experts */
+  const void* w_down;        /* [E/P, H, I] bf16 */
+  const void* w_shared_gate; /* [I, H] */
+  const void* w_shared_up;   /* [I, H] */
+  const void* w_shared_down; /* [H, I] */
+  const void* w_shared_expert_gate; /* [1, H] */
+  void* out;                 /* [T, H] bf16 */
+  void* peer_bufs[LB_EP_MAX_RANKS]; /* every rank's exchange buffer as mapped in this
+                                     * process ([rank] = own), from lb_ep_buffer_* */
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t phases;            /* 0 = all; else a mask of LB_EP_PHASE_* (the phases of
+                              * one call must run in order; used to run several ranks'
+                              * phases interleaved on one device in tests) */
+  void* timing_events[4];    /* optional: around the dispatch ([0],[1]) and the expert
+                              * GEMMs ([2],[3]) */
+} LbEpArgs;
+
+int lb_ep_workspace_size(const LbEpArgs* args, size_t* bytes);
+int lb_ep_moe_forward(const LbEpArgs* args, void* stream);
+
 /* ---------------------------------------------------------------- KV cache store
  * k_cache/v_cache[slot] = k/v[i] for slot_mapping[i] != -1, rows of Hkv*D bf16.
  * k, v: [N, Hkv, D] with token stride k_stride / v_stride (elements), heads packed. */

@@ -23,8 +23,14 @@ EXPORTS = [
     "lb_gemm_workspace_size", "lb_gemm_bf16", "lb_router_topk",
     "lb_moe_permute_workspace_size", "lb_moe_permute", "lb_moe_permute_noalloc",
     "lb_moe_workspace_size",
-    "lb_moe_forward", "lb_store_kvcache", "lb_pod_workspace_size", "lb_pod_attn_oproj",
+    "lb_moe_forward", "lb_ep_buffer_size", "lb_ep_buffer_alloc", "lb_ep_buffer_open",
+    "lb_ep_buffer_close", "lb_ep_buffer_free", "lb_ep_workspace_size", "lb_ep_moe_forward",
+    "lb_store_kvcache", "lb_pod_workspace_size", "lb_pod_attn_oproj",
 ]
+
+LB_EP_MAX_RANKS = 8
+LB_EP_IPC_HANDLE_BYTES = 64
+LB_EP_PHASE_DISPATCH, LB_EP_PHASE_EXPERTS, LB_EP_PHASE_COMBINE = 1, 2, 4
 
 vp = C.c_void_p
 i64 = C.c_int64
@@ -43,6 +49,18 @@ class LbMoeArgs(C.Structure):
         ("workspace_bytes", C.c_size_t), ("timing_events", vp * 4),
         ("routing_given", i32), ("topk_weights_f32", vp), ("no_shared", i32),
         ("pair_rows", vp), ("pair_index", vp),
+    ]
+
+
+class LbEpArgs(C.Structure):
+    _fields_ = [
+        ("num_tokens", i64), ("capacity", i64), ("hidden", i64), ("num_experts", i64),
+        ("top_k", i64), ("inter", i64), ("rank", i32), ("world", i32),
+        ("x", vp), ("w_router", vp), ("w_gate_up", vp), ("w_down", vp),
+        ("w_shared_gate", vp), ("w_shared_up", vp), ("w_shared_down", vp),
+        ("w_shared_expert_gate", vp), ("out", vp), ("peer_bufs", vp * LB_EP_MAX_RANKS),
+        ("workspace", vp), ("workspace_bytes", C.c_size_t), ("phases", i32),
+        ("timing_events", vp * 4),
     ]
 
 
@@ -82,6 +100,14 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.lb_moe_permute_noalloc.argtypes = [vp, i64, i64, i64, i64, vp, vp, vp, vp]
     L.lb_moe_workspace_size.argtypes = [C.POINTER(LbMoeArgs), C.POINTER(C.c_size_t)]
     L.lb_moe_forward.argtypes = [C.POINTER(LbMoeArgs), vp]
+    L.lb_ep_buffer_size.restype = C.c_size_t
+    L.lb_ep_buffer_size.argtypes = [i64, i64, i64, i64]
+    L.lb_ep_buffer_alloc.argtypes = [C.c_size_t, C.POINTER(vp), vp]
+    L.lb_ep_buffer_open.argtypes = [vp, C.POINTER(vp)]
+    L.lb_ep_buffer_close.argtypes = [vp]
+    L.lb_ep_buffer_free.argtypes = [vp]
+    L.lb_ep_workspace_size.argtypes = [C.POINTER(LbEpArgs), C.POINTER(C.c_size_t)]
+    L.lb_ep_moe_forward.argtypes = [C.POINTER(LbEpArgs), vp]
     L.lb_store_kvcache.argtypes = [vp, i64, vp, i64, vp, vp, vp, i64, i64, i64, vp]
     L.lb_pod_workspace_size.argtypes = [C.POINTER(LbPodArgs), C.POINTER(C.c_size_t)]
     L.lb_pod_attn_oproj.argtypes = [C.POINTER(LbPodArgs), vp]

@@ -14,6 +14,7 @@
 
 #include "lb_gemm_launch.cuh"
 #include "lb_host.h"
+#include "lb_moe_core.h"
 
 namespace lb {
 
@@ -255,44 +256,31 @@ __global__ void k_gather_rows(const __nv_bfloat16* __restrict__ x, int H,
 }
 
 // ------------------------------------------------------------------------------ host
-struct MoeWs {
-  int* status;
-  __nv_bfloat16* logits;
-  int32_t* ids;
-  float* wf;
-  __nv_bfloat16* wb;
-  int* chunk_hist;
-  int* counts;
-  int* row_start;
-  int* mtile_start;
-  int32_t* perm_token;
-  float* perm_w;
-  int32_t* row_of;
-  __nv_bfloat16* a_packed;
-  __nv_bfloat16* act;
-  __nv_bfloat16* yw;
-};
+void carve_core(Carve& c, size_t T_sh, size_t T_r, size_t k, size_t H, size_t nl, size_t I,
+                MoeWs& w) {
+  const size_t rows = T_sh + T_r * k;
+  w.chunk_hist = c.take<int>((size_t)perm_chunks((int)T_r, (int)k) * nl);
+  w.counts = c.take<int>(nl + 2);
+  w.row_start = c.take<int>(nl + 2);
+  w.mtile_start = c.take<int>(nl + 2);
+  w.perm_token = c.take<int32_t>(rows);
+  w.perm_w = c.take<float>(rows);
+  w.row_of = c.take<int32_t>(T_r * k);
+  w.a_packed = c.take<__nv_bfloat16>(rows * H);
+  w.act = c.take<__nv_bfloat16>(rows * I);
+  w.yw = c.take<__nv_bfloat16>(rows * H);
+}
 
 static size_t carve_moe(const LbMoeArgs& a, void* base, MoeWs& w) {
   const size_t T = a.num_tokens, k = a.top_k, H = a.hidden, E = a.num_experts;
   const size_t nl = a.num_local_experts, I = a.inter;
-  const size_t rows = (a.no_shared ? 0 : T) + T * k;
   Carve c(base, ~size_t(0));
   w.status = c.take<int>(64);
   w.logits = c.take<__nv_bfloat16>(a.routing_given ? 0 : T * E);
   w.ids = c.take<int32_t>(T * k);
   w.wf = c.take<float>(a.routing_given ? 0 : T * k);
   w.wb = c.take<__nv_bfloat16>(T * k);
-  w.chunk_hist = c.take<int>((size_t)perm_chunks((int)T, (int)k) * nl);
-  w.counts = c.take<int>(nl + 2);
-  w.row_start = c.take<int>(nl + 2);
-  w.mtile_start = c.take<int>(nl + 2);
-  w.perm_token = c.take<int32_t>(rows);
-  w.perm_w = c.take<float>(rows);
-  w.row_of = c.take<int32_t>(T * k);
-  w.a_packed = c.take<__nv_bfloat16>(rows * H);
-  w.act = c.take<__nv_bfloat16>(rows * I);
-  w.yw = c.take<__nv_bfloat16>(rows * H);
+  carve_core(c, a.no_shared ? 0 : T, T, k, H, nl, I, w);
   return c.off + 256;
 }
 
@@ -327,9 +315,9 @@ static int check_moe(const LbMoeArgs* a) {
   return LB_OK;
 }
 
-static int launch_topk(const __nv_bfloat16* logits, long long ld, int T, int E, int k,
-                       int32_t* ids, float* wf, __nv_bfloat16* wb, const __nv_bfloat16* x,
-                       const __nv_bfloat16* wsg, int H, float* sg, cudaStream_t st) {
+int launch_topk(const __nv_bfloat16* logits, long long ld, int T, int E, int k, int32_t* ids,
+                float* wf, __nv_bfloat16* wb, const __nv_bfloat16* x, const __nv_bfloat16* wsg,
+                int H, float* sg, cudaStream_t st) {
   if (T == 0) return LB_OK;
   const int threads = 256, wpb = threads / 32;
   const int grid = (T + wpb - 1) / wpb;
@@ -525,8 +513,7 @@ __global__ void k_moe_combine(const __nv_bfloat16* __restrict__ yw, const int32_
 static int run_permute_chunked(const int32_t* ids, const float* wf, int T, int k, int expert_base,
                                int nl, int* chunk_hist, int* counts, int* row_start,
                                int* mtile_start, int32_t* perm_token, float* perm_w,
-                               int32_t* row_of, cudaStream_t st, bool has_shared = true) {
-  const int T0 = has_shared ? T : 0;
+                               int32_t* row_of, cudaStream_t st, int T0) {
   const int n = T * k;
   const int nc = perm_chunks(T, k);
   LB_CUDA_CHECK(cudaMemsetAsync(row_of, 0xff, sizeof(int32_t) * (size_t)n, st));
@@ -548,6 +535,97 @@ static int run_permute_chunked(const int32_t* ids, const float* wf, int T, int k
     k_perm_chunk_scatter<<<nc, 32, sizeof(int) * nl, st>>>(ids, wf, T, k, expert_base, nl, chunk_hist,
                                                            row_start, perm_token, perm_w, row_of);
     { int _rc = launched("k_perm_chunk_scatter"); if (_rc) return _rc; }
+  }
+  return LB_OK;
+}
+
+// ------------------------------------------------------------------------------ core
+int moe_core(const MoeCore& c, const MoeWs& w, cudaStream_t st) {
+  const int T = c.T_r, H = c.H, k = c.k, I = c.I, nl = c.nl;
+  const int T0 = c.T_sh;
+  const int G = nl + 1;
+  const bool shared = T0 > 0;
+  const int32_t* ids = c.ids;
+  const float* wf = c.wf;
+  // 3. permutation (routed pairs of the local experts) and gather of their input rows
+  int rc = run_permute_chunked(ids, wf, T, k, c.expert_base, nl, w.chunk_hist, w.counts,
+                               w.row_start, w.mtile_start, w.perm_token, w.perm_w, w.row_of, st,
+                               T0);
+  if (rc) return rc;
+  if (nl > 0) {
+    const long long vec = (long long)T * k * (H / 8);
+    const int grid = (int)std::max<long long>(1, std::min<long long>(num_sms() * 8, (vec + 255) / 256));
+    k_gather_rows<<<grid, 256, 0, st>>>(c.x_r, H, w.perm_token, w.row_start + G, T0, w.a_packed);
+    { int _rc = launched("k_gather_rows"); if (_rc) return _rc; }
+  }
+  const long long rows = (long long)T0 + (long long)T * k;
+  const long long max_mtiles = ((long long)T * k) / GEMM_BM + nl + (T0 + GEMM_BM - 1) / GEMM_BM;
+  const bool any_gemm = shared || nl > 0;
+
+  // 4. grouped gate/up GEMM with SwiGLU: act[rows, I]
+  if (any_gemm) {
+    constexpr int BN = 256;
+    CUtensorMap tA, tAsh, tB, tB0, tB1;
+    if ((rc = make_tmap_bf16_2d(&tA, w.a_packed, rows, H, H, GEMM_BM, 64))) return rc;
+    if ((rc = make_tmap_bf16_2d(&tAsh, shared ? c.x_sh : c.x_r, shared ? T0 : T, H, H, GEMM_BM, 64))) return rc;
+    if (nl > 0 && (rc = make_tmap_bf16_3d(&tB, c.w_gate_up, nl, 2 * I, H, H, (uint64_t)2 * I * H,
+                                          BN / 2, 64)))
+      return rc;
+    if (shared) {
+      if ((rc = make_tmap_bf16_3d(&tB0, c.w_sh_gate, 1, I, H, H, (uint64_t)I * H, BN / 2, 64)))
+        return rc;
+      if ((rc = make_tmap_bf16_3d(&tB1, c.w_sh_up, 1, I, H, H, (uint64_t)I * H, BN / 2, 64)))
+        return rc;
+    }
+    if (nl == 0) tB = tB0;
+    if (!shared) tB0 = tB1 = tB;
+    GemmArgs g = gemm_args_default(w.status);
+    g.mtile_start = w.mtile_start;
+    g.row_start = w.row_start;
+    g.num_groups = G;
+    g.n_tiles = (2 * I) / BN;
+    g.k_blocks = H / 64;
+    g.shared_group = shared ? 0 : -1;
+    g.b_group_base = 1;
+    g.b_half_offset = I;
+    g.out = w.act;
+    g.ldo = I;
+    g.out_rows = (int)rows;
+    g.out_cols = I;
+    const int grid = (int)std::min<long long>(num_sms(), max_mtiles * g.n_tiles);
+    record_event(c.events ? c.events[0] : nullptr, st);
+    if ((rc = launch_gemm<BN, 4, EPI_SWIGLU, true>(tA, tAsh, tB, tB0, tB1, g, grid, st))) return rc;
+    record_event(c.events ? c.events[1] : nullptr, st);
+  }
+  // 5. grouped down GEMM of every group (shared expert = group 0), each row scaled by its
+  //    routing weight (shared rows: sigmoid gate): yw[rows, H]
+  if (any_gemm) {
+    constexpr int BN = 256;
+    CUtensorMap tA, tB, tBs;
+    if ((rc = make_tmap_bf16_2d(&tA, w.act, rows, I, I, GEMM_BM, 64))) return rc;
+    if (nl > 0 && (rc = make_tmap_bf16_3d(&tB, c.w_down, nl, H, I, I, (uint64_t)H * I, BN, 64)))
+      return rc;
+    if (shared && (rc = make_tmap_bf16_3d(&tBs, c.w_sh_down, 1, H, I, I, (uint64_t)H * I, BN, 64)))
+      return rc;
+    if (nl == 0) tB = tBs;
+    if (!shared) tBs = tB;
+    GemmArgs g = gemm_args_default(w.status);
+    g.mtile_start = w.mtile_start;
+    g.row_start = w.row_start;
+    g.num_groups = G;
+    g.n_tiles = H / BN;
+    g.k_blocks = I / 64;
+    g.shared_group = shared ? 0 : -1;
+    g.b_group_base = 1;
+    g.row_scale = w.perm_w;
+    g.out = w.yw;
+    g.ldo = H;
+    g.out_rows = (int)rows;
+    g.out_cols = H;
+    const int grid = (int)std::min<long long>(num_sms(), max_mtiles * g.n_tiles);
+    record_event(c.events ? c.events[2] : nullptr, st);
+    if ((rc = launch_gemm<BN, 4, EPI_SCALE_BF16, false>(tA, tA, tB, tBs, tBs, g, grid, st))) return rc;
+    record_event(c.events ? c.events[3] : nullptr, st);
   }
   return LB_OK;
 }
@@ -624,7 +702,7 @@ int lb_moe_permute(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base
   int* chunk_hist = c.take<int>((size_t)perm_chunks((int)T, (int)k) * nl);
   return run_permute_chunked(ids, nullptr, (int)T, (int)k, (int)expert_base, (int)nl, chunk_hist,
                              counts, row_start, mt, perm_token, nullptr, row_of,
-                             static_cast<cudaStream_t>(stream));
+                             static_cast<cudaStream_t>(stream), (int)T);
 }
 
 int lb_moe_permute_noalloc(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base,
@@ -704,85 +782,27 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
     ids = ids_out;
     wf = w.wf;
   }
-  // 3. permutation (routed pairs of the local experts) and gather of their input rows
-  rc = run_permute_chunked(ids, wf, T, k, (int)a->expert_base, nl, w.chunk_hist, w.counts,
-                           w.row_start, w.mtile_start, w.perm_token, w.perm_w, w.row_of, st,
-                           shared);
-  if (rc) return rc;
-  if (nl > 0) {
-    const long long vec = (long long)T * k * (H / 8);
-    const int grid = (int)std::max<long long>(1, std::min<long long>(num_sms() * 8, (vec + 255) / 256));
-    k_gather_rows<<<grid, 256, 0, st>>>(x, H, w.perm_token, w.row_start + G, T0, w.a_packed);
-    { int _rc = launched("k_gather_rows"); if (_rc) return _rc; }
-  }
-  const long long rows = (long long)T0 + (long long)T * k;
-  const long long max_mtiles = ((long long)T * k) / GEMM_BM + nl + (T0 + GEMM_BM - 1) / GEMM_BM;
-  const bool any_gemm = shared || nl > 0;
-
-  // 4. grouped gate/up GEMM with SwiGLU: act[rows, I]
-  if (any_gemm) {
-    constexpr int BN = 256;
-    CUtensorMap tA, tAsh, tB, tB0, tB1;
-    if ((rc = make_tmap_bf16_2d(&tA, w.a_packed, rows, H, H, GEMM_BM, 64))) return rc;
-    if ((rc = make_tmap_bf16_2d(&tAsh, x, T, H, H, GEMM_BM, 64))) return rc;
-    if (nl > 0 && (rc = make_tmap_bf16_3d(&tB, a->w_gate_up, nl, 2 * I, H, H, (uint64_t)2 * I * H,
-                                          BN / 2, 64)))
-      return rc;
-    if (shared) {
-      if ((rc = make_tmap_bf16_3d(&tB0, a->w_shared_gate, 1, I, H, H, (uint64_t)I * H, BN / 2, 64)))
-        return rc;
-      if ((rc = make_tmap_bf16_3d(&tB1, a->w_shared_up, 1, I, H, H, (uint64_t)I * H, BN / 2, 64)))
-        return rc;
-    }
-    if (nl == 0) tB = tB0;
-    if (!shared) tB0 = tB1 = tB;
-    GemmArgs g = gemm_args_default(w.status);
-    g.mtile_start = w.mtile_start;
-    g.row_start = w.row_start;
-    g.num_groups = G;
-    g.n_tiles = (2 * I) / BN;
-    g.k_blocks = H / 64;
-    g.shared_group = shared ? 0 : -1;
-    g.b_group_base = 1;
-    g.b_half_offset = I;
-    g.out = w.act;
-    g.ldo = I;
-    g.out_rows = (int)rows;
-    g.out_cols = I;
-    const int grid = (int)std::min<long long>(num_sms(), max_mtiles * g.n_tiles);
-    record_event(a->timing_events[0], st);
-    if ((rc = launch_gemm<BN, 4, EPI_SWIGLU, true>(tA, tAsh, tB, tB0, tB1, g, grid, st))) return rc;
-    record_event(a->timing_events[1], st);
-  }
-  // 5. grouped down GEMM of every group (shared expert = group 0), each row scaled by its
-  //    routing weight (shared rows: sigmoid gate): yw[rows, H]
-  if (any_gemm) {
-    constexpr int BN = 256;
-    CUtensorMap tA, tB, tBs;
-    if ((rc = make_tmap_bf16_2d(&tA, w.act, rows, I, I, GEMM_BM, 64))) return rc;
-    if (nl > 0 && (rc = make_tmap_bf16_3d(&tB, a->w_down, nl, H, I, I, (uint64_t)H * I, BN, 64)))
-      return rc;
-    if (shared && (rc = make_tmap_bf16_3d(&tBs, a->w_shared_down, 1, H, I, I, (uint64_t)H * I, BN, 64)))
-      return rc;
-    if (nl == 0) tB = tBs;
-    if (!shared) tBs = tB;
-    GemmArgs g = gemm_args_default(w.status);
-    g.mtile_start = w.mtile_start;
-    g.row_start = w.row_start;
-    g.num_groups = G;
-    g.n_tiles = H / BN;
-    g.k_blocks = I / 64;
-    g.shared_group = shared ? 0 : -1;
-    g.b_group_base = 1;
-    g.row_scale = w.perm_w;
-    g.out = w.yw;
-    g.ldo = H;
-    g.out_rows = (int)rows;
-    g.out_cols = H;
-    const int grid = (int)std::min<long long>(num_sms(), max_mtiles * g.n_tiles);
-    record_event(a->timing_events[2], st);
-    if ((rc = launch_gemm<BN, 4, EPI_SCALE_BF16, false>(tA, tA, tB, tBs, tBs, g, grid, st))) return rc;
-    record_event(a->timing_events[3], st);
+  // 3.-5. permutation, gather, grouped gate/up (SwiGLU) and down GEMMs
+  {
+    MoeCore c{};
+    c.T_sh = T0;
+    c.T_r = T;
+    c.H = H;
+    c.k = k;
+    c.I = I;
+    c.nl = nl;
+    c.expert_base = (int)a->expert_base;
+    c.x_sh = x;
+    c.x_r = x;
+    c.ids = ids;
+    c.wf = wf;
+    c.w_gate_up = a->w_gate_up;
+    c.w_down = a->w_down;
+    c.w_sh_gate = a->w_shared_gate;
+    c.w_sh_up = a->w_shared_up;
+    c.w_sh_down = a->w_shared_down;
+    c.events = a->timing_events;
+    if ((rc = moe_core(c, w, st))) return rc;
   }
   // 6. combine: out[t] = yw[t] (shared) + sum_j yw[row_of[t, j]] + sum_j pair_rows[pair_index[t, j]]
   {

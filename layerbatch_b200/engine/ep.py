@@ -1,0 +1,131 @@
+"""Expert-parallel MoE over NVLink peer memory: the host side of ``lb_ep_moe_forward``.
+
+``EPExchange`` owns this rank's exchange buffer (allocated by the library with
+``cudaMalloc`` and exported as a CUDA IPC handle), all-gathers the handles over the
+process group and maps every other rank's buffer, so the dispatch and return kernels can
+store token rows straight into the owner's / source's memory over NVLink.  The reference
+has no expert parallelism (every rank holds every expert, nanovllm/models/qwen3_5.py:
+795-800); the result of one call equals ``Qwen3_5SparseMoeBlock.forward`` on this rank's
+tokens (qwen3_5.py:899-905).
+
+Exchange buffers are sized for ``capacity`` tokens per rank and call.  No host
+synchronisation happens per call: routing tables, row counts and the epoch flags that
+order the phases across GPUs all live on the devices.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from .._lib import LB_EP_IPC_HANDLE_BYTES, LB_EP_MAX_RANKS, LbEpArgs, check, lib, ptr, stream_ptr
+
+
+class EPExchange:
+    """This rank's mapping of the exchange buffers of one expert-parallel group."""
+
+    def __init__(self, capacity: int, hidden: int, top_k: int, group=None, device=None,
+                 _local=None):
+        self.capacity, self.hidden, self.top_k = capacity, hidden, top_k
+        self.device = torch.device(device) if device is not None else \
+            torch.device("cuda", torch.cuda.current_device())
+        self._opened, self._owned = [], []
+        self.group = group
+        if _local is not None:            # emulated ranks in one process (tests)
+            self.rank, self.world, self.peers = _local
+            return
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > LB_EP_MAX_RANKS:
+            raise ValueError(f"expert-parallel group of {self.world} > {LB_EP_MAX_RANKS} ranks")
+        L = lib()
+        nbytes = L.lb_ep_buffer_size(self.world, capacity, hidden, top_k)
+        own, handle = _alloc(nbytes)
+        self._owned.append(own)
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+        every = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(every, mine, group=group)
+        self.peers = []
+        for r, h in enumerate(every):
+            if r == self.rank:
+                self.peers.append(own)
+                continue
+            hb = (C.c_uint8 * LB_EP_IPC_HANDLE_BYTES).from_buffer_copy(bytes(h.cpu().tolist()))
+            p = C.c_void_p()
+            check(L.lb_ep_buffer_open(hb, C.byref(p)), "lb_ep_buffer_open")
+            self._opened.append(p.value)
+            self.peers.append(p.value)
+        dist.barrier(group=group)
+
+    @classmethod
+    def emulated(cls, world: int, capacity: int, hidden: int, top_k: int, device=None):
+        """``world`` ranks' exchanges in one process on one device (single-GPU tests):
+        the phases of all ranks are then issued in order on one stream."""
+        nbytes = lib().lb_ep_buffer_size(world, capacity, hidden, top_k)
+        bufs = [_alloc(nbytes)[0] for _ in range(world)]
+        out = [cls(capacity, hidden, top_k, device=device, _local=(r, world, list(bufs)))
+               for r in range(world)]
+        out[0]._owned = bufs
+        return out
+
+    def close(self):
+        """Unmap the peers and free this rank's buffer (all ranks must be done with it)."""
+        torch.cuda.synchronize(self.device)
+        L = lib()
+        for p in self._opened:
+            check(L.lb_ep_buffer_close(p), "lb_ep_buffer_close")
+        for p in self._owned:
+            check(L.lb_ep_buffer_free(p), "lb_ep_buffer_free")
+        self._opened, self._owned = [], []
+
+
+def _alloc(nbytes):
+    h = (C.c_uint8 * LB_EP_IPC_HANDLE_BYTES)()
+    p = C.c_void_p()
+    check(lib().lb_ep_buffer_alloc(nbytes, C.byref(p), h), "lb_ep_buffer_alloc")
+    return p.value, h
+
+
+def ep_args(block, x: torch.Tensor, ex: EPExchange, out: torch.Tensor, phases: int = 0,
+            events=None) -> LbEpArgs:
+    T, H = x.shape
+    a = LbEpArgs()
+    a.num_tokens, a.capacity, a.hidden = T, ex.capacity, H
+    a.num_experts, a.top_k = block.num_experts, block.top_k
+    a.inter = block.experts.down_proj.shape[2]
+    a.rank, a.world = ex.rank, ex.world
+    a.x, a.out = ptr(x), ptr(out)
+    a.w_router = ptr(block.gate.weight)
+    a.w_gate_up = ptr(block.experts.gate_up_proj)
+    a.w_down = ptr(block.experts.down_proj)
+    se = block.shared_expert
+    a.w_shared_gate, a.w_shared_up = ptr(se.gate_proj.weight), ptr(se.up_proj.weight)
+    a.w_shared_down = ptr(se.down_proj.weight)
+    a.w_shared_expert_gate = ptr(block.shared_expert_gate.weight)
+    for r, p in enumerate(ex.peers):
+        a.peer_bufs[r] = p
+    a.phases = phases
+    ops._events(a, events)
+    return a
+
+
+def ep_moe_forward_nvlink(block, x: torch.Tensor, ex: EPExchange, out=None, phases: int = 0,
+                          events=None, ws_tag: str | None = None) -> torch.Tensor:
+    """One expert-parallel MoE block call on this rank's tokens ``x [T, H]`` (T <= the
+    exchange capacity).  ``block`` holds this rank's expert shard
+    (``Qwen3_5SparseMoeBlock(..., ep_rank, ep_size)``)."""
+    x = x.contiguous()
+    if x.shape[0] > ex.capacity:
+        raise ValueError(f"{x.shape[0]} tokens exceed the exchange capacity {ex.capacity}")
+    if out is None:
+        out = torch.empty_like(x)
+    a = ep_args(block, x, ex, out, phases, events)
+    L = lib()
+    n = C.c_size_t(0)
+    check(L.lb_ep_workspace_size(C.byref(a), C.byref(n)), "lb_ep_workspace_size")
+    ws = ops.workspace(n.value, x.device, ws_tag or f"ep{ex.rank}")
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    check(L.lb_ep_moe_forward(C.byref(a), stream_ptr()), "lb_ep_moe_forward")
+    return out

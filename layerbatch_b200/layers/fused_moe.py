@@ -82,8 +82,19 @@ class Qwen3_5SparseMoeBlock(nn.Module):
         self.experts = Qwen3_5Experts(self.local_experts, hidden_size, moe_intermediate_size)
         self.shared_expert = Qwen3_5SharedExpertMLP(hidden_size, shared_expert_intermediate_size)
         self.shared_expert_gate = nn.Linear(hidden_size, 1, bias=False)
+        self.ep_exchange = None
+
+    def attach_exchange(self, exchange) -> None:
+        """Use the NVLink peer-memory exchange (``engine.ep.EPExchange``) for expert
+        parallelism instead of the NCCL all-to-all path."""
+        if exchange.world != self.ep_size or exchange.rank != self.ep_rank:
+            raise ValueError("exchange group does not match ep_rank / ep_size")
+        self.ep_exchange = exchange
 
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        if self.ep_exchange is not None:
+            from ..engine.ep import ep_moe_forward_nvlink
+            return ep_moe_forward_nvlink(self, hidden_states, self.ep_exchange)
         if self.ep_size > 1:
             from ..engine.sharding import ep_moe_forward
             return ep_moe_forward(self, hidden_states)

@@ -1,0 +1,78 @@
+"""Expert-parallel MoE over peer memory (``lb_ep_moe_forward``), emulated on one GPU.
+
+P ranks live in one process: each has its own exchange buffer, expert shard, tokens and
+workspace, and every rank maps every buffer.  The three phases of a call are issued for
+all ranks in order on one stream (all dispatches, then all expert phases, then all
+combines), so each bounded wait finds its flags already set.  Each rank's output must
+match the single-GPU block on its own tokens and the fp32 oracle; two consecutive calls
+exercise the per-call epochs and buffer reuse.  The real multi-GPU run is in
+``test_multigpu.py``.
+"""
+import pytest
+import torch
+
+from layerbatch_b200 import ops
+from layerbatch_b200 import workloads as W
+from layerbatch_b200._lib import LB_EP_PHASE_COMBINE, LB_EP_PHASE_DISPATCH, LB_EP_PHASE_EXPERTS
+from layerbatch_b200.engine.ep import EPExchange, ep_moe_forward_nvlink
+from layerbatch_b200.layers.fused_moe import Qwen3_5SparseMoeBlock
+from oracle import moe as OM
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda")
+
+
+def ep_blocks(pd, P, H, E, k, I, dev):
+    blks = []
+    for r in range(P):
+        b = Qwen3_5SparseMoeBlock(H, E, k, I, I, ep_rank=r, ep_size=P).to(torch.bfloat16).to(dev)
+        with torch.no_grad():
+            b.gate.weight.copy_(pd.router)
+            b.load_expert_shard(pd.gate_up, pd.down)
+            b.shared_expert.gate_proj.weight.copy_(pd.sh_gate)
+            b.shared_expert.up_proj.weight.copy_(pd.sh_up)
+            b.shared_expert.down_proj.weight.copy_(pd.sh_down)
+            b.shared_expert_gate.weight.copy_(pd.sh_gate_w)
+        blks.append(b)
+    return blks
+
+
+@pytest.mark.parametrize("P,E,k,Ts,C", [(4, 64, 8, [200, 64, 0, 150], 256),
+                                        (2, 512, 10, [96, 33], 128)])
+def test_ep_nvlink_emulated_ranks(cuda, P, E, k, Ts, C):
+    H, I = 2048, 512
+    p = W.make_moe_params(H, E, I, I, k, seed=7)
+    pd = p.to(cuda)
+    blks = ep_blocks(pd, P, H, E, k, I, cuda)
+    exs = EPExchange.emulated(P, C, H, k, device=cuda)
+    try:
+        for call in range(2):
+            xs = [W.make_moe_input(T, H, seed=100 * call + r).to(cuda) if T else
+                  torch.empty(0, H, dtype=torch.bfloat16, device=cuda) for r, T in enumerate(Ts)]
+            outs = [torch.empty_like(x) for x in xs]
+            for ph in (LB_EP_PHASE_DISPATCH, LB_EP_PHASE_EXPERTS, LB_EP_PHASE_COMBINE):
+                for r in range(P):
+                    ep_moe_forward_nvlink(blks[r], xs[r], exs[r], out=outs[r], phases=ph,
+                                          ws_tag=f"ep_emu{r}")
+            torch.cuda.synchronize()
+            for r in range(P):
+                assert ops.device_status(ops._WS[(torch.cuda.current_device(), f"ep_emu{r}")]) == 0
+                if Ts[r] == 0:
+                    continue
+                ref, logits, ids, _ = ops.moe_forward(
+                    xs[r], pd.router, pd.gate_up, pd.down, pd.sh_gate, pd.sh_up, pd.sh_down,
+                    pd.sh_gate_w, k, return_routing=True, ws_tag="ep_ref")
+                _, wf, _ = ops.router_topk(logits, k)
+                torch.cuda.synchronize()
+                y32 = OM.moe_block_fp32(xs[r].cpu(), p, ids.cpu().long(), wf.cpu())
+                assert OM.rel_err(outs[r].cpu(), y32) <= TOL, (call, r)
+                assert OM.rel_err(outs[r].cpu(), ref.cpu()) <= TOL, (call, r)
+    finally:
+        exs[0].close()

@@ -1,9 +1,10 @@
-"""Tensor / expert parallel on 2 GPUs with NCCL (skipped with fewer than 2 GPUs).
+"""Tensor / expert parallel on 2 GPUs (skipped with fewer than 2 GPUs).
 
 Each rank compares the sharded result with the single-GPU library call on the same
-inputs: attention TP by KV head with the fp32 o_proj all-reduce, and the MoE block with
-experts split over the ranks and the all-to-all exchange.  NVLS is off (plain NCCL
-transport) and the process group has a short timeout.
+inputs: attention TP by KV head with the fp32 o_proj all-reduce, the MoE block with
+experts split over the ranks and the NCCL all-to-all exchange, and the MoE block with the
+NVLink peer-memory exchange (``lb_ep_moe_forward``).  NVLS is off (plain NCCL transport,
+no multicast objects) and the process group has a short timeout.
 """
 import datetime
 import os
@@ -74,6 +75,77 @@ def _worker(rank, world, port, q):
         q.put((rank, "ok", errs))
     except Exception as e:
         q.put((rank, "fail", repr(e)))
+
+
+def _nvlink_worker(rank, world, port, q):
+    try:
+        import sys
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        import torch.distributed as dist
+        from layerbatch_b200 import ops
+        from layerbatch_b200 import workloads as W
+        from layerbatch_b200.engine.ep import EPExchange, ep_moe_forward_nvlink
+        from layerbatch_b200.layers.fused_moe import Qwen3_5SparseMoeBlock
+        from oracle import moe as OM
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        H, E, I, k, C = 2048, 512, 512, 10, 512
+        p = W.make_moe_params(H, E, I, I, k, seed=0).to(dev)
+        blk = Qwen3_5SparseMoeBlock(H, E, k, I, I, ep_rank=rank, ep_size=world).to(torch.bfloat16).to(dev)
+        with torch.no_grad():
+            blk.gate.weight.copy_(p.router)
+            blk.load_expert_shard(p.gate_up, p.down)
+            blk.shared_expert.gate_proj.weight.copy_(p.sh_gate)
+            blk.shared_expert.up_proj.weight.copy_(p.sh_up)
+            blk.shared_expert.down_proj.weight.copy_(p.sh_down)
+            blk.shared_expert_gate.weight.copy_(p.sh_gate_w)
+        ex = EPExchange(C, H, k, device=dev)
+        errs = {}
+        for call, T in enumerate([384 + 64 * rank, 200 - 150 * rank, 512]):
+            x = W.make_moe_input(T, H, seed=50 + 10 * call + rank).to(dev)
+            y = ep_moe_forward_nvlink(blk, x, ex)
+            y1 = ops.moe_forward(x, p.router, p.gate_up, p.down, p.sh_gate, p.sh_up, p.sh_down,
+                                 p.sh_gate_w, k, ws_tag="moe_full")
+            torch.cuda.synchronize()
+            errs[f"call{call}"] = OM.rel_err(y.float(), y1.float())
+        errs["status"] = ops.device_status(ops._WS[(rank, f"ep{rank}")])
+        dist.barrier()
+        ex.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok", errs))
+    except Exception as e:
+        q.put((rank, "fail", repr(e)))
+
+
+def _run2(fn):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=fn, args=(r, 2, port, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    res = sorted(q.get(timeout=300) for _ in range(2))
+    for pr in procs:
+        pr.join(timeout=60)
+        if pr.is_alive():
+            pr.kill()
+    return res
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_ep_moe_nvlink_exchange_on_two_gpus():
+    res = _run2(_nvlink_worker)
+    assert all(r[1] == "ok" for r in res), res
+    for _, _, errs in res:
+        assert errs.pop("status") == 0, errs
+        assert all(v <= 2e-2 for v in errs.values()), errs
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
