@@ -211,6 +211,47 @@ int lb_store_kvcache(const void* k, int64_t k_stride, const void* v, int64_t v_s
                      void* k_cache, void* v_cache, const int32_t* slot_mapping, int64_t N,
                      int64_t num_slots, int64_t row_elems, void* stream);
 
+/* ---------------------------------------------------------------- attention prologue
+ * The full-attention prologue after the projections (nanovllm/models/qwen3_5.py:707-736)
+ * fused with store_kvcache (nanovllm/layers/attention.py:50-80), one launch, for every
+ * token n, query head h and KV head g:
+ *   q_out[n,h]  = RoPE(RMSNorm_1pw(q_in[n,h], q_norm_w))
+ *   k_cache[s]  = RoPE(RMSNorm_1pw(k_in[n,g], k_norm_w))   s = slot_mapping[n] (-1: skip)
+ *   v_cache[s]  = v_in[n,g]
+ * RMSNorm_1pw(x, w) = bf16(fp32 x * rsqrt(mean(x^2) + eps) * (1 + w)) (qwen3_5.py:48-55);
+ * RoPE rotates the first rotary_dim dims as two halves with the caller's fp32 cache rows
+ * [cos | sin] at positions[n] (rotary_embedding.py:5-54) and rounds to bf16.  q_in may be
+ * the query half of q_proj's [N, Hq, 2D] output (q_in_stride_head = 2D), which leaves
+ * the gate half in place for lb_pod_attn_oproj. */
+typedef struct LbPrologueArgs {
+  int64_t num_tokens;          /* N */
+  int64_t num_q_heads;         /* Hq */
+  int64_t num_kv_heads;        /* Hkv */
+  int64_t head_dim;            /* D (256) */
+  int64_t rotary_dim;          /* rotated dims (multiple of 16, <= D) */
+  float eps;
+  const void* q_in;            /* bf16, element (n, h, d) at n*q_in_stride_tok + h*q_in_stride_head + d */
+  int64_t q_in_stride_tok, q_in_stride_head;
+  const void* k_in;            /* [N, Hkv*D] bf16 rows, token stride k_in_stride_tok */
+  int64_t k_in_stride_tok;
+  const void* v_in;            /* [N, Hkv*D] bf16 */
+  int64_t v_in_stride_tok;
+  const void* q_norm_w;        /* [D] bf16  self_attn.q_norm.weight */
+  const void* k_norm_w;        /* [D] bf16  self_attn.k_norm.weight */
+  const float* cos_sin_cache;  /* [max_position, rotary_dim] fp32 (rotary_emb.cos_sin_cache) */
+  int64_t max_position;
+  const int64_t* positions;    /* [N] */
+  const int32_t* slot_mapping; /* [N] */
+  void* k_cache;               /* [num_slots, Hkv*D] bf16 (paged cache viewed as rows) */
+  void* v_cache;
+  int64_t num_slots;
+  void* q_out;                 /* bf16 [N, Hq, D] with the strides below */
+  int64_t q_out_stride_tok, q_out_stride_head;
+  int* status;                 /* optional device status word (LB_DEV_BAD_INDEX) */
+} LbPrologueArgs;
+
+int lb_attn_prologue(const LbPrologueArgs* args, void* stream);
+
 /* ---------------------------------------------------------------- POD attention + o_proj
  * One batch of sequences, prefill chunks and decode steps mixed in any order.
  * Sequence b owns query rows [cu_seqlens_q[b], cu_seqlens_q[b+1]) which are its last

@@ -25,7 +25,7 @@ EXPORTS = [
     "lb_moe_workspace_size",
     "lb_moe_forward", "lb_ep_buffer_size", "lb_ep_buffer_alloc", "lb_ep_buffer_open",
     "lb_ep_buffer_close", "lb_ep_buffer_free", "lb_ep_workspace_size", "lb_ep_moe_forward",
-    "lb_store_kvcache", "lb_pod_workspace_size", "lb_pod_attn_oproj",
+    "lb_store_kvcache", "lb_attn_prologue", "lb_pod_workspace_size", "lb_pod_attn_oproj",
 ]
 
 LB_EP_MAX_RANKS = 8
@@ -61,6 +61,19 @@ class LbEpArgs(C.Structure):
         ("w_shared_expert_gate", vp), ("out", vp), ("peer_bufs", vp * LB_EP_MAX_RANKS),
         ("workspace", vp), ("workspace_bytes", C.c_size_t), ("phases", i32),
         ("timing_events", vp * 4),
+    ]
+
+
+class LbPrologueArgs(C.Structure):
+    _fields_ = [
+        ("num_tokens", i64), ("num_q_heads", i64), ("num_kv_heads", i64), ("head_dim", i64),
+        ("rotary_dim", i64), ("eps", C.c_float),
+        ("q_in", vp), ("q_in_stride_tok", i64), ("q_in_stride_head", i64),
+        ("k_in", vp), ("k_in_stride_tok", i64), ("v_in", vp), ("v_in_stride_tok", i64),
+        ("q_norm_w", vp), ("k_norm_w", vp), ("cos_sin_cache", vp), ("max_position", i64),
+        ("positions", vp), ("slot_mapping", vp), ("k_cache", vp), ("v_cache", vp),
+        ("num_slots", i64), ("q_out", vp), ("q_out_stride_tok", i64),
+        ("q_out_stride_head", i64), ("status", vp),
     ]
 
 
@@ -108,6 +121,7 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.lb_ep_buffer_free.argtypes = [vp]
     L.lb_ep_workspace_size.argtypes = [C.POINTER(LbEpArgs), C.POINTER(C.c_size_t)]
     L.lb_ep_moe_forward.argtypes = [C.POINTER(LbEpArgs), vp]
+    L.lb_attn_prologue.argtypes = [C.POINTER(LbPrologueArgs), vp]
     L.lb_store_kvcache.argtypes = [vp, i64, vp, i64, vp, vp, vp, i64, i64, i64, vp]
     L.lb_pod_workspace_size.argtypes = [C.POINTER(LbPodArgs), C.POINTER(C.c_size_t)]
     L.lb_pod_attn_oproj.argtypes = [C.POINTER(LbPodArgs), vp]

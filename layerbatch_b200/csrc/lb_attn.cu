@@ -31,6 +31,87 @@ __global__ void k_store_kvcache(const __nv_bfloat16* __restrict__ k, long long k
 }
 
 
+// ------------------------------------------------------------------------------ prologue
+// One warp per (token, head): heads [0, Hq) are query heads, [Hq, Hq + Hkv) KV heads.
+// A lane holds 8 consecutive dims (D = 256).  The RMSNorm and RoPE follow the reference's
+// fp32 operation order with explicit rounding (no contraction), so the bf16 results match
+// it up to the order of the sum of squares.
+__global__ void __launch_bounds__(256) k_attn_prologue(const LbPrologueArgs a) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  const int Hq = (int)a.num_q_heads, Hkv = (int)a.num_kv_heads;
+  const int nh = Hq + Hkv;
+  if (warp >= a.num_tokens * nh) return;
+  const long long n = warp / nh;
+  const int h = warp - (int)(n * nh);
+  const bool is_q = h < Hq;
+  const int g = h - Hq;
+  constexpr int D = POD_D;
+  const long long slot = is_q ? 0 : (long long)a.slot_mapping[n];
+  if (!is_q && slot >= a.num_slots) {
+    if (a.status) report(a.status, LB_DEV_BAD_INDEX);
+    return;
+  }
+  if (!is_q && slot < 0) return;   // padding token: nothing to store
+  const __nv_bfloat16* src = is_q
+      ? static_cast<const __nv_bfloat16*>(a.q_in) + n * a.q_in_stride_tok + (long long)h * a.q_in_stride_head
+      : static_cast<const __nv_bfloat16*>(a.k_in) + n * a.k_in_stride_tok + (long long)g * D;
+  const uint4 raw = reinterpret_cast<const uint4*>(src)[lane];
+  float x[8] = {bf16_lo(raw.x), bf16_hi(raw.x), bf16_lo(raw.y), bf16_hi(raw.y),
+                bf16_lo(raw.z), bf16_hi(raw.z), bf16_lo(raw.w), bf16_hi(raw.w)};
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+  const float rstd = 1.0f / sqrtf(__fadd_rn(ss / (float)D, a.eps));
+  const uint4 wr = reinterpret_cast<const uint4*>(is_q ? a.q_norm_w : a.k_norm_w)[lane];
+  const float w[8] = {bf16_lo(wr.x), bf16_hi(wr.x), bf16_lo(wr.y), bf16_hi(wr.y),
+                      bf16_lo(wr.z), bf16_hi(wr.z), bf16_lo(wr.w), bf16_hi(wr.w)};
+  float y[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    y[i] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[i], rstd), __fadd_rn(1.0f, w[i]))));
+  // partial RoPE: dims [0, rot/2) pair with [rot/2, rot); lanes < rot/16 hold the first
+  // half, the next rot/16 lanes the second
+  const int rot = (int)a.rotary_dim;
+  const int hl = rot / 16;
+  const bool first = lane < hl, second = lane >= hl && lane < 2 * hl;
+  const int partner = first ? lane + hl : (second ? lane - hl : lane);
+  float pv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) pv[i] = __shfl_sync(0xffffffffu, y[i], partner);
+  if (first || second) {
+    long long pos = a.positions[n];
+    if (pos < 0 || pos >= a.max_position) {
+      if (a.status) report(a.status, LB_DEV_BAD_INDEX);
+      pos = pos < 0 ? 0 : a.max_position - 1;
+    }
+    const float* cs = a.cos_sin_cache + pos * rot;
+    const int f0 = (first ? lane : lane - hl) * 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float c = cs[f0 + i], sn = cs[rot / 2 + f0 + i];
+      const float r = first ? __fsub_rn(__fmul_rn(y[i], c), __fmul_rn(pv[i], sn))   // x1 c - x2 s
+                            : __fadd_rn(__fmul_rn(y[i], c), __fmul_rn(pv[i], sn));  // x2 c + x1 s
+      y[i] = __bfloat162float(__float2bfloat16_rn(r));
+    }
+  }
+  const uint4 outv = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
+                                pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+  if (is_q) {
+    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.q_out) + n * a.q_out_stride_tok +
+                         (long long)h * a.q_out_stride_head;
+    reinterpret_cast<uint4*>(dst)[lane] = outv;
+  } else {
+    const long long row = slot * (long long)Hkv * D + (long long)g * D;
+    reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.k_cache) + row)[lane] = outv;
+    const __nv_bfloat16* vs = static_cast<const __nv_bfloat16*>(a.v_in) + n * a.v_in_stride_tok + (long long)g * D;
+    reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.v_cache) + row)[lane] =
+        reinterpret_cast<const uint4*>(vs)[lane];
+  }
+}
+
 // ------------------------------------------------------------------------------ plan
 // One block.  Phase 1: per-sequence item counts and block-wide exclusive scans give every
 // sequence its first item slots (kept in shared memory).  Phase 2: one warp per sequence
@@ -455,6 +536,35 @@ int lb_store_kvcache(const void* k, int64_t k_stride, const void* v, int64_t v_s
       v_stride, static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),
       slot_mapping, (int)N, num_slots, (int)row_elems);
   { int _rc = launched("k_store_kvcache"); if (_rc) return _rc; }
+  return LB_OK;
+}
+
+int lb_attn_prologue(const LbPrologueArgs* a, void* stream) {
+  LB_REQUIRE(a != nullptr, "lb_attn_prologue: null args");
+  LB_REQUIRE(a->head_dim == POD_D, "lb_attn_prologue: head_dim must be 256");
+  LB_REQUIRE(a->num_tokens >= 0 && a->num_q_heads > 0 && a->num_kv_heads > 0 &&
+                 a->num_tokens * (a->num_q_heads + a->num_kv_heads) < (1ll << 31),
+             "lb_attn_prologue: bad sizes");
+  LB_REQUIRE(a->rotary_dim >= 0 && a->rotary_dim <= a->head_dim && a->rotary_dim % 16 == 0,
+             "lb_attn_prologue: rotary_dim must be a multiple of 16 and <= head_dim");
+  LB_REQUIRE(a->q_in && a->k_in && a->v_in && a->q_norm_w && a->k_norm_w && a->positions &&
+                 a->slot_mapping && a->k_cache && a->v_cache && a->q_out &&
+                 (a->rotary_dim == 0 || a->cos_sin_cache),
+             "lb_attn_prologue: null pointer");
+  LB_REQUIRE(a->max_position > 0 && a->num_slots >= 0, "lb_attn_prologue: bad cache sizes");
+  LB_REQUIRE(aligned16(a->q_in) && aligned16(a->k_in) && aligned16(a->v_in) &&
+                 aligned16(a->q_norm_w) && aligned16(a->k_norm_w) && aligned16(a->k_cache) &&
+                 aligned16(a->v_cache) && aligned16(a->q_out),
+             "lb_attn_prologue: tensors must be 16-byte aligned");
+  LB_REQUIRE(a->q_in_stride_tok % 8 == 0 && a->q_in_stride_head % 8 == 0 &&
+                 a->k_in_stride_tok % 8 == 0 && a->v_in_stride_tok % 8 == 0 &&
+                 a->q_out_stride_tok % 8 == 0 && a->q_out_stride_head % 8 == 0,
+             "lb_attn_prologue: strides must be multiples of 8 elements");
+  if (a->num_tokens == 0) return LB_OK;
+  const long long warps = a->num_tokens * (a->num_q_heads + a->num_kv_heads);
+  const long long blocks = (warps * 32 + 255) / 256;
+  k_attn_prologue<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(*a);
+  { int _rc = launched("k_attn_prologue"); if (_rc) return _rc; }
   return LB_OK;
 }
 

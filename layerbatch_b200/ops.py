@@ -10,7 +10,7 @@ import ctypes as C
 
 import torch
 
-from ._lib import LbMoeArgs, LbPodArgs, check, lib, ptr, stream_ptr
+from ._lib import LbMoeArgs, LbPodArgs, LbPrologueArgs, check, lib, ptr, stream_ptr
 
 _WS: dict = {}
 
@@ -173,6 +173,45 @@ def store_kvcache(k, v, k_cache, v_cache, slot_mapping):
     check(lib().lb_store_kvcache(k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
                                  k_cache.data_ptr(), v_cache.data_ptr(), sm.data_ptr(), N, slots,
                                  row, stream_ptr()), "lb_store_kvcache")
+
+
+def attn_prologue(q_in, k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions, slot_mapping,
+                  k_cache, v_cache, eps, q_out=None, status=None):
+    """Fused (1+w) RMSNorm + partial RoPE of query and key, and the K/V cache store
+    (reference qwen3_5.py:730-736 and attention.py:50-80).
+
+    ``q_in [N, Hq, D]`` may be a strided view (the query half of q_proj's output);
+    ``k_in``/``v_in`` are ``[N, Hkv, D]`` with packed heads; ``cos_sin_cache`` is the
+    rotary module's fp32 ``[max_position, (1,) rotary_dim]`` buffer.  Returns ``q_out``
+    ``[N, Hq, D]`` (allocated when not given).
+    """
+    N, Hq, D = q_in.shape
+    Hkv = k_in.shape[1]
+    for t, name in ((k_in, "k_in"), (v_in, "v_in")):
+        if t.stride(-1) != 1 or t.stride(-2) != D:
+            raise ValueError(f"{name} must be [N, Hkv, D] with packed heads")
+    if q_in.stride(-1) != 1:
+        raise ValueError("q_in must have a contiguous last dim")
+    if q_out is None:
+        q_out = torch.empty(N, Hq, D, dtype=q_in.dtype, device=q_in.device)
+    cs = cos_sin_cache.reshape(cos_sin_cache.shape[0], -1)
+    if cs.dtype != torch.float32 or not cs.is_contiguous():
+        raise ValueError("cos_sin_cache must be a contiguous fp32 [max_position, rotary_dim]")
+    pos = positions.to(torch.int64)
+    sm = slot_mapping.to(torch.int32)
+    row = k_cache.shape[-2] * k_cache.shape[-1]
+    a = LbPrologueArgs(
+        num_tokens=N, num_q_heads=Hq, num_kv_heads=Hkv, head_dim=D, rotary_dim=cs.shape[1],
+        eps=float(eps), q_in=q_in.data_ptr(), q_in_stride_tok=q_in.stride(0),
+        q_in_stride_head=q_in.stride(1), k_in=k_in.data_ptr(), k_in_stride_tok=k_in.stride(0),
+        v_in=v_in.data_ptr(), v_in_stride_tok=v_in.stride(0), q_norm_w=q_norm_w.data_ptr(),
+        k_norm_w=k_norm_w.data_ptr(), cos_sin_cache=cs.data_ptr(), max_position=cs.shape[0],
+        positions=pos.data_ptr(), slot_mapping=sm.data_ptr(), k_cache=k_cache.data_ptr(),
+        v_cache=v_cache.data_ptr(), num_slots=k_cache.numel() // row, q_out=q_out.data_ptr(),
+        q_out_stride_tok=q_out.stride(0), q_out_stride_head=q_out.stride(1),
+        status=ptr(status))
+    check(lib().lb_attn_prologue(C.byref(a), stream_ptr()), "lb_attn_prologue")
+    return q_out
 
 
 def pod_args(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o, scale,

@@ -15,7 +15,11 @@ TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``).  Restates:
   (no prefix) both agree, and the golden vectors pin that case;
 * the split-KV online softmax with LSE merge of the POD kernel
   (nanovllm/layers/pod_kernels.py:102-159 and 205-231), in fp32;
-* ``o * sigmoid(gate)`` then o_proj (nanovllm/models/qwen3_5.py:742-746).
+* ``o * sigmoid(gate)`` then o_proj (nanovllm/models/qwen3_5.py:742-746);
+* the full-attention prologue (qwen3_5.py:707-736): the per-head (query, gate) split of the
+  q_proj output, the (1 + w) RMSNorm of query and key (qwen3_5.py:39-55) and the partial
+  rotary embedding of their first ``rotary_dim`` dims with the fp32 cos/sin cache
+  (nanovllm/layers/rotary_embedding.py:5-54).
 """
 from __future__ import annotations
 
@@ -190,3 +194,51 @@ def attn_oproj_fp32(batch):
 def default_scale(head_dim):
     """qwen3_5.py:638: ``head_dim ** -0.5``."""
     return head_dim ** -0.5 if head_dim else math.nan
+
+
+# ------------------------------------------------------------------------------ prologue
+def rmsnorm_1pw(x, w, eps):
+    """qwen3_5.py:48-55: fp32 ``x * rsqrt(mean(x^2) + eps) * (1 + w)``, back to x's dtype."""
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (y * (1.0 + w.float())).to(x.dtype)
+
+
+def rope_cos_sin_cache(rotary_dim, max_position, base):
+    """rotary_embedding.py:26-33: ``[max_position, 1, rotary_dim]`` fp32, cos then sin."""
+    inv_freq = 1.0 / (base ** (torch.arange(0, rotary_dim, 2, dtype=torch.float) / rotary_dim))
+    t = torch.arange(max_position, dtype=torch.float)
+    freqs = torch.einsum("i,j -> ij", t, inv_freq)
+    return torch.cat((freqs.cos(), freqs.sin()), dim=-1).unsqueeze_(1)
+
+
+def _rotate(x, cos, sin):
+    """rotary_embedding.py:6-14 (halves of the rotated dims, fp32, back to x's dtype)."""
+    x1, x2 = torch.chunk(x.float(), 2, dim=-1)
+    return torch.cat((x1 * cos - x2 * sin, x2 * cos + x1 * sin), dim=-1).to(x.dtype)
+
+
+def partial_rope(positions, query, key, cos_sin_cache):
+    """rotary_embedding.py:36-54: rotate the first ``rotary_dim`` dims of every head."""
+    rot = cos_sin_cache.shape[-1]
+    cos, sin = cos_sin_cache[positions.long()].chunk(2, dim=-1)
+    out = []
+    for x in (query, key):
+        out.append(torch.cat([_rotate(x[..., :rot], cos, sin), x[..., rot:]], dim=-1))
+    return out[0], out[1]
+
+
+def attn_prologue(q_out, k_raw, v_raw, q_norm_w, k_norm_w, cos_sin_cache, positions, eps,
+                  num_heads, head_dim):
+    """qwen3_5.py:707-736 after the projections: ``q_out [N, Hq*2D]`` -> (query [N,Hq,D]
+    normed + rotated, gate [N, Hq*D], key [N,Hkv,D] normed + rotated, value [N,Hkv,D])."""
+    N = q_out.shape[0]
+    q3 = q_out.view(N, num_heads, 2 * head_dim)
+    query, gate = q3.chunk(2, dim=-1)
+    gate = gate.reshape(N, num_heads * head_dim)
+    k = k_raw.view(N, -1, head_dim)
+    v = v_raw.view(N, -1, head_dim)
+    query = rmsnorm_1pw(query, q_norm_w, eps)
+    k = rmsnorm_1pw(k, k_norm_w, eps)
+    query, k = partial_rope(positions, query, k, cos_sin_cache)
+    return query, gate, k, v

@@ -12,7 +12,11 @@ Reference entry points exercised:
 * ``Qwen3_5TopKRouter.forward`` (qwen3_5.py:767-774);
 * ``sdpa_decode_paged`` and ``sdpa_prefill_varlen`` (nanovllm/layers/sdpa_fallback.py);
 * the output gate and o_proj of ``Qwen3_5FullAttention.forward`` (qwen3_5.py:742-746)
-  through the reference's ``RowParallelLinear`` (nanovllm/layers/linear.py:138-159).
+  through the reference's ``RowParallelLinear`` (nanovllm/layers/linear.py:138-159);
+* the attention prologue of ``Qwen3_5FullAttention.forward`` (qwen3_5.py:707-736): the
+  (query, gate) split, ``Qwen3_5RMSNorm`` on query and key (qwen3_5.py:39-55) and
+  ``RotaryEmbedding`` (partial, theta 1e7, nanovllm/layers/rotary_embedding.py:17-54),
+  called uncompiled through ``RotaryEmbedding.forward.__wrapped__``.
 
 Usage: ``python tests/golden/make_golden.py --ref <reference checkout>``
 """
@@ -73,14 +77,70 @@ def tie_inputs():
     return x, w, k
 
 
+PROLOGUE_CASES = {
+    # name: (N, Hq, Hkv, D, rotary_dim, max_position, theta, positions seed)
+    "prologue_small": (7, 16, 2, 256, 64, 40000, 1.0e7, 11),
+}
+
+
+def prologue_inputs(N, Hq, Hkv, D, max_pos, seed):
+    g = torch.Generator().manual_seed(seed)
+    q_out = torch.randn(N, Hq * 2 * D, generator=g).to(torch.bfloat16)
+    k_raw = (3.0 * torch.randn(N, Hkv * D, generator=g)).to(torch.bfloat16)
+    v_raw = torch.randn(N, Hkv * D, generator=g).to(torch.bfloat16)
+    q_w = (0.1 * torch.randn(D, generator=g)).to(torch.bfloat16)
+    k_w = (0.1 * torch.randn(D, generator=g)).to(torch.bfloat16)
+    pos = torch.randint(0, max_pos, (N,), generator=g, dtype=torch.long)
+    pos[0], pos[1] = 0, max_pos - 1
+    return q_out, k_raw, v_raw, q_w, k_w, pos
+
+
+def prologue_goldens(out):
+    from nanovllm.models.qwen3_5 import Qwen3_5RMSNorm
+    from nanovllm.layers.rotary_embedding import RotaryEmbedding
+    for name, (N, Hq, Hkv, D, rot, max_pos, theta, seed) in PROLOGUE_CASES.items():
+        q_out, k_raw, v_raw, q_w, k_w, pos = prologue_inputs(N, Hq, Hkv, D, max_pos, seed)
+        qn = Qwen3_5RMSNorm(D, eps=1e-6).to(torch.bfloat16)
+        kn = Qwen3_5RMSNorm(D, eps=1e-6).to(torch.bfloat16)
+        rope = RotaryEmbedding(D, rot, max_pos, theta)
+        with torch.no_grad():
+            qn.weight.copy_(q_w)
+            kn.weight.copy_(k_w)
+            query, gate = q_out.view(N, Hq, 2 * D).chunk(2, dim=-1)
+            gate = gate.reshape(N, Hq * D)
+            k = k_raw.view(N, Hkv, D)
+            query = qn(query)
+            k = kn(k)
+            query, k = RotaryEmbedding.forward.__wrapped__(rope, pos, query, k)
+        out[name] = dict(shape=(N, Hq, Hkv, D, rot, max_pos, theta, seed), query=query,
+                         gate=gate, key=k, cos_sin_rows=rope.cos_sin_cache[pos].clone(),
+                         in_sha=sha(q_out, k_raw, v_raw, q_w, k_w, pos))
+        print(name, "done")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("LB_REFERENCE_PATH", ""))
     ap.add_argument("--out", default=HERE)
+    ap.add_argument("--only", default="", help="regenerate only these cases "
+                    "(comma list of prefixes; others are kept from the existing file)")
     args = ap.parse_args()
     if not args.ref or not os.path.isdir(args.ref):
         sys.exit("pass --ref <path to the reference project>")
     sys.path.insert(0, args.ref)
+    if args.only:
+        path = os.path.join(args.out, "golden.pt")
+        out = torch.load(path, weights_only=False)
+        if "prologue" in args.only:
+            prologue_goldens(out)
+        for rec in out.values():
+            if isinstance(rec, dict):
+                for key, val in rec.items():
+                    if torch.is_tensor(val):
+                        rec[key] = val.detach().clone().contiguous()
+        torch.save(out, path)
+        print("updated", path, os.path.getsize(path), "bytes")
+        return
     import torch.distributed as dist
     from nanovllm.models.qwen3_5 import Qwen3_5SparseMoeBlock, Qwen3_5TopKRouter
     from nanovllm.layers.sdpa_fallback import sdpa_decode_paged, sdpa_prefill_varlen
@@ -155,6 +215,8 @@ def main():
         out[name] = dict(prefill=pf, attn=o,
                          in_sha=sha(b.q, b.gate, b.k_cache, b.v_cache, b.block_tables, b.w_o))
         print(name, "done")
+
+    prologue_goldens(out)
 
     dist.destroy_process_group()
     for rec in out.values():

@@ -9,7 +9,8 @@ import torch
 from layerbatch_b200 import workloads as W
 from oracle import attention as OA
 from oracle import moe as OM
-from tests.golden.make_golden import MOE_CASES, DECODE_CASES, PREFILL_CASES, moe_inputs, sha, tie_inputs
+from tests.golden.make_golden import (MOE_CASES, DECODE_CASES, PREFILL_CASES, PROLOGUE_CASES,
+                                     moe_inputs, prologue_inputs, sha, tie_inputs)
 
 
 def assert_bf16_match(a, b, min_exact=0.99, rel=1e-2):
@@ -136,3 +137,18 @@ def test_prefix_prefill_is_bottom_right_causal():
     first = OA.paged_attention(b.q[:1], b.k_cache, b.v_cache, b.block_tables, first_ctx,
                                torch.tensor([0, 1], dtype=torch.int32), b.scale)
     assert torch.allclose(o[0], first[0], atol=1e-5)
+
+
+@pytest.mark.parametrize("name", list(PROLOGUE_CASES))
+def test_prologue_oracle_matches_reference(golden, name):
+    """(query, gate) split, (1+w) RMSNorm and partial RoPE of the full-attention prologue."""
+    g = golden[name]
+    N, Hq, Hkv, D, rot, max_pos, theta, seed = PROLOGUE_CASES[name]
+    q_out, k_raw, v_raw, q_w, k_w, pos = prologue_inputs(N, Hq, Hkv, D, max_pos, seed)
+    assert sha(q_out, k_raw, v_raw, q_w, k_w, pos) == g["in_sha"]
+    cache = OA.rope_cos_sin_cache(rot, max_pos, theta)
+    assert torch.equal(cache[pos], g["cos_sin_rows"])
+    query, gate, k, _ = OA.attn_prologue(q_out, k_raw, v_raw, q_w, k_w, cache, pos, 1e-6, Hq, D)
+    assert torch.equal(gate, g["gate"])
+    assert_bf16_match(query, g["query"], min_exact=0.999, rel=1e-2)
+    assert_bf16_match(k, g["key"], min_exact=0.999, rel=1e-2)
