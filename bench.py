@@ -13,9 +13,11 @@ flush is needed between steps.
     python bench.py --impl reference ...   # the reference's CPU path (restated) only
 
 Under torchrun (``--gpus N``, N even) the c4 step is sharded: ranks form tensor-parallel
-pairs that split the attention by KV head (fp32 o_proj partials all-reduced over NCCL),
-the pairs run different batches (data parallel), and the 512 experts are split over all N
-ranks with NCCL all-to-all dispatch and return.  Each GPU keeps one c4 batch of work, so
+pairs that split the attention by KV head (the o_proj GEMM stores its fp32 partial tiles
+into the owning rank's memory over NVLink and the owners reduce and send back the bf16
+rows), the pairs run different batches (data parallel), and the 512 experts are split
+over all N ranks with the NVLink peer-memory dispatch and return of lb_ep_moe_forward.
+No NCCL collective is on the data path.  Each GPU keeps one c4 batch of work, so
 scaling is weak.  Rank 0 prints one JSON line; the time is the max over ranks of
 CUDA-event time.
 
@@ -279,6 +281,10 @@ def run_ours(args, rank, world, device):
             torch.cuda.empty_cache()
             from layerbatch_b200.engine.ep import EPExchange
             ep_block.attach_exchange(EPExchange(T_moe, 2048, 10, device=device))
+    tp_ex = None
+    if sharded and tp > 1:
+        from layerbatch_b200.engine.peer import TPExchange
+        tp_ex = TPExchange(attn.num_tokens, 2048, group=tp_group, device=device)
     tokens = (attn.num_tokens // tp) if attn is not None else T_moe
     max_q = max(attn.qlen_list) if attn is not None else 0
     hint = ops.pod_work_hint(attn.ctx_list, attn.qlen_list) if attn is not None else None
@@ -298,7 +304,7 @@ def run_ours(args, rank, world, device):
             if sharded:
                 S.tp_attention_oproj(shard, qq, gg, attn.k_cache, attn.v_cache, bt, cl, cu,
                                      attn.w_o, attn.scale, group=tp_group, max_q_len=max_q,
-                                     events=ev_a, out=oa, work_hint=hint)
+                                     events=ev_a, out=oa, work_hint=hint, exchange=tp_ex)
             else:
                 ops.pod_attn_oproj(qq, gg, attn.k_cache, attn.v_cache, bt, cl, cu, attn.w_o,
                                    attn.scale, out=oa, max_q_len=max_q, events=ev_a,
@@ -359,8 +365,9 @@ def run_ours(args, rank, world, device):
         t_g1 = statistics.mean(e[0].elapsed_time(e[1]) for e in ev_moe) * 1e-3
         t_g2 = statistics.mean(e[2].elapsed_time(e[3]) for e in ev_moe) * 1e-3
         res["moe_gemm"] = {"gate_up_ms": t_g1 * 1e3, "down_ms": t_g2 * 1e3}
-    res["parallelism"] = (f"tp{tp} x dp{world // tp} attention (KV-head shards, fp32 o_proj "
-                          f"all-reduce), ep{world} MoE (NVLink peer-memory dispatch/return)"
+    res["parallelism"] = (f"tp{tp} x dp{world // tp} attention (KV-head shards, o_proj GEMM "
+                          f"reducing over NVLink peer memory), ep{world} MoE (NVLink "
+                          f"peer-memory dispatch/return)"
                           if sharded else
                           ("single GPU" if world == 1 else
                            f"dp{world}: per-rank batches, experts replicated"))

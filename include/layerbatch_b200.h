@@ -159,7 +159,9 @@ int lb_moe_forward(const LbMoeArgs* args, void* stream);
 #define LB_EP_IPC_HANDLE_BYTES 64
 
 /* Bytes of one rank's exchange buffer for `world` ranks, up to `capacity` tokens per rank
- * and call, rows of `hidden` bf16 and `top_k` routed experts. */
+ * and call, rows of `hidden` bf16 and `top_k` routed experts.  The buffer calls
+ * (alloc / open / close / free) are generic: the tensor-parallel o_proj buffers of
+ * lb_pod_attn_oproj use them too. */
 size_t lb_ep_buffer_size(int64_t world, int64_t capacity, int64_t hidden, int64_t top_k);
 /* cudaMalloc + zero a buffer on the current device and export its CUDA IPC handle
  * (LB_EP_IPC_HANDLE_BYTES bytes written to ipc_handle). */
@@ -294,7 +296,27 @@ typedef struct LbPodArgs {
    * of the decode sequences; they set how many SMs start on prefill tiles */
   int64_t prefill_pairs_hint;
   int64_t decode_tokens_hint;
+  /* ---- tensor parallel o_proj (optional; tp_size <= 1 = off).  This rank holds a slice
+   * of the heads and W_o's matching columns; the o_proj GEMM stores each fp32 128-row
+   * tile of its partial straight into the inbox of the rank that owns the tile (tile m
+   * -> rank m % tp_size, NVLink stores), the owner sums the tp_size partials in rank
+   * order and sends the bf16 rows to every rank, so `out` (bf16) ends with the
+   * all-reduced result on every rank: RowParallelLinear's fp32 all-reduce
+   * (nanovllm/layers/linear.py:149-157) fused into the GEMM. */
+  int32_t tp_rank, tp_size;
+  int64_t tp_capacity;             /* rows the TP buffers were sized for (>= num_tokens) */
+  void* tp_bufs[LB_EP_MAX_RANKS];  /* every rank's TP buffer (lb_tp_buffer_size bytes,
+                                    * from lb_ep_buffer_alloc / lb_ep_buffer_open) */
+  int32_t tp_phases;               /* 0 = all; else a mask of LB_TP_PHASE_* (tests) */
 } LbPodArgs;
+
+#define LB_TP_PHASE_ATTN 1    /* attention, merge, o_proj GEMM to the owners + signal */
+#define LB_TP_PHASE_REDUCE 2  /* wait, sum the owned rows, send them to every rank */
+#define LB_TP_PHASE_GATHER 4  /* wait, copy the rows other ranks own into out */
+
+/* Bytes of one rank's tensor-parallel exchange buffer for `world` ranks, up to
+ * `capacity` rows of `hidden` outputs. */
+size_t lb_tp_buffer_size(int64_t world, int64_t capacity, int64_t hidden);
 
 int lb_pod_workspace_size(const LbPodArgs* args, size_t* bytes);
 int lb_pod_attn_oproj(const LbPodArgs* args, void* stream);

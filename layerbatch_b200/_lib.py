@@ -25,12 +25,14 @@ EXPORTS = [
     "lb_moe_workspace_size",
     "lb_moe_forward", "lb_ep_buffer_size", "lb_ep_buffer_alloc", "lb_ep_buffer_open",
     "lb_ep_buffer_close", "lb_ep_buffer_free", "lb_ep_workspace_size", "lb_ep_moe_forward",
-    "lb_store_kvcache", "lb_attn_prologue", "lb_pod_workspace_size", "lb_pod_attn_oproj",
+    "lb_store_kvcache", "lb_attn_prologue", "lb_tp_buffer_size", "lb_pod_workspace_size",
+    "lb_pod_attn_oproj",
 ]
 
 LB_EP_MAX_RANKS = 8
 LB_EP_IPC_HANDLE_BYTES = 64
 LB_EP_PHASE_DISPATCH, LB_EP_PHASE_EXPERTS, LB_EP_PHASE_COMBINE = 1, 2, 4
+LB_TP_PHASE_ATTN, LB_TP_PHASE_REDUCE, LB_TP_PHASE_GATHER = 1, 2, 4
 
 vp = C.c_void_p
 i64 = C.c_int64
@@ -89,6 +91,8 @@ class LbPodArgs(C.Structure):
         ("cu_seqlens_q", vp), ("w_o", vp), ("attn_out", vp), ("out", vp),
         ("out_fp32", i32), ("workspace", vp), ("workspace_bytes", C.c_size_t),
         ("timing_events", vp * 4), ("prefill_pairs_hint", i64), ("decode_tokens_hint", i64),
+        ("tp_rank", i32), ("tp_size", i32), ("tp_capacity", i64),
+        ("tp_bufs", vp * LB_EP_MAX_RANKS), ("tp_phases", i32),
     ]
 
 
@@ -121,6 +125,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.lb_ep_buffer_free.argtypes = [vp]
     L.lb_ep_workspace_size.argtypes = [C.POINTER(LbEpArgs), C.POINTER(C.c_size_t)]
     L.lb_ep_moe_forward.argtypes = [C.POINTER(LbEpArgs), vp]
+    L.lb_tp_buffer_size.restype = C.c_size_t
+    L.lb_tp_buffer_size.argtypes = [i64, i64, i64]
     L.lb_attn_prologue.argtypes = [C.POINTER(LbPrologueArgs), vp]
     L.lb_store_kvcache.argtypes = [vp, i64, vp, i64, vp, vp, vp, i64, i64, i64, vp]
     L.lb_pod_workspace_size.argtypes = [C.POINTER(LbPodArgs), C.POINTER(C.c_size_t)]

@@ -292,6 +292,78 @@ __global__ void k_f32_to_bf16(const float* __restrict__ src, __nv_bfloat16* __re
   }
 }
 
+// ------------------------------------------------------------------------------ tensor parallel
+struct TpReduce {
+  int* hdr;                                // this rank's header
+  const float* inbox;                      // this rank's inbox [P][cap][H]
+  __nv_bfloat16* out;                      // [N, H]
+  __nv_bfloat16* gather[LB_PEER_MAX];      // every rank's gather region [cap][H]
+  int* peer_hdr[LB_PEER_MAX];
+  int P, rank, N, H;
+  long long cap;
+  int* status;
+};
+
+// Rows of the 128-row tiles this rank owns (tile m -> rank m % P): the P partials summed
+// in rank order in fp32, rounded once to bf16, written to out and to every other rank's
+// gather region (NVLink stores).  The last CTA publishes the epoch to the other ranks.
+__global__ void __launch_bounds__(256) k_tp_reduce(const TpReduce a) {
+  if ((int)threadIdx.x < a.P) peer_wait(a.hdr + TPH_PART + threadIdx.x, a.hdr[TPH_EPOCH], a.status);
+  __syncthreads();
+  const int nmt = (a.N + GEMM_BM - 1) / GEMM_BM;
+  const int owned = nmt > a.rank ? (nmt - a.rank + a.P - 1) / a.P : 0;
+  const int vpr = a.H / 8;
+  const long long units = (long long)owned * GEMM_BM * vpr;
+  for (long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x; u < units;
+       u += (long long)gridDim.x * blockDim.x) {
+    const int j = (int)(u / ((long long)GEMM_BM * vpr));
+    const int rem = (int)(u - (long long)j * GEMM_BM * vpr);
+    const int r = rem / vpr, c = rem - r * vpr;
+    const int row = (a.rank + a.P * j) * GEMM_BM + r;
+    if (row >= a.N) continue;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < a.P; ++s) {
+      const float4* src =
+          reinterpret_cast<const float4*>(a.inbox + ((long long)s * a.cap + row) * a.H) + 2 * c;
+      const float4 x0 = src[0], x1 = src[1];
+      acc[0] += x0.x; acc[1] += x0.y; acc[2] += x0.z; acc[3] += x0.w;
+      acc[4] += x1.x; acc[5] += x1.y; acc[6] += x1.z; acc[7] += x1.w;
+    }
+    const uint4 o = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                               pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+    reinterpret_cast<uint4*>(a.out + (long long)row * a.H)[c] = o;
+    for (int p = 0; p < a.P; ++p)
+      if (p != a.rank) reinterpret_cast<uint4*>(a.gather[p] + (long long)row * a.H)[c] = o;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(a.hdr + TPH_DONE_RED, 1) == (int)gridDim.x - 1) {
+    __threadfence_system();
+    const int epoch = a.hdr[TPH_EPOCH];
+    a.hdr[TPH_DONE_RED] = 0;
+    for (int p = 0; p < a.P; ++p)
+      if (p != a.rank) st_release_sys(a.peer_hdr[p] + TPH_GATH + a.rank, epoch);
+  }
+}
+
+// Waits for every other rank's reduced rows, then copies the rows they own into out.
+__global__ void __launch_bounds__(256) k_tp_gather(int* hdr, const __nv_bfloat16* __restrict__ gather,
+                                                   __nv_bfloat16* __restrict__ out, int P, int rank,
+                                                   int N, int H, int* status) {
+  if ((int)threadIdx.x < P && (int)threadIdx.x != rank)
+    peer_wait(hdr + TPH_GATH + threadIdx.x, hdr[TPH_EPOCH], status);
+  __syncthreads();
+  const int vpr = H / 8;
+  const long long units = (long long)N * vpr;
+  for (long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x; u < units;
+       u += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(u / vpr), c = (int)(u - (long long)row * vpr);
+    if ((row / GEMM_BM) % P == rank) continue;
+    reinterpret_cast<uint4*>(out + (long long)row * H)[c] =
+        reinterpret_cast<const uint4*>(gather + (long long)row * H)[c];
+  }
+}
+
 // ------------------------------------------------------------------------------ host
 struct PodPlan {
   int split_tokens, max_splits, max_ctx, pf_cap, dec_cap, gqa, grid, n_pf_ctas;
@@ -338,6 +410,17 @@ static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
   LB_REQUIRE(a->gate == nullptr || (a->gate_stride_head % 8 == 0 && a->gate_stride_tok % 8 == 0 &&
                                     a->gate_stride_head >= POD_D),
              "lb_pod: gate strides must be multiples of 8 elements with contiguous heads");
+  if (a->tp_size > 1) {
+    LB_REQUIRE(a->tp_size <= LB_EP_MAX_RANKS && a->tp_rank >= 0 && a->tp_rank < a->tp_size,
+               "lb_pod: need 1 < tp_size <= %d and 0 <= tp_rank < tp_size", LB_EP_MAX_RANKS);
+    LB_REQUIRE(a->w_o && !a->out_fp32 && a->hidden % 256 == 0,
+               "lb_pod: tensor parallel o_proj needs w_o, a bf16 out and hidden % 256 == 0");
+    LB_REQUIRE(a->tp_capacity >= a->num_tokens, "lb_pod: num_tokens exceeds tp_capacity");
+    LB_REQUIRE((a->tp_phases & ~7) == 0, "lb_pod: unknown tp_phases bits");
+    for (int r = 0; r < a->tp_size; ++r)
+      LB_REQUIRE(a->tp_bufs[r] && (reinterpret_cast<uintptr_t>(a->tp_bufs[r]) & 255) == 0,
+                 "lb_pod: tp buffer %d missing or not 256-byte aligned", r);
+  }
   const long long HD = a->num_q_heads * POD_D;
   LB_REQUIRE(HD % 64 == 0, "lb_pod: Hq*D must be a multiple of 64");
   pl.gqa = (int)(a->num_q_heads / a->num_kv_heads);
@@ -404,7 +487,8 @@ static size_t carve_pod(const LbPodArgs& a, const PodPlan& pl, void* base, PodWs
   return c.off + 256;
 }
 
-static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaStream_t st) {
+// Plan, POD attention kernel and split merge (+ gate): writes the o_proj input rows.
+static int pod_attention(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaStream_t st) {
   const int B = (int)a.num_seqs, N = (int)a.num_tokens;
   if (B == 0 || N == 0) return LB_OK;
   int rc;
@@ -482,8 +566,96 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
                                           w.part_lse, p.gate, a.gate_stride_tok, a.gate_stride_head,
                                           p.ogated, p.attn_out);
   { int _rc = launched("k_pod_merge"); if (_rc) return _rc; }
+  return LB_OK;
+}
 
+// Tensor-parallel o_proj: GEMM with the peer-store epilogue, owner reduction, gather.
+static int tp_oproj(const LbPodArgs& a, const PodWs& w, cudaStream_t st, int phases) {
+  const int N = (int)a.num_tokens, P = a.tp_size, rank = a.tp_rank;
+  const int K = (int)(a.num_q_heads * POD_D), Hd = (int)a.hidden;
+  const int nsm = num_sms();
+  TpPeers tp{};
+  for (int r = 0; r < P; ++r) {
+    uint8_t* base = static_cast<uint8_t*>(a.tp_bufs[r]);
+    tp.hdr[r] = reinterpret_cast<int*>(base);
+    tp.inbox[r] = reinterpret_cast<float*>(base + TP_HEADER_BYTES);
+  }
+  tp.rank = rank;
+  tp.size = P;
+  tp.inbox_rows = a.tp_capacity;
+  uint8_t* own = static_cast<uint8_t*>(a.tp_bufs[rank]);
+  int* hdr = tp.hdr[rank];
+  const size_t inbox_bytes = (size_t)P * a.tp_capacity * Hd * sizeof(float);
+  auto gather_of = [&](int r) {
+    return reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(a.tp_bufs[r]) + TP_HEADER_BYTES +
+                                            inbox_bytes);
+  };
+  int rc;
+  if (phases & LB_TP_PHASE_ATTN) {
+    constexpr int BN = 256;
+    CUtensorMap tA, tB;
+    // an empty rank still launches (its CTAs publish the epoch); its maps point at W_o
+    const void* A = N > 0 ? static_cast<const void*>(w.ogated) : a.w_o;
+    if ((rc = make_tmap_bf16_2d(&tA, A, std::max(N, 1), K, K, GEMM_BM, 64))) return rc;
+    if ((rc = make_tmap_bf16_3d(&tB, a.w_o, 1, Hd, K, K, (uint64_t)K * Hd, BN, 64))) return rc;
+    GemmArgs g = gemm_args_default(w.status);
+    g.single_m = N;
+    g.single_row_base = 0;
+    g.n_tiles = Hd / BN;
+    g.splits = 1;
+    g.k_blocks = K / 64;
+    g.out = nullptr;
+    g.ldo = Hd;
+    g.out_rows = N;
+    g.out_cols = Hd;
+    g.tp = tp;
+    const long long tiles = (long long)((N + GEMM_BM - 1) / GEMM_BM) * g.n_tiles;
+    const int grid = (int)std::max<long long>(1, std::min<long long>(tiles, nsm));
+    record_event(a.timing_events[2], st);
+    if ((rc = launch_gemm<BN, 4, EPI_F32_PEER, false>(tA, tA, tB, tB, tB, g, grid, st))) return rc;
+  }
+  if (phases & LB_TP_PHASE_REDUCE) {
+    TpReduce d{};
+    d.hdr = hdr;
+    d.inbox = reinterpret_cast<const float*>(own + TP_HEADER_BYTES);
+    d.out = static_cast<__nv_bfloat16*>(a.out);
+    for (int r = 0; r < P; ++r) {
+      d.gather[r] = gather_of(r);
+      d.peer_hdr[r] = tp.hdr[r];
+    }
+    d.P = P;
+    d.rank = rank;
+    d.N = N;
+    d.H = Hd;
+    d.cap = a.tp_capacity;
+    d.status = w.status;
+    const long long units = (long long)N * (Hd / 8) / P + Hd;
+    const int grid = (int)std::max<long long>(1, std::min<long long>(nsm * 2, (units + 255) / 256));
+    k_tp_reduce<<<grid, 256, 0, st>>>(d);
+    { int _rc = launched("k_tp_reduce"); if (_rc) return _rc; }
+  }
+  if (phases & LB_TP_PHASE_GATHER) {
+    const long long units = (long long)N * (Hd / 8);
+    const int grid = (int)std::max<long long>(1, std::min<long long>(nsm * 2, (units + 255) / 256));
+    k_tp_gather<<<grid, 256, 0, st>>>(hdr, gather_of(rank), static_cast<__nv_bfloat16*>(a.out), P,
+                                       rank, N, Hd, w.status);
+    { int _rc = launched("k_tp_gather"); if (_rc) return _rc; }
+    record_event(a.timing_events[3], st);
+  }
+  return LB_OK;
+}
+
+static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaStream_t st) {
+  const bool tp = a.tp_size > 1;
+  const int phases = (tp && a.tp_phases) ? a.tp_phases : 7;
+  int rc;
+  if (phases & LB_TP_PHASE_ATTN) {
+    if ((rc = pod_attention(a, pl, w, st))) return rc;
+  }
   if (a.w_o == nullptr) return LB_OK;  // attention only
+  if (tp) return tp_oproj(a, w, st, phases);
+  const int N = (int)a.num_tokens;
+  if (a.num_seqs == 0 || N == 0) return LB_OK;
   // o_proj: out[N, hidden] = ogated[N, Hq*D] . W_o^T
   const int K = (int)(a.num_q_heads * POD_D), Hd = (int)a.hidden;
   const int nsm = num_sms();
@@ -566,6 +738,12 @@ int lb_attn_prologue(const LbPrologueArgs* a, void* stream) {
   k_attn_prologue<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(*a);
   { int _rc = launched("k_attn_prologue"); if (_rc) return _rc; }
   return LB_OK;
+}
+
+size_t lb_tp_buffer_size(int64_t world, int64_t capacity, int64_t hidden) {
+  if (world < 1 || capacity < 0 || hidden < 0) return 0;
+  return (size_t)TP_HEADER_BYTES + (size_t)world * capacity * hidden * sizeof(float) +
+         (size_t)capacity * hidden * sizeof(__nv_bfloat16) + 256;
 }
 
 int lb_pod_workspace_size(const LbPodArgs* a, size_t* bytes) {

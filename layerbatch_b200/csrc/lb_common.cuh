@@ -278,6 +278,32 @@ __device__ __forceinline__ void st_global_v4(void* p, uint4 v) {
   *reinterpret_cast<uint4*>(p) = v;
 }
 
+// ------------------------------------------------------------------------------ peers
+// System-scope flag accesses between GPUs that map each other's memory.
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait until a flag another GPU writes reaches `epoch` (epochs only grow).
+// Gives up after LB_SPIN_LIMIT_CYCLES with LB_DEV_TIMEOUT in the status word.
+__device__ __forceinline__ bool peer_wait(const int* flag, int epoch, int* status) {
+  const long long t0 = clock64();
+  while (ld_acquire_sys(flag) - epoch < 0) {
+    if (clock64() - t0 > (long long)LB_SPIN_LIMIT_CYCLES) {
+      report(status, LB_DEV_TIMEOUT);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
 __device__ __forceinline__ void red_add_v4_f32(float* p, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b),
                "f"(c), "f"(d)

@@ -57,29 +57,6 @@ struct EpPeers {
   uint8_t* p[LB_EP_MAX_RANKS];
 };
 
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Bounded wait until the flag another GPU writes reaches `epoch`.
-__device__ __forceinline__ bool ep_wait(const int* flag, int epoch, int* status) {
-  const long long t0 = clock64();
-  while (ld_acquire_sys(flag) - epoch < 0) {
-    if (clock64() - t0 > (long long)LB_SPIN_LIMIT_CYCLES) {
-      report(status, LB_DEV_TIMEOUT);
-      return false;
-    }
-    __nanosleep(64);
-  }
-  return true;
-}
-
 // Ranks owning at least one of a token's k experts (bit r), experts in ranges of `epr`.
 __device__ __forceinline__ unsigned ep_dest_mask(const int32_t* ids, int k, int epr, int P,
                                                  int* status) {
@@ -226,7 +203,7 @@ __global__ void __launch_bounds__(256) k_ep_recv_prepare(int* hdr, int32_t* __re
   __shared__ int s_cnt[LB_EP_MAX_RANKS];
   if ((int)threadIdx.x < P) {
     const int epoch = hdr[EPH_EPOCH];
-    ep_wait(hdr + EPH_DISP + threadIdx.x, epoch, status);
+    peer_wait(hdr + EPH_DISP + threadIdx.x, epoch, status);
     int c = ld_acquire_sys(hdr + EPH_COUNT + threadIdx.x);
     if (c < 0 || c > C) {
       report(status, LB_DEV_BAD_INDEX);
@@ -320,7 +297,7 @@ __global__ void __launch_bounds__(256) k_ep_combine(const __nv_bfloat16* __restr
                                                     int H, int P, int C, int* hdr,
                                                     const __nv_bfloat16* ret, int* status,
                                                     __nv_bfloat16* __restrict__ out) {
-  if ((int)threadIdx.x < P) ep_wait(hdr + EPH_RET + threadIdx.x, hdr[EPH_EPOCH], status);
+  if ((int)threadIdx.x < P) peer_wait(hdr + EPH_RET + threadIdx.x, hdr[EPH_EPOCH], status);
   __syncthreads();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;

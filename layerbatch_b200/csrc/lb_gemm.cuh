@@ -13,6 +13,7 @@
 
 #include <cuda.h>
 #include "lb_common.cuh"
+#include "lb_peer.h"
 
 namespace lb {
 
@@ -26,6 +27,8 @@ enum EpiKind : int {
   EPI_SCALE_BF16 = 2,  // C = bf16(acc * row_scale[row])
   EPI_COMBINE = 3,     // out[t] = bf16(tok_scale[t] * acc + sum_j yw[row_of[t, j]])
   EPI_F32_RED = 4,     // out32 += acc (split-K partials, vector reductions)
+  EPI_F32_PEER = 5,    // fp32 tile -> inbox of the rank owning its m-tile (tensor parallel);
+                       // the last CTA publishes the call's epoch to every rank
 };
 
 struct GemmArgs {
@@ -52,7 +55,11 @@ struct GemmArgs {
   int top_k;
   int out_rows;                // rows of `out` (bounds check)
   int out_cols;                // columns of `out` (bounds check)
+  TpPeers tp;                  // EPI_F32_PEER
 };
+
+constexpr int EPI_STAGE_LD = 36;  // floats per row of the peer-store transpose buffer
+constexpr int EPI_STAGE_BYTES = 4 * 32 * EPI_STAGE_LD * 4 + 16;
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -116,6 +123,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_mt = reinterpret_cast<int*>(bars) + S::BAR_BYTES / 4;
+  // EPI_F32_PEER: per epilogue warp a 32 x EPI_STAGE_LD fp32 transpose buffer
+  float* s_stage = reinterpret_cast<float*>(
+      (reinterpret_cast<uintptr_t>(s_mt + p.num_groups + 2) + 15) & ~static_cast<uintptr_t>(15));
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -301,6 +311,37 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tmem_ld32(tbase + ch * 32, v);
           tmem_wait_ld();
           const int col = c.n * BN + ch * 32;
+          if constexpr (EPI == EPI_F32_PEER) {
+            // Rank s's partial of a row goes to region s of the inbox of the rank owning
+            // the row's m-tile.  The warp's 32 x 32 fp32 block is transposed through
+            // shared memory so that every store writes 128-byte row segments (8 lanes per
+            // row): large NVLink writes instead of 16-byte ones.
+            float* stg = s_stage + quad * (32 * EPI_STAGE_LD);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              *reinterpret_cast<float4*>(stg + lane * EPI_STAGE_LD + 4 * i) =
+                  make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                              __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+            __syncwarp();
+            const int owner = c.m % p.tp.size;
+            float* inbox = p.tp.inbox[0];
+#pragma unroll
+            for (int r = 1; r < LB_PEER_MAX; ++r)
+              if (r == owner) inbox = p.tp.inbox[r];
+            const int warp_row0 = quad * 32;            // first tile row of this warp
+            const long long row0 = (long long)(out_row - row_in_tile) + warp_row0;
+            const int cc = (lane & 7) * 4;
+#pragma unroll
+            for (int jr = 0; jr < 8; ++jr) {
+              const int r = 4 * jr + (lane >> 3);
+              const float4 val = *reinterpret_cast<const float4*>(stg + r * EPI_STAGE_LD + cc);
+              if (warp_row0 + r < valid_rows && row0 + r < p.out_rows && col + 32 <= p.out_cols)
+                *reinterpret_cast<float4*>(
+                    inbox + ((long long)p.tp.rank * p.tp.inbox_rows + row0 + r) * p.ldo + col + cc) = val;
+            }
+            __syncwarp();
+            continue;
+          }
           if (!row_ok || col + 32 > p.out_cols) {
             // nothing to store for this row / chunk
           } else if constexpr (EPI == EPI_F32_RED) {
@@ -359,6 +400,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   }
 
+  if constexpr (EPI == EPI_F32_PEER) {
+    // every tile of this CTA is stored: the last CTA to get here tells every rank that
+    // this rank's partials of the call are in place
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int* own = p.tp.hdr[p.tp.rank];
+      if (atomicAdd(own + TPH_DONE_GEMM, 1) == (int)gridDim.x - 1) {
+        __threadfence_system();
+        const int epoch = own[TPH_EPOCH] + 1;
+        own[TPH_EPOCH] = epoch;
+        own[TPH_DONE_GEMM] = 0;
+        for (int r = 0; r < p.tp.size; ++r) st_release_sys(p.tp.hdr[r] + TPH_PART + p.tp.rank, epoch);
+      }
+    }
+  }
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();

@@ -11,7 +11,8 @@ int launch_gemm(const CUtensorMap& tA, const CUtensorMap& tAsh, const CUtensorMa
                 const CUtensorMap& tBsh0, const CUtensorMap& tBsh1, const GemmArgs& a,
                 int grid, cudaStream_t st) {
   auto kern = k_gemm<BN, STAGES, EPI, TWO_HALVES>;
-  const size_t smem = GemmSmem<BN, STAGES>::bytes(a.num_groups);
+  const size_t smem = GemmSmem<BN, STAGES>::bytes(a.num_groups) +
+                      (EPI == EPI_F32_PEER ? EPI_STAGE_BYTES : 0);
   if ((int)smem > max_smem_optin())
     return fail(LB_ERR_UNSUPPORTED, "gemm: %zu bytes of shared memory exceed the limit", smem);
   LB_CUDA_CHECK(

@@ -20,72 +20,31 @@ import torch
 import torch.distributed as dist
 
 from .. import ops
-from .._lib import LB_EP_IPC_HANDLE_BYTES, LB_EP_MAX_RANKS, LbEpArgs, check, lib, ptr, stream_ptr
+from .._lib import LB_EP_MAX_RANKS, LbEpArgs, check, lib, ptr, stream_ptr
+from .peer import PeerBuffers
 
 
-class EPExchange:
-    """This rank's mapping of the exchange buffers of one expert-parallel group."""
+class EPExchange(PeerBuffers):
+    """This rank's mapping of the exchange buffers of one expert-parallel group, sized
+    for ``capacity`` tokens per rank and call."""
 
     def __init__(self, capacity: int, hidden: int, top_k: int, group=None, device=None,
                  _local=None):
         self.capacity, self.hidden, self.top_k = capacity, hidden, top_k
-        self.device = torch.device(device) if device is not None else \
-            torch.device("cuda", torch.cuda.current_device())
-        self._opened, self._owned = [], []
-        self.group = group
-        if _local is not None:            # emulated ranks in one process (tests)
-            self.rank, self.world, self.peers = _local
-            return
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
-        if self.world > LB_EP_MAX_RANKS:
-            raise ValueError(f"expert-parallel group of {self.world} > {LB_EP_MAX_RANKS} ranks")
-        L = lib()
-        nbytes = L.lb_ep_buffer_size(self.world, capacity, hidden, top_k)
-        own, handle = _alloc(nbytes)
-        self._owned.append(own)
-        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
-        every = [torch.empty_like(mine) for _ in range(self.world)]
-        dist.all_gather(every, mine, group=group)
-        self.peers = []
-        for r, h in enumerate(every):
-            if r == self.rank:
-                self.peers.append(own)
-                continue
-            hb = (C.c_uint8 * LB_EP_IPC_HANDLE_BYTES).from_buffer_copy(bytes(h.cpu().tolist()))
-            p = C.c_void_p()
-            check(L.lb_ep_buffer_open(hb, C.byref(p)), "lb_ep_buffer_open")
-            self._opened.append(p.value)
-            self.peers.append(p.value)
-        dist.barrier(group=group)
+        world = _local[1] if _local is not None else dist.get_world_size(group)
+        if world > LB_EP_MAX_RANKS:
+            raise ValueError(f"expert-parallel group of {world} > {LB_EP_MAX_RANKS} ranks")
+        super().__init__(lib().lb_ep_buffer_size(world, capacity, hidden, top_k), group,
+                         device, _local)
 
     @classmethod
     def emulated(cls, world: int, capacity: int, hidden: int, top_k: int, device=None):
         """``world`` ranks' exchanges in one process on one device (single-GPU tests):
         the phases of all ranks are then issued in order on one stream."""
         nbytes = lib().lb_ep_buffer_size(world, capacity, hidden, top_k)
-        bufs = [_alloc(nbytes)[0] for _ in range(world)]
-        out = [cls(capacity, hidden, top_k, device=device, _local=(r, world, list(bufs)))
-               for r in range(world)]
-        out[0]._owned = bufs
-        return out
-
-    def close(self):
-        """Unmap the peers and free this rank's buffer (all ranks must be done with it)."""
-        torch.cuda.synchronize(self.device)
-        L = lib()
-        for p in self._opened:
-            check(L.lb_ep_buffer_close(p), "lb_ep_buffer_close")
-        for p in self._owned:
-            check(L.lb_ep_buffer_free(p), "lb_ep_buffer_free")
-        self._opened, self._owned = [], []
-
-
-def _alloc(nbytes):
-    h = (C.c_uint8 * LB_EP_IPC_HANDLE_BYTES)()
-    p = C.c_void_p()
-    check(lib().lb_ep_buffer_alloc(nbytes, C.byref(p), h), "lb_ep_buffer_alloc")
-    return p.value, h
+        return cls._emulated(world, nbytes, device,
+                             lambda _local: cls(capacity, hidden, top_k, device=device,
+                                                _local=_local))
 
 
 def ep_args(block, x: torch.Tensor, ex: EPExchange, out: torch.Tensor, phases: int = 0,

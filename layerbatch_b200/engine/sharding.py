@@ -145,10 +145,22 @@ def shard_attention_tensors(shard: TPShard, q, gate, k_cache, v_cache, w_o, head
 
 def tp_attention_oproj(shard: TPShard, q, gate, k_cache, v_cache, block_tables, context_lens,
                        cu_seqlens_q, w_o, scale, group=None, max_q_len=None, events=None,
-                       out=None, work_hint=None):
-    """This rank's heads -> fp32 o_proj partial -> fp32 all-reduce -> bf16 ``[N, H]``."""
+                       out=None, work_hint=None, exchange=None, tp_phases=0):
+    """This rank's heads -> fp32 o_proj partial -> all-reduce -> bf16 ``[N, H]``.
+
+    With ``exchange`` (an ``engine.peer.TPExchange`` of the TP group) the reduction runs
+    inside the library call: the o_proj GEMM stores each fp32 tile into the inbox of the
+    rank owning it over NVLink, owners sum in rank order and send the bf16 rows back (no
+    NCCL).  Without it, an fp32 NCCL all-reduce of the partials, like the reference."""
     from .. import ops
     N = q.shape[0]
+    if exchange is not None and shard.tp_size > 1:
+        if out is None:
+            out = torch.empty(N, w_o.shape[0], dtype=torch.bfloat16, device=q.device)
+        return ops.pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens,
+                                  cu_seqlens_q, w_o, scale, out=out, max_q_len=max_q_len,
+                                  ws_tag=f"tp_attn{exchange.rank}", events=events,
+                                  work_hint=work_hint, tp=exchange, tp_phases=tp_phases)
     partial = torch.empty(N, w_o.shape[0], dtype=torch.float32, device=q.device)
     ops.pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q,
                        w_o, scale, out=partial, max_q_len=max_q_len, ws_tag="tp_attn",

@@ -244,12 +244,15 @@ def pod_work_hint(ctx_list, qlen_list):
 
 def pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o,
                    scale, out=None, attn_out=None, max_q_len=None, kv_split_pages=0,
-                   ws_tag="pod", events=None, work_hint=None):
+                   ws_tag="pod", events=None, work_hint=None, tp=None, tp_phases=0):
     """Fused paged attention (prefill + decode mixed) -> sigmoid gate -> o_proj.
 
     ``gate`` may be None (no output gate).  With ``w_o=None`` only the attention runs and
     ``attn_out`` [N, Hq*D] receives it; the function then returns ``attn_out``.
     ``out`` may be fp32 to receive the o_proj partial sums unrounded (tensor parallel).
+    ``tp`` (an ``engine.peer.TPExchange``): this rank holds a head slice and W_o's matching
+    columns; the o_proj partials are reduced over the group through peer memory inside
+    the call and ``out`` (bf16) receives the all-reduced result.
     """
     N, Hq, D = q.shape
     for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache)):
@@ -267,6 +270,11 @@ def pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seq
                  kv_split_pages)
     if work_hint is not None:
         a.prefill_pairs_hint, a.decode_tokens_hint = int(work_hint[0]), int(work_hint[1])
+    if tp is not None and tp.world > 1:
+        a.tp_rank, a.tp_size, a.tp_capacity = tp.rank, tp.world, tp.capacity
+        for r, p in enumerate(tp.peers):
+            a.tp_bufs[r] = p
+        a.tp_phases = tp_phases
     _events(a, events)
     need = C.c_size_t(0)
     check(lib().lb_pod_workspace_size(C.byref(a), C.byref(need)), "lb_pod_workspace_size")

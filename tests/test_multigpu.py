@@ -53,6 +53,16 @@ def _worker(rank, world, port, q):
         tp = S.tp_attention_oproj(shard, qs, gs, kc, vc, b.block_tables, b.context_lens,
                                   b.cu_seqlens_q, wo, b.scale, max_q_len=300)
         errs["tp"] = OM.rel_err(tp.float(), full.float())
+        # the same with the o_proj reduction fused over peer memory (no NCCL)
+        from layerbatch_b200.engine.peer import TPExchange
+        tpx = TPExchange(1024, 2048, device=dev)
+        for _ in range(2):
+            tp2 = S.tp_attention_oproj(shard, qs, gs, kc, vc, b.block_tables, b.context_lens,
+                                       b.cu_seqlens_q, wo, b.scale, max_q_len=300, exchange=tpx)
+        torch.cuda.synchronize()
+        errs["tp_peer"] = OM.rel_err(tp2.float(), full.float())
+        dist.barrier()
+        tpx.close()
         # ---- MoE, expert parallel with all-to-all
         H, E, I, k, T = 2048, 64, 512, 8, 96 + 32 * rank
         p = W.make_moe_params(H, E, I, I, k, seed=0).to(dev)
@@ -165,4 +175,4 @@ def test_tp_attention_and_ep_moe_on_two_gpus():
             pr.kill()
     assert all(r[1] == "ok" for r in res), res
     for _, _, errs in res:
-        assert errs["tp"] <= 2e-2 and errs["ep"] <= 2e-2, errs
+        assert errs["tp"] <= 2e-2 and errs["ep"] <= 2e-2 and errs["tp_peer"] <= 2e-2, errs
