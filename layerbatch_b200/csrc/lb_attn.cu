@@ -114,8 +114,9 @@ __global__ void __launch_bounds__(256) k_attn_prologue(const LbPrologueArgs a) {
 
 // ------------------------------------------------------------------------------ plan
 // One block.  Phase 1: per-sequence item counts and block-wide exclusive scans give every
-// sequence its first item slots (kept in shared memory).  Phase 2: one warp per sequence
-// writes its items with the lanes in parallel.  Queue order is longest first, so the
+// sequence its first item slots (kept in shared memory).  Phase 2: each thread writes the
+// decode items of its own sequences; prefill sequences (many items each) are written by
+// the lanes of their thread's warp together.  Queue order is longest first, so the
 // dynamic scheduler ends on short items: prefill tiles latest query tile first; decode
 // items all full-length splits first, then every sequence's shorter last split.
 __global__ void k_pod_plan(const int32_t* __restrict__ ctx_lens, const int32_t* __restrict__ cu,
@@ -177,28 +178,41 @@ __global__ void k_pod_plan(const int32_t* __restrict__ ctx_lens, const int32_t* 
     }
   }
   __syncthreads();
-  const int warp = tid / 32, lane = tid % 32;
-  for (int b = warp; b < B; b += 32) {
-    const int qlen = cu[b + 1] - cu[b];
-    const int ctx = ctx_lens[b];
-    if (qlen <= 0 || ctx < qlen || ctx > max_ctx) continue;
-    if (qlen == 1) {
+  // Phase 2: every thread writes the decode items of its own sequences; the prefill
+  // sequences of a warp's threads are written by the whole warp, one after another.
+  const int lane = tid % 32;
+  for (int kk = 0; kk < per; ++kk) {
+    const int b = b0 + kk;
+    int qlen = 0, ctx = 0;
+    bool valid = b < b1;
+    if (valid) {
+      qlen = cu[b + 1] - cu[b];
+      ctx = ctx_lens[b];
+      valid = !(qlen <= 0 || ctx < qlen || ctx > max_ctx);
+    }
+    if (valid && qlen == 1) {
       const int nf = ctx / split_tokens;
       const int n = Hkv * nf;
       const int o = s_off[B + b];
-      for (int i = lane; i < n; i += 32)
+      for (int i = 0; i < n; ++i)
         if (o + i < dec_cap) dec_items[o + i] = make_int4(b, i % Hkv, i / Hkv, 0);
       if (ctx % split_tokens) {
         const int orr = s_off[2 * B + b];
-        for (int i = lane; i < Hkv; i += 32)
+        for (int i = 0; i < Hkv; ++i)
           if (orr + i < dec_cap) dec_items[orr + i] = make_int4(b, i, nf, 0);
       }
-    } else {
-      const int nqt = (qlen + POD_KV - 1) / POD_KV;
+    }
+    unsigned pfm = __ballot_sync(0xffffffffu, valid && qlen > 1);
+    while (pfm) {
+      const int src = __ffs(pfm) - 1;
+      pfm &= pfm - 1;
+      const int bb = __shfl_sync(0xffffffffu, b, src);
+      const int ql = __shfl_sync(0xffffffffu, qlen, src);
+      const int nqt = (ql + POD_KV - 1) / POD_KV;
       const int n = Hq * nqt;
-      const int o = s_off[b];
+      const int o = s_off[bb];
       for (int i = lane; i < n; i += 32)
-        if (o + i < pf_cap) pf_items[o + i] = make_int4(b, i % Hq, nqt - 1 - i / Hq, 0);
+        if (o + i < pf_cap) pf_items[o + i] = make_int4(bb, i % Hq, nqt - 1 - i / Hq, 0);
     }
   }
   if (tid == 1023) {

@@ -153,3 +153,43 @@ def test_full_attention_layer_prefill(cuda):
     finally:
         reset_context()
     assert OM.rel_err(y.cpu(), ref) <= TOL
+
+
+def test_full_attention_layer_mixed_step_from_scheduler(cuda):
+    """One step of the mixed scheduler (a prompt chunk on its cached prefix plus decode
+    tokens of finished prompts) through the layer in one POD launch."""
+    from layerbatch_b200.engine.batch_builder import (MixedScheduler, Sequence, prepare_mixed,
+                                                      set_mixed_context)
+    m = _module(cuda, seed=12)
+    sched = MixedScheduler(num_blocks=24, max_num_batched_tokens=700, chunk_size=600)
+    seqs = [Sequence([0] * n, max_tokens=4) for n in (900, 130, 257)]
+    for s in seqs:
+        sched.add(s)
+    for _ in range(2):                          # the three prompts, in chunks
+        b = sched.schedule()
+        sched.postprocess(b, {s.seq_id: 1 for s in seqs})
+    late = Sequence([0] * 800, max_tokens=4)
+    sched.add(late)
+    b = sched.schedule()                        # 3 decodes + the first 600 of the late prompt
+    sched.postprocess(b, {s.seq_id: 1 for s in seqs + [late]})
+    step = sched.schedule()                     # 3 decodes + its last 200 on a 600 prefix
+    assert [(i.start, i.length) for i in step.prefill] == [(600, 200)]
+    assert step.prefill and step.decode, "expected a mixed step"
+    meta = prepare_mixed(step)
+    N = int(meta["cu_seqlens_q"][-1])
+    g = torch.Generator().manual_seed(13)
+    x = torch.randn(N, 2048, generator=g).to(torch.bfloat16)
+    # cache: earlier steps' K/V stand in as random values; this step overwrites its slots
+    kc = torch.randn(24, 256, 2, 256, generator=g).to(torch.bfloat16)
+    vc = torch.randn(24, 256, 2, 256, generator=g).to(torch.bfloat16)
+    ref = _oracle_layer(m, x, meta["positions"], kc.clone(), vc.clone(), meta["slot_mapping"],
+                        meta["block_tables"], meta["context_lens"], meta["cu_seqlens_q"])
+    m.attn.k_cache, m.attn.v_cache = kc.to(cuda), vc.to(cuda)
+    dmeta = prepare_mixed(step, device=cuda)
+    set_mixed_context(dmeta)
+    try:
+        y = m(dmeta["positions"], x.to(cuda))
+        torch.cuda.synchronize()
+    finally:
+        reset_context()
+    assert OM.rel_err(y.cpu(), ref) <= TOL
