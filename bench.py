@@ -110,6 +110,37 @@ def attn_work(b):
 
 
 # ---------------------------------------------------------------------------- clocks
+def nvml_handle(device_index: int):
+    """NVML handle of a CUDA device, matched by PCI bus id (CUDA and NVML may order
+    devices differently)."""
+    import pynvml
+    pynvml.nvmlInit()
+    pr = torch.cuda.get_device_properties(device_index)
+    bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+    try:
+        return pynvml.nvmlDeviceGetHandleByPciBusId_v2(bus)
+    except Exception:
+        return pynvml.nvmlDeviceGetHandleByIndex(device_index)
+
+
+def bind_to_gpu_cpus(device_index: int) -> list:
+    """Pin this process to the host cores NVML reports as close to the GPU (its NUMA
+    node), so pinned host buffers and the copy threads live next to the GPU's PCIe link.
+    Process-local; changes no GPU setting.  Returns the cores (empty if unknown)."""
+    try:
+        import pynvml
+        h = nvml_handle(device_index)
+        n = os.cpu_count() or 1
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (n + 63) // 64)
+        cpus = [64 * w + b for w, m in enumerate(words) for b in range(64) if (m >> b) & 1]
+        cpus = [c for c in cpus if c < n]
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return cpus
+    except Exception:
+        return []
+
+
 class ClockSampler:
     """Samples SM clock and throttle reasons through NVML while running (read-only)."""
 
@@ -131,7 +162,7 @@ class ClockSampler:
             import pynvml
             pynvml.nvmlInit()
             self._nv = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self._h = nvml_handle(self.index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
             self.ok = True
             self._t = threading.Thread(target=self._run, daemon=True)
@@ -504,6 +535,9 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if world > 1:
+        # the reference-arm CPU sample (rank 0, N=1 only) keeps every host core
+        bind_to_gpu_cpus(local)
     res = run_ours(args, rank, world, device)
 
     cpu = None

@@ -531,8 +531,8 @@ static int pod_attention(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, 
                                     a.q_stride_head, POD_KV, 1, 64)))
       return rc;
   }
-  LB_CUDA_CHECK(cudaFuncSetAttribute(k_pod_plan, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)(3 * sizeof(int) * B)));
+  if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(k_pod_plan), (int)(3 * sizeof(int) * B))))
+    return rc;
   k_pod_plan<<<1, 1024, 3 * sizeof(int) * B, st>>>(a.context_lens, a.cu_seqlens_q, B, (int)a.num_q_heads,
                                  (int)a.num_kv_heads, pl.split_tokens, pl.max_splits, pl.max_ctx,
                                  pl.pf_cap, pl.dec_cap, w.pf_items, w.counters, w.dec_items, w.status);
@@ -567,7 +567,7 @@ static int pod_attention(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, 
   p.n_prefill_ctas = pl.n_pf_ctas;
   p.scale_log2 = a.sm_scale * 1.4426950408889634f;
   p.qd_bytes = 4 * qd_rows * 128;
-  LB_CUDA_CHECK(cudaFuncSetAttribute(k_pod_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, POD_SMEM));
+  if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(k_pod_attn), POD_SMEM))) return rc;
   record_event(a.timing_events[0], st);
   k_pod_attn<<<pl.grid, POD_THREADS, POD_SMEM, st>>>(tmK, tmV, tmK64, tmV64, tmQd, tmQp, p);
   { int _rc = launched("k_pod_attn"); if (_rc) return _rc; }

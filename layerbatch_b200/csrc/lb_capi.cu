@@ -4,6 +4,8 @@
 #include <cstdarg>
 #include <cstring>
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "lb_gemm_launch.cuh"
 #include "lb_host.h"
@@ -100,6 +102,24 @@ int launched(const char* what) {
 
 void record_event(void* ev, cudaStream_t st) {
   if (ev) cudaEventRecord(static_cast<cudaEvent_t>(ev), st);
+}
+
+int ensure_smem_attr(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<const void*, int>, int>> done;  // ((func, dev), bytes)
+  int dev = 0;
+  LB_CUDA_CHECK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  for (auto& e : done)
+    if (e.first.first == func && e.first.second == dev) {
+      if (e.second >= bytes) return LB_OK;
+      LB_CUDA_CHECK(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+      e.second = bytes;
+      return LB_OK;
+    }
+  LB_CUDA_CHECK(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.push_back({{func, dev}, bytes});
+  return LB_OK;
 }
 
 int num_sms() {

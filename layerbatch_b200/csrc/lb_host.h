@@ -53,6 +53,11 @@ void record_event(void* ev, cudaStream_t st);
 int num_sms();
 int max_smem_optin();
 
+// Raise a kernel's dynamic shared-memory limit on the current device to at least `bytes`.
+// The attribute is set once per (kernel, device) and cached, so steady-state calls (and
+// calls made while a stream is being captured into a CUDA graph) make no runtime call.
+int ensure_smem_attr(const void* func, int bytes);
+
 // Bump allocator over a caller-provided workspace (256-byte aligned sub-buffers).
 struct Carve {
   uint8_t* base;
