@@ -15,6 +15,7 @@ __global__ void k_store_kvcache(const __nv_bfloat16* __restrict__ k, long long k
                                 __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
                                 const int32_t* __restrict__ slots, int n, long long num_slots,
                                 int row_elems) {
+  pdl_entry();
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (w >= n) return;
@@ -37,6 +38,7 @@ __global__ void k_store_kvcache(const __nv_bfloat16* __restrict__ k, long long k
 // fp32 operation order with explicit rounding (no contraction), so the bf16 results match
 // it up to the order of the sum of squares.
 __global__ void __launch_bounds__(256) k_attn_prologue(const LbPrologueArgs a) {
+  pdl_entry();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   const int Hq = (int)a.num_q_heads, Hkv = (int)a.num_kv_heads;
@@ -124,6 +126,7 @@ __global__ void k_pod_plan(const int32_t* __restrict__ ctx_lens, const int32_t* 
                            int max_ctx, int pf_cap, int dec_cap, int4* __restrict__ pf_items,
                            int* __restrict__ counters, int4* __restrict__ dec_items,
                            int* __restrict__ status) {
+  pdl_entry();
   __shared__ int s_pf[1024], s_full[1024], s_rem[1024];
   extern __shared__ int s_off[];  // [3 * B]: first prefill / full-split / last-split item
   const int tid = threadIdx.x;
@@ -233,6 +236,7 @@ __global__ void k_pod_merge(const int32_t* __restrict__ ctx_lens, const int32_t*
                             const float* __restrict__ part_o, const float* __restrict__ part_lse,
                             const __nv_bfloat16* __restrict__ gate, long long gst, long long gsh,
                             __nv_bfloat16* __restrict__ ogated, __nv_bfloat16* __restrict__ attn_out) {
+  pdl_entry();
   extern __shared__ float wts[];  // [max_splits][Hq]
   const int b = blockIdx.x;
   const int q0 = cu[b];
@@ -293,6 +297,7 @@ __global__ void k_pod_merge(const int32_t* __restrict__ ctx_lens, const int32_t*
 
 __global__ void k_f32_to_bf16(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst,
                               long long rows, int cols, long long ld_dst) {
+  pdl_entry();
   const long long n = rows * (cols / 4);
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
@@ -322,6 +327,7 @@ struct TpReduce {
 // in rank order in fp32, rounded once to bf16, written to out and to every other rank's
 // gather region (NVLink stores).  The last CTA publishes the epoch to the other ranks.
 __global__ void __launch_bounds__(256) k_tp_reduce(const TpReduce a) {
+  pdl_entry();
   if ((int)threadIdx.x < a.P) peer_wait(a.hdr + TPH_PART + threadIdx.x, a.hdr[TPH_EPOCH], a.status);
   __syncthreads();
   const int nmt = (a.N + GEMM_BM - 1) / GEMM_BM;
@@ -364,6 +370,7 @@ __global__ void __launch_bounds__(256) k_tp_reduce(const TpReduce a) {
 __global__ void __launch_bounds__(256) k_tp_gather(int* hdr, const __nv_bfloat16* __restrict__ gather,
                                                    __nv_bfloat16* __restrict__ out, int P, int rank,
                                                    int N, int H, int* status) {
+  pdl_entry();
   if ((int)threadIdx.x < P && (int)threadIdx.x != rank)
     peer_wait(hdr + TPH_GATH + threadIdx.x, hdr[TPH_EPOCH], status);
   __syncthreads();
@@ -533,7 +540,7 @@ static int pod_attention(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, 
   }
   if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(k_pod_plan), (int)(3 * sizeof(int) * B))))
     return rc;
-  k_pod_plan<<<1, 1024, 3 * sizeof(int) * B, st>>>(a.context_lens, a.cu_seqlens_q, B, (int)a.num_q_heads,
+  launch_k(k_pod_plan, 1, 1024, 3 * sizeof(int) * B, st, a.context_lens, a.cu_seqlens_q, B, (int)a.num_q_heads,
                                  (int)a.num_kv_heads, pl.split_tokens, pl.max_splits, pl.max_ctx,
                                  pl.pf_cap, pl.dec_cap, w.pf_items, w.counters, w.dec_items, w.status);
   { int _rc = launched("k_pod_plan"); if (_rc) return _rc; }
@@ -569,13 +576,13 @@ static int pod_attention(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, 
   p.qd_bytes = 4 * qd_rows * 128;
   if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(k_pod_attn), POD_SMEM))) return rc;
   record_event(a.timing_events[0], st);
-  k_pod_attn<<<pl.grid, POD_THREADS, POD_SMEM, st>>>(tmK, tmV, tmK64, tmV64, tmQd, tmQp, p);
+  launch_k(k_pod_attn, pl.grid, POD_THREADS, POD_SMEM, st, tmK, tmV, tmK64, tmV64, tmQd, tmQp, p);
   { int _rc = launched("k_pod_attn"); if (_rc) return _rc; }
   record_event(a.timing_events[1], st);
 
   const size_t merge_smem = sizeof(float) * (size_t)pl.max_splits * a.num_q_heads;
   LB_REQUIRE(merge_smem <= 48 * 1024, "lb_pod: too many decode splits (%d)", pl.max_splits);
-  k_pod_merge<<<B, 256, merge_smem, st>>>(a.context_lens, a.cu_seqlens_q, (int)a.num_q_heads,
+  launch_k(k_pod_merge, B, 256, merge_smem, st, a.context_lens, a.cu_seqlens_q, (int)a.num_q_heads,
                                           pl.split_tokens, pl.max_splits, pl.max_ctx, w.part_o,
                                           w.part_lse, p.gate, a.gate_stride_tok, a.gate_stride_head,
                                           p.ogated, p.attn_out);
@@ -645,13 +652,13 @@ static int tp_oproj(const LbPodArgs& a, const PodWs& w, cudaStream_t st, int pha
     d.status = w.status;
     const long long units = (long long)N * (Hd / 8) / P + Hd;
     const int grid = (int)std::max<long long>(1, std::min<long long>(nsm * 2, (units + 255) / 256));
-    k_tp_reduce<<<grid, 256, 0, st>>>(d);
+    launch_k(k_tp_reduce, grid, 256, 0, st, d);
     { int _rc = launched("k_tp_reduce"); if (_rc) return _rc; }
   }
   if (phases & LB_TP_PHASE_GATHER) {
     const long long units = (long long)N * (Hd / 8);
     const int grid = (int)std::max<long long>(1, std::min<long long>(nsm * 2, (units + 255) / 256));
-    k_tp_gather<<<grid, 256, 0, st>>>(hdr, gather_of(rank), static_cast<__nv_bfloat16*>(a.out), P,
+    launch_k(k_tp_gather, grid, 256, 0, st, hdr, gather_of(rank), static_cast<__nv_bfloat16*>(a.out), P,
                                        rank, N, Hd, w.status);
     { int _rc = launched("k_tp_gather"); if (_rc) return _rc; }
     record_event(a.timing_events[3], st);
@@ -694,7 +701,7 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
   }
   const long long n4 = (long long)N * (Hd / 4);
   const int g = (int)std::max<long long>(1, std::min<long long>(nsm * 4, (n4 + 255) / 256));
-  k_f32_to_bf16<<<g, 256, 0, st>>>(w.o32, static_cast<__nv_bfloat16*>(a.out), N, Hd, Hd);
+  launch_k(k_f32_to_bf16, g, 256, 0, st, w.o32, static_cast<__nv_bfloat16*>(a.out), N, Hd, Hd);
   { int _rc = launched("k_f32_to_bf16"); if (_rc) return _rc; }
   record_event(a.timing_events[3], st);
   return LB_OK;
@@ -717,7 +724,7 @@ int lb_store_kvcache(const void* k, int64_t k_stride, const void* v, int64_t v_s
   if (N == 0) return LB_OK;
   const int threads = 256;
   const long long blocks = (N * 32 + threads - 1) / threads;
-  k_store_kvcache<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_k(k_store_kvcache, (unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream), 
       static_cast<const __nv_bfloat16*>(k), k_stride, static_cast<const __nv_bfloat16*>(v),
       v_stride, static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),
       slot_mapping, (int)N, num_slots, (int)row_elems);
@@ -749,7 +756,7 @@ int lb_attn_prologue(const LbPrologueArgs* a, void* stream) {
   if (a->num_tokens == 0) return LB_OK;
   const long long warps = a->num_tokens * (a->num_q_heads + a->num_kv_heads);
   const long long blocks = (warps * 32 + 255) / 256;
-  k_attn_prologue<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(*a);
+  launch_k(k_attn_prologue, (unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream), *a);
   { int _rc = launched("k_attn_prologue"); if (_rc) return _rc; }
   return LB_OK;
 }

@@ -2,6 +2,7 @@
 // entry point and the device status word.
 #include <atomic>
 #include <cstdarg>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <utility>
@@ -98,6 +99,14 @@ int launched(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(LB_ERR_CUDA, "launch of %s failed: %s", what, cudaGetErrorString(e));
   return LB_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LB_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 void record_event(void* ev, cudaStream_t st) {

@@ -25,6 +25,16 @@ __device__ __forceinline__ void report(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
 
+// Programmatic dependent launch: every kernel of the library first lets the next kernel
+// in its stream be scheduled (it launches once all of this grid's CTAs have started),
+// then waits until the previous kernel has completed and its memory is visible.  The
+// next kernel's launch latency and prologue thus overlap this kernel's work and tail.
+// Both are no-ops for a kernel launched without the programmatic-serialization
+// attribute.
+__device__ __forceinline__ void pdl_entry() {
+  asm volatile("griddepcontrol.launch_dependents;\n\tgriddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

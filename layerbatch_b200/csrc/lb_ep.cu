@@ -79,6 +79,7 @@ __device__ __forceinline__ unsigned ep_dest_mask(const int32_t* ids, int k, int 
 __global__ void __launch_bounds__(1024) k_ep_route(const int32_t* __restrict__ ids, int T, int k,
                                                    int epr, int P, int32_t* __restrict__ slot,
                                                    int* __restrict__ send_count, int* status) {
+  pdl_entry();
   __shared__ int s_w[32][LB_EP_MAX_RANKS];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int per = (T + 1023) / 1024;
@@ -145,6 +146,7 @@ struct EpDispatch {
 // region (NVLink stores for other ranks), with the k ids and weights.  The last CTA to
 // finish publishes the row counts and this call's epoch to every destination.
 __global__ void __launch_bounds__(256) k_ep_dispatch(const EpDispatch d) {
+  pdl_entry();
   const int lane = threadIdx.x & 31;
   const int wpb = blockDim.x / 32;
   const int nvec = d.H / 8;
@@ -200,6 +202,7 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const EpDispatch d) {
 // recv region (past that source's count) as routed nowhere.
 __global__ void __launch_bounds__(256) k_ep_recv_prepare(int* hdr, int32_t* __restrict__ recv_ids,
                                                          int P, int C, int k, int* status) {
+  pdl_entry();
   __shared__ int s_cnt[LB_EP_MAX_RANKS];
   if ((int)threadIdx.x < P) {
     const int epoch = hdr[EPH_EPOCH];
@@ -235,6 +238,7 @@ struct EpReturn {
 // source's region.  The last CTA publishes the epoch to every source.
 template <int MAXS>  // H <= MAXS * 256
 __global__ void __launch_bounds__(256) k_ep_return(const EpReturn d) {
+  pdl_entry();
   const int lane = threadIdx.x & 31;
   const int wpb = blockDim.x / 32;
   int* hdr = reinterpret_cast<int*>(d.peers.p[d.rank]);
@@ -297,6 +301,7 @@ __global__ void __launch_bounds__(256) k_ep_combine(const __nv_bfloat16* __restr
                                                     int H, int P, int C, int* hdr,
                                                     const __nv_bfloat16* ret, int* status,
                                                     __nv_bfloat16* __restrict__ out) {
+  pdl_entry();
   if ((int)threadIdx.x < P) peer_wait(hdr + EPH_RET + threadIdx.x, hdr[EPH_EPOCH], status);
   __syncthreads();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
@@ -480,7 +485,7 @@ int lb_ep_moe_forward(const LbEpArgs* a, void* stream) {
                        static_cast<const __nv_bfloat16*>(a->w_shared_expert_gate), H, w.m.perm_w, st);
       if (rc) return rc;
     }
-    k_ep_route<<<1, 1024, 0, st>>>(w.m.ids, T, k, epr, P, w.slot, w.send_count, w.m.status);
+    launch_k(k_ep_route, 1, 1024, 0, st, w.m.ids, T, k, epr, P, w.slot, w.send_count, w.m.status);
     if ((rc = launched("k_ep_route"))) return rc;
     EpDispatch d;
     d.x = x;
@@ -500,7 +505,7 @@ int lb_ep_moe_forward(const LbEpArgs* a, void* stream) {
     d.peers = peers;
     d.status = w.m.status;
     const int grid = std::max(1, std::min(nsm * 2, (T + 7) / 8));
-    k_ep_dispatch<<<grid, 256, 0, st>>>(d);
+    launch_k(k_ep_dispatch, grid, 256, 0, st, d);
     if ((rc = launched("k_ep_dispatch"))) return rc;
     record_event(a->timing_events[1], st);
   }
@@ -510,7 +515,7 @@ int lb_ep_moe_forward(const LbEpArgs* a, void* stream) {
     {
       const long long n = (long long)P * C * k;
       const int grid = (int)std::max<long long>(1, std::min<long long>(nsm, (n + 255) / 256));
-      k_ep_recv_prepare<<<grid, 256, 0, st>>>(hdr, recv_ids, P, C, k, w.m.status);
+      launch_k(k_ep_recv_prepare, grid, 256, 0, st, hdr, recv_ids, P, C, k, w.m.status);
       if ((rc = launched("k_ep_recv_prepare"))) return rc;
     }
     MoeCore c{};
@@ -549,11 +554,11 @@ int lb_ep_moe_forward(const LbEpArgs* a, void* stream) {
     d.status = w.m.status;
     const int grid = std::max(1, std::min(nsm * 2, (P * C + 7) / 8));
     if (H <= 2048)
-      k_ep_return<8><<<grid, 256, 0, st>>>(d);
+      launch_k(k_ep_return<8>, grid, 256, 0, st, d);
     else if (H <= 4096)
-      k_ep_return<16><<<grid, 256, 0, st>>>(d);
+      launch_k(k_ep_return<16>, grid, 256, 0, st, d);
     else
-      k_ep_return<32><<<grid, 256, 0, st>>>(d);
+      launch_k(k_ep_return<32>, grid, 256, 0, st, d);
     if ((rc = launched("k_ep_return"))) return rc;
   }
 
@@ -562,11 +567,11 @@ int lb_ep_moe_forward(const LbEpArgs* a, void* stream) {
     const __nv_bfloat16* ret = reinterpret_cast<const __nv_bfloat16*>(own + L.ret);
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a->out);
     if (H <= 2048)
-      k_ep_combine<8><<<blocks, 256, 0, st>>>(w.m.yw, w.slot, T, H, P, C, hdr, ret, w.m.status, out);
+      launch_k(k_ep_combine<8>, blocks, 256, 0, st, w.m.yw, w.slot, T, H, P, C, hdr, ret, w.m.status, out);
     else if (H <= 4096)
-      k_ep_combine<16><<<blocks, 256, 0, st>>>(w.m.yw, w.slot, T, H, P, C, hdr, ret, w.m.status, out);
+      launch_k(k_ep_combine<16>, blocks, 256, 0, st, w.m.yw, w.slot, T, H, P, C, hdr, ret, w.m.status, out);
     else
-      k_ep_combine<32><<<blocks, 256, 0, st>>>(w.m.yw, w.slot, T, H, P, C, hdr, ret, w.m.status, out);
+      launch_k(k_ep_combine<32>, blocks, 256, 0, st, w.m.yw, w.slot, T, H, P, C, hdr, ret, w.m.status, out);
     if ((rc = launched("k_ep_combine"))) return rc;
   }
   return LB_OK;

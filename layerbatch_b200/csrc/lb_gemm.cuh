@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA_sh,
            const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmB_sh0,
            const __grid_constant__ CUtensorMap tmB_sh1, const GemmArgs p) {
+  pdl_entry();
   using S = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(

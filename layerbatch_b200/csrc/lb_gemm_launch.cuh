@@ -17,7 +17,7 @@ int launch_gemm(const CUtensorMap& tA, const CUtensorMap& tAsh, const CUtensorMa
     return fail(LB_ERR_UNSUPPORTED, "gemm: %zu bytes of shared memory exceed the limit", smem);
   if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)smem)) return rc;
   if (grid <= 0) return LB_OK;
-  kern<<<grid, GEMM_THREADS, smem, st>>>(tA, tAsh, tB, tBsh0, tBsh1, a);
+  launch_k(kern, grid, GEMM_THREADS, smem, st, tA, tAsh, tB, tBsh0, tBsh1, a);
   { int _rc = launched("kern"); if (_rc) return _rc; }
   return LB_OK;
 }

@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/layerbatch_b200.h"
 
@@ -48,6 +49,28 @@ int make_tmap_bf16_3d_box(CUtensorMap* m, const void* base, uint64_t d2, uint64_
 
 // Count one kernel launch of this library and check the launch error.
 int launched(const char* what);
+
+// Whether kernels are launched with programmatic stream serialization (programmatic
+// dependent launch); on unless the environment sets LB_PDL=0.
+bool pdl_enabled();
+
+// Launch `kern` on `st` with the programmatic-serialization attribute (see pdl_entry in
+// the device helpers); errors surface through launched().
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  (void)cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 void record_event(void* ev, cudaStream_t st);
 
 int num_sms();

@@ -32,6 +32,7 @@ __global__ void k_router_topk(const __nv_bfloat16* __restrict__ logits, long lon
                               __nv_bfloat16* __restrict__ wb, const __nv_bfloat16* __restrict__ x,
                               const __nv_bfloat16* __restrict__ wsg, int H,
                               float* __restrict__ sg) {
+  pdl_entry();
   const int warps_per_block = blockDim.x / 32;
   const int t = blockIdx.x * warps_per_block + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -113,6 +114,7 @@ __global__ void k_router_topk(const __nv_bfloat16* __restrict__ logits, long lon
 // routing is given and the top-k kernel (which also computes it) does not run.
 __global__ void k_shared_gate(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wsg,
                               int T, int H, float* __restrict__ sg) {
+  pdl_entry();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (t >= T) return;
@@ -135,6 +137,7 @@ __global__ void k_shared_gate(const __nv_bfloat16* __restrict__ x, const __nv_bf
 // counts[1+e] += #pairs routed to local expert e (block-local histogram first).
 __global__ void k_moe_count(const int32_t* __restrict__ ids, int n, int expert_base, int nl,
                             int* __restrict__ counts) {
+  pdl_entry();
   extern __shared__ int hist[];
   for (int i = threadIdx.x; i < nl; i += blockDim.x) hist[i] = 0;
   __syncthreads();
@@ -151,6 +154,7 @@ __global__ void k_moe_count(const int32_t* __restrict__ ids, int n, int expert_b
 // group 0 (shared expert) holding T rows.  One block of 1024 threads, G <= 2047.
 __global__ void k_moe_scan(const int* __restrict__ counts, int G, int T,
                            int* __restrict__ row_start, int* __restrict__ mtile_start) {
+  pdl_entry();
   __shared__ int s_rows[1024], s_tiles[1024];
   const int tid = threadIdx.x;
   int r[2], tl[2];
@@ -194,6 +198,7 @@ __global__ void k_moe_scatter(const int32_t* __restrict__ ids, const float* __re
                               int T, int k, int expert_base, const int* __restrict__ row_start,
                               int32_t* __restrict__ perm_token, float* __restrict__ perm_w,
                               int32_t* __restrict__ row_of) {
+  pdl_entry();
   __shared__ int warp_cnt[32];
   const int g = blockIdx.x + 1;
   const int e_global = expert_base + blockIdx.x;
@@ -234,6 +239,7 @@ __global__ void k_moe_scatter(const int32_t* __restrict__ ids, const float* __re
 
 // Identity map of the shared-expert rows [0, T).
 __global__ void k_iota(int32_t* __restrict__ p, int n) {
+  pdl_entry();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = i;
 }
 
@@ -242,6 +248,7 @@ __global__ void k_gather_rows(const __nv_bfloat16* __restrict__ x, int H,
                               const int32_t* __restrict__ perm_token,
                               const int* __restrict__ row_end_ptr, int row_begin,
                               __nv_bfloat16* __restrict__ a_packed) {
+  pdl_entry();
   const int row_end = *row_end_ptr;
   const int vec_per_row = H / 8;
   const long long n = (long long)(row_end - row_begin) * vec_per_row;
@@ -324,7 +331,7 @@ int launch_topk(const __nv_bfloat16* logits, long long ld, int T, int E, int k, 
   const int vpl = (E + 31) / 32;
 #define LB_TOPK_CASE(V)                                                                   \
   if (vpl <= V) {                                                                         \
-    k_router_topk<V><<<grid, threads, 0, st>>>(logits, ld, T, E, k, ids, wf, wb, x, wsg, H, \
+    launch_k(k_router_topk<V>, grid, threads, 0, st, logits, ld, T, E, k, ids, wf, wb, x, wsg, H, \
                                                sg);                                       \
     { int _rc = launched("k_router_topk"); if (_rc) return _rc; }                                          \
     return LB_OK;                                                                         \
@@ -348,17 +355,17 @@ static int run_permute(const int32_t* ids, const float* wf, int T, int k, int ex
   const int n = T * k;
   if (n > 0) {
     const int grid = std::min(num_sms() * 2, (n + 1023) / 1024);
-    k_moe_count<<<std::max(grid, 1), 1024, sizeof(int) * nl, st>>>(ids, n, expert_base, nl, counts);
+    launch_k(k_moe_count, std::max(grid, 1), 1024, sizeof(int) * nl, st, ids, n, expert_base, nl, counts);
     { int _rc = launched("k_moe_count"); if (_rc) return _rc; }
   }
-  k_moe_scan<<<1, 1024, 0, st>>>(counts, G, T, row_start, mtile_start);
+  launch_k(k_moe_scan, 1, 1024, 0, st, counts, G, T, row_start, mtile_start);
   { int _rc = launched("k_moe_scan"); if (_rc) return _rc; }
   if (T > 0) {
-    k_iota<<<std::min(1024, (T + 255) / 256), 256, 0, st>>>(perm_token, T);
+    launch_k(k_iota, std::min(1024, (T + 255) / 256), 256, 0, st, perm_token, T);
     { int _rc = launched("k_iota"); if (_rc) return _rc; }
   }
   if (n > 0) {
-    k_moe_scatter<<<nl, 256, 0, st>>>(ids, wf, T, k, expert_base, row_start, perm_token, perm_w,
+    launch_k(k_moe_scatter, nl, 256, 0, st, ids, wf, T, k, expert_base, row_start, perm_token, perm_w,
                                       row_of);
     { int _rc = launched("k_moe_scatter"); if (_rc) return _rc; }
   }
@@ -373,6 +380,7 @@ static int run_permute(const int32_t* ids, const float* wf, int T, int k, int ex
 // result equals the sequential definition bit for bit.
 __global__ void k_perm_chunk_hist(const int32_t* __restrict__ ids, int T, int k, int expert_base,
                                   int nl, int* __restrict__ chunk_hist) {
+  pdl_entry();
   extern __shared__ int hist[];
   for (int i = threadIdx.x; i < nl; i += blockDim.x) hist[i] = 0;
   __syncthreads();
@@ -393,6 +401,7 @@ __global__ void k_perm_chunk_hist(const int32_t* __restrict__ ids, int T, int k,
 // expert's total into counts[1 + e].
 __global__ void k_perm_expert_scan(int* __restrict__ chunk_hist, int n_chunks, int nl,
                                    int* __restrict__ counts) {
+  pdl_entry();
   const int e = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (e >= nl) return;
@@ -422,6 +431,7 @@ __global__ void k_perm_chunk_scatter(const int32_t* __restrict__ ids, const floa
                                      const int* __restrict__ row_start,
                                      int32_t* __restrict__ perm_token, float* __restrict__ perm_w,
                                      int32_t* __restrict__ row_of) {
+  pdl_entry();
   extern __shared__ int cnt[];
   const int lane = threadIdx.x;
   const int nc = gridDim.x;
@@ -463,6 +473,7 @@ __global__ void k_moe_combine(const __nv_bfloat16* __restrict__ yw, const int32_
                               const __nv_bfloat16* __restrict__ pair_rows,
                               const int32_t* __restrict__ pair_index,
                               __nv_bfloat16* __restrict__ out) {
+  pdl_entry();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (t >= T) return;
@@ -518,21 +529,21 @@ static int run_permute_chunked(const int32_t* ids, const float* wf, int T, int k
   const int nc = perm_chunks(T, k);
   LB_CUDA_CHECK(cudaMemsetAsync(row_of, 0xff, sizeof(int32_t) * (size_t)n, st));
   if (nc > 0 && nl > 0) {
-    k_perm_chunk_hist<<<nc, PERM_CHUNK, sizeof(int) * nl, st>>>(ids, T, k, expert_base, nl, chunk_hist);
+    launch_k(k_perm_chunk_hist, nc, PERM_CHUNK, sizeof(int) * nl, st, ids, T, k, expert_base, nl, chunk_hist);
     { int _rc = launched("k_perm_chunk_hist"); if (_rc) return _rc; }
-    k_perm_expert_scan<<<(nl + 7) / 8, 256, 0, st>>>(chunk_hist, nc, nl, counts);
+    launch_k(k_perm_expert_scan, (nl + 7) / 8, 256, 0, st, chunk_hist, nc, nl, counts);
     { int _rc = launched("k_perm_expert_scan"); if (_rc) return _rc; }
   } else if (nl > 0) {
     LB_CUDA_CHECK(cudaMemsetAsync(counts, 0, sizeof(int) * (nl + 2), st));
   }
-  k_moe_scan<<<1, 1024, 0, st>>>(counts, nl + 1, T0, row_start, mtile_start);
+  launch_k(k_moe_scan, 1, 1024, 0, st, counts, nl + 1, T0, row_start, mtile_start);
   { int _rc = launched("k_moe_scan"); if (_rc) return _rc; }
   if (T0 > 0) {
-    k_iota<<<std::min(1024, (T0 + 255) / 256), 256, 0, st>>>(perm_token, T0);
+    launch_k(k_iota, std::min(1024, (T0 + 255) / 256), 256, 0, st, perm_token, T0);
     { int _rc = launched("k_iota"); if (_rc) return _rc; }
   }
   if (nc > 0 && nl > 0) {
-    k_perm_chunk_scatter<<<nc, 32, sizeof(int) * nl, st>>>(ids, wf, T, k, expert_base, nl, chunk_hist,
+    launch_k(k_perm_chunk_scatter, nc, 32, sizeof(int) * nl, st, ids, wf, T, k, expert_base, nl, chunk_hist,
                                                            row_start, perm_token, perm_w, row_of);
     { int _rc = launched("k_perm_chunk_scatter"); if (_rc) return _rc; }
   }
@@ -555,7 +566,7 @@ int moe_core(const MoeCore& c, const MoeWs& w, cudaStream_t st) {
   if (nl > 0) {
     const long long vec = (long long)T * k * (H / 8);
     const int grid = (int)std::max<long long>(1, std::min<long long>(num_sms() * 8, (vec + 255) / 256));
-    k_gather_rows<<<grid, 256, 0, st>>>(c.x_r, H, w.perm_token, w.row_start + G, T0, w.a_packed);
+    launch_k(k_gather_rows, grid, 256, 0, st, c.x_r, H, w.perm_token, w.row_start + G, T0, w.a_packed);
     { int _rc = launched("k_gather_rows"); if (_rc) return _rc; }
   }
   const long long rows = (long long)T0 + (long long)T * k;
@@ -760,7 +771,7 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
     wf = a->topk_weights_f32;
     if (shared) {
       // the shared-expert gate lands in perm_w[0:T) (see below)
-      k_shared_gate<<<(T * 32 + 255) / 256, 256, 0, st>>>(
+      launch_k(k_shared_gate, (T * 32 + 255) / 256, 256, 0, st, 
           x, static_cast<const __nv_bfloat16*>(a->w_shared_expert_gate), T, H, w.perm_w);
       { int _rc = launched("k_shared_gate"); if (_rc) return _rc; }
     }
@@ -810,11 +821,11 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a->out);
     const __nv_bfloat16* pr = static_cast<const __nv_bfloat16*>(a->pair_rows);
     if (H <= 2048)
-      k_moe_combine<8><<<blocks, 256, 0, st>>>(w.yw, w.row_of, T, k, H, shared, pr, a->pair_index, out);
+      launch_k(k_moe_combine<8>, blocks, 256, 0, st, w.yw, w.row_of, T, k, H, shared, pr, a->pair_index, out);
     else if (H <= 4096)
-      k_moe_combine<16><<<blocks, 256, 0, st>>>(w.yw, w.row_of, T, k, H, shared, pr, a->pair_index, out);
+      launch_k(k_moe_combine<16>, blocks, 256, 0, st, w.yw, w.row_of, T, k, H, shared, pr, a->pair_index, out);
     else
-      k_moe_combine<32><<<blocks, 256, 0, st>>>(w.yw, w.row_of, T, k, H, shared, pr, a->pair_index, out);
+      launch_k(k_moe_combine<32>, blocks, 256, 0, st, w.yw, w.row_of, T, k, H, shared, pr, a->pair_index, out);
     { int _rc = launched("k_moe_combine"); if (_rc) return _rc; }
   }
   (void)E;

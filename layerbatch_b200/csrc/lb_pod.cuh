@@ -171,6 +171,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
                const __grid_constant__ CUtensorMap tmK64, const __grid_constant__ CUtensorMap tmV64,
                const __grid_constant__ CUtensorMap tmQd, const __grid_constant__ CUtensorMap tmQp,
                const PodParams p) {
+  pdl_entry();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
