@@ -261,7 +261,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
-__device__ __forceinline__ float sigmoid_f(float g) { return 1.0f / (1.0f + __expf(-g)); }
+// sigmoid with the fast exponential and reciprocal (a few ulp of fp32; the result is
+// rounded to bf16 right after)
+__device__ __forceinline__ float sigmoid_f(float g) { return __fdividef(1.0f, 1.0f + __expf(-g)); }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
@@ -300,12 +302,18 @@ __device__ __forceinline__ void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+#ifndef LB_PEER_WAIT_CYCLES
+// ~1 s at 1.9 GHz: how long a kernel waits for another GPU's flag before it reports
+// LB_DEV_TIMEOUT (a peer that died or never made the call) and gives up.
+#define LB_PEER_WAIT_CYCLES (1ull << 31)
+#endif
+
 // Bounded wait until a flag another GPU writes reaches `epoch` (epochs only grow).
-// Gives up after LB_SPIN_LIMIT_CYCLES with LB_DEV_TIMEOUT in the status word.
+// Gives up after LB_PEER_WAIT_CYCLES with LB_DEV_TIMEOUT in the status word.
 __device__ __forceinline__ bool peer_wait(const int* flag, int epoch, int* status) {
   const long long t0 = clock64();
   while (ld_acquire_sys(flag) - epoch < 0) {
-    if (clock64() - t0 > (long long)LB_SPIN_LIMIT_CYCLES) {
+    if (clock64() - t0 > (long long)LB_PEER_WAIT_CYCLES) {
       report(status, LB_DEV_TIMEOUT);
       return false;
     }

@@ -76,3 +76,31 @@ def test_ep_nvlink_emulated_ranks(cuda, P, E, k, Ts, C):
                 assert OM.rel_err(outs[r].cpu(), ref.cpu()) <= TOL, (call, r)
     finally:
         exs[0].close()
+
+
+def test_peer_wait_times_out_and_reports(cuda):
+    """Failure detection without a fault: rank 0 of an emulated pair runs its phases but
+    rank 1 never makes the call, so the flags rank 0 waits for are never set.  Each wait
+    gives up after its time limit (~1 s), the kernels finish, the workspace status word
+    reads LB_DEV_TIMEOUT on the host, and the context keeps working."""
+    H, E, I, k, C = 2048, 64, 512, 8, 64
+    p = W.make_moe_params(H, E, I, I, k, seed=8)
+    pd = p.to(cuda)
+    blks = ep_blocks(pd, 2, H, E, k, I, cuda)
+    exs = EPExchange.emulated(2, C, H, k, device=cuda)
+    try:
+        x = W.make_moe_input(32, H, seed=9).to(cuda)
+        ep_moe_forward_nvlink(blks[0], x, exs[0], ws_tag="ep_dead_peer")   # rank 1 absent
+        torch.cuda.synchronize()
+        ws = ops._WS[(torch.cuda.current_device(), "ep_dead_peer")]
+        assert ops.device_status(ws) == 1          # LB_DEV_TIMEOUT
+        # the device is still usable: a normal call runs and is correct
+        y, logits, ids, _ = ops.moe_forward(x, pd.router, pd.gate_up, pd.down, pd.sh_gate,
+                                            pd.sh_up, pd.sh_down, pd.sh_gate_w, k,
+                                            return_routing=True, ws_tag="ep_after_timeout")
+        _, wf, _ = ops.router_topk(logits, k)
+        torch.cuda.synchronize()
+        y32 = OM.moe_block_fp32(x.cpu(), p, ids.cpu().long(), wf.cpu())
+        assert OM.rel_err(y.cpu(), y32) <= TOL
+    finally:
+        exs[0].close()

@@ -68,3 +68,26 @@ def test_tp_oproj_peer_reduction_emulated(cuda, P, Hq, Hkv, decode, prefill):
     finally:
         if exs is not None:
             exs[0].close()
+
+
+def test_tp_reduce_wait_times_out_and_reports(cuda):
+    """Rank 0 of an emulated TP pair reduces while rank 1 never computes its partials: the
+    owner's wait gives up after its time limit with LB_DEV_TIMEOUT, and the context
+    stays usable."""
+    b = W.make_attn_batch([700, 900], [], seed=45).to(cuda)
+    exs = TPExchange.emulated(2, 256, 2048, device=cuda)
+    try:
+        sh = S.attention_shard(16, 2, 0, 2)
+        qs, gs, kc, vc, wo = S.shard_attention_tensors(sh, b.q, b.gate, b.k_cache, b.v_cache,
+                                                       b.w_o, 256)
+        ops.pod_attn_oproj(qs, gs, kc, vc, b.block_tables, b.context_lens, b.cu_seqlens_q, wo,
+                           b.scale, max_q_len=1, ws_tag="tp_dead_peer", tp=exs[0])
+        torch.cuda.synchronize()
+        assert ops.device_status(ops._WS[(torch.cuda.current_device(), "tp_dead_peer")]) == 1
+        full = ops.pod_attn_oproj(b.q, b.gate, b.k_cache, b.v_cache, b.block_tables,
+                                  b.context_lens, b.cu_seqlens_q, b.w_o, b.scale, max_q_len=1,
+                                  ws_tag="tp_after_timeout")
+        torch.cuda.synchronize()
+        assert bool(torch.isfinite(full.float()).all())
+    finally:
+        exs[0].close()
