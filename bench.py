@@ -298,11 +298,23 @@ def run_ours(args, rank, world, device):
         W.apply_zipf_bias(p, x)
         moe = (p, x)
         if sharded:
+            # Experts are placed by popularity (heaviest first to the least-loaded rank),
+            # from the routing counts of a separate calibration batch of the same
+            # distribution summed over the ranks, so every rank computes the same placement.
+            from layerbatch_b200.engine.ep import placement_by_load
+            with torch.no_grad():
+                xc = W.make_moe_input(T_moe, 2048, seed=5000 + rank, device=device)
+                xc[:, 0] = x[:, 0]          # the Zipf bias column of the benchmark inputs
+                ids_c, _, _ = ops.router_topk(ops.gemm(xc, p.router), 10)
+                loads = torch.bincount(ids_c.reshape(-1).long(), minlength=512).float()
+                torch.distributed.all_reduce(loads)
+                del xc
+            placement = placement_by_load(loads, world)
             ep_block = Qwen3_5SparseMoeBlock(2048, 512, 10, 512, 512, ep_rank=rank,
                                              ep_size=world).to(torch.bfloat16).to(device)
             with torch.no_grad():
                 ep_block.gate.weight.copy_(p.router)
-                ep_block.load_expert_shard(p.gate_up, p.down)
+                ep_block.load_expert_shard(p.gate_up, p.down, placement=placement)
                 ep_block.shared_expert.gate_proj.weight.copy_(p.sh_gate)
                 ep_block.shared_expert.up_proj.weight.copy_(p.sh_up)
                 ep_block.shared_expert.down_proj.weight.copy_(p.sh_down)
@@ -398,7 +410,7 @@ def run_ours(args, rank, world, device):
         res["moe_gemm"] = {"gate_up_ms": t_g1 * 1e3, "down_ms": t_g2 * 1e3}
     res["parallelism"] = (f"tp{tp} x dp{world // tp} attention (KV-head shards, o_proj GEMM "
                           f"reducing over NVLink peer memory), ep{world} MoE (NVLink "
-                          f"peer-memory dispatch/return)"
+                          f"peer-memory dispatch/return, experts placed by popularity)"
                           if sharded else
                           ("single GPU" if world == 1 else
                            f"dp{world}: per-rank batches, experts replicated"))

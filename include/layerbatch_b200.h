@@ -201,6 +201,12 @@ typedef struct LbEpArgs {
                               * phases interleaved on one device in tests) */
   void* timing_events[4];    /* optional: around the dispatch ([0],[1]) and the expert
                               * GEMMs ([2],[3]) */
+  const int32_t* expert_slot; /* optional [E] device array: expert e lives in slot
+                               * expert_slot[e] (rank slot / (E/P), local index slot %
+                               * (E/P) of that rank's w_gate_up / w_down); NULL = expert e
+                               * in slot e (contiguous ranges).  Lets a placement by
+                               * popularity balance the ranks' expert load.  Must be a
+                               * permutation of [0, E) and the same on every rank. */
 } LbEpArgs;
 
 int lb_ep_workspace_size(const LbEpArgs* args, size_t* bytes);

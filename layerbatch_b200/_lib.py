@@ -62,7 +62,7 @@ class LbEpArgs(C.Structure):
         ("w_shared_gate", vp), ("w_shared_up", vp), ("w_shared_down", vp),
         ("w_shared_expert_gate", vp), ("out", vp), ("peer_bufs", vp * LB_EP_MAX_RANKS),
         ("workspace", vp), ("workspace_bytes", C.c_size_t), ("phases", i32),
-        ("timing_events", vp * 4),
+        ("timing_events", vp * 4), ("expert_slot", vp),
     ]
 
 

@@ -57,12 +57,14 @@ struct EpPeers {
   uint8_t* p[LB_EP_MAX_RANKS];
 };
 
-// Ranks owning at least one of a token's k experts (bit r), experts in ranges of `epr`.
+// Ranks owning at least one of a token's k experts (bit r): expert e sits in slot
+// slot[e] (identity when slot is null), rank = slot / epr.
 __device__ __forceinline__ unsigned ep_dest_mask(const int32_t* ids, int k, int epr, int P,
-                                                 int* status) {
+                                                 const int32_t* slot, int* status) {
   unsigned m = 0;
   for (int j = 0; j < k; ++j) {
-    const int e = ids[j];
+    int e = ids[j];
+    if (slot && e >= 0 && e < epr * P) e = slot[e];
     const int r = e >= 0 ? e / epr : -1;
     if (r < 0 || r >= P) {
       report(status, LB_DEV_BAD_INDEX);
@@ -78,7 +80,9 @@ __device__ __forceinline__ unsigned ep_dest_mask(const int32_t* ids, int k, int 
 // row to rank r (token order), -1 if none; send_count[r] = rows sent to r.
 __global__ void __launch_bounds__(1024) k_ep_route(const int32_t* __restrict__ ids, int T, int k,
                                                    int epr, int P, int32_t* __restrict__ slot,
-                                                   int* __restrict__ send_count, int* status) {
+                                                   int* __restrict__ send_count,
+                                                   const int32_t* __restrict__ expert_slot,
+                                                   int* status) {
   pdl_entry();
   __shared__ int s_w[32][LB_EP_MAX_RANKS];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -88,7 +92,7 @@ __global__ void __launch_bounds__(1024) k_ep_route(const int32_t* __restrict__ i
 #pragma unroll
   for (int r = 0; r < LB_EP_MAX_RANKS; ++r) cnt[r] = 0;
   for (int t = t0; t < t1; ++t) {
-    const unsigned m = ep_dest_mask(ids + (long long)t * k, k, epr, P, status);
+    const unsigned m = ep_dest_mask(ids + (long long)t * k, k, epr, P, expert_slot, status);
 #pragma unroll
     for (int r = 0; r < LB_EP_MAX_RANKS; ++r) cnt[r] += (m >> r) & 1u;
   }
@@ -124,7 +128,7 @@ __global__ void __launch_bounds__(1024) k_ep_route(const int32_t* __restrict__ i
 #pragma unroll
   for (int r = 0; r < LB_EP_MAX_RANKS; ++r) base[r] = s_w[wid][r] + incl[r] - cnt[r];
   for (int t = t0; t < t1; ++t) {
-    const unsigned m = ep_dest_mask(ids + (long long)t * k, k, epr, P, nullptr);
+    const unsigned m = ep_dest_mask(ids + (long long)t * k, k, epr, P, expert_slot, nullptr);
     for (int r = 0; r < P; ++r) slot[(long long)t * P + r] = ((m >> r) & 1u) ? base[r]++ : -1;
   }
 }
@@ -199,9 +203,13 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const EpDispatch d) {
 
 // ------------------------------------------------------------------------------ owner
 // Waits for every source's dispatch of this call, then marks the unused rows of each
-// recv region (past that source's count) as routed nowhere.
+// recv region (past that source's count) as routed nowhere and, with a placement table,
+// turns the received global expert ids into slots (this rank's experts are then the slots
+// [rank * E/P, (rank + 1) * E/P), the range the grouped GEMMs select).
 __global__ void __launch_bounds__(256) k_ep_recv_prepare(int* hdr, int32_t* __restrict__ recv_ids,
-                                                         int P, int C, int k, int* status) {
+                                                         int P, int C, int k, int E,
+                                                         const int32_t* __restrict__ expert_slot,
+                                                         int* status) {
   pdl_entry();
   __shared__ int s_cnt[LB_EP_MAX_RANKS];
   if ((int)threadIdx.x < P) {
@@ -220,7 +228,12 @@ __global__ void __launch_bounds__(256) k_ep_recv_prepare(int* hdr, int32_t* __re
        f += (long long)gridDim.x * blockDim.x) {
     const long long row = f / k;
     const int s = (int)(row / C), i = (int)(row - (long long)s * C);
-    if (i >= s_cnt[s]) recv_ids[f] = -1;
+    if (i >= s_cnt[s]) {
+      recv_ids[f] = -1;
+    } else if (expert_slot) {
+      const int e = recv_ids[f];
+      recv_ids[f] = (e >= 0 && e < E) ? expert_slot[e] : -1;
+    }
   }
 }
 
@@ -485,7 +498,8 @@ int lb_ep_moe_forward(const LbEpArgs* a, void* stream) {
                        static_cast<const __nv_bfloat16*>(a->w_shared_expert_gate), H, w.m.perm_w, st);
       if (rc) return rc;
     }
-    launch_k(k_ep_route, 1, 1024, 0, st, w.m.ids, T, k, epr, P, w.slot, w.send_count, w.m.status);
+    launch_k(k_ep_route, 1, 1024, 0, st, w.m.ids, T, k, epr, P, w.slot, w.send_count,
+             a->expert_slot, w.m.status);
     if ((rc = launched("k_ep_route"))) return rc;
     EpDispatch d;
     d.x = x;
@@ -515,7 +529,8 @@ int lb_ep_moe_forward(const LbEpArgs* a, void* stream) {
     {
       const long long n = (long long)P * C * k;
       const int grid = (int)std::max<long long>(1, std::min<long long>(nsm, (n + 255) / 256));
-      launch_k(k_ep_recv_prepare, grid, 256, 0, st, hdr, recv_ids, P, C, k, w.m.status);
+      launch_k(k_ep_recv_prepare, grid, 256, 0, st, hdr, recv_ids, P, C, k, E, a->expert_slot,
+               w.m.status);
       if ((rc = launched("k_ep_recv_prepare"))) return rc;
     }
     MoeCore c{};

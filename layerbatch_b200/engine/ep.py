@@ -66,8 +66,29 @@ def ep_args(block, x: torch.Tensor, ex: EPExchange, out: torch.Tensor, phases: i
     for r, p in enumerate(ex.peers):
         a.peer_bufs[r] = p
     a.phases = phases
+    slot = getattr(block, "expert_slot", None)
+    if slot is not None:
+        a.expert_slot = slot.data_ptr()
     ops._events(a, events)
     return a
+
+
+def placement_by_load(loads, world: int) -> torch.Tensor:
+    """Experts of every rank by popularity: heaviest expert first, each to the rank with
+    the least load so far that still has room (E/P experts per rank).  ``loads`` [E] are
+    routed pairs per expert from a calibration batch (the same on every rank).  Returns the
+    placement: global expert ids in slot order (rank r holds slots [r*E/P, (r+1)*E/P))."""
+    loads = torch.as_tensor(loads, dtype=torch.float64).cpu()
+    E = loads.numel()
+    epr = E // world
+    order = sorted(range(E), key=lambda e: (-float(loads[e]), e))
+    acc = [0.0] * world
+    held = [[] for _ in range(world)]
+    for e in order:
+        r = min((r for r in range(world) if len(held[r]) < epr), key=lambda r: (acc[r], r))
+        held[r].append(e)
+        acc[r] += float(loads[e])
+    return torch.tensor([e for r in range(world) for e in sorted(held[r])], dtype=torch.int64)
 
 
 def ep_moe_forward_nvlink(block, x: torch.Tensor, ex: EPExchange, out=None, phases: int = 0,

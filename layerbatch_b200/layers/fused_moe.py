@@ -83,6 +83,7 @@ class Qwen3_5SparseMoeBlock(nn.Module):
         self.shared_expert = Qwen3_5SharedExpertMLP(hidden_size, shared_expert_intermediate_size)
         self.shared_expert_gate = nn.Linear(hidden_size, 1, bias=False)
         self.ep_exchange = None
+        self.expert_slot = None   # [E] int32 slot of every expert (custom placement)
 
     def attach_exchange(self, exchange) -> None:
         """Use the NVLink peer-memory exchange (``engine.ep.EPExchange``) for expert
@@ -96,6 +97,9 @@ class Qwen3_5SparseMoeBlock(nn.Module):
             from ..engine.ep import ep_moe_forward_nvlink
             return ep_moe_forward_nvlink(self, hidden_states, self.ep_exchange)
         if self.ep_size > 1:
+            if getattr(self, "expert_slot", None) is not None:
+                raise NotImplementedError("a custom expert placement needs the NVLink exchange "
+                                          "(attach_exchange)")
             from ..engine.sharding import ep_moe_forward
             return ep_moe_forward(self, hidden_states)
         return fused_moe(hidden_states, self.gate.weight, self.experts.gate_up_proj,
@@ -103,9 +107,25 @@ class Qwen3_5SparseMoeBlock(nn.Module):
                          self.shared_expert.up_proj.weight, self.shared_expert.down_proj.weight,
                          self.shared_expert_gate.weight, self.top_k)
 
-    def load_expert_shard(self, gate_up_full: torch.Tensor, down_full: torch.Tensor):
-        """Copy this rank's slice of full ``[E, ...]`` expert tensors (expert parallel)."""
+    def load_expert_shard(self, gate_up_full: torch.Tensor, down_full: torch.Tensor,
+                          placement=None):
+        """Copy this rank's experts out of full ``[E, ...]`` expert tensors (expert
+        parallel).  Without ``placement`` rank r holds experts [r*E/P, (r+1)*E/P); with it
+        (global expert ids in slot order, e.g. ``engine.ep.placement_by_load``) rank r
+        holds ``placement[r*E/P:(r+1)*E/P]``, which the NVLink exchange routes by."""
         s, e = self.expert_base, self.expert_base + self.local_experts
         with torch.no_grad():
-            self.experts.gate_up_proj.copy_(gate_up_full[s:e])
-            self.experts.down_proj.copy_(down_full[s:e])
+            if placement is None:
+                self.experts.gate_up_proj.copy_(gate_up_full[s:e])
+                self.experts.down_proj.copy_(down_full[s:e])
+                self.expert_slot = None
+                return
+            pl = torch.as_tensor(placement, dtype=torch.int64)
+            if sorted(pl.tolist()) != list(range(self.num_experts)):
+                raise ValueError("placement must be a permutation of the experts")
+            idx = pl[s:e].to(gate_up_full.device)
+            self.experts.gate_up_proj.copy_(gate_up_full[idx])
+            self.experts.down_proj.copy_(down_full[idx])
+            slot = torch.empty(self.num_experts, dtype=torch.int32)
+            slot[pl] = torch.arange(self.num_experts, dtype=torch.int32)
+            self.expert_slot = slot.to(self.experts.gate_up_proj.device)

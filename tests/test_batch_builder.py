@@ -82,3 +82,23 @@ def test_preemption_frees_blocks_and_recomputes():
     # 3 blocks cannot hold both once they grow: the newer one was preempted and waits
     assert b.status == SequenceStatus.WAITING or a.status == SequenceStatus.WAITING
     assert sum(len(s.block_table) for s in sched.running) <= 3
+
+
+def test_expert_placement_by_load_balances_ranks():
+    from layerbatch_b200.engine.ep import placement_by_load
+    g = torch.Generator().manual_seed(0)
+    loads = (1.0 / torch.arange(1, 513).double() ** 1.1)[torch.randperm(512, generator=g)] * 1e5
+    for P in (2, 4, 8):
+        pl = placement_by_load(loads, P)
+        assert sorted(pl.tolist()) == list(range(512))
+        epr = 512 // P
+        per = [float(loads[pl[r * epr:(r + 1) * epr]].sum()) for r in range(P)]
+        contig = [float(loads[r * epr:(r + 1) * epr].sum()) for r in range(P)]
+        mean = sum(per) / P
+        # never worse than contiguous ranges, and within 5 % of the lower bound of any
+        # placement with E/P experts per rank: the mean, or the heaviest expert plus the
+        # E/P - 1 lightest ones
+        srt = loads.sort().values
+        bound = max(mean, float(srt[-1]) + float(srt[:epr - 1].sum()))
+        assert max(per) <= max(contig) + 1e-6
+        assert max(per) <= bound * 1.05 + 1e-6

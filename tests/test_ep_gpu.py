@@ -29,13 +29,13 @@ def cuda():
     return torch.device("cuda")
 
 
-def ep_blocks(pd, P, H, E, k, I, dev):
+def ep_blocks(pd, P, H, E, k, I, dev, placement=None):
     blks = []
     for r in range(P):
         b = Qwen3_5SparseMoeBlock(H, E, k, I, I, ep_rank=r, ep_size=P).to(torch.bfloat16).to(dev)
         with torch.no_grad():
             b.gate.weight.copy_(pd.router)
-            b.load_expert_shard(pd.gate_up, pd.down)
+            b.load_expert_shard(pd.gate_up, pd.down, placement=placement)
             b.shared_expert.gate_proj.weight.copy_(pd.sh_gate)
             b.shared_expert.up_proj.weight.copy_(pd.sh_up)
             b.shared_expert.down_proj.weight.copy_(pd.sh_down)
@@ -44,13 +44,17 @@ def ep_blocks(pd, P, H, E, k, I, dev):
     return blks
 
 
-@pytest.mark.parametrize("P,E,k,Ts,C", [(4, 64, 8, [200, 64, 0, 150], 256),
-                                        (2, 512, 10, [96, 33], 128)])
-def test_ep_nvlink_emulated_ranks(cuda, P, E, k, Ts, C):
+@pytest.mark.parametrize("P,E,k,Ts,C,placed", [(4, 64, 8, [200, 64, 0, 150], 256, False),
+                                               (2, 512, 10, [96, 33], 128, False),
+                                               (4, 64, 8, [120, 7, 250, 64], 256, True)])
+def test_ep_nvlink_emulated_ranks(cuda, P, E, k, Ts, C, placed):
     H, I = 2048, 512
     p = W.make_moe_params(H, E, I, I, k, seed=7)
     pd = p.to(cuda)
-    blks = ep_blocks(pd, P, H, E, k, I, cuda)
+    placement = None
+    if placed:   # experts spread over the ranks by a seeded permutation
+        placement = torch.randperm(E, generator=torch.Generator().manual_seed(3))
+    blks = ep_blocks(pd, P, H, E, k, I, cuda, placement)
     exs = EPExchange.emulated(P, C, H, k, device=cuda)
     try:
         for call in range(2):
