@@ -146,30 +146,36 @@ struct EpDispatch {
   int* status;
 };
 
-// One warp per token: its row is read once and stored to every destination rank's recv
-// region (NVLink stores for other ranks), with the k ids and weights.  The last CTA to
-// finish publishes the row counts and this call's epoch to every destination.
+// One warp per token: its row is read once (all of a lane's 16-byte pieces in flight
+// together) and stored to every destination rank's recv region (NVLink stores for other
+// ranks), with the k ids and weights.  The last CTA to finish publishes the row counts and
+// this call's epoch to every destination.
+template <int MAXS>  // H <= MAXS * 256
 __global__ void __launch_bounds__(256) k_ep_dispatch(const EpDispatch d) {
   pdl_entry();
   const int lane = threadIdx.x & 31;
   const int wpb = blockDim.x / 32;
   const int nvec = d.H / 8;
+  const int stripes = d.H / 256;
   for (int t = blockIdx.x * wpb + (int)(threadIdx.x >> 5); t < d.T; t += gridDim.x * wpb) {
     int sl[LB_EP_MAX_RANKS];
 #pragma unroll
     for (int r = 0; r < LB_EP_MAX_RANKS; ++r)
       sl[r] = r < d.P ? d.slot[(long long)t * d.P + r] : -1;
-    const uint4* src = reinterpret_cast<const uint4*>(d.x + (long long)t * d.H);
-    for (int c = lane; c < nvec; c += 32) {
-      const uint4 v = src[c];
+    const uint4* src = reinterpret_cast<const uint4*>(d.x + (long long)t * d.H) + lane;
+    uint4 v[MAXS];
 #pragma unroll
-      for (int r = 0; r < LB_EP_MAX_RANKS; ++r)
-        if (sl[r] >= 0) {
-          uint4* dst = reinterpret_cast<uint4*>(d.peers.p[r] + d.off_x) +
-                       ((long long)d.rank * d.C + sl[r]) * nvec + c;
-          *dst = v;
-        }
-    }
+    for (int u = 0; u < MAXS; ++u)
+      if (u < stripes) v[u] = src[u * 32];
+#pragma unroll
+    for (int r = 0; r < LB_EP_MAX_RANKS; ++r)
+      if (sl[r] >= 0) {
+        uint4* dst = reinterpret_cast<uint4*>(d.peers.p[r] + d.off_x) +
+                     ((long long)d.rank * d.C + sl[r]) * nvec + lane;
+#pragma unroll
+        for (int u = 0; u < MAXS; ++u)
+          if (u < stripes) dst[u * 32] = v[u];
+      }
     if (lane < d.k) {
       const int32_t id = d.ids[(long long)t * d.k + lane];
       const float w = d.wf[(long long)t * d.k + lane];
@@ -518,8 +524,13 @@ int lb_ep_moe_forward(const LbEpArgs* a, void* stream) {
     d.off_w = L.w;
     d.peers = peers;
     d.status = w.m.status;
-    const int grid = std::max(1, std::min(nsm * 2, (T + 7) / 8));
-    launch_k(k_ep_dispatch, grid, 256, 0, st, d);
+    const int grid = std::max(1, std::min(nsm * 4, (T + 7) / 8));
+    if (H <= 2048)
+      launch_k(k_ep_dispatch<8>, grid, 256, 0, st, d);
+    else if (H <= 4096)
+      launch_k(k_ep_dispatch<16>, grid, 256, 0, st, d);
+    else
+      launch_k(k_ep_dispatch<32>, grid, 256, 0, st, d);
     if ((rc = launched("k_ep_dispatch"))) return rc;
     record_event(a->timing_events[1], st);
   }
@@ -567,7 +578,7 @@ int lb_ep_moe_forward(const LbEpArgs* a, void* stream) {
     d.off_ret = L.ret;
     d.peers = peers;
     d.status = w.m.status;
-    const int grid = std::max(1, std::min(nsm * 2, (P * C + 7) / 8));
+    const int grid = std::max(1, std::min(nsm * 4, (P * C + 7) / 8));
     if (H <= 2048)
       launch_k(k_ep_return<8>, grid, 256, 0, st, d);
     else if (H <= 4096)
