@@ -58,8 +58,8 @@ def load_peaks():
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one k_pod_attn launch on the
 # single-GPU workload, from one ncu capture of the current kernel (summaries under
 # profiles/); re-captured whenever the kernel changes.
-NCU_POD_TRAFFIC = {"c1": 293285376 + 4167936, "c2": 1220580608 + 22867968,
-                   "c4": 9130017024 + 59481088}
+NCU_POD_TRAFFIC = {"c1": 293292288 + 4175616, "c2": 1220569344 + 23076352,
+                   "c4": 9129402112 + 60164096}
 
 # ---------------------------------------------------------------------------- workloads
 CONFIGS = {
