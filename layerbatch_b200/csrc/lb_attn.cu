@@ -620,8 +620,7 @@ static int tp_oproj(const LbPodArgs& a, const PodWs& w, cudaStream_t st, int pha
     if ((rc = make_tmap_bf16_2d(&tA, A, std::max(N, 1), K, K, GEMM_BM, 64))) return rc;
     if ((rc = make_tmap_bf16_3d(&tB, a.w_o, 1, Hd, K, K, (uint64_t)K * Hd, BN, 64))) return rc;
     GemmArgs g = gemm_args_default(w.status);
-    g.single_m = N;
-    g.single_row_base = 0;
+    g.m = N;
     g.n_tiles = Hd / BN;
     g.splits = 1;
     g.k_blocks = K / 64;
@@ -633,7 +632,7 @@ static int tp_oproj(const LbPodArgs& a, const PodWs& w, cudaStream_t st, int pha
     const long long tiles = (long long)((N + GEMM_BM - 1) / GEMM_BM) * g.n_tiles;
     const int grid = (int)std::max<long long>(1, std::min<long long>(tiles, nsm));
     record_event(a.timing_events[2], st);
-    if ((rc = launch_gemm<BN, 4, EPI_F32_PEER, false>(tA, tA, tB, tB, tB, g, grid, st))) return rc;
+    if ((rc = launch_gemm<BN, 4, EPI_F32_PEER>(tA, tB, g, grid, st))) return rc;
   }
   if (phases & LB_TP_PHASE_REDUCE) {
     TpReduce d{};

@@ -206,8 +206,7 @@ int lb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
   rc = make_tmap_bf16_3d(&tB, B, 1, N, K, ldb, ldb * N, BN, 64);
   if (rc) return rc;
   GemmArgs a = gemm_args_default(static_cast<int*>(workspace));
-  a.single_m = (int)M;
-  a.single_row_base = 0;
+  a.m = (int)M;
   a.n_tiles = (int)(N / BN);
   a.splits = splits;
   a.k_blocks = (int)(K / 64) / splits;
@@ -219,17 +218,17 @@ int lb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
   const int grid = (int)std::min<long long>(tiles, num_sms());
   if (c_is_fp32) {
     switch (BN) {
-      case 256: return launch_gemm<256, 4, EPI_F32_RED, false>(tA, tA, tB, tB, tB, a, grid, st);
-      case 128: return launch_gemm<128, 6, EPI_F32_RED, false>(tA, tA, tB, tB, tB, a, grid, st);
-      case 64: return launch_gemm<64, 8, EPI_F32_RED, false>(tA, tA, tB, tB, tB, a, grid, st);
-      default: return launch_gemm<32, 8, EPI_F32_RED, false>(tA, tA, tB, tB, tB, a, grid, st);
+      case 256: return launch_gemm<256, 4, EPI_F32_RED>(tA, tB, a, grid, st);
+      case 128: return launch_gemm<128, 6, EPI_F32_RED>(tA, tB, a, grid, st);
+      case 64: return launch_gemm<64, 8, EPI_F32_RED>(tA, tB, a, grid, st);
+      default: return launch_gemm<32, 8, EPI_F32_RED>(tA, tB, a, grid, st);
     }
   }
   switch (BN) {
-    case 256: return launch_gemm<256, 4, EPI_BF16, false>(tA, tA, tB, tB, tB, a, grid, st);
-    case 128: return launch_gemm<128, 6, EPI_BF16, false>(tA, tA, tB, tB, tB, a, grid, st);
-    case 64: return launch_gemm<64, 8, EPI_BF16, false>(tA, tA, tB, tB, tB, a, grid, st);
-    default: return launch_gemm<32, 8, EPI_BF16, false>(tA, tA, tB, tB, tB, a, grid, st);
+    case 256: return launch_gemm<256, 4, EPI_BF16>(tA, tB, a, grid, st);
+    case 128: return launch_gemm<128, 6, EPI_BF16>(tA, tB, a, grid, st);
+    case 64: return launch_gemm<64, 8, EPI_BF16>(tA, tB, a, grid, st);
+    default: return launch_gemm<32, 8, EPI_BF16>(tA, tB, a, grid, st);
   }
 }
 

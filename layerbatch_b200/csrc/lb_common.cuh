@@ -260,10 +260,10 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
-// sigmoid with the fast exponential and reciprocal (a few ulp of fp32; the result is
-// rounded to bf16 right after)
+// sigmoid and silu with the fast exponential and reciprocal (a few ulp of fp32; the
+// results are rounded to bf16 right after)
 __device__ __forceinline__ float sigmoid_f(float g) { return __fdividef(1.0f, 1.0f + __expf(-g)); }
+__device__ __forceinline__ float silu_f(float g) { return g * sigmoid_f(g); }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {

@@ -1,8 +1,8 @@
-// Persistent grouped GEMM on sm_100a tensor cores: C[g] = A[g] . B[g]^T, bf16 in, f32
-// accumulate in TMEM, with fused epilogues for the MoE and o_proj hot path.
+// Persistent GEMM on sm_100a tensor cores: C = A . B^T, bf16 in, f32 accumulate in TMEM,
+// with the epilogues of the dense projections (router logits, o_proj and its split-K and
+// tensor-parallel forms).  The grouped expert GEMMs live in lb_gemm_tok.cuh.
 //
-// Layout: A rows are packed per group (rows [row_start[g], row_start[g+1])), K contiguous.
-// B is a 3-D tensor [G, N, K] (K contiguous), i.e. nn.Linear / expert weight layout.
+// Layout: A [M, K] and B [N, K] (K contiguous), i.e. activations times an nn.Linear weight.
 // Tiles are 128 x BN x 64 (M x N x K); one CTA per SM walks a static tile sequence:
 //   warp 0      : TMA producer (one elected lane)
 //   warp 1      : TMEM allocator + tcgen05.mma issuer (one elected lane)
@@ -23,9 +23,6 @@ constexpr int GEMM_THREADS = 192;
 
 enum EpiKind : int {
   EPI_BF16 = 0,        // C = bf16(acc)
-  EPI_SWIGLU = 1,      // act = bf16(silu(acc[:, :BN/2]) * acc[:, BN/2:])
-  EPI_SCALE_BF16 = 2,  // C = bf16(acc * row_scale[row])
-  EPI_COMBINE = 3,     // out[t] = bf16(tok_scale[t] * acc + sum_j yw[row_of[t, j]])
   EPI_F32_RED = 4,     // out32 += acc (split-K partials, vector reductions)
   EPI_F32_PEER = 5,    // fp32 tile -> inbox of the rank owning its m-tile (tensor parallel);
                        // the last CTA publishes the call's epoch to every rank
@@ -33,29 +30,15 @@ enum EpiKind : int {
 
 struct GemmArgs {
   int* status;
-  const int* mtile_start;  // [G+1] cumulative 128-row tiles per group; null => one group
-  const int* row_start;    // [G+1] first packed row per group; null => 0
-  int num_groups;          // G
-  int single_m;            // rows of the single group (mtile_start == null)
-  int single_row_base;     // first A row of the single group
+  int m;                   // rows of A and C
   int n_tiles;             // N / BN
   int k_blocks;            // K / 64 handled by one split
   int splits;              // split-K factor
-  int shared_group;        // group whose A/B come from the *_sh tensor maps (-1: none)
-  int b_group_base;        // routed B depth coordinate = g - b_group_base
-  int b_half_offset;       // two-half B tiles: row offset of the second half in tmB
-  // epilogue
   void* out;
   long long ldo;
-  const float* row_scale;      // EPI_SCALE_BF16
-  const float* tok_scale;      // EPI_COMBINE
-  const __nv_bfloat16* yw;     // EPI_COMBINE
-  long long ldyw;
-  const int* row_of;           // EPI_COMBINE: [T, top_k] permuted row or -1
-  int top_k;
-  int out_rows;                // rows of `out` (bounds check)
-  int out_cols;                // columns of `out` (bounds check)
-  TpPeers tp;                  // EPI_F32_PEER
+  int out_rows;            // rows of `out` (bounds check)
+  int out_cols;            // columns of `out` (bounds check)
+  TpPeers tp;              // EPI_F32_PEER
 };
 
 constexpr int EPI_STAGE_LD = 36;  // floats per row of the peer-store transpose buffer
@@ -68,46 +51,25 @@ struct GemmSmem {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int BAR_BYTES = 256;
   static constexpr int TMEM_COLS = 2 * BN;
-  static size_t bytes(int num_groups) {
-    return 1024 + (size_t)STAGES * STAGE_BYTES + BAR_BYTES + 4 * (size_t)(num_groups + 2);
-  }
+  static size_t bytes() { return 1024 + (size_t)STAGES * STAGE_BYTES + BAR_BYTES; }
 };
 
 struct TileCoord {
-  int g, m, n, ks;
+  int m, n, ks;
 };
 
-__device__ __forceinline__ void decode_tile(int t, const GemmArgs& p, const int* s_mt,
-                                            TileCoord& c) {
-  const int per = p.n_tiles * p.splits;
-  int g = 0, mt = 0, base = 0;
-  if (p.mtile_start == nullptr) {
-    mt = (p.single_m + GEMM_BM - 1) / GEMM_BM;
-  } else {
-    // The table may be a window of a larger one, so s_mt[0] need not be 0.
-    const int q = t / per + s_mt[0];
-    int lo = 0, hi = p.num_groups - 1;  // largest g with s_mt[g] <= q
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (s_mt[mid] <= q) lo = mid; else hi = mid - 1;
-    }
-    g = lo;
-    mt = s_mt[g + 1] - s_mt[g];
-    base = (s_mt[g] - s_mt[0]) * per;
-  }
-  const int l = t - base;
-  c.g = g;
-  c.m = l % mt;
-  const int rest = l / mt;
-  c.ks = rest % p.splits;
-  c.n = rest / p.splits;
+// Tile t -> (m-tile, n-tile, split), m fastest, then the split: CTAs that run at the
+// same time share the B tile.
+__device__ __forceinline__ TileCoord decode_tile(int t, const GemmArgs& p) {
+  const int mt = (p.m + GEMM_BM - 1) / GEMM_BM;
+  const int rest = t / mt;
+  return TileCoord{t % mt, rest / p.splits, rest % p.splits};
 }
 
-template <int BN, int STAGES, int EPI, bool TWO_HALVES>
+template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA_sh,
-           const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmB_sh0,
-           const __grid_constant__ CUtensorMap tmB_sh1, const GemmArgs p) {
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+           const GemmArgs p) {
   pdl_entry();
   using S = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -123,10 +85,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* s_mt = reinterpret_cast<int*>(bars) + S::BAR_BYTES / 4;
   // EPI_F32_PEER: per epilogue warp a 32 x EPI_STAGE_LD fp32 transpose buffer
-  float* s_stage = reinterpret_cast<float*>(
-      (reinterpret_cast<uintptr_t>(s_mt + p.num_groups + 2) + 15) & ~static_cast<uintptr_t>(15));
+  float* s_stage = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + S::BAR_BYTES);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -148,19 +108,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tmem_alloc(tmem_slot, S::TMEM_COLS);
     tmem_relinquish();
   }
-  if (p.mtile_start != nullptr) {
-    for (int i = threadIdx.x; i <= p.num_groups; i += blockDim.x) s_mt[i] = p.mtile_start[i];
-  }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  int total;
-  if (p.mtile_start == nullptr)
-    total = ((p.single_m + GEMM_BM - 1) / GEMM_BM) * p.n_tiles * p.splits;
-  else
-    total = (s_mt[p.num_groups] - s_mt[0]) * p.n_tiles * p.splits;
-  if (p.single_m <= 0 && p.mtile_start == nullptr) total = 0;
+  const int total =
+      p.m > 0 ? ((p.m + GEMM_BM - 1) / GEMM_BM) * p.n_tiles * p.splits : 0;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -171,38 +124,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;
       for (int t = blockIdx.x; t < total && !*s_abort; t += gridDim.x) {
-        TileCoord c;
-        decode_tile(t, p, s_mt, c);
-        const bool sh = (c.g == p.shared_group);
-        int a_row;
-        if (p.mtile_start == nullptr)
-          a_row = p.single_row_base + c.m * GEMM_BM;
-        else
-          a_row = (sh ? 0 : p.row_start[c.g]) + c.m * GEMM_BM;
-        const void* mapA = sh ? (const void*)&tmA_sh : (const void*)&tmA;
-        const int bdepth = c.g - p.b_group_base;
+        const TileCoord c = decode_tile(t, p);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.status)) { *s_abort = 1; break; }
           mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
           const int kc = (c.ks * p.k_blocks + kb) * GEMM_BK;
-          tma_load_2d(sA + stage * S::A_BYTES, mapA, &full[stage], kc, a_row);
-          uint8_t* dB = sB + stage * S::B_BYTES;
-          if (TWO_HALVES) {
-            const int r0 = c.n * (BN / 2);
-            if (sh) {
-              tma_load_3d(dB, &tmB_sh0, &full[stage], kc, r0, 0);
-              tma_load_3d(dB + S::B_BYTES / 2, &tmB_sh1, &full[stage], kc, r0, 0);
-            } else {
-              tma_load_3d(dB, &tmB, &full[stage], kc, r0, bdepth);
-              tma_load_3d(dB + S::B_BYTES / 2, &tmB, &full[stage], kc, r0 + p.b_half_offset,
-                          bdepth);
-            }
-          } else {
-            if (sh)
-              tma_load_3d(dB, &tmB_sh0, &full[stage], kc, c.n * BN, 0);
-            else
-              tma_load_3d(dB, &tmB, &full[stage], kc, c.n * BN, bdepth);
-          }
+          tma_load_2d(sA + stage * S::A_BYTES, &tmA, &full[stage], kc, c.m * GEMM_BM);
+          tma_load_3d(sB + stage * S::B_BYTES, &tmB, &full[stage], kc, c.n * BN, 0);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -262,136 +190,73 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     int buf = 0;
     uint32_t aphase = 0;
     for (int t = blockIdx.x; t < total && !*s_abort; t += gridDim.x) {
-      TileCoord c;
-      decode_tile(t, p, s_mt, c);
+      const TileCoord c = decode_tile(t, p);
       if (!mbar_wait(&tfull[buf], aphase, p.status)) { *s_abort = 1; break; }
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * BN;
 
-      // row bookkeeping
-      int valid_rows, out_row;
-      if (p.mtile_start == nullptr) {
-        valid_rows = p.single_m - c.m * GEMM_BM;
-        out_row = c.m * GEMM_BM + row_in_tile;
-      } else {
-        valid_rows = (p.row_start[c.g + 1] - p.row_start[c.g]) - c.m * GEMM_BM;
-        out_row = p.row_start[c.g] + c.m * GEMM_BM + row_in_tile;
-      }
+      const int valid_rows = p.m - c.m * GEMM_BM;
+      const int out_row = c.m * GEMM_BM + row_in_tile;
       const bool row_ok = row_in_tile < valid_rows && out_row < p.out_rows;
 
-      if constexpr (EPI == EPI_SWIGLU) {
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
 #pragma unroll 1
-        for (int ch = 0; ch < BN / 64; ++ch) {
-          uint32_t g[32], u[32];
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld32(tbase + ch * 32, v);
+        tmem_wait_ld();
+        const int col = c.n * BN + ch * 32;
+        if constexpr (EPI == EPI_F32_PEER) {
+          // Rank s's partial of a row goes to region s of the inbox of the rank owning
+          // the row's m-tile.  The warp's 32 x 32 fp32 block is transposed through
+          // shared memory so that every store writes 128-byte row segments (8 lanes per
+          // row): large NVLink writes instead of 16-byte ones.
+          float* stg = s_stage + quad * (32 * EPI_STAGE_LD);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4*>(stg + lane * EPI_STAGE_LD + 4 * i) =
+                make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                            __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
           __syncwarp();
-          tmem_ld32(tbase + ch * 32, g);
-          tmem_ld32(tbase + BN / 2 + ch * 32, u);
-          tmem_wait_ld();
-          const int col = c.n * (BN / 2) + ch * 32;
-          if (row_ok && col + 32 <= p.out_cols) {
-            uint32_t o[16];
+          const int owner = c.m % p.tp.size;
+          float* inbox = p.tp.inbox[0];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float a0 = silu_f(__uint_as_float(g[2 * i])) * __uint_as_float(u[2 * i]);
-              const float a1 =
-                  silu_f(__uint_as_float(g[2 * i + 1])) * __uint_as_float(u[2 * i + 1]);
-              o[i] = pack_bf16x2(a0, a1);
-            }
-            uint4* dst = reinterpret_cast<uint4*>(out + (long long)out_row * p.ldo + col);
+          for (int r = 1; r < LB_PEER_MAX; ++r)
+            if (r == owner) inbox = p.tp.inbox[r];
+          const int warp_row0 = quad * 32;            // first tile row of this warp
+          const long long row0 = (long long)(out_row - row_in_tile) + warp_row0;
+          const int cc = (lane & 7) * 4;
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          for (int jr = 0; jr < 8; ++jr) {
+            const int r = 4 * jr + (lane >> 3);
+            const float4 val = *reinterpret_cast<const float4*>(stg + r * EPI_STAGE_LD + cc);
+            if (warp_row0 + r < valid_rows && row0 + r < p.out_rows && col + 32 <= p.out_cols)
+              *reinterpret_cast<float4*>(
+                  inbox + ((long long)p.tp.rank * p.tp.inbox_rows + row0 + r) * p.ldo + col + cc) = val;
           }
+          __syncwarp();
+          continue;
         }
-      } else {
-#pragma unroll 1
-        for (int ch = 0; ch < BN / 32; ++ch) {
-          uint32_t v[32];
-          __syncwarp();
-          tmem_ld32(tbase + ch * 32, v);
-          tmem_wait_ld();
-          const int col = c.n * BN + ch * 32;
-          if constexpr (EPI == EPI_F32_PEER) {
-            // Rank s's partial of a row goes to region s of the inbox of the rank owning
-            // the row's m-tile.  The warp's 32 x 32 fp32 block is transposed through
-            // shared memory so that every store writes 128-byte row segments (8 lanes per
-            // row): large NVLink writes instead of 16-byte ones.
-            float* stg = s_stage + quad * (32 * EPI_STAGE_LD);
+        if (!row_ok || col + 32 > p.out_cols) {
+          // nothing to store for this row / chunk
+        } else if constexpr (EPI == EPI_F32_RED) {
+          float* out = reinterpret_cast<float*>(p.out) + (long long)out_row * p.ldo + col;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              *reinterpret_cast<float4*>(stg + lane * EPI_STAGE_LD + 4 * i) =
-                  make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                              __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-            __syncwarp();
-            const int owner = c.m % p.tp.size;
-            float* inbox = p.tp.inbox[0];
+          for (int i = 0; i < 8; ++i)
+            red_add_v4_f32(out + 4 * i, __uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                           __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+        } else {
+          float f[32];
 #pragma unroll
-            for (int r = 1; r < LB_PEER_MAX; ++r)
-              if (r == owner) inbox = p.tp.inbox[r];
-            const int warp_row0 = quad * 32;            // first tile row of this warp
-            const long long row0 = (long long)(out_row - row_in_tile) + warp_row0;
-            const int cc = (lane & 7) * 4;
+          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+          uint4* dst = reinterpret_cast<uint4*>(out + (long long)out_row * p.ldo + col);
 #pragma unroll
-            for (int jr = 0; jr < 8; ++jr) {
-              const int r = 4 * jr + (lane >> 3);
-              const float4 val = *reinterpret_cast<const float4*>(stg + r * EPI_STAGE_LD + cc);
-              if (warp_row0 + r < valid_rows && row0 + r < p.out_rows && col + 32 <= p.out_cols)
-                *reinterpret_cast<float4*>(
-                    inbox + ((long long)p.tp.rank * p.tp.inbox_rows + row0 + r) * p.ldo + col + cc) = val;
-            }
-            __syncwarp();
-            continue;
-          }
-          if (!row_ok || col + 32 > p.out_cols) {
-            // nothing to store for this row / chunk
-          } else if constexpr (EPI == EPI_F32_RED) {
-            float* out = reinterpret_cast<float*>(p.out) + (long long)out_row * p.ldo + col;
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              red_add_v4_f32(out + 4 * i, __uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                             __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-          } else {
-            float f[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
-            if constexpr (EPI == EPI_SCALE_BF16) {
-              const float s = p.row_scale[out_row];
-#pragma unroll
-              for (int i = 0; i < 32; ++i) f[i] *= s;
-            }
-            if constexpr (EPI == EPI_COMBINE) {
-              const float s = p.tok_scale[out_row];
-#pragma unroll
-              for (int i = 0; i < 32; ++i) f[i] *= s;
-              for (int j = 0; j < p.top_k; ++j) {
-                const int r = p.row_of[(long long)out_row * p.top_k + j];
-                if (r < 0) continue;
-                const uint4* src =
-                    reinterpret_cast<const uint4*>(p.yw + (long long)r * p.ldyw + col);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  const uint4 w = src[q];
-                  f[8 * q + 0] += bf16_lo(w.x);
-                  f[8 * q + 1] += bf16_hi(w.x);
-                  f[8 * q + 2] += bf16_lo(w.y);
-                  f[8 * q + 3] += bf16_hi(w.y);
-                  f[8 * q + 4] += bf16_lo(w.z);
-                  f[8 * q + 5] += bf16_hi(w.z);
-                  f[8 * q + 6] += bf16_lo(w.w);
-                  f[8 * q + 7] += bf16_hi(w.w);
-                }
-              }
-            }
-            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
-            uint4* dst = reinterpret_cast<uint4*>(out + (long long)out_row * p.ldo + col);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(pack_bf16x2(f[8 * i], f[8 * i + 1]),
-                                  pack_bf16x2(f[8 * i + 2], f[8 * i + 3]),
-                                  pack_bf16x2(f[8 * i + 4], f[8 * i + 5]),
-                                  pack_bf16x2(f[8 * i + 6], f[8 * i + 7]));
-          }
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(pack_bf16x2(f[8 * i], f[8 * i + 1]),
+                                pack_bf16x2(f[8 * i + 2], f[8 * i + 3]),
+                                pack_bf16x2(f[8 * i + 4], f[8 * i + 5]),
+                                pack_bf16x2(f[8 * i + 6], f[8 * i + 7]));
         }
       }
       tc_fence_before();

@@ -1,37 +1,45 @@
-// Host-side launcher for the grouped tcgen05 GEMM kernel template.
+// Host-side launchers of the tcgen05 GEMM kernel templates (dense and grouped expert).
 #pragma once
 
 #include "lb_gemm.cuh"
+#include "lb_gemm_tok.cuh"
 #include "lb_host.h"
 
 namespace lb {
 
-template <int BN, int STAGES, int EPI, bool TWO_HALVES>
-int launch_gemm(const CUtensorMap& tA, const CUtensorMap& tAsh, const CUtensorMap& tB,
-                const CUtensorMap& tBsh0, const CUtensorMap& tBsh1, const GemmArgs& a,
-                int grid, cudaStream_t st) {
-  auto kern = k_gemm<BN, STAGES, EPI, TWO_HALVES>;
-  const size_t smem = GemmSmem<BN, STAGES>::bytes(a.num_groups) +
-                      (EPI == EPI_F32_PEER ? EPI_STAGE_BYTES : 0);
+template <int BN, int STAGES, int EPI>
+int launch_gemm(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& a, int grid,
+                cudaStream_t st) {
+  auto kern = k_gemm<BN, STAGES, EPI>;
+  const size_t smem = GemmSmem<BN, STAGES>::bytes() + (EPI == EPI_F32_PEER ? EPI_STAGE_BYTES : 0);
   if ((int)smem > max_smem_optin())
     return fail(LB_ERR_UNSUPPORTED, "gemm: %zu bytes of shared memory exceed the limit", smem);
   if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)smem)) return rc;
   if (grid <= 0) return LB_OK;
-  launch_k(kern, grid, GEMM_THREADS, smem, st, tA, tAsh, tB, tBsh0, tBsh1, a);
-  { int _rc = launched("kern"); if (_rc) return _rc; }
+  launch_k(kern, grid, GEMM_THREADS, smem, st, tA, tB, a);
+  { int _rc = launched("k_gemm"); if (_rc) return _rc; }
+  return LB_OK;
+}
+
+template <int TN, int NBUF, int STAGES, int EPI, int EPW>
+int launch_gemm_tok(const CUtensorMap& tW, const CUtensorMap& tWsh0, const CUtensorMap& tWsh1,
+                    const CUtensorMap& tX, const CUtensorMap& tXsh, const TokArgs& a, int grid,
+                    cudaStream_t st) {
+  auto kern = k_gemm_tok<TN, NBUF, STAGES, EPI, EPW>;
+  const size_t smem = TokSmem<TN, NBUF, STAGES>::bytes(a.num_groups);
+  if ((int)smem > max_smem_optin())
+    return fail(LB_ERR_UNSUPPORTED, "gemm_tok: %zu bytes of shared memory exceed the limit", smem);
+  if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)smem)) return rc;
+  if (grid <= 0) return LB_OK;
+  launch_k(kern, grid, 64 + 32 * EPW, smem, st, tW, tWsh0, tWsh1, tX, tXsh, a);
+  { int _rc = launched("k_gemm_tok"); if (_rc) return _rc; }
   return LB_OK;
 }
 
 inline GemmArgs gemm_args_default(int* status) {
   GemmArgs a{};
   a.status = status;
-  a.mtile_start = nullptr;
-  a.row_start = nullptr;
-  a.num_groups = 1;
   a.splits = 1;
-  a.shared_group = -1;
-  a.b_group_base = 0;
-  a.b_half_offset = 0;
   return a;
 }
 

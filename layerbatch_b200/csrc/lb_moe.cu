@@ -13,6 +13,7 @@
 #include <mutex>
 
 #include "lb_gemm_launch.cuh"
+
 #include "lb_host.h"
 #include "lb_moe_core.h"
 
@@ -570,72 +571,87 @@ int moe_core(const MoeCore& c, const MoeWs& w, cudaStream_t st) {
     { int _rc = launched("k_gather_rows"); if (_rc) return _rc; }
   }
   const long long rows = (long long)T0 + (long long)T * k;
-  const long long max_mtiles = ((long long)T * k) / GEMM_BM + nl + (T0 + GEMM_BM - 1) / GEMM_BM;
+  // token tiles over all groups <= rows / TN + groups
+  auto max_units = [&](int TN, int n_fb) {
+    return (long long)n_fb * (rows / TN + G);
+  };
   const bool any_gemm = shared || nl > 0;
 
-  // 4. grouped gate/up GEMM with SwiGLU: act[rows, I]
+  // 4. grouped gate/up GEMM with SwiGLU: act[rows, I].  Accumulator 0 holds gate rows
+  //    fb*128.., accumulator 1 the up rows I + fb*128.. of the same expert.
   if (any_gemm) {
-    constexpr int BN = 256;
-    CUtensorMap tA, tAsh, tB, tB0, tB1;
-    if ((rc = make_tmap_bf16_2d(&tA, w.a_packed, rows, H, H, GEMM_BM, 64))) return rc;
-    if ((rc = make_tmap_bf16_2d(&tAsh, shared ? c.x_sh : c.x_r, shared ? T0 : T, H, H, GEMM_BM, 64))) return rc;
-    if (nl > 0 && (rc = make_tmap_bf16_3d(&tB, c.w_gate_up, nl, 2 * I, H, H, (uint64_t)2 * I * H,
-                                          BN / 2, 64)))
+    // 128-token tiles, double-buffered accumulators, 4-stage ring (48 KB per stage); two
+    // epilogue warps per TMEM lane quadrant for the SwiGLU epilogue
+    constexpr int TN = 128, NBUF = 2, STAGES = 4, EPW = 8;
+    CUtensorMap tX, tXsh, tW, tW0, tW1;
+    if ((rc = make_tmap_bf16_2d(&tX, w.a_packed, rows, H, H, TOK_BOX, 64))) return rc;
+    if ((rc = make_tmap_bf16_2d(&tXsh, shared ? c.x_sh : c.x_r, shared ? T0 : T, H, H, TOK_BOX, 64)))
+      return rc;
+    if (nl > 0 && (rc = make_tmap_bf16_3d(&tW, c.w_gate_up, nl, 2 * I, H, H, (uint64_t)2 * I * H,
+                                          TOK_FB, 64)))
       return rc;
     if (shared) {
-      if ((rc = make_tmap_bf16_3d(&tB0, c.w_sh_gate, 1, I, H, H, (uint64_t)I * H, BN / 2, 64)))
+      if ((rc = make_tmap_bf16_3d(&tW0, c.w_sh_gate, 1, I, H, H, (uint64_t)I * H, TOK_FB, 64)))
         return rc;
-      if ((rc = make_tmap_bf16_3d(&tB1, c.w_sh_up, 1, I, H, H, (uint64_t)I * H, BN / 2, 64)))
+      if ((rc = make_tmap_bf16_3d(&tW1, c.w_sh_up, 1, I, H, H, (uint64_t)I * H, TOK_FB, 64)))
         return rc;
     }
-    if (nl == 0) tB = tB0;
-    if (!shared) tB0 = tB1 = tB;
-    GemmArgs g = gemm_args_default(w.status);
-    g.mtile_start = w.mtile_start;
+    if (nl == 0) tW = tW0;
+    if (!shared) tW0 = tW1 = tW;
+    TokArgs g{};
+    g.status = w.status;
     g.row_start = w.row_start;
     g.num_groups = G;
-    g.n_tiles = (2 * I) / BN;
+    g.n_fb = I / TOK_FB;
+    g.fb_stride = TOK_FB;
+    g.acc1_off = I;
+    g.acc1_off_sh = 0;
     g.k_blocks = H / 64;
     g.shared_group = shared ? 0 : -1;
-    g.b_group_base = 1;
-    g.b_half_offset = I;
+    g.w_group_base = 1;
     g.out = w.act;
     g.ldo = I;
     g.out_rows = (int)rows;
     g.out_cols = I;
-    const int grid = (int)std::min<long long>(num_sms(), max_mtiles * g.n_tiles);
+    const int grid = (int)std::min<long long>(num_sms(), max_units(TN, g.n_fb));
     record_event(c.events ? c.events[0] : nullptr, st);
-    if ((rc = launch_gemm<BN, 4, EPI_SWIGLU, true>(tA, tAsh, tB, tB0, tB1, g, grid, st))) return rc;
+    if ((rc = launch_gemm_tok<TN, NBUF, STAGES, TOK_EPI_SWIGLU, EPW>(tW, tW0, tW1, tX, tXsh, g, grid, st)))
+      return rc;
     record_event(c.events ? c.events[1] : nullptr, st);
   }
   // 5. grouped down GEMM of every group (shared expert = group 0), each row scaled by its
-  //    routing weight (shared rows: sigmoid gate): yw[rows, H]
+  //    routing weight (shared rows: sigmoid gate): yw[rows, H].  Accumulators 0 / 1 hold
+  //    output features fb*256 + [0, 128) / [128, 256).
   if (any_gemm) {
-    constexpr int BN = 256;
-    CUtensorMap tA, tB, tBs;
-    if ((rc = make_tmap_bf16_2d(&tA, w.act, rows, I, I, GEMM_BM, 64))) return rc;
-    if (nl > 0 && (rc = make_tmap_bf16_3d(&tB, c.w_down, nl, H, I, I, (uint64_t)H * I, BN, 64)))
+    constexpr int TN = 128, NBUF = 2, STAGES = 4, EPW = 4;
+    CUtensorMap tX, tW, tWs;
+    if ((rc = make_tmap_bf16_2d(&tX, w.act, rows, I, I, TOK_BOX, 64))) return rc;
+    if (nl > 0 && (rc = make_tmap_bf16_3d(&tW, c.w_down, nl, H, I, I, (uint64_t)H * I, TOK_FB, 64)))
       return rc;
-    if (shared && (rc = make_tmap_bf16_3d(&tBs, c.w_sh_down, 1, H, I, I, (uint64_t)H * I, BN, 64)))
+    if (shared && (rc = make_tmap_bf16_3d(&tWs, c.w_sh_down, 1, H, I, I, (uint64_t)H * I, TOK_FB, 64)))
       return rc;
-    if (nl == 0) tB = tBs;
-    if (!shared) tBs = tB;
-    GemmArgs g = gemm_args_default(w.status);
-    g.mtile_start = w.mtile_start;
+    if (nl == 0) tW = tWs;
+    if (!shared) tWs = tW;
+    TokArgs g{};
+    g.status = w.status;
     g.row_start = w.row_start;
     g.num_groups = G;
-    g.n_tiles = H / BN;
+    g.n_fb = H / (2 * TOK_FB);
+    g.fb_stride = 2 * TOK_FB;
+    g.acc1_off = TOK_FB;
+    g.acc1_off_sh = TOK_FB;
     g.k_blocks = I / 64;
     g.shared_group = shared ? 0 : -1;
-    g.b_group_base = 1;
+    g.w_group_base = 1;
     g.row_scale = w.perm_w;
     g.out = w.yw;
     g.ldo = H;
     g.out_rows = (int)rows;
     g.out_cols = H;
-    const int grid = (int)std::min<long long>(num_sms(), max_mtiles * g.n_tiles);
+    const int grid = (int)std::min<long long>(num_sms(), max_units(TN, g.n_fb));
     record_event(c.events ? c.events[2] : nullptr, st);
-    if ((rc = launch_gemm<BN, 4, EPI_SCALE_BF16, false>(tA, tA, tB, tBs, tBs, g, grid, st))) return rc;
+    if ((rc = launch_gemm_tok<TN, NBUF, STAGES, TOK_EPI_SCALE, EPW>(tW, tWs, tWs, tX, tX, g, grid, st)))
+      return rc;
     record_event(c.events ? c.events[3] : nullptr, st);
   }
   return LB_OK;
