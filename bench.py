@@ -55,9 +55,11 @@ def load_peaks():
         return dict(PEAKS_FALLBACK, source="fallback")
 
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one k_pod_attn launch on the
-# single-GPU workload, from one ncu capture of the current kernel (summaries under
-# profiles/); re-captured whenever the kernel changes.
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the dominant
+# kernel on the single-GPU workload, from one ncu capture of the current kernel
+# (summaries under profiles/); re-captured whenever the kernel changes.  k_pod_attn for
+# the attention workloads, the grouped gate/up GEMM (k_gemm_tok, SwiGLU) for c3.
+NCU_GATE_UP_TRAFFIC = {"c3s": 1556182016 + 6260480, "c3l": 2548653056 + 86476800}
 NCU_POD_TRAFFIC = {"c1": 293292288 + 4175616, "c2": 1220569344 + 23076352,
                    "c4": 9129402112 + 60164096}
 
@@ -107,6 +109,18 @@ def attn_work(b):
     flops = 4.0 * pairs * Hq * D
     bytes_ = kv_tokens * Hkv * D * 2 * 2 + 3 * b.num_tokens * Hq * D * 2
     return flops, bytes_
+
+
+def moe_work(T, hit, H=2048, I=512, k=10):
+    """Algorithmic bytes and FLOPs of the two grouped expert GEMMs for T tokens whose
+    routing hits `hit` experts: each hit expert's weights once, the shared expert's once,
+    every routed pair's and shared row's input read once and output written once."""
+    rows = T * k + T
+    gate_up = {"bytes": (hit + 1) * 2 * I * H * 2 + rows * H * 2 + rows * I * 2,
+               "flops": 2.0 * rows * H * 2 * I}
+    down = {"bytes": (hit + 1) * H * I * 2 + rows * I * 2 + rows * H * 2,
+            "flops": 2.0 * rows * I * H}
+    return gate_up, down
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -297,6 +311,12 @@ def run_ours(args, rank, world, device):
         x = W.make_moe_input(T_moe, 2048, seed=seed, device=device)
         W.apply_zipf_bias(p, x)
         moe = (p, x)
+        if not sharded:
+            # experts the step's routing hits (the weights the grouped GEMMs must read)
+            with torch.no_grad():
+                ids_w, _, _ = ops.router_topk(ops.gemm(x, p.router), 10)
+                moe_hit = int(torch.unique(ids_w).numel())
+                del ids_w
         if sharded:
             # Experts are placed by popularity (heaviest first to the least-loaded rank),
             # from the routing counts of a separate calibration batch of the same
@@ -407,7 +427,13 @@ def run_ours(args, rank, world, device):
     if moe and not sharded:
         t_g1 = statistics.mean(e[0].elapsed_time(e[1]) for e in ev_moe) * 1e-3
         t_g2 = statistics.mean(e[2].elapsed_time(e[3]) for e in ev_moe) * 1e-3
-        res["moe_gemm"] = {"gate_up_ms": t_g1 * 1e3, "down_ms": t_g2 * 1e3}
+        res["moe_gemm"] = {"gate_up_ms": t_g1 * 1e3, "down_ms": t_g2 * 1e3,
+                           "experts_hit": moe_hit}
+        gu, dn = moe_work(T_moe, moe_hit)
+        res["moe_gate_up"] = dict(gu, ms=t_g1 * 1e3, gbs=gu["bytes"] / t_g1 / 1e9,
+                                  tflops=gu["flops"] / t_g1 / 1e12)
+        res["moe_gemm"].update(gate_up_gbs=gu["bytes"] / t_g1 / 1e9,
+                               down_gbs=dn["bytes"] / t_g2 / 1e9)
     res["parallelism"] = (f"tp{tp} x dp{world // tp} attention (KV-head shards, o_proj GEMM "
                           f"reducing over NVLink peer memory), ep{world} MoE (NVLink "
                           f"peer-memory dispatch/return, experts placed by popularity)"
@@ -575,6 +601,22 @@ def main():
             roof.update({"kernel": "k_pod_attn", "traffic": traffic,
                          "peak_source": peaks["source"], "kernel_ms": a["ms"],
                          "algorithmic_bytes": a["bytes"], "algorithmic_flops": a["flops"]})
+        elif "moe_gate_up" in res:
+            # MoE-only workloads: the dominant kernel is the grouped gate/up GEMM
+            g = res["moe_gate_up"]
+            t_hbm = g["bytes"] / (peaks["hbm_gbs"] * 1e9)
+            t_tc = g["flops"] / (peaks["bf16_tflops"] * 1e12)
+            if t_hbm >= t_tc:
+                roof = {"bound": "hbm", "achieved": g["gbs"], "peak": peaks["hbm_gbs"],
+                        "unit": "GB/s", "frac": g["gbs"] / peaks["hbm_gbs"]}
+            else:
+                roof = {"bound": "tensor", "achieved": g["tflops"], "peak": peaks["bf16_tflops"],
+                        "unit": "TFLOP/s", "frac": g["tflops"] / peaks["bf16_tflops"]}
+            roof.update({"kernel": "k_gemm_tok (gate/up, SwiGLU)",
+                         "traffic": NCU_GATE_UP_TRAFFIC.get(args.config) if world == 1 else None,
+                         "peak_source": peaks["source"], "kernel_ms": g["ms"],
+                         "algorithmic_bytes": g["bytes"], "algorithmic_flops": g["flops"],
+                         "tensor_frac": g["tflops"] / peaks["bf16_tflops"]})
         line = {
             "metric": "hot-path tokens/s", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
