@@ -199,7 +199,19 @@ int lb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
   if (M == 0) return LB_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
-  const int BN = (N % 256 == 0 && M > 512) ? 256 : (N % 128 == 0 ? 128 : (N % 64 == 0 ? 64 : 32));
+  int BN = N % 128 == 0 ? 128 : (N % 64 == 0 ? 64 : 32);
+  if (N % 256 == 0 && M > 512) {
+    // 256-wide tiles unless 128-wide ones finish sooner: a tile's time taken as
+    // proportional to the rows it loads (128 of A + BN of B), times the waves of tiles
+    // over the SMs (the router logits, M 4608 x N 512: 72 tiles of 256 leave half the
+    // SMs idle, 144 tiles of 128 fill them in one wave)
+    const long long mt = (M + GEMM_BM - 1) / GEMM_BM;
+    auto cost = [&](int bn) {
+      const long long tiles = mt * (N / bn) * splits;
+      return ((tiles + num_sms() - 1) / num_sms()) * (GEMM_BM + bn);
+    };
+    BN = cost(256) <= cost(128) ? 256 : 128;
+  }
   CUtensorMap tA, tB;
   int rc = make_tmap_bf16_2d(&tA, A, M, K, lda, GEMM_BM, 64);
   if (rc) return rc;
