@@ -6,7 +6,7 @@
 // drains that queue, then switches once to the other queue, so prefill (tensor-bound)
 // and decode (HBM-bound) items overlap across SMs and the tail is balanced.
 //
-// Roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + tcgen05.mma issuer,
+// Roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM owner + tcgen05.mma issuer,
 // warps 2..9 = softmax / epilogue: two warpgroups, one thread per TMEM lane each.  Decode
 // items use warpgroup 0 only; prefill items split every score row between the two
 // warpgroups (32 keys each) and each warpgroup owns half of the O columns.
@@ -20,8 +20,9 @@
 // V^T read MN-major straight from the V tile).  Online softmax keeps per-head state in
 // the 128 softmax threads; partial O and the log2-sum-exp of each split go to the
 // workspace and k_pod_merge combines them.
-// Prefill item (b, q_head, q_tile): S = Q . K^T (M = 128 queries, N = 128 keys) and
-// O += P . V (N = 256 dims, V MN-major), O accumulating in TMEM with per-row rescaling;
+// Prefill item (b, q_head, q_tile): S = Q . K^T (M = 128 queries, N = 64 keys) and
+// O += P . V (N = 256 dims, V MN-major, P bf16 read from TMEM as the A operand), O
+// accumulating in TMEM with per-row rescaling;
 // bottom-right causal mask; the epilogue applies sigmoid(gate) and writes bf16 rows of
 // the o_proj input.
 #pragma once
@@ -45,18 +46,22 @@ constexpr int POD_MISC = 2048;
 constexpr int POD_SMEM = 1024 + POD_DATA + POD_MISC;
 constexpr int POD_TMEM_COLS = 512;
 constexpr int DEC_SLOTS = 3;
-// prefill: 64-key K/V tiles (32 KB) in a 4-slot ring so loads run two tiles ahead
+// prefill: 64-key K/V tiles (32 KB) in separate K and V rings, K three tiles deep (the
+// next S MMA waits on K), V two; P goes to TMEM, not shared memory
 constexpr int PF_KV = 64;
 constexpr int PF_CHUNK = PF_KV * 128;            // 8 KB: one 64-dim chunk of a prefill tile
 constexpr int PF_TILE = 4 * PF_CHUNK;            // 32 KB
-constexpr int PF_SLOTS = 2;                      // per ring: K and V have separate rings
-constexpr int PF_P_BYTES = POD_KV * PF_KV * 2;   // 16 KB prefill P (128 queries x 64 keys)
-// prefill shared-memory map: [K ring 2 x 32 KB][V ring 2 x 32 KB][Q 64 KB][P x2]
+constexpr int PF_KSLOTS = 3;                     // K ring: barriers kv_*[0, 3)
+constexpr int PF_VSLOTS = 2;                     // V ring: barriers kv_*[3, 5)
+// prefill shared-memory map: [K ring 3 x 32 KB][V ring 2 x 32 KB][Q 64 KB]
 constexpr int PF_K_OFF = 0;
-constexpr int PF_V_OFF = PF_SLOTS * PF_TILE;
-constexpr int PF_Q_OFF = PF_V_OFF + PF_SLOTS * PF_TILE;
-constexpr int PF_P_OFF = PF_Q_OFF + POD_QP_BYTES;
-static_assert(PF_P_OFF + 2 * PF_P_BYTES <= POD_DATA, "prefill shared-memory map exceeds the data region");
+constexpr int PF_V_OFF = PF_KSLOTS * PF_TILE;
+constexpr int PF_Q_OFF = PF_V_OFF + PF_VSLOTS * PF_TILE;
+static_assert(PF_Q_OFF + POD_QP_BYTES <= POD_DATA, "prefill shared-memory map exceeds the data region");
+// prefill TMEM map: S double buffer [0, 128) (fp32 128 x 64 each), bf16 P double buffer
+// [PF_P_COL, PF_P_COL + 64) (128 x 64 keys, two keys per 32-bit column, the A operand of
+// the PV MMA read from TMEM), O [256, 512)
+constexpr int PF_P_COL = 128;
 // decode shared-memory map: [ring 3 x 64 KB][Q x2][P^T x2]
 static_assert(DEC_SLOTS * POD_TILE + 2 * POD_QD_BYTES + 2 * POD_PD_BYTES <= POD_DATA,
               "decode shared-memory map exceeds the data region");
@@ -89,7 +94,7 @@ struct PodParams {
 };
 
 struct PodBars {
-  uint64_t kv_full[4], kv_empty[4];
+  uint64_t kv_full[5], kv_empty[5];
   uint64_t item_full[2], item_empty[2];
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full[2], o_full[2];
@@ -189,9 +194,9 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
   const bool pf_first = (int)blockIdx.x < p.n_prefill_ctas;
   for (int pass = 0; pass < 2; ++pass) {
     const bool prefill = (pass == 0) ? pf_first : !pf_first;
-    const int nslots = DEC_SLOTS;   // decode ring (prefill uses two PF_SLOTS rings)
+    const int nslots = DEC_SLOTS;   // decode ring (prefill: the PF_KSLOTS / PF_VSLOTS rings)
     if (threadIdx.x == 0) {
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < 5; ++i) {
         mbar_init(&bars->kv_full[i], 1);
         mbar_init(&bars->kv_empty[i], 1);
       }
@@ -270,8 +275,8 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           ++cnt.item;
           if (prefill) {
             for (int j = 0; j < ntiles && !*abortp; ++j) {
-              const int slot = cnt.kv % PF_SLOTS;
-              if (!mbar_wait(&bars->kv_empty[slot], ((cnt.kv / PF_SLOTS) & 1) ^ 1, p.status)) { *abortp = 1; break; }
+              const int slot = cnt.kv % PF_KSLOTS;
+              if (!mbar_wait(&bars->kv_empty[slot], ((cnt.kv / PF_KSLOTS) & 1) ^ 1, p.status)) { *abortp = 1; break; }
               const int row = kv_page_row(p, b, j * PF_KV);
               mbar_arrive_expect_tx(&bars->kv_full[slot], PF_TILE);
               uint8_t* dst = smem + PF_K_OFF + slot * PF_TILE;
@@ -316,14 +321,14 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           const int kv_end = min(ctx, ctx - qlen + (it.z + 1) * POD_KV);
           const int ntiles = (kv_end + PF_KV - 1) / PF_KV;
           for (int j = 0; j < ntiles && !*abortp; ++j) {
-            const int slot = cnt.kv2 % PF_SLOTS;
-            if (!mbar_wait(&bars->kv_empty[2 + slot], ((cnt.kv2 / PF_SLOTS) & 1) ^ 1, p.status)) { *abortp = 1; break; }
+            const int slot = cnt.kv2 % PF_VSLOTS;
+            if (!mbar_wait(&bars->kv_empty[PF_KSLOTS + slot], ((cnt.kv2 / PF_VSLOTS) & 1) ^ 1, p.status)) { *abortp = 1; break; }
             const int row = kv_page_row(p, b, j * PF_KV);
-            mbar_arrive_expect_tx(&bars->kv_full[2 + slot], PF_TILE);
+            mbar_arrive_expect_tx(&bars->kv_full[PF_KSLOTS + slot], PF_TILE);
             uint8_t* dst = smem + PF_V_OFF + slot * PF_TILE;
 #pragma unroll
             for (int c = 0; c < 4; ++c)
-              tma_load_3d(dst + c * PF_CHUNK, &tmV64, &bars->kv_full[2 + slot], c * 64, kvh, row);
+              tma_load_3d(dst + c * PF_CHUNK, &tmV64, &bars->kv_full[PF_KSLOTS + slot], c * 64, kvh, row);
             ++cnt.kv2;
           }
         }
@@ -360,9 +365,9 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           bool ok = true;
           for (int j = 0; j <= ntiles && ok; ++j) {
             if (j < ntiles) {
-              // ---- S_j  (prefill: K ring slots 0-1; decode: unified ring)
+              // ---- S_j  (prefill: K ring; decode: unified ring)
               const uint32_t kp = prefill ? base + j : base + dec_pos_k(j);
-              const int ring = prefill ? PF_SLOTS : nslots;
+              const int ring = prefill ? PF_KSLOTS : nslots;
               const int ks = kp % ring;
               const int sb = cnt.s & 1;
               if (!mbar_wait(&bars->s_empty[sb], ((cnt.s >> 1) & 1) ^ 1, p.status) ||
@@ -397,11 +402,11 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               ++cnt.s;
             }
             if (j > 0) {
-              // ---- PV_{j-1}  (prefill: V ring slots 2-3; decode: unified ring)
+              // ---- PV_{j-1}  (prefill: V ring; decode: unified ring)
               const int jj = j - 1;
               const uint32_t vp = prefill ? vbase + jj : base + dec_pos_v(jj, ntiles);
-              const int ring = prefill ? PF_SLOTS : nslots;
-              const int vs = (prefill ? 2 : 0) + (int)(vp % ring);
+              const int ring = prefill ? PF_VSLOTS : nslots;
+              const int vs = (prefill ? PF_KSLOTS : 0) + (int)(vp % ring);
               const int ob = cnt.o & 1;
               if (!mbar_wait(&bars->p_full[ob], (cnt.o >> 1) & 1, p.status) ||
                   !mbar_wait(&bars->kv_full[vs], (vp / ring) & 1, p.status)) { ok = false; break; }
@@ -409,13 +414,14 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               const uint32_t vaddr = prefill ? smem_u32(smem + PF_V_OFF + (vp % ring) * PF_TILE)
                                              : smem_u32(kv_base + vs * POD_TILE);
               if (prefill) {
-                const uint32_t paddr = smem_u32(smem + PF_P_OFF + ob * PF_P_BYTES);
+                // A = P from TMEM: 16 keys (8 columns) per MMA
+                const uint32_t pcol = tmem + PF_P_COL + ob * (PF_KV / 2);
                 const uint32_t d = tmem + 256;
 #pragma unroll
                 for (int kk = 0; kk < PF_KV / 16; ++kk)
-                  umma_bf16(d, umma_desc_sw128(paddr + kk * 32, 16, 1024),
-                            umma_desc_sw128(vaddr + kk * 2048, PF_CHUNK, 1024), idesc_o,
-                            (jj | kk) != 0);
+                  umma_bf16_ts(d, pcol + kk * 8,
+                               umma_desc_sw128(vaddr + kk * 2048, PF_CHUNK, 1024), idesc_o,
+                               (jj | kk) != 0);
               } else {
                 const uint32_t paddr =
                     smem_u32(smem + DEC_SLOTS * POD_TILE + 2 * POD_QD_BYTES + ob * POD_PD_BYTES);
@@ -558,14 +564,12 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               if (!mbar_wait(&bars->o_full[need & 1], (need >> 1) & 1, p.status)) { ok = false; break; }
               tc_fence_after();
             }
-            const uint32_t paddr = smem_u32(smem + PF_P_OFF + (pv & 1) * PF_P_BYTES);
+            {
+              // this warpgroup's 32 keys of the row, two per column, into P buffer (pv & 1)
+              uint32_t pk[HALF / 2];
 #pragma unroll
-            for (int c = 0; c < HALF / 8; ++c) {
-              const uint32_t a = paddr + sw128_off(row, wg * HALF + c * 8);
-              st_shared_v4(a, pack_bf16x2(s[c * 8], s[c * 8 + 1]),
-                           pack_bf16x2(s[c * 8 + 2], s[c * 8 + 3]),
-                           pack_bf16x2(s[c * 8 + 4], s[c * 8 + 5]),
-                           pack_bf16x2(s[c * 8 + 6], s[c * 8 + 7]));
+              for (int c = 0; c < HALF / 2; ++c) pk[c] = pack_bf16x2(s[2 * c], s[2 * c + 1]);
+              tmem_st16(tl + PF_P_COL + (pv & 1) * (PF_KV / 2) + wg * (HALF / 2), pk);
             }
             if (rescale) {   // this warpgroup's half of the O columns
 #pragma unroll 1
@@ -583,15 +587,16 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             // bytes; P is 0 there, but 0 * NaN would poison O, so zero those V rows
             if (j * PF_KV + PF_KV > ctx) {
               const uint32_t vp = vbase + j;
-              if (!mbar_wait(&bars->kv_full[2 + vp % PF_SLOTS], (vp / PF_SLOTS) & 1, p.status)) { ok = false; break; }
+              if (!mbar_wait(&bars->kv_full[PF_KSLOTS + vp % PF_VSLOTS], (vp / PF_VSLOTS) & 1, p.status)) { ok = false; break; }
               if (wg == 0 && row < PF_KV && j * PF_KV + row >= ctx) {
-                const uint32_t v = smem_u32(smem + PF_V_OFF + (vp % PF_SLOTS) * PF_TILE) + row * 128;
+                const uint32_t v = smem_u32(smem + PF_V_OFF + (vp % PF_VSLOTS) * PF_TILE) + row * 128;
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
 #pragma unroll
                   for (int u = 0; u < 8; ++u) st_shared_v4(v + c * PF_CHUNK + u * 16, 0, 0, 0, 0);
               }
             }
+            tmem_wait_st();
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&bars->p_full[pv & 1]);
