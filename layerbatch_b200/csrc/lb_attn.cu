@@ -298,16 +298,15 @@ __global__ void k_pod_merge(const int32_t* __restrict__ ctx_lens, const int32_t*
 __global__ void k_f32_to_bf16(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst,
                               long long rows, int cols, long long ld_dst) {
   pdl_entry();
-  const long long n = rows * (cols / 4);
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / (cols / 4);
-    const int c = (int)(i % (cols / 4)) * 4;
-    const float4 v = *reinterpret_cast<const float4*>(src + r * cols + c);
-    uint2 o;
-    o.x = pack_bf16x2(v.x, v.y);
-    o.y = pack_bf16x2(v.z, v.w);
-    *reinterpret_cast<uint2*>(dst + r * ld_dst + c) = o;
+  // one block per row (grid-stride), the block's threads across the row's 4-float groups
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    for (int c = threadIdx.x * 4; c < cols; c += blockDim.x * 4) {
+      const float4 v = *reinterpret_cast<const float4*>(src + r * cols + c);
+      uint2 o;
+      o.x = pack_bf16x2(v.x, v.y);
+      o.y = pack_bf16x2(v.z, v.w);
+      *reinterpret_cast<uint2*>(dst + r * ld_dst + c) = o;
+    }
   }
 }
 
@@ -333,27 +332,28 @@ __global__ void __launch_bounds__(256) k_tp_reduce(const TpReduce a) {
   const int nmt = (a.N + GEMM_BM - 1) / GEMM_BM;
   const int owned = nmt > a.rank ? (nmt - a.rank + a.P - 1) / a.P : 0;
   const int vpr = a.H / 8;
-  const long long units = (long long)owned * GEMM_BM * vpr;
-  for (long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x; u < units;
-       u += (long long)gridDim.x * blockDim.x) {
-    const int j = (int)(u / ((long long)GEMM_BM * vpr));
-    const int rem = (int)(u - (long long)j * GEMM_BM * vpr);
-    const int r = rem / vpr, c = rem - r * vpr;
-    const int row = (a.rank + a.P * j) * GEMM_BM + r;
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  // one warp per owned row: q-th owned row = row q % 128 of the (q / 128)-th owned tile
+  for (int q = blockIdx.x * wpb + (int)(threadIdx.x >> 5); q < owned * GEMM_BM;
+       q += gridDim.x * wpb) {
+    const int row = (a.rank + a.P * (q / GEMM_BM)) * GEMM_BM + q % GEMM_BM;
     if (row >= a.N) continue;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int s = 0; s < a.P; ++s) {
-      const float4* src =
-          reinterpret_cast<const float4*>(a.inbox + ((long long)s * a.cap + row) * a.H) + 2 * c;
-      const float4 x0 = src[0], x1 = src[1];
-      acc[0] += x0.x; acc[1] += x0.y; acc[2] += x0.z; acc[3] += x0.w;
-      acc[4] += x1.x; acc[5] += x1.y; acc[6] += x1.z; acc[7] += x1.w;
+    for (int c = lane; c < vpr; c += 32) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int s = 0; s < a.P; ++s) {
+        const float4* src =
+            reinterpret_cast<const float4*>(a.inbox + ((long long)s * a.cap + row) * a.H) + 2 * c;
+        const float4 x0 = src[0], x1 = src[1];
+        acc[0] += x0.x; acc[1] += x0.y; acc[2] += x0.z; acc[3] += x0.w;
+        acc[4] += x1.x; acc[5] += x1.y; acc[6] += x1.z; acc[7] += x1.w;
+      }
+      const uint4 o = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                 pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+      reinterpret_cast<uint4*>(a.out + (long long)row * a.H)[c] = o;
+      for (int p = 0; p < a.P; ++p)
+        if (p != a.rank) reinterpret_cast<uint4*>(a.gather[p] + (long long)row * a.H)[c] = o;
     }
-    const uint4 o = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
-                               pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
-    reinterpret_cast<uint4*>(a.out + (long long)row * a.H)[c] = o;
-    for (int p = 0; p < a.P; ++p)
-      if (p != a.rank) reinterpret_cast<uint4*>(a.gather[p] + (long long)row * a.H)[c] = o;
   }
   __threadfence_system();
   __syncthreads();
@@ -375,13 +375,15 @@ __global__ void __launch_bounds__(256) k_tp_gather(int* hdr, const __nv_bfloat16
     peer_wait(hdr + TPH_GATH + threadIdx.x, hdr[TPH_EPOCH], status);
   __syncthreads();
   const int vpr = H / 8;
-  const long long units = (long long)N * vpr;
-  for (long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x; u < units;
-       u += (long long)gridDim.x * blockDim.x) {
-    const int row = (int)(u / vpr), c = (int)(u - (long long)row * vpr);
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  // one warp per row
+  for (int row = blockIdx.x * wpb + (int)(threadIdx.x >> 5); row < N; row += gridDim.x * wpb) {
     if ((row / GEMM_BM) % P == rank) continue;
-    reinterpret_cast<uint4*>(out + (long long)row * H)[c] =
-        reinterpret_cast<const uint4*>(gather + (long long)row * H)[c];
+    const uint4* src = reinterpret_cast<const uint4*>(gather + (long long)row * H);
+    uint4* dst = reinterpret_cast<uint4*>(out + (long long)row * H);
+#pragma unroll 8
+    for (int c = lane; c < vpr; c += 32) dst[c] = src[c];
   }
 }
 
@@ -698,8 +700,7 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
     record_event(a.timing_events[3], st);
     return rc;
   }
-  const long long n4 = (long long)N * (Hd / 4);
-  const int g = (int)std::max<long long>(1, std::min<long long>(nsm * 4, (n4 + 255) / 256));
+  const int g = (int)std::max<long long>(1, std::min<long long>(nsm * 4, N));
   launch_k(k_f32_to_bf16, g, 256, 0, st, w.o32, static_cast<__nv_bfloat16*>(a.out), N, Hd, Hd);
   { int _rc = launched("k_f32_to_bf16"); if (_rc) return _rc; }
   record_event(a.timing_events[3], st);

@@ -268,6 +268,30 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// mbar_wait called by all 32 lanes of a warp together, with one outcome for the warp: a
+// lane that ran out of time makes every lane see the failure, so the warp leaves its loop
+// as a whole (warp-synchronous and .sync.aligned instructions that follow stay converged).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status) {
+  const bool ok = mbar_wait(bar, parity, status);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Named barrier among `nthreads` threads that also ORs a predicate over them: every
+// participant gets true if any passed true.  Used where threads that may have seen a
+// failed wait must still meet the others, so that all of them leave together.
+__device__ __forceinline__ bool named_bar_any(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred q, p;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // Named barrier among `nthreads` threads (ids 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -244,22 +244,23 @@ __global__ void k_iota(int32_t* __restrict__ p, int n) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = i;
 }
 
-// a_packed[r] = x[perm_token[r]] for packed rows r in [T, row_start[G]); 16-byte vectors.
+// a_packed[r] = x[perm_token[r]] for packed rows r in [row_begin, *row_end_ptr): one warp
+// per row, 16-byte vectors.
 __global__ void k_gather_rows(const __nv_bfloat16* __restrict__ x, int H,
                               const int32_t* __restrict__ perm_token,
                               const int* __restrict__ row_end_ptr, int row_begin,
                               __nv_bfloat16* __restrict__ a_packed) {
   pdl_entry();
   const int row_end = *row_end_ptr;
-  const int vec_per_row = H / 8;
-  const long long n = (long long)(row_end - row_begin) * vec_per_row;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int r = row_begin + (int)(i / vec_per_row);
-    const int c = (int)(i % vec_per_row);
-    const int t = perm_token[r];
-    reinterpret_cast<uint4*>(a_packed + (long long)r * H)[c] =
-        reinterpret_cast<const uint4*>(x + (long long)t * H)[c];
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  const int vpr = H / 8;
+  for (int r = row_begin + blockIdx.x * wpb + (int)(threadIdx.x >> 5); r < row_end;
+       r += gridDim.x * wpb) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + (long long)perm_token[r] * H);
+    uint4* dst = reinterpret_cast<uint4*>(a_packed + (long long)r * H);
+#pragma unroll 8
+    for (int c = lane; c < vpr; c += 32) dst[c] = src[c];
   }
 }
 
@@ -565,8 +566,8 @@ int moe_core(const MoeCore& c, const MoeWs& w, cudaStream_t st) {
                                T0);
   if (rc) return rc;
   if (nl > 0) {
-    const long long vec = (long long)T * k * (H / 8);
-    const int grid = (int)std::max<long long>(1, std::min<long long>(num_sms() * 8, (vec + 255) / 256));
+    const long long rows_r = (long long)T * k;
+    const int grid = (int)std::max<long long>(1, std::min<long long>(num_sms() * 8, (rows_r + 7) / 8));
     launch_k(k_gather_rows, grid, 256, 0, st, c.x_r, H, w.perm_token, w.row_start + G, T0, w.a_packed);
     { int _rc = launched("k_gather_rows"); if (_rc) return _rc; }
   }

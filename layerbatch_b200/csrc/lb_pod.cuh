@@ -466,13 +466,18 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
       const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
       const int tid = threadIdx.x - 64 - 128 * wg;
       const int nthr = prefill ? 256 : 128;   // threads taking part in this mode
+      // The softmax threads of a mode meet at every named barrier, also after a failed
+      // wait: waits are warp-uniform (mbar_wait_warp) and every exit from the item loop
+      // is decided at a barrier that ORs the failures, so no thread is left waiting at a
+      // barrier the others have passed.
       while (prefill || wg == 0) {
         const int islot = cnt.item & 1;
         const uint32_t iph = (cnt.item >> 1) & 1;
-        if (!mbar_wait(&bars->item_full[islot], iph, p.status)) { *abortp = 1; break; }
-        const int4 it = bars->items[islot];
+        const bool got = mbar_wait_warp(&bars->item_full[islot], iph, p.status);
+        const int4 it = got ? bars->items[islot] : make_int4(-1, 0, 0, 0);
         ++cnt.item;
-        if (it.x < 0 || *abortp) break;
+        if (!got) *abortp = 1;
+        if (named_bar_any(4, nthr, !got || it.x < 0 || *abortp)) break;
         const int b = it.x;
         const int ctx = p.context_lens[b];
         const int q0 = p.cu_seqlens_q[b];
@@ -495,7 +500,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           for (int j = 0; j < ntiles; ++j) {
             const uint32_t pv = pv0 + j;
             const int sb = cnt.s & 1;
-            if (!mbar_wait(&bars->s_full[sb], (cnt.s >> 1) & 1, p.status)) { ok = false; break; }
+            if (!mbar_wait_warp(&bars->s_full[sb], (cnt.s >> 1) & 1, p.status)) { ok = false; break; }
             tc_fence_after();
             // both warpgroups read the whole score row (for the row max); each then
             // exponentiates and writes its own half of the keys
@@ -561,7 +566,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             const bool rescale = (j > 0) && __any_sync(0xffffffffu, alpha != 1.f);
             if (j >= 2 || (rescale && j >= 1)) {
               const uint32_t need = rescale ? pv - 1 : pv - 2;
-              if (!mbar_wait(&bars->o_full[need & 1], (need >> 1) & 1, p.status)) { ok = false; break; }
+              if (!mbar_wait_warp(&bars->o_full[need & 1], (need >> 1) & 1, p.status)) { ok = false; break; }
               tc_fence_after();
             }
             {
@@ -587,7 +592,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             // bytes; P is 0 there, but 0 * NaN would poison O, so zero those V rows
             if (j * PF_KV + PF_KV > ctx) {
               const uint32_t vp = vbase + j;
-              if (!mbar_wait(&bars->kv_full[PF_KSLOTS + vp % PF_VSLOTS], (vp / PF_VSLOTS) & 1, p.status)) { ok = false; break; }
+              if (!mbar_wait_warp(&bars->kv_full[PF_KSLOTS + vp % PF_VSLOTS], (vp / PF_VSLOTS) & 1, p.status)) { ok = false; break; }
               if (wg == 0 && row < PF_KV && j * PF_KV + row >= ctx) {
                 const uint32_t v = smem_u32(smem + PF_V_OFF + (vp % PF_VSLOTS) * PF_TILE) + row * 128;
 #pragma unroll
@@ -601,15 +606,14 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             tc_fence_before();
             mbar_arrive(&bars->p_full[pv & 1]);
           }
-          if (!ok) { *abortp = 1; break; }
           // last PV (completion implies all earlier ones)
-          {
+          if (ok) {
             const uint32_t last = cnt.o - 1;
-            if (!mbar_wait(&bars->o_full[last & 1], (last >> 1) & 1, p.status)) { *abortp = 1; break; }
+            ok = mbar_wait_warp(&bars->o_full[last & 1], (last >> 1) & 1, p.status);
             tc_fence_after();
           }
           bars->psum[wg][row] = l;
-          named_bar_sync(2, 256);
+          if (named_bar_any(2, 256, !ok)) { *abortp = 1; break; }
           l += bars->psum[wg ^ 1][row];
           const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
           const long long tok = (long long)q0 + qrow;
@@ -684,10 +688,12 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             a1[h] = 0.f;
             ap[h] = 1.f;
           }
-          for (int j = 0; j <= ntiles && ok; ++j) {
+          for (int j = 0; j <= ntiles; ++j) {
             if (j < ntiles) {
               const int sb = cnt.s & 1;
-              if (!mbar_wait(&bars->s_full[sb], (cnt.s >> 1) & 1, p.status)) { ok = false; break; }
+              // a failed wait (here or earlier in the item) is agreed on at this tile's
+              // barrier below, where all 128 threads leave the item together
+              if (ok) ok = mbar_wait_warp(&bars->s_full[sb], (cnt.s >> 1) & 1, p.status);
               tc_fence_after();
               uint32_t r[16];
               {
@@ -719,7 +725,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
                 for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
                 if (lane == 0) bars->red[par][quad][h] = v;
               }
-              named_bar_sync(1, 128);
+              if (named_bar_any(1, 128, !ok)) { ok = false; break; }
               const int ob = cnt.o & 1;
               const uint32_t pt = smem_u32(smem + DEC_SLOTS * POD_TILE + 2 * POD_QD_BYTES +
                                            ob * POD_PD_BYTES);
@@ -741,8 +747,9 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               // could be NaN, and 0 * NaN would poison O^T)
               if (t_begin + (j + 1) * POD_KV > t_end) {
                 const uint32_t vp = kvbase + dec_pos_v(j, ntiles);
-                if (!mbar_wait(&bars->kv_full[vp % nslots], (vp / nslots) & 1, p.status)) { ok = false; break; }
-                if (!valid) {
+                if (!mbar_wait_warp(&bars->kv_full[vp % nslots], (vp / nslots) & 1, p.status)) {
+                  ok = false;
+                } else if (!valid) {
                   const uint32_t v = smem_u32(kv_base + (vp % nslots) * POD_TILE) + row * 128;
 #pragma unroll
                   for (int c = 0; c < 4; ++c)
@@ -753,10 +760,30 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               fence_proxy_async_smem();
               tc_fence_before();
               mbar_arrive(&bars->p_full[ob]);
-              if (j > 0) {
+              if (j > 0 && ok) {
                 // accumulate O_{j-1} (scale of tile j-1), deferred behind P_j
                 const int pb = ob ^ 1;
-                if (!mbar_wait(&bars->o_full[pb], ((cnt.o - 1) >> 1) & 1, p.status)) { ok = false; break; }
+                ok = mbar_wait_warp(&bars->o_full[pb], ((cnt.o - 1) >> 1) & 1, p.status);
+                if (ok) {
+                  tc_fence_after();
+                  uint32_t o0[16], o1[16];
+                  dec_load_o(tl + DEC_O_COL + pb * 128, o0, o1);
+#pragma unroll
+                  for (int h = 0; h < 16; ++h) {
+                    a0[h] = a0[h] * ap[h] + __uint_as_float(o0[h]);
+                    a1[h] = a1[h] * ap[h] + __uint_as_float(o1[h]);
+                  }
+                  tc_fence_before();
+                }
+              }
+#pragma unroll
+              for (int h = 0; h < 16; ++h) ap[h] = al[h];
+              ++cnt.o;
+            } else {
+              // final O
+              const int pb = (cnt.o - 1) & 1;
+              if (ok) ok = mbar_wait_warp(&bars->o_full[pb], ((cnt.o - 1) >> 1) & 1, p.status);
+              if (ok) {
                 tc_fence_after();
                 uint32_t o0[16], o1[16];
                 dec_load_o(tl + DEC_O_COL + pb * 128, o0, o1);
@@ -767,25 +794,8 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
                 }
                 tc_fence_before();
               }
-#pragma unroll
-              for (int h = 0; h < 16; ++h) ap[h] = al[h];
-              ++cnt.o;
-            } else {
-              // final O
-              const int pb = (cnt.o - 1) & 1;
-              if (!mbar_wait(&bars->o_full[pb], ((cnt.o - 1) >> 1) & 1, p.status)) { ok = false; break; }
-              tc_fence_after();
-              uint32_t o0[16], o1[16];
-              dec_load_o(tl + DEC_O_COL + pb * 128, o0, o1);
-#pragma unroll
-              for (int h = 0; h < 16; ++h) {
-                a0[h] = a0[h] * ap[h] + __uint_as_float(o0[h]);
-                a1[h] = a1[h] * ap[h] + __uint_as_float(o1[h]);
-              }
-              tc_fence_before();
             }
           }
-          if (!ok) { *abortp = 1; break; }
           // row sums across the 128 threads
 #pragma unroll
           for (int h = 0; h < 16; ++h) {
@@ -794,7 +804,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
             if (lane == 0) bars->lred[quad][h] = v;
           }
-          named_bar_sync(1, 128);
+          if (named_bar_any(1, 128, !ok)) { *abortp = 1; break; }
           const long long pbase = ((long long)b * p.max_splits + split) * p.Hq;
 #pragma unroll
           for (int h = 0; h < 16; ++h) {
@@ -816,7 +826,7 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < 5; ++i) {
         mbar_inval(&bars->kv_full[i]);
         mbar_inval(&bars->kv_empty[i]);
       }
