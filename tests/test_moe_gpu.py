@@ -118,6 +118,35 @@ def test_moe_block(cuda, T, H, E, I, k, zipf):
     assert torch.isfinite(out.float()).all()
 
 
+def test_grouped_gemm_token_tile_edges(cuda):
+    """Experts whose row counts sit on both sides of the MMA widths and token tiles of the
+    grouped GEMMs (N = rows rounded up to 16, 128-row token tiles, 32-row boxes), with the
+    shared expert as a multi-tile group and two feature blocks in both GEMMs."""
+    counts = [0, 1, 15, 16, 17, 31, 32, 33, 127, 128, 129, 255, 256, 257, 300, 5]
+    E, H, I, k = len(counts), 512, 256, 1
+    T = sum(counts)
+    g = torch.Generator().manual_seed(7)
+    ids = torch.cat([torch.full((c,), e, dtype=torch.int64) for e, c in enumerate(counts)])
+    ids = ids[torch.randperm(T, generator=g)].view(T, k)
+    w = torch.rand(T, k, generator=g) + 0.25
+    p = W.make_moe_params(H, E, I, I, 4, seed=11)
+    x = W.make_moe_input(T, H, seed=12)
+    pd = p.to(cuda)
+    out = ops.moe_forward(x.to(cuda), None, pd.gate_up, pd.down, pd.sh_gate, pd.sh_up,
+                          pd.sh_down, pd.sh_gate_w, k, topk_ids=ids.to(cuda).int(),
+                          topk_weights=w.to(cuda), num_experts=E, ws_tag="moe_edges")
+    torch.cuda.synchronize()
+    assert ops.device_status(ops.workspace(0, cuda, "moe_edges")) == 0
+    y32 = OM.moe_block_fp32(x, p, ids, w)
+    err = OM.rel_err(out.cpu(), y32)
+    assert err <= TOL, err
+    # every expert's rows, empty and one-row experts included, carry their own output
+    for e, c in enumerate(counts):
+        if c:
+            tok = (ids[:, 0] == e).nonzero().flatten()
+            assert OM.rel_err(out.cpu()[tok], y32[tok]) <= TOL, (e, c)
+
+
 def test_moe_block_vs_reference_golden(cuda, golden):
     """Against the reference's own bf16 output where routing agrees."""
     g = golden["moe_c0"]
