@@ -477,7 +477,7 @@ static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
   if (a->max_q_len > 1) {
     // Starting split of the SMs between the queues (CTAs that finish their queue switch
     // to the other, so this only sets where they start).  Work is counted in SM-seconds
-    // at the per-SM rates this kernel reaches on B200: prefill ~4.1 TFLOP/s per SM,
+    // at the per-SM rates this kernel reaches on B200: prefill ~5.5 TFLOP/s per SM,
     // decode ~60 GB/s of KV per SM, with decode as a whole capped at ~6.9 TB/s of HBM.
     // The prefill CTAs get the share that finishes their queue when the decode queue is
     // done, plus 10% so that decode CTAs, not the long prefill tiles, form the tail.
@@ -487,7 +487,7 @@ static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
       pf_pairs = pf_rows * (pl.max_ctx / 4.0);
       dec_tok = (double)(a->num_seqs - 1) * (pl.max_ctx / 2.0);
     }
-    const double w_pf = pf_pairs * a->num_q_heads * POD_D * 4.0 / 4.1e12;
+    const double w_pf = pf_pairs * a->num_q_heads * POD_D * 4.0 / 5.5e12;
     const double dec_bytes = dec_tok * a->num_kv_heads * POD_D * 4.0;
     const double w_dec = dec_bytes / 60.0e9;
     const double t_end = std::max(dec_bytes / 6.9e12, (w_pf + w_dec) / nsm);
