@@ -776,7 +776,6 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int T = (int)a->num_tokens, H = (int)a->hidden, E = (int)a->num_experts;
   const int k = (int)a->top_k, I = (int)a->inter, nl = (int)a->num_local_experts;
-  const int G = nl + 1;
   const bool shared = !a->no_shared;
   const int T0 = shared ? T : 0;  // rows of group 0 (the shared expert)
   if (T == 0) return LB_OK;
