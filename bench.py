@@ -1,36 +1,48 @@
 #!/usr/bin/env python
-"""Benchmark of the LayerBatch hot path on B200: gated full-attention layer (POD paged
+"""Benchmark of the LayerBatch hot path on B200: the gated full-attention layer (merged
+q/k/v projection, (1+w) RMSNorm + partial RoPE prologue with the K/V store, POD paged
 attention over prefill + decode, sigmoid gate, o_proj) followed by the Qwen3.5 MoE layer.
 
 Default workload (``--config c4``): 512 decode sequences with contexts ~U[1024,16384] plus
 one 4096-token prefill chunk through the attention layer (Hq=16, Hkv=2, D=256, H=2048,
-256-token pages, shuffled block tables), then the MoE layer (E=512 top-10, I=512, one
-shared expert, Zipf(1.1) routing skew) on the step's 4608 tokens.  One step = both layers
-on one batch.  Inputs exceed L2 (the KV cache and expert weights are gigabytes), so no L2
-flush is needed between steps.
+256-token pages, shuffled block tables, RoPE theta 1e7 on 64 dims), then the MoE layer
+(E=512 top-10, I=512, one shared expert, Zipf(1.1) routing skew) on the step's 4608 tokens.
+One step = both layers on one batch, from hidden states to layer outputs.  Inputs exceed
+L2 (the KV cache and expert weights are gigabytes), so no L2 flush is needed between steps.
+The other configs are the attention + o_proj call alone (c1, c2) and the MoE layer alone
+(c3s, c3l).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1|c2|c3s|c3l|c4]
     python bench.py --impl reference ...   # the reference's CPU path (restated) only
 
 Under torchrun (``--gpus N``, N even) the c4 step is sharded: ranks form tensor-parallel
-pairs that split the attention by KV head (the o_proj GEMM stores its fp32 partial tiles
-into the owning rank's memory over NVLink and the owners reduce and send back the bf16
-rows), the pairs run different batches (data parallel), and the 512 experts are split
-over all N ranks with the NVLink peer-memory dispatch and return of lb_ep_moe_forward.
-No NCCL collective is on the data path.  Each GPU keeps one c4 batch of work, so
-scaling is weak.  Rank 0 prints one JSON line; the time is the max over ranks of
-CUDA-event time.
+pairs that split the attention by KV head (each rank projects, normalises and attends its
+own heads; the o_proj GEMM stores its fp32 partial tiles into the owning rank's memory
+over NVLink and the owners reduce and send back the bf16 rows), the pairs run different
+batches (data parallel), and the 512 experts are split over all N ranks with the NVLink
+peer-memory dispatch and return of lb_ep_moe_forward.  No NCCL collective is on the data
+path.  Each GPU keeps one c4 batch of work, so scaling is weak.  Rank 0 prints one JSON
+line; the time is the max over ranks of CUDA-event time.
 
-``value`` is device throughput with inputs resident in HBM.  ``e2e`` is the same step
-through the same public calls in a serving loop: each step uploads its inputs from
-pinned host memory and downloads its outputs, on copy streams that overlap the previous
-and next steps' kernels (double-buffered device inputs and outputs).
+``value`` is device throughput with inputs resident in HBM, timed over K steps with no
+events inside them; a second pass over K steps records CUDA events between the stages for
+the per-phase times and the roofline kernel's duration.  ``e2e`` is the same step through
+the same public calls in a serving loop: each step uploads its inputs (hidden states and
+batch metadata) from pinned host memory and downloads its outputs, on copy streams that
+overlap the previous and next steps' kernels (double-buffered device inputs and outputs).
+After the timed loops every workspace's device status word must be 0 and every output
+finite, else the run fails.
+
+The reference arm (``--impl reference``) and ``cpu_baseline`` time the reference's CPU code
+for the same step (restated in ``oracle/``: torch linears, the prologue, paged SDPA for
+decode and prefill, gate + o_proj, the sparse MoE path) on FULL steps of the workload, all
+host threads; the reference arm bounds its run by ``--ref-budget-s`` seconds and reports
+the steps it timed.
 """
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import sys
@@ -70,35 +82,39 @@ CONFIGS = {
           "-> POD attention + gate + o_proj",
     "c3s": "c3: MoE E=512 top-10 I=512 +shared, H=2048, T=256 (decode batch), Zipf(1.1)",
     "c3l": "c3: MoE E=512 top-10 I=512 +shared, H=2048, T=8192 (prefill batch), Zipf(1.1)",
-    "c4": "c4: 512 decode seqs ctx~U[1024,16384] + 4096-token prefill chunk -> gated attention"
-          " + o_proj (Hq16/Hkv2/D256/H2048), then MoE E=512 top-10 I=512 +shared at T=4608, "
-          "Zipf(1.1)",
+    "c4": "c4: 512 decode seqs ctx~U[1024,16384] + 4096-token prefill chunk -> gated "
+          "full-attention layer from hidden states (q/k/v proj, q/k (1+w) RMSNorm, RoPE "
+          "theta 1e7 on 64 dims, K/V store, POD attention, sigmoid gate, o_proj; "
+          "Hq16/Hkv2/D256/H2048), then MoE E=512 top-10 I=512 +shared at T=4608, Zipf(1.1)",
 }
+LAYER_CONFIGS = ("c4",)      # configs that run the whole attention layer from hidden states
+MOE_TOKENS = {"c3s": 256, "c3l": 8192}
 
 
-def attn_batch_for(cfg, seed, device):
+def config_dict(cfg, tokens_per_gpu):
+    """The ``config`` object of the JSON line; identical on both arms."""
+    return {"workload": CONFIGS[cfg], "tokens_per_step_per_gpu": tokens_per_gpu,
+            "l2": "inputs larger than L2 (KV cache and expert weights are GBs)"}
+
+
+def tokens_per_step(cfg):
+    return {"c1": 64, "c2": 2048 + 128, "c3s": 256, "c3l": 8192, "c4": 4096 + 512}[cfg]
+
+
+def attn_batch_for(cfg, seed, device, **kw):
     from layerbatch_b200 import workloads as W
     if cfg == "c1":
-        return W.c1_batch(seed=seed, device=device)
+        return W.c1_batch(seed=seed, device=device, **kw)
     if cfg == "c2":
-        return W.c2_batch(seed=seed, device=device)
+        return W.c2_batch(seed=seed, device=device, **kw)
     if cfg == "c4":
-        return W.c4_attn_batch(seed=seed, device=device)
+        return W.c4_attn_batch(seed=seed, device=device, **kw)
     return None
 
 
-def moe_tokens_for(cfg, attn):
-    if cfg == "c3s":
-        return 256
-    if cfg == "c3l":
-        return 8192
-    if cfg == "c4":
-        return attn.num_tokens
-    return 0
-
-
 def attn_work(b):
-    """Algorithmic FLOPs and bytes of the attention kernel for one batch."""
+    """Algorithmic FLOPs and bytes of the attention kernel for one batch: every KV byte of
+    every context read once, the query and gate rows read once, the gated row written."""
     Hq, D = b.q.shape[1], b.q.shape[2]
     Hkv = b.k_cache.shape[2]
     kv_tokens = sum(b.ctx_list)
@@ -111,16 +127,30 @@ def attn_work(b):
     return flops, bytes_
 
 
-def moe_work(T, hit, H=2048, I=512, k=10):
-    """Algorithmic bytes and FLOPs of the two grouped expert GEMMs for T tokens whose
-    routing hits `hit` experts: each hit expert's weights once, the shared expert's once,
-    every routed pair's and shared row's input read once and output written once."""
+def moe_work(T, hit, H=2048, I=512, k=10, E=512):
+    """Algorithmic bytes and FLOPs of the MoE layer and of its two grouped expert GEMMs.
+
+    Bytes: every weight the routing needs read once (the hit experts', the shared
+    expert's; for the layer also the router's and the shared gate's), the T input rows
+    read once and the T output rows written once.  The rows passed between the layer's
+    kernels (gathered inputs, SwiGLU activations, weighted expert rows) are scratch and
+    not counted.  FLOPs: 2 per multiply-add of every routed pair and shared row."""
     rows = T * k + T
-    gate_up = {"bytes": (hit + 1) * 2 * I * H * 2 + rows * H * 2 + rows * I * 2,
-               "flops": 2.0 * rows * H * 2 * I}
-    down = {"bytes": (hit + 1) * H * I * 2 + rows * I * 2 + rows * H * 2,
-            "flops": 2.0 * rows * I * H}
-    return gate_up, down
+    x_b = out_b = T * H * 2
+    gate_up = {"bytes": (hit + 1) * 2 * I * H * 2 + x_b, "flops": 2.0 * rows * H * 2 * I}
+    down = {"bytes": (hit + 1) * H * I * 2 + out_b, "flops": 2.0 * rows * I * H}
+    layer = {"bytes": E * H * 2 + gate_up["bytes"] + down["bytes"] + H * 2,
+             "flops": 2.0 * T * H * E + gate_up["flops"] + down["flops"] + 2.0 * T * H}
+    return gate_up, down, layer
+
+
+def layer_proj_work(N, H=2048, Hq=16, Hkv=2, D=256):
+    """Algorithmic bytes / FLOPs of the projection GEMM and the prologue for N tokens."""
+    cols = Hq * 2 * D + 2 * Hkv * D
+    gemm = {"bytes": cols * H * 2 + N * H * 2 + N * cols * 2, "flops": 2.0 * N * H * cols}
+    # prologue: query + key + value rows read once; query written, K/V stored once
+    pro = {"bytes": 2 * N * (Hq + 2 * Hkv) * D * 2, "flops": 0.0}
+    return gemm, pro
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -163,7 +193,7 @@ class ClockSampler:
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
                0x100: "display_clock_setting"}
 
-    def __init__(self, index, period=0.01):
+    def __init__(self, index, period=0.005):
         self.index, self.period = index, period
         self.samples, self.reasons = [], 0
         self.max_mhz = None
@@ -212,71 +242,103 @@ class ClockSampler:
 _CPU_INPUTS: dict = {}
 
 
-def _cached(key, fn):
-    if key not in _CPU_INPUTS:
-        _CPU_INPUTS[key] = fn()
-    return _CPU_INPUTS[key]
-
-
-def cpu_reference_sample(cfg, seed=1):
-    """Time the reference's CPU path (restated in ``oracle/``) on a bounded sample and
-    extrapolate it to one full step of ``cfg``.  Returns (tokens/s, cores, description)."""
+def cpu_inputs(cfg):
+    """The workload's full inputs on the host, built once per process.  Same shapes and
+    distributions as the GPU arm (K/V pages tiled from a seeded N(0,1) block of 512 pages:
+    the values do not change the CPU's work)."""
+    if cfg in _CPU_INPUTS:
+        return _CPU_INPUTS[cfg]
     from layerbatch_b200 import workloads as W
+    d = {}
+    if cfg in ("c1", "c2", "c4"):
+        b = attn_batch_for(cfg, 1, "cpu", tile_pages=512)
+        d["attn"] = b
+        if cfg in LAYER_CONFIGS:
+            d["lp"] = W.make_attn_layer_params(seed=0)
+            d["pos"], d["slots"] = W.layer_positions_slots(b)
+            d["x_attn"] = W.make_layer_input(b.num_tokens, 2048, seed=7)
+    if cfg in ("c3s", "c3l", "c4"):
+        T = MOE_TOKENS.get(cfg) or d["attn"].num_tokens
+        p = W.make_moe_params(2048, 512, 512, 512, 10, seed=0)
+        x = W.make_moe_input(T, 2048, seed=1)
+        W.apply_zipf_bias(p, x)
+        d["moe"] = (p, x)
+    _CPU_INPUTS[cfg] = d
+    return d
+
+
+def cpu_reference_step(cfg):
+    """One full step of ``cfg`` through the reference's CPU code (restated in oracle/):
+    the attention layer's linears, prologue and K/V store (qwen3_5.py:705-736,
+    attention.py:50-80), paged SDPA for the decode sequences and the prefill chunk
+    (sdpa_fallback.py:61-159), ``o * sigmoid(gate)`` and o_proj (qwen3_5.py:742-746), and
+    the MoE block's sparse path (qwen3_5.py:815-905).  Returns seconds."""
+    import torch.nn.functional as F
     from oracle import attention as OA
     from oracle import moe as OM
+    d = cpu_inputs(cfg)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        b = d.get("attn")
+        if b is not None:
+            N, Hq, D = b.q.shape
+            if "lp" in d:
+                lp = d["lp"]
+                x = d["x_attn"]
+                qd = Hq * 2 * D
+                kd = b.k_cache.shape[2] * D
+                q_out = F.linear(x, lp.w_qkv[:qd])
+                k_raw = F.linear(x, lp.w_qkv[qd:qd + kd])
+                v_raw = F.linear(x, lp.w_qkv[qd + kd:])
+                q, gate, k, v = OA.attn_prologue(
+                    q_out, k_raw, v_raw, lp.q_norm_w, lp.k_norm_w,
+                    lp.cos_sin_cache.view(-1, 1, lp.cos_sin_cache.shape[1]), d["pos"], lp.eps,
+                    Hq, D)
+                OA.store_kvcache(k, v, b.k_cache, b.v_cache, d["slots"])
+            else:
+                q, gate = b.q, b.gate.reshape(N, -1)
+            npf = b.num_prefill
+            parts = []
+            if npf:
+                e = int(b.cu_seqlens_q[npf])
+                o = OA.paged_prefill_bf16(q[:e], b.k_cache, b.v_cache, b.block_tables[:npf],
+                                          b.context_lens[:npf], b.cu_seqlens_q[:npf + 1],
+                                          b.scale)
+                parts.append(o.reshape(e, -1))
+            if b.num_seqs > npf:
+                e = int(b.cu_seqlens_q[npf])
+                o = OA.paged_decode_bf16(q[e:], b.k_cache, b.v_cache, b.block_tables[npf:],
+                                         b.context_lens[npf:], b.scale)
+                parts.append(o.reshape(N - e, -1))
+            OA.gate_oproj_bf16(torch.cat(parts, 0), gate.reshape(N, -1), b.w_o)
+        if "moe" in d:
+            p, x = d["moe"]
+            OM.moe_block_bf16(x, p, "sparse")
+    return time.perf_counter() - t0
+
+
+def cpu_reference_run(cfg, warmup, steps, budget_s):
+    """Warm-up then timed FULL steps until ``steps`` or the time budget; returns
+    (tokens/s of the median step, steps timed, warm-ups run, cores, description)."""
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    t_total = 0.0
-    parts = []
-    full_tokens = 0
-    with torch.no_grad():
-        if cfg in ("c1", "c2", "c4"):
-            full = {"c1": (64, (512, 4096), None), "c2": (128, (256, 8192), (2048, 2048)),
-                    "c4": (512, (1024, 16384), (0, 4096))}[cfg]
-            n_dec, (lo, hi), pf = full
-            ns = min(16, n_dec)
-            dec = W.uniform_ctx(ns, lo, hi, seed)
-            b = _cached(("dec", cfg), lambda: W.make_attn_batch(dec, (), seed=seed))
-            t0 = time.perf_counter()
-            o = OA.paged_decode_bf16(b.q, b.k_cache, b.v_cache, b.block_tables, b.context_lens,
-                                     b.scale)
-            OA.gate_oproj_bf16(o.flatten(1, -1), b.gate.reshape(ns, -1), b.w_o)
-            t_dec = (time.perf_counter() - t0) * n_dec / ns
-            parts.append(f"{ns}/{n_dec} decode seqs (x{n_dec / ns:.0f})")
-            t_total += t_dec
-            full_tokens += n_dec
-            if pf is not None:
-                prefix, chunk = pf
-                sc = 512
-                bp = _cached(("pf", cfg), lambda: W.make_attn_batch(
-                    [], [(min(prefix, sc), sc)], seed=seed))
-                t0 = time.perf_counter()
-                o = OA.paged_prefill_bf16(bp.q, bp.k_cache, bp.v_cache, bp.block_tables,
-                                          bp.context_lens, bp.cu_seqlens_q, bp.scale)
-                OA.gate_oproj_bf16(o.reshape(sc, -1), bp.gate.reshape(sc, -1), bp.w_o)
-                dt = time.perf_counter() - t0
-                pairs_s = sc * min(prefix, sc) + sc * (sc + 1) / 2
-                pairs_f = chunk * prefix + chunk * (chunk + 1) / 2
-                t_total += dt * pairs_f / pairs_s
-                parts.append(f"{sc}-token prefill chunk (x{pairs_f / pairs_s:.0f} by causal pairs)")
-                full_tokens += chunk
-        if cfg in ("c3s", "c3l", "c4"):
-            T_full = {"c3s": 256, "c3l": 8192, "c4": 4608}[cfg]
-            Ts = min(256, T_full)
-            def mk():
-                p = W.make_moe_params(2048, 512, 512, 512, 10, seed=0)
-                x = W.make_moe_input(Ts, 2048, seed=seed)
-                W.apply_zipf_bias(p, x)
-                return p, x
-            p, x = _cached(("moe", Ts), mk)
-            t0 = time.perf_counter()
-            OM.moe_block_bf16(x, p, "sparse")
-            dt = time.perf_counter() - t0
-            t_total += dt * T_full / Ts
-            parts.append(f"MoE sparse path at T={Ts} (x{T_full / Ts:.0f})")
-            if cfg != "c4":
-                full_tokens = T_full
-    return full_tokens / t_total, cores, "; ".join(parts) + f"; {cores} threads"
+    t_start = time.perf_counter()
+    cpu_inputs(cfg)
+    t_setup = time.perf_counter() - t_start
+    n_w = 0
+    for _ in range(max(1, min(warmup, 1))):
+        cpu_reference_step(cfg)
+        n_w += 1
+    times = []
+    while len(times) < max(1, steps):
+        times.append(cpu_reference_step(cfg))
+        if time.perf_counter() - t_start + times[-1] > budget_s:
+            break
+    med = statistics.median(times)
+    desc = (f"full {cfg} step (every token and sequence of the workload), median of "
+            f"{len(times)} timed step(s) after {n_w} warm-up; {cores} threads; "
+            f"input setup {t_setup:.0f} s untimed")
+    return tokens_per_step(cfg) / med, len(times), n_w, cores, desc
 
 
 # ---------------------------------------------------------------------------- GPU side
@@ -286,26 +348,40 @@ def run_ours(args, rank, world, device):
     cfg = args.config
     seed = 1 + rank
     sharded = world > 1 and cfg == "c4"
+    layer = cfg in LAYER_CONFIGS
     tp = 2 if (sharded and world % 2 == 0) else 1
-    tp_group, shard, ep_block = None, None, None
+    tp_group, ep_block = None, None
+    lp = None
     if sharded:
         # TP pairs by KV head, data parallel across pairs, experts split over all ranks.
         # Per-GPU work stays that of one c4 batch: a TP pair runs tp batches.
-        from layerbatch_b200.engine import sharding as S
         from layerbatch_b200.layers.fused_moe import Qwen3_5SparseMoeBlock
         groups = [torch.distributed.new_group(list(range(g * tp, (g + 1) * tp)))
                   for g in range(world // tp)] if tp > 1 else []
-        gid, tp_rank = rank // tp, rank % tp
+        gid = rank // tp
         tp_group = groups[gid] if tp > 1 else None
-        shard = S.attention_shard(16, 2, tp_rank, tp)
         dec = W.uniform_ctx(512 * tp, 1024, 16384, seed=100 + gid)
         attn = W.make_attn_batch(dec, [(0, 4096)] * tp, Hq=16 // tp, Hkv=2 // tp, H=2048,
                                  seed=1000 + rank, device=device)
         attn.scale = 256 ** -0.5
+        lp = W.make_attn_layer_params(Hq=16 // tp, Hkv=2 // tp, seed=2000 + rank,
+                                      device=device)
+        x_attn = W.make_layer_input(attn.num_tokens, 2048, seed=3000 + gid, device=device)
     else:
         attn = attn_batch_for(cfg, seed, device)
-    T_moe = moe_tokens_for(cfg, attn) if not sharded else 4608
+        if layer:
+            lp = W.make_attn_layer_params(seed=0, device=device)
+            x_attn = W.make_layer_input(attn.num_tokens, 2048, seed=7, device=device)
+    if layer:
+        pos, slots = W.layer_positions_slots(attn)
+        pos, slots = pos.to(device), slots.to(device)
+        Hq_l, Hkv_l = attn.q.shape[1], attn.k_cache.shape[2]
+        qkv_buf = torch.empty(attn.num_tokens, lp.w_qkv.shape[0], dtype=torch.bfloat16,
+                              device=device)
+        q_buf = torch.empty_like(attn.q)
+    T_moe = 4608 if sharded else (MOE_TOKENS.get(cfg) or (attn.num_tokens if cfg == "c4" else 0))
     moe = None
+    moe_hit = None
     if T_moe:
         p = W.make_moe_params(2048, 512, 512, 512, 10, seed=0, device=device)
         x = W.make_moe_input(T_moe, 2048, seed=seed, device=device)
@@ -317,7 +393,7 @@ def run_ours(args, rank, world, device):
                 ids_w, _, _ = ops.router_topk(ops.gemm(x, p.router), 10)
                 moe_hit = int(torch.unique(ids_w).numel())
                 del ids_w
-        if sharded:
+        else:
             # Experts are placed by popularity (heaviest first to the least-loaded rank),
             # from the routing counts of a separate calibration batch of the same
             # distribution summed over the ranks, so every rank computes the same placement.
@@ -351,57 +427,75 @@ def run_ours(args, rank, world, device):
     tokens = (attn.num_tokens // tp) if attn is not None else T_moe
     max_q = max(attn.qlen_list) if attn is not None else 0
     hint = ops.pod_work_hint(attn.ctx_list, attn.qlen_list) if attn is not None else None
+    pod_tag = "pod" if not sharded else f"tp_attn{rank}"
 
     a_out = torch.empty(attn.num_tokens, attn.w_o.shape[0], dtype=torch.bfloat16,
                         device=device) if attn is not None else None
     m_out = torch.empty_like(moe[1]) if moe else None
 
-    def step(ev_a=None, ev_m=None, q=None, gate=None, x=None, meta=None, out_a=None,
-             out_m=None):
+    def step(ev=None, inp=None, out_a=None, out_m=None):
+        """One step.  ``ev``: dict of event lists for the phase pass; ``inp``: device input
+        buffers of the e2e loop (else the resident inputs)."""
+        ev = ev or {}
+        inp = inp or {}
         if attn is not None:
-            qq = q if q is not None else attn.q
-            gg = gate if gate is not None else attn.gate
-            bt, cl, cu = meta if meta is not None else (attn.block_tables, attn.context_lens,
-                                                        attn.cu_seqlens_q)
+            bt, cl, cu = inp.get("meta") or (attn.block_tables, attn.context_lens,
+                                              attn.cu_seqlens_q)
             oa = out_a if out_a is not None else a_out
-            if sharded:
-                S.tp_attention_oproj(shard, qq, gg, attn.k_cache, attn.v_cache, bt, cl, cu,
-                                     attn.w_o, attn.scale, group=tp_group, max_q_len=max_q,
-                                     events=ev_a, out=oa, work_hint=hint, exchange=tp_ex)
+            if layer:
+                if "attn0" in ev:
+                    ev["attn0"].record()
+                ops.gated_attention_layer(
+                    inp.get("x_attn", x_attn), lp.w_qkv, Hq_l, Hkv_l, lp.q_norm_w,
+                    lp.k_norm_w, lp.cos_sin_cache, lp.eps, inp.get("pos", pos),
+                    inp.get("slots", slots), attn.k_cache, attn.v_cache, bt, cl, cu, attn.w_o,
+                    attn.scale, out=oa, max_q_len=max_q, work_hint=hint, events=ev.get("pod"),
+                    qkv=qkv_buf, q=q_buf, ws_tag=pod_tag, tp=tp_ex,
+                    stage_events=ev.get("stages"))
             else:
-                ops.pod_attn_oproj(qq, gg, attn.k_cache, attn.v_cache, bt, cl, cu, attn.w_o,
-                                   attn.scale, out=oa, max_q_len=max_q, events=ev_a,
+                if "attn0" in ev:
+                    ev["attn0"].record()
+                ops.pod_attn_oproj(inp.get("q", attn.q), inp.get("gate", attn.gate),
+                                   attn.k_cache, attn.v_cache, bt, cl, cu, attn.w_o,
+                                   attn.scale, out=oa, max_q_len=max_q, events=ev.get("pod"),
                                    work_hint=hint)
+            if "attn1" in ev:
+                ev["attn1"].record()
         if moe:
             pm, xm = moe
-            xx = x if x is not None else xm
+            xx = inp.get("x_moe", xm)
             om = out_m if out_m is not None else m_out
+            if "moe0" in ev:
+                ev["moe0"].record()
             if sharded:
                 from layerbatch_b200.engine.ep import ep_moe_forward_nvlink
                 ep_moe_forward_nvlink(ep_block, xx, ep_block.ep_exchange, out=om)
             else:
                 ops.moe_forward(xx, pm.router, pm.gate_up, pm.down, pm.sh_gate, pm.sh_up,
-                                pm.sh_down, pm.sh_gate_w, 10, out=om, events=ev_m)
+                                pm.sh_down, pm.sh_gate_w, 10, out=om, events=ev.get("moe"))
+            if "moe1" in ev:
+                ev["moe1"].record()
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
 
+    def mk():
+        return torch.cuda.Event(enable_timing=True)
+
     K, Wu = args.steps, args.warmup
     for _ in range(Wu):
         step()
     torch.cuda.synchronize()
-    ev_attn = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K)]
-    ev_moe = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
-    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # ---------------- the timed region: K steps, no events inside them
+    st, en = mk(), mk()
     n0 = ops.launch_count()
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(torch.cuda.current_device()) as clk:
         st.record()
-        for i in range(K):
-            step(ev_attn[i] if attn is not None else None,
-                 ev_moe[i] if (moe and not sharded) else None)
+        for _ in range(K):
+            step()
         en.record()
         torch.cuda.synchronize()
     barrier()
@@ -411,29 +505,67 @@ def run_ours(args, rank, world, device):
     if world > 1:
         torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
     ms = float(ms_t)
-    ws_status = 0
-    for tag in ("pod", "moe", "tp_attn", "ep_owner", "ep_source"):
-        if (torch.cuda.current_device(), tag) in ops._WS:
-            ws_status |= ops.device_status(ops._WS[(torch.cuda.current_device(), tag)])
 
-    res = {"ms": ms, "tokens": tokens, "launches": launches, "clocks": clk.summary(),
-           "device_status": ws_status}
+    # ---------------- phase pass: K more steps with events between the stages
+    evs = []
+    for _ in range(K):
+        e = {"attn0": mk(), "attn1": mk(), "moe0": mk(), "moe1": mk(),
+             "pod": [mk() for _ in range(4)], "moe": [mk() for _ in range(4)],
+             "stages": [mk(), mk()]}
+        if sharded:
+            e.pop("moe")
+        evs.append(e)
+    for i in range(K):
+        step(ev=evs[i] if attn is not None or moe else None)
+    torch.cuda.synchronize()
+
+    def mean_ms(a, b):
+        return statistics.mean(a(e).elapsed_time(b(e)) for e in evs)
+
+    res = {"ms": ms, "tokens": tokens, "launches": launches, "launches_per_step": launches / K,
+           "clocks": clk.summary()}
     peaks = load_peaks()
+    phases = {}
     if attn is not None:
-        t_attn = statistics.mean(e[0].elapsed_time(e[1]) for e in ev_attn) * 1e-3
+        t_attn = mean_ms(lambda e: e["pod"][0], lambda e: e["pod"][1]) * 1e-3
         flops, byts = attn_work(attn)
         res["attn"] = {"ms": t_attn * 1e3, "flops": flops, "bytes": byts,
                        "gbs": byts / t_attn / 1e9, "tflops": flops / t_attn / 1e12}
-    if moe and not sharded:
-        t_g1 = statistics.mean(e[0].elapsed_time(e[1]) for e in ev_moe) * 1e-3
-        t_g2 = statistics.mean(e[2].elapsed_time(e[3]) for e in ev_moe) * 1e-3
-        res["moe_gemm"] = {"gate_up_ms": t_g1 * 1e3, "down_ms": t_g2 * 1e3,
-                           "experts_hit": moe_hit}
-        gu, dn = moe_work(T_moe, moe_hit)
-        res["moe_gate_up"] = dict(gu, ms=t_g1 * 1e3, gbs=gu["bytes"] / t_g1 / 1e9,
-                                  tflops=gu["flops"] / t_g1 / 1e12)
-        res["moe_gemm"].update(gate_up_gbs=gu["bytes"] / t_g1 / 1e9,
-                               down_gbs=dn["bytes"] / t_g2 / 1e9)
+        if layer:
+            phases["qkv_gemm"] = mean_ms(lambda e: e["attn0"], lambda e: e["stages"][0])
+            phases["prologue"] = mean_ms(lambda e: e["stages"][0], lambda e: e["stages"][1])
+            phases["plan"] = mean_ms(lambda e: e["stages"][1], lambda e: e["pod"][0])
+        else:
+            phases["plan"] = mean_ms(lambda e: e["attn0"], lambda e: e["pod"][0])
+        phases["pod_attn"] = t_attn * 1e3
+        phases["merge_oproj"] = mean_ms(lambda e: e["pod"][1], lambda e: e["attn1"])
+        phases["attention_layer"] = mean_ms(lambda e: e["attn0"], lambda e: e["attn1"])
+        if layer:
+            g, pr = layer_proj_work(attn.num_tokens, Hq=Hq_l, Hkv=Hkv_l)
+            res["proj"] = {"gemm_gbs": g["bytes"] / phases["qkv_gemm"] / 1e6,
+                           "gemm_tflops": g["flops"] / phases["qkv_gemm"] / 1e9,
+                           "prologue_gbs": pr["bytes"] / phases["prologue"] / 1e6}
+    if moe:
+        phases["moe_layer"] = mean_ms(lambda e: e["moe0"], lambda e: e["moe1"])
+        if not sharded:
+            t_g1 = mean_ms(lambda e: e["moe"][0], lambda e: e["moe"][1]) * 1e-3
+            t_g2 = mean_ms(lambda e: e["moe"][2], lambda e: e["moe"][3]) * 1e-3
+            phases["moe_gate_up"] = t_g1 * 1e3
+            phases["moe_down"] = t_g2 * 1e3
+            gu, dn, ly = moe_work(T_moe, moe_hit)
+            t_l = phases["moe_layer"] * 1e-3
+            res["moe_gate_up"] = dict(gu, ms=t_g1 * 1e3, gbs=gu["bytes"] / t_g1 / 1e9,
+                                      tflops=gu["flops"] / t_g1 / 1e12)
+            res["moe_layer"] = {"ms": t_l * 1e3, "experts_hit": moe_hit,
+                                "algorithmic_bytes": ly["bytes"],
+                                "algorithmic_flops": ly["flops"],
+                                "gbs": ly["bytes"] / t_l / 1e9,
+                                "frac": ly["bytes"] / t_l / 1e9 / peaks["hbm_gbs"],
+                                "gate_up_frac": gu["bytes"] / t_g1 / 1e9 / peaks["hbm_gbs"],
+                                "down_frac": dn["bytes"] / t_g2 / 1e9 / peaks["hbm_gbs"],
+                                "bytes_counted": "weights hit + shared + router, x, out "
+                                                 "(no scratch rows)"}
+    res["phases_ms"] = {k: round(v, 4) for k, v in phases.items()}
     res["parallelism"] = (f"tp{tp} x dp{world // tp} attention (KV-head shards, o_proj GEMM "
                           f"reducing over NVLink peer memory), ep{world} MoE (NVLink "
                           f"peer-memory dispatch/return, experts placed by popularity)"
@@ -450,23 +582,27 @@ def run_ours(args, rank, world, device):
     if not args.no_e2e:
         pin = {}
         if attn is not None:
-            pin["q"] = attn.q.cpu().pin_memory()
-            pin["gate"] = attn.gate.cpu().pin_memory()
+            if layer:
+                pin["x_attn"] = x_attn.cpu().pin_memory()
+                pin["pos"] = pos.cpu().pin_memory()
+                pin["slots"] = slots.cpu().pin_memory()
+            else:
+                pin["q"] = attn.q.cpu().pin_memory()
+                pin["gate"] = attn.gate.cpu().pin_memory()
             pin["meta"] = [t.cpu().pin_memory() for t in
                            (attn.block_tables, attn.context_lens, attn.cu_seqlens_q)]
         if moe:
-            pin["x"] = moe[1].cpu().pin_memory()
+            pin["x_moe"] = moe[1].cpu().pin_memory()
         bufs, host_out = [], []
         for _ in range(2):
             bd = {}
+            for name, v in pin.items():
+                bd[name] = ([torch.empty(t.shape, dtype=t.dtype, device=device) for t in v]
+                            if isinstance(v, list) else
+                            torch.empty(v.shape, dtype=v.dtype, device=device))
             if attn is not None:
-                bd["q"] = torch.empty_like(attn.q)
-                bd["gate"] = torch.empty_like(attn.gate)
-                bd["meta"] = [torch.empty_like(t) for t in
-                              (attn.block_tables, attn.context_lens, attn.cu_seqlens_q)]
                 bd["out_a"] = torch.empty_like(a_out)
             if moe:
-                bd["x"] = torch.empty_like(moe[1])
                 bd["out_m"] = torch.empty_like(m_out)
             bufs.append(bd)
             host_out.append({k: torch.empty(bd[k].shape, dtype=bd[k].dtype).pin_memory()
@@ -487,18 +623,16 @@ def run_ours(args, rank, world, device):
             bd, ho = bufs[k], host_out[k]
             with torch.cuda.stream(s_in):
                 s_in.wait_event(ev_used[k])          # step i-2 is done reading buffer k
-                if attn is not None:
-                    bd["q"].copy_(pin["q"], non_blocking=True)
-                    bd["gate"].copy_(pin["gate"], non_blocking=True)
-                    for dst, src in zip(bd["meta"], pin["meta"]):
-                        dst.copy_(src, non_blocking=True)
-                if moe:
-                    bd["x"].copy_(pin["x"], non_blocking=True)
+                for name, v in pin.items():
+                    if isinstance(v, list):
+                        for dst, src in zip(bd[name], v):
+                            dst.copy_(src, non_blocking=True)
+                    else:
+                        bd[name].copy_(v, non_blocking=True)
                 ev_in[k].record(s_in)
             comp.wait_event(ev_in[k])
             comp.wait_event(ev_out[k])                # step i-2's outputs have been read
-            step(q=bd.get("q"), gate=bd.get("gate"), x=bd.get("x"), meta=bd.get("meta"),
-                 out_a=bd.get("out_a"), out_m=bd.get("out_m"))
+            step(inp={n: bd[n] for n in pin}, out_a=bd.get("out_a"), out_m=bd.get("out_m"))
             ev_used[k].record(comp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_used[k])
@@ -511,7 +645,7 @@ def run_ours(args, rank, world, device):
         torch.cuda.synchronize()
         barrier()
         Ke = max(4, K // 2)
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2, e2 = mk(), mk()
         s2.record(comp)
         s_in.wait_event(s2)
         for i in range(Ke):
@@ -525,6 +659,23 @@ def run_ours(args, rank, world, device):
         if world > 1:
             torch.distributed.all_reduce(mt, op=torch.distributed.ReduceOp.MAX)
         res["e2e"] = {"ms": float(mt), "h2d": h2d, "d2h": d2h}
+        for ho in host_out:
+            for name, h in ho.items():
+                if not bool(torch.isfinite(h.float()).all()):
+                    res.setdefault("errors", []).append(f"e2e output {name} not finite")
+
+    # ---------------- outside the timed regions: device status words and outputs
+    status = 0
+    for (dev_i, tag), ws in list(ops._WS.items()):
+        if dev_i == torch.cuda.current_device():
+            status |= ops.device_status(ws)
+    for name, t in (("attention output", a_out), ("moe output", m_out)):
+        if t is not None and not bool(torch.isfinite(t.float()).all()):
+            res.setdefault("errors", []).append(f"{name} not finite")
+    if status:
+        res.setdefault("errors", []).append(f"device status word {status} (1 = a bounded "
+                                            f"wait timed out, 2 = an index was out of range)")
+    res["device_status"] = status
     return res
 
 
@@ -537,29 +688,28 @@ def main():
     ap.add_argument("--config", choices=list(CONFIGS), default="c4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ref-budget-s", type=float, default=240.0,
+                    help="wall-clock bound of the reference arm's CPU run")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    cfg_desc = {"workload": CONFIGS[args.config]}
+    cfg_desc = config_dict(args.config, tokens_per_step(args.config))
 
     if args.impl == "reference":
         # The reference path is CPU code: rank 0 alone times it on the host cores.
         if rank != 0:
             return
-        vals = []
-        for i in range(args.warmup + args.steps):
-            v, cores, sample = cpu_reference_sample(args.config)
-            if i >= args.warmup:
-                vals.append(v)
-        v = statistics.median(vals)
+        v, n, n_w, cores, sample = cpu_reference_run(args.config, args.warmup, args.steps,
+                                                     args.ref_budget_s)
         line = {"metric": "hot-path tokens/s", "value": v, "unit": "tokens/s",
-                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-                "config": dict(cfg_desc, parallelism="host CPU"), "impl": "reference",
+                "n_gpus": args.gpus, "steps": n, "warmup": n_w,
+                "ms_per_step": tokens_per_step(args.config) / v * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded)", "config": cfg_desc,
+                "impl": "reference", "parallelism": "host CPU",
                 "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores,
                                  "kind": "port", "sample": sample},
                 "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -577,10 +727,16 @@ def main():
         # the reference-arm CPU sample (rank 0, N=1 only) keeps every host core
         bind_to_gpu_cpus(local)
     res = run_ours(args, rank, world, device)
+    errors = list(res.get("errors", []))
+    if world > 1:
+        bad = torch.tensor([len(errors)], dtype=torch.int32, device=device)
+        torch.distributed.all_reduce(bad)
+        if int(bad) and not errors:
+            errors.append("another rank reported an error")
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, sample = cpu_reference_sample(args.config)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not errors:
+        v, n, n_w, cores, sample = cpu_reference_run(args.config, 1, 1, 60.0)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
 
     if rank == 0:
@@ -622,23 +778,24 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": res["ms"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-            "config": dict(cfg_desc, tokens_per_step_per_gpu=res["tokens"],
-                           l2="inputs larger than L2 (KV cache and expert weights are GBs)",
-                           parallelism=res["parallelism"]),
+            "config": cfg_desc, "parallelism": res["parallelism"],
             "roofline": roof, "cpu_baseline": cpu, "clocks": res["clocks"],
-            "gpu_launches": res["launches"],
+            "gpu_launches": res["launches"], "phases_ms": res["phases_ms"],
         }
-        if "moe_gemm" in res:
-            line["moe_gemm_ms"] = res["moe_gemm"]
+        for key in ("moe_layer", "proj"):
+            if key in res:
+                line[key] = res[key]
         if "e2e" in res:
             e = res["e2e"]
             line["e2e"] = {"value": res["tokens"] * world / (e["ms"] * 1e-3), "unit": "tokens/s",
                            "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"]}
-        if res["device_status"]:
-            line["device_status"] = res["device_status"]
+        if errors:
+            line["errors"] = errors
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+    if errors:
+        sys.exit(1)
 
 
 if __name__ == "__main__":

@@ -81,22 +81,27 @@ int lb_router_topk(const void* logits, int64_t ld, int64_t T, int64_t E, int64_t
  * torch.where(expert_mask[e]) order).
  * Outputs: row_start [G+1] (G = num_local_experts + 1), perm_token [T + T*k] (token of
  * each packed row; rows past row_start[G] are untouched), row_of [T*k] (packed row of
- * pair (t,j) or -1).  workspace: lb_moe_permute_workspace_size(). */
+ * pair (t,j) or -1).  With T = 0 only row_start is written (ids, perm_token and row_of
+ * may be NULL).  workspace: lb_moe_permute_workspace_size(). */
 size_t lb_moe_permute_workspace_size(int64_t T, int64_t k, int64_t num_local_experts);
 int lb_moe_permute(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base,
                    int64_t num_local_experts, int32_t* row_start, int32_t* perm_token,
                    int32_t* row_of, void* workspace, size_t workspace_bytes, void* stream);
 
 /* The same permutation for callers that cannot allocate device memory (no workspace):
- * a plugin host whose enqueue hook forbids allocation, code that runs while a stream is
- * being captured into a CUDA graph under a no-allocation policy, or a foreign-language
- * binding without a device allocator.  No counterpart in the reference (which allocates
- * with torch inside the MoE module).  Scratch is a fixed 8,464-byte array in the
- * library's static device memory, held by every GPU that loads the library until exit.
- * Limit: num_local_experts <= 1024 (larger returns LB_ERR_UNSUPPORTED).  The first call
- * on each device looks up that array's address (cudaGetSymbolAddress) and caches it; make
- * that first call before any stream capture.  All calls on a device share the array, so
- * calls that overlap on the GPU (different streams, no ordering between them) race. */
+ * a plugin host whose enqueue hook forbids allocation, or a foreign-language binding
+ * without a device allocator.  No counterpart in the reference (which allocates with
+ * torch inside the MoE module).  Scratch is a fixed 8,464-byte array in the library's
+ * static device memory, held by every GPU that loads the library until exit.
+ * Limits: num_local_experts <= 1024 and T*k <= 2^20 pairs (larger returns
+ * LB_ERR_UNSUPPORTED): without per-chunk scratch every local expert scans all pairs, so
+ * the work grows as num_local_experts * T * k and the cap keeps a call in the
+ * low-millisecond range.  The first call on each device looks up that array's address
+ * (cudaGetSymbolAddress) and caches it for the life of the process; make that first call
+ * before any stream capture, and do not use the entry point on a device after
+ * cudaDeviceReset (the cached address then names memory that is no longer mapped).  All
+ * calls on a device share the array, so calls that overlap on the GPU (different
+ * streams, no ordering between them) race. */
 int lb_moe_permute_noalloc(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base,
                            int64_t num_local_experts, int32_t* row_start, int32_t* perm_token,
                            int32_t* row_of, void* stream);

@@ -352,9 +352,9 @@ static int run_permute(const int32_t* ids, const float* wf, int T, int k, int ex
                        int nl, int* counts, int* row_start, int* mtile_start, int32_t* perm_token,
                        float* perm_w, int32_t* row_of, cudaStream_t st) {
   const int G = nl + 1;
-  LB_CUDA_CHECK(cudaMemsetAsync(counts, 0, sizeof(int) * (G + 1), st));
-  LB_CUDA_CHECK(cudaMemsetAsync(row_of, 0xff, sizeof(int32_t) * (size_t)T * k, st));
   const int n = T * k;
+  LB_CUDA_CHECK(cudaMemsetAsync(counts, 0, sizeof(int) * (G + 1), st));
+  if (n > 0) LB_CUDA_CHECK(cudaMemsetAsync(row_of, 0xff, sizeof(int32_t) * (size_t)n, st));
   if (n > 0) {
     const int grid = std::min(num_sms() * 2, (n + 1023) / 1024);
     launch_k(k_moe_count, std::max(grid, 1), 1024, sizeof(int) * nl, st, ids, n, expert_base, nl, counts);
@@ -529,7 +529,7 @@ static int run_permute_chunked(const int32_t* ids, const float* wf, int T, int k
                                int32_t* row_of, cudaStream_t st, int T0) {
   const int n = T * k;
   const int nc = perm_chunks(T, k);
-  LB_CUDA_CHECK(cudaMemsetAsync(row_of, 0xff, sizeof(int32_t) * (size_t)n, st));
+  if (n > 0) LB_CUDA_CHECK(cudaMemsetAsync(row_of, 0xff, sizeof(int32_t) * (size_t)n, st));
   if (nc > 0 && nl > 0) {
     launch_k(k_perm_chunk_hist, nc, PERM_CHUNK, sizeof(int) * nl, st, ids, T, k, expert_base, nl, chunk_hist);
     { int _rc = launched("k_perm_chunk_hist"); if (_rc) return _rc; }
@@ -664,6 +664,9 @@ int moe_core(const MoeCore& c, const MoeWs& w, cudaStream_t st) {
 // library holds LB_NOALLOC_SCRATCH_INTS * 4 bytes (8,464 bytes) of it until the process
 // exits, and every call on a device shares it.
 constexpr int LB_NOALLOC_MAX_LOCAL_EXPERTS = 1024;
+// k_moe_scatter runs one CTA per local expert over all T*k pairs: the cap bounds a call's
+// work to num_local_experts * 2^20 id reads (L2-resident).
+constexpr long long LB_NOALLOC_MAX_PAIRS = 1ll << 20;
 constexpr int LB_NOALLOC_SCRATCH_INTS = 64 + 2 * (LB_NOALLOC_MAX_LOCAL_EXPERTS + 2);
 static __device__ __align__(256) int g_permute_scratch[LB_NOALLOC_SCRATCH_INTS];
 
@@ -673,7 +676,8 @@ static int* g_noalloc_addr[LB_NOALLOC_MAX_DEVICES] = {};
 
 // Device address of g_permute_scratch on the current device.  In host code the array's
 // name only stands in for the symbol; the address a kernel may use comes from
-// cudaGetSymbolAddress, looked up once per device (with that device current) and cached.
+// cudaGetSymbolAddress, looked up once per device (with that device current) and cached
+// for the life of the process (a cudaDeviceReset invalidates it).
 static int noalloc_scratch(int** out) {
   int dev = -1;
   LB_CUDA_CHECK(cudaGetDevice(&dev));
@@ -717,7 +721,8 @@ size_t lb_moe_permute_workspace_size(int64_t T, int64_t k, int64_t nl) {
 int lb_moe_permute(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base,
                    int64_t nl, int32_t* row_start, int32_t* perm_token, int32_t* row_of,
                    void* workspace, size_t workspace_bytes, void* stream) {
-  LB_REQUIRE(ids && row_start && perm_token && row_of, "lb_moe_permute: null pointer");
+  LB_REQUIRE(row_start && (T == 0 || (ids && perm_token && row_of)),
+             "lb_moe_permute: null pointer");
   LB_REQUIRE(T >= 0 && k > 0 && k <= 32 && nl > 0 && nl <= 2046 && expert_base >= 0,
              "lb_moe_permute: bad sizes");
   LB_REQUIRE(T * k < (1ll << 30), "lb_moe_permute: too many pairs");
@@ -736,10 +741,15 @@ int lb_moe_permute(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base
 int lb_moe_permute_noalloc(const int32_t* ids, int64_t T, int64_t k, int64_t expert_base,
                            int64_t nl, int32_t* row_start, int32_t* perm_token, int32_t* row_of,
                            void* stream) {
-  LB_REQUIRE(ids && row_start && perm_token && row_of, "lb_moe_permute_noalloc: null pointer");
+  LB_REQUIRE(row_start && (T == 0 || (ids && perm_token && row_of)),
+             "lb_moe_permute_noalloc: null pointer");
   LB_REQUIRE(T >= 0 && k > 0 && k <= 32 && expert_base >= 0 && nl > 0,
              "lb_moe_permute_noalloc: bad sizes");
-  LB_REQUIRE(T * k < (1ll << 30), "lb_moe_permute_noalloc: too many pairs");
+  if (T * k > LB_NOALLOC_MAX_PAIRS)
+    return fail(LB_ERR_UNSUPPORTED,
+                "lb_moe_permute_noalloc: %lld (token, slot) pairs exceed the limit of %lld "
+                "(use lb_moe_permute with a workspace)",
+                (long long)(T * k), LB_NOALLOC_MAX_PAIRS);
   if (nl > LB_NOALLOC_MAX_LOCAL_EXPERTS)
     return fail(LB_ERR_UNSUPPORTED,
                 "lb_moe_permute_noalloc: %lld local experts exceed the fixed scratch limit of %d "

@@ -214,6 +214,52 @@ def attn_prologue(q_in, k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions
     return q_out
 
 
+def gated_attention_layer(x, w_qkv, num_heads, num_kv_heads, q_norm_w, k_norm_w,
+                          cos_sin_cache, eps, positions, slot_mapping, k_cache, v_cache,
+                          block_tables, context_lens, cu_seqlens_q, w_o, scale, out=None,
+                          max_q_len=None, work_hint=None, events=None, qkv=None, q=None,
+                          attn_out=None, ws_tag="pod", tp=None, tp_phases=0,
+                          stage_events=None):
+    """The whole gated full-attention layer from its hidden states
+    (``Qwen3_5FullAttention.forward``, nanovllm/models/qwen3_5.py:705-746), three library
+    calls:
+
+    1. one GEMM for the three projections: ``qkv = x @ w_qkv.T`` with ``w_qkv`` =
+       ``[q_proj.weight; k_proj.weight; v_proj.weight]`` (``[Hq*2D + 2*Hkv*D, H]``);
+    2. ``lb_attn_prologue``: (1+w) RMSNorm and partial RoPE of query and key, the K/V of the
+       new tokens stored into the paged cache at ``slot_mapping``;
+    3. ``lb_pod_attn_oproj``: attention over the cache for every sequence of the batch,
+       ``* sigmoid(gate)`` (the gate read in place from q_proj's output) and o_proj.
+
+    ``qkv`` ``[N, Hq*2D + 2*Hkv*D]`` and ``q`` ``[N, Hq, D]`` may be given as preallocated
+    buffers (CUDA-graph capture); ``attn_out`` ``[N, Hq*D]`` optionally receives the
+    attention output before the gate.  The prologue reports bad positions or slots in the
+    status word of the workspace tagged ``ws_tag + "_prologue"``.  ``stage_events`` (up to
+    two ``torch.cuda.Event``) are recorded after the GEMM and after the prologue.
+    """
+    N = x.shape[0]
+    Hq, Hkv = num_heads, num_kv_heads
+    D = k_cache.shape[-1]
+    if w_qkv.shape[0] != Hq * 2 * D + 2 * Hkv * D:
+        raise ValueError("w_qkv must stack q_proj [Hq*2D], k_proj [Hkv*D] and v_proj [Hkv*D] rows")
+    stage_events = list(stage_events or []) + [None, None]
+    qkv = gemm(x, w_qkv, out=qkv)
+    if stage_events[0] is not None:
+        stage_events[0].record()
+    q3 = qkv[:, :Hq * 2 * D].view(N, Hq, 2 * D)
+    k_in = qkv[:, Hq * 2 * D:Hq * 2 * D + Hkv * D].view(N, Hkv, D)
+    v_in = qkv[:, Hq * 2 * D + Hkv * D:].view(N, Hkv, D)
+    status = workspace(256, x.device, ws_tag + "_prologue").view(torch.int32)[:1]
+    q = attn_prologue(q3[..., :D], k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions,
+                      slot_mapping, k_cache, v_cache, eps, q_out=q, status=status)
+    if stage_events[1] is not None:
+        stage_events[1].record()
+    return pod_attn_oproj(q, q3[..., D:], k_cache, v_cache, block_tables, context_lens,
+                          cu_seqlens_q, w_o, scale, out=out, attn_out=attn_out,
+                          max_q_len=max_q_len, ws_tag=ws_tag, events=events,
+                          work_hint=work_hint, tp=tp, tp_phases=tp_phases)
+
+
 def pod_args(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o, scale,
              out, attn_out=None, max_q_len=None, kv_split_pages=0) -> LbPodArgs:
     N, Hq, D = q.shape

@@ -12,6 +12,10 @@ Shapes follow the five benchmark configurations of the hot path:
 * ``c4``: hybrid pair: c1-shaped attention over 512 decode sequences with
   ctx ~ U[1024,16384] plus one 4096-token prefill chunk, then the c3 MoE at T=4608.
 
+The whole gated attention layer (``make_attn_layer_params`` / ``layer_positions_slots``)
+starts from hidden states: one merged q/k/v projection, the (1+w) RMSNorm + partial RoPE
+prologue with the K/V store of the new tokens, then POD attention, gate and o_proj.
+
 Weights are N(0, 0.02) bf16, activations N(0, 1) bf16.  Small cases are drawn from a
 CPU ``torch.Generator`` so that the CPU oracle and the GPU path see identical bytes;
 large bench cases may be drawn directly on the device (``device='cuda'``), which gives
@@ -201,7 +205,7 @@ class AttnBatch:
 
 
 def make_attn_batch(decode_ctx, prefill=(), Hq=16, Hkv=2, D=256, H=2048, seed=1,
-                    device="cpu", extra_blocks=0, w_std=0.02) -> AttnBatch:
+                    device="cpu", extra_blocks=0, w_std=0.02, tile_pages=0) -> AttnBatch:
     """Build a paged batch.
 
     decode_ctx: list of context lengths (cached + 1) of the decode sequences.
@@ -209,6 +213,9 @@ def make_attn_batch(decode_ctx, prefill=(), Hq=16, Hkv=2, D=256, H=2048, seed=1,
     Pages are drawn as a seeded random permutation of the block pool (shuffled tables).
     The K/V cache holds N(0,1) values for every slot (new tokens' K/V are assumed
     already stored, as the reference stores them before attending, attention.py:103).
+    ``tile_pages > 0`` draws only that many pages of N(0,1) K/V and repeats them over the
+    pool: a gigabyte-sized host cache in seconds, for CPU timing where values do not
+    change the work.
     """
     g = _gen(seed, device)
     gcpu = torch.Generator().manual_seed(seed + 1000)
@@ -227,8 +234,20 @@ def make_attn_batch(decode_ctx, prefill=(), Hq=16, Hkv=2, D=256, H=2048, seed=1,
     N = sum(qlen_list)
     q = _randn(g, (N, Hq, D), 1.0, device)
     gate = _randn(g, (N, Hq, D), 1.0, device)
-    k_cache = _randn(g, (num_blocks, BLOCK_SIZE, Hkv, D), 1.0, device)
-    v_cache = _randn(g, (num_blocks, BLOCK_SIZE, Hkv, D), 1.0, device)
+    if tile_pages > 0 and num_blocks > tile_pages:
+        caches = []
+        for _ in range(2):
+            blk = _randn(g, (tile_pages, BLOCK_SIZE, Hkv, D), 1.0, device)
+            c = torch.empty((num_blocks, BLOCK_SIZE, Hkv, D), dtype=torch.bfloat16,
+                            device=device)
+            for i in range(0, num_blocks, tile_pages):
+                n = min(tile_pages, num_blocks - i)
+                c[i:i + n] = blk[:n]
+            caches.append(c)
+        k_cache, v_cache = caches
+    else:
+        k_cache = _randn(g, (num_blocks, BLOCK_SIZE, Hkv, D), 1.0, device)
+        v_cache = _randn(g, (num_blocks, BLOCK_SIZE, Hkv, D), 1.0, device)
     w_o = _randn(g, (H, Hq * D), w_std, device)
     cu = torch.zeros(B + 1, dtype=torch.int32)
     cu[1:] = torch.cumsum(torch.tensor(qlen_list, dtype=torch.int64), 0).to(torch.int32)
@@ -256,3 +275,77 @@ def c2_batch(seed=1, device="cpu", **kw):
 def c4_attn_batch(seed=1, device="cpu", **kw):
     return make_attn_batch(uniform_ctx(512, 1024, 16384, seed), [(0, 4096)], seed=seed,
                            device=device, **kw)
+
+
+# ----------------------------------------------------------------------------------------
+# The whole gated attention layer (projections and prologue in front of the POD call)
+# ----------------------------------------------------------------------------------------
+@dataclass
+class AttnLayerParams:
+    """Weights of one gated full-attention layer (nanovllm/models/qwen3_5.py:587-746)
+    besides ``w_o`` (which lives in the ``AttnBatch``).
+
+    ``w_qkv`` stacks ``q_proj.weight [Hq*2D, H]`` (query and gate interleaved per head,
+    qwen3_5.py:710-713), ``k_proj.weight [Hkv*D, H]`` and ``v_proj.weight [Hkv*D, H]`` so
+    that one GEMM computes all three projections.  ``cos_sin_cache`` is the rotary module's
+    fp32 ``[max_position, rotary_dim]`` table (rotary_embedding.py:26-33).
+    """
+    w_qkv: torch.Tensor
+    q_norm_w: torch.Tensor
+    k_norm_w: torch.Tensor
+    cos_sin_cache: torch.Tensor
+    num_heads: int
+    num_kv_heads: int
+    head_dim: int
+    eps: float = 1e-6
+
+    def split(self, qkv: torch.Tensor):
+        """Views of one ``[N, Hq*2D + 2*Hkv*D]`` projection output: query ``[N, Hq, D]``,
+        gate ``[N, Hq, D]`` (both strided inside q_proj's per-head ``[query | gate]``),
+        key and value ``[N, Hkv, D]``."""
+        N = qkv.shape[0]
+        Hq, Hkv, D = self.num_heads, self.num_kv_heads, self.head_dim
+        q3 = qkv[:, :Hq * 2 * D].view(N, Hq, 2 * D)
+        k = qkv[:, Hq * 2 * D:Hq * 2 * D + Hkv * D].view(N, Hkv, D)
+        v = qkv[:, Hq * 2 * D + Hkv * D:].view(N, Hkv, D)
+        return q3[..., :D], q3[..., D:], k, v
+
+
+def rotary_cache(rotary_dim: int, max_position: int, base: float) -> torch.Tensor:
+    """fp32 ``[max_position, rotary_dim]`` cos|sin table built with the reference's own
+    torch operations (rotary_embedding.py:26-33), so every device reads identical bits."""
+    from .layers.full_attention import RotaryEmbedding
+    rope = RotaryEmbedding(rotary_dim, rotary_dim, max_position, base)
+    return rope.cos_sin_cache.reshape(max_position, rotary_dim).contiguous()
+
+
+def make_attn_layer_params(H=2048, Hq=16, Hkv=2, D=256, rotary_dim=64, theta=1.0e7,
+                           max_position=16384 + 4096, seed=0, device="cpu",
+                           std=0.02) -> AttnLayerParams:
+    g = _gen(seed, device)
+    w_qkv = _randn(g, (Hq * 2 * D + 2 * Hkv * D, H), std, device)
+    q_norm_w = _randn(g, (D,), std, device)
+    k_norm_w = _randn(g, (D,), std, device)
+    cs = rotary_cache(rotary_dim, max_position, theta).to(device)
+    return AttnLayerParams(w_qkv, q_norm_w, k_norm_w, cs, Hq, Hkv, D)
+
+
+def layer_positions_slots(batch: AttnBatch):
+    """Positions and KV slots of the batch's new tokens: sequence b's query rows are its
+    last ``qlen_b`` positions of ``ctx_b`` (model_runner.py:493-657); the slot of position
+    p is ``block_tables[b, p // 256] * 256 + p % 256``.  Returns CPU (int64, int32)."""
+    bt = batch.block_tables.cpu()
+    pos, slot = [], []
+    for b, (c, L) in enumerate(zip(batch.ctx_list, batch.qlen_list)):
+        p = torch.arange(c - L, c, dtype=torch.int64)
+        pos.append(p)
+        slot.append(bt[b, p // BLOCK_SIZE].to(torch.int64) * BLOCK_SIZE + p % BLOCK_SIZE)
+    if not pos:
+        return torch.zeros(0, dtype=torch.int64), torch.zeros(0, dtype=torch.int32)
+    return torch.cat(pos), torch.cat(slot).to(torch.int32)
+
+
+def make_layer_input(N, H, seed=7, device="cpu") -> torch.Tensor:
+    """Hidden states entering the attention layer, N(0, 1) bf16."""
+    g = _gen(seed, device)
+    return _randn(g, (N, H), 1.0, device)

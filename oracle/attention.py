@@ -30,15 +30,15 @@ import torch.nn.functional as F
 
 
 def store_kvcache(k, v, k_cache, v_cache, slot_mapping):
-    """attention.py:50-80: ``cache.flat[slot] = row`` for slot != -1."""
+    """attention.py:50-80: ``cache.flat[slot] = row`` for slot != -1 (one indexed copy of
+    the kept rows, the index-assignment form of attention.py:62-70)."""
     nb, bs, hkv, d = k_cache.shape
     kc = k_cache.view(nb * bs, hkv, d)
     vc = v_cache.view(nb * bs, hkv, d)
-    for i, s in enumerate(slot_mapping.tolist()):
-        if s == -1:
-            continue
-        kc[s] = k[i]
-        vc[s] = v[i]
+    keep = slot_mapping.long() != -1
+    s = slot_mapping.long()[keep]
+    kc[s] = k[keep].to(kc.dtype)
+    vc[s] = v[keep].to(vc.dtype)
 
 
 def gather_pages(cache, table_row, n):
@@ -112,7 +112,7 @@ def paged_attention(q, k_cache, v_cache, block_tables, context_lens, cu_seqlens_
     Computed in ``dtype`` (fp32 by default) with an explicit mask.  Returns ``[N, Hq, D]``.
     """
     cu = cu_seqlens_q.tolist()
-    out = torch.empty(q.shape, dtype=dtype)
+    out = torch.empty(q.shape, dtype=dtype, device=q.device)
     hq = q.shape[1]
     for b, c in enumerate(context_lens.tolist()):
         s, e = cu[b], cu[b + 1]
@@ -127,12 +127,33 @@ def paged_attention(q, k_cache, v_cache, block_tables, context_lens, cu_seqlens_
         v = v.repeat_interleave(hq // hkv, dim=1)
         qq = q[s:e].to(dtype)                            # [L, Hq, D]
         sc = torch.einsum("lhd,chd->hlc", qq, k) * scale
-        qpos = torch.arange(c - L, c).view(L, 1)
-        kpos = torch.arange(c).view(1, c)
+        qpos = torch.arange(c - L, c, device=q.device).view(L, 1)
+        kpos = torch.arange(c, device=q.device).view(1, c)
         sc = sc.masked_fill((kpos > qpos).unsqueeze(0), float("-inf"))
         p = torch.softmax(sc, dim=-1)
         out[s:e] = torch.einsum("hlc,chd->lhd", p, v)
     return out
+
+
+def attention_rows_fp32(q_rows, positions, k, v, scale):
+    """Attention of selected query rows of ONE sequence over its gathered keys, in fp32.
+
+    Row i sits at absolute position ``positions[i]`` and sees keys ``[0, positions[i]]``:
+    the bottom-right causal rule of a chunk on a cached prefix (attention.py:104-141,
+    flash-attn varlen) and, for the last position, the decode query
+    (sdpa_fallback.py:121-159).  ``q_rows [R, Hq, D]``, ``k``/``v`` ``[C, Hkv, D]``;
+    returns ``[R, Hq, D]`` fp32.  Lets a check cover a sample of a long chunk's rows
+    without the whole ``[L, C]`` score matrix.
+    """
+    hq, hkv = q_rows.shape[1], k.shape[1]
+    kk = k.float().repeat_interleave(hq // hkv, dim=1)
+    vv = v.float().repeat_interleave(hq // hkv, dim=1)
+    sc = torch.einsum("rhd,chd->hrc", q_rows.float(), kk) * scale
+    kpos = torch.arange(k.shape[0], device=k.device).view(1, -1)
+    mask = kpos > positions.to(k.device).view(-1, 1)
+    sc = sc.masked_fill(mask.unsqueeze(0), float("-inf"))
+    p = torch.softmax(sc, dim=-1)
+    return torch.einsum("hrc,chd->rhd", p, vv)
 
 
 def split_kv_decode_fp32(q, k_cache, v_cache, block_tables, context_lens, scale, num_splits):

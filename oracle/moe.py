@@ -153,10 +153,13 @@ def moe_block_bf16(x, p, path="sparse", ids=None, w=None):
 
 # ---------------------------------------------------------------- fp32 oracle
 def moe_block_fp32(x, p, ids, w):
-    """The block in fp32 for a fixed routing (ids [T,k], w [T,k] fp32).  Returns fp32."""
+    """The block in fp32 for a fixed routing (ids [T,k], w [T,k] fp32).  Returns fp32.
+
+    Plain torch, so it runs wherever its inputs live: the tests also evaluate it on the
+    GPU (fp32 matmuls, TF32 off) to check full-size launches row by row."""
     xf = x.float()
     T, k = ids.shape
-    out = torch.zeros(T, p.hidden, dtype=torch.float32)
+    out = torch.zeros(T, p.hidden, dtype=torch.float32, device=xf.device)
     ids = ids.long()
     for e in torch.unique(ids).tolist():
         tok, pos = torch.where(ids == e)

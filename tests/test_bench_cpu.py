@@ -1,6 +1,6 @@
 """bench.py on the CPU: the algorithmic work behind its roofline numbers, and the
-reference arm's JSON line (the reference's CPU path, restated in oracle/, timed on a
-bounded sample)."""
+reference arm's JSON line (the reference's CPU path, restated in oracle/, timed on full
+steps of the workload)."""
 import json
 import os
 import subprocess
@@ -25,18 +25,40 @@ def test_attention_work_counts_kv_bytes_and_causal_pairs():
     assert byts == kv_tokens * Hkv * D * 2 * 2 + 3 * b.num_tokens * Hq * D * 2
 
 
-def test_moe_work_is_the_hit_experts_weights_plus_rows():
-    gu, dn = bench.moe_work(256, 367)
+def test_moe_work_counts_weights_inputs_and_outputs_not_scratch_rows():
+    gu, dn, layer = bench.moe_work(256, 367)
     rows = 256 * 10 + 256
-    assert gu["bytes"] == 368 * 2 * 512 * 2048 * 2 + rows * 2048 * 2 + rows * 512 * 2
-    assert dn["bytes"] == 368 * 2048 * 512 * 2 + rows * 512 * 2 + rows * 2048 * 2
+    x = out = 256 * 2048 * 2
+    # the hit experts' and the shared expert's weights, the token rows once; the gathered
+    # rows, activations and weighted expert rows between the kernels are scratch
+    assert gu["bytes"] == 368 * 2 * 512 * 2048 * 2 + x
+    assert dn["bytes"] == 368 * 2048 * 512 * 2 + out
+    assert layer["bytes"] == 512 * 2048 * 2 + gu["bytes"] + dn["bytes"] + 2048 * 2
     assert gu["flops"] == 2.0 * rows * 2048 * 1024 and dn["flops"] == 2.0 * rows * 512 * 2048
+    assert layer["flops"] == 2.0 * 256 * 2048 * 512 + gu["flops"] + dn["flops"] + 2.0 * 256 * 2048
+
+
+def test_both_arms_describe_the_same_config():
+    for cfg in bench.CONFIGS:
+        d = bench.config_dict(cfg, bench.tokens_per_step(cfg))
+        assert set(d) == {"workload", "tokens_per_step_per_gpu", "l2"}
+    assert bench.tokens_per_step("c4") == 4096 + 512
+
+
+def test_layer_positions_and_slots_follow_the_block_tables():
+    b = W.make_attn_batch([300, 1000], [(512, 256)], seed=1)
+    pos, slots = W.layer_positions_slots(b)
+    assert pos.tolist()[:2] == [512, 513] and pos.tolist()[-2:] == [299, 999]
+    bt = b.block_tables
+    for i, (n, p) in enumerate([(0, 512), (255, 767), (256, 299), (257, 999)]):
+        seq = 0 if n < 256 else n - 255
+        assert int(slots[n]) == int(bt[seq, p // 256]) * 256 + p % 256
 
 
 def test_reference_arm_prints_the_contract_line():
     r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
-                        "--steps", "1", "--warmup", "0"], capture_output=True, text=True,
-                       timeout=600, cwd=ROOT)
+                        "--config", "c1", "--steps", "2", "--warmup", "0"],
+                       capture_output=True, text=True, timeout=600, cwd=ROOT)
     assert r.returncode == 0, r.stderr[-2000:]
     line = json.loads(r.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference"
@@ -45,3 +67,6 @@ def test_reference_arm_prints_the_contract_line():
     cb = line["cpu_baseline"]
     assert cb["value"] == line["value"] and cb["cores"] >= 1 and cb["kind"] in ("port", "reference")
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+    # full steps of the workload, the same config object as the GPU arm's line
+    assert "full c1 step" in cb["sample"] and 1 <= line["steps"] <= 2
+    assert line["config"] == bench.config_dict("c1", 64)

@@ -12,7 +12,6 @@ import torch
 
 from layerbatch_b200 import ops
 from layerbatch_b200 import workloads as W
-from oracle import moe as OM
 
 pytestmark = pytest.mark.gpu
 
@@ -66,6 +65,8 @@ def test_step_captured_in_cuda_graph_on_external_stream(cuda):
         with torch.cuda.stream(ext):
             g.replay()
         torch.cuda.synchronize()
-        assert OM.rel_err(out_a.float(), ref_a.float()) <= 1e-3, it
-        assert torch.equal(out_m, ref_m), it     # the MoE path is deterministic
+        # both layers are deterministic (fixed reduction orders, no atomics on values),
+        # so a replay reproduces the eager call bit for bit
+        assert torch.equal(out_a, ref_a), it
+        assert torch.equal(out_m, ref_m), it
     del g
