@@ -469,7 +469,8 @@ def run_ours(args, rank, world, device):
                 ev["moe0"].record()
             if sharded:
                 from layerbatch_b200.engine.ep import ep_moe_forward_nvlink
-                ep_moe_forward_nvlink(ep_block, xx, ep_block.ep_exchange, out=om)
+                ep_moe_forward_nvlink(ep_block, xx, ep_block.ep_exchange, out=om,
+                                      events=ev.get("moe"))
             else:
                 ops.moe_forward(xx, pm.router, pm.gate_up, pm.down, pm.sh_gate, pm.sh_up,
                                 pm.sh_down, pm.sh_gate_w, 10, out=om, events=ev.get("moe"))
@@ -512,8 +513,6 @@ def run_ours(args, rank, world, device):
         e = {"attn0": mk(), "attn1": mk(), "moe0": mk(), "moe1": mk(),
              "pod": [mk() for _ in range(4)], "moe": [mk() for _ in range(4)],
              "stages": [mk(), mk()]}
-        if sharded:
-            e.pop("moe")
         evs.append(e)
     for i in range(K):
         step(ev=evs[i] if attn is not None or moe else None)
@@ -538,7 +537,11 @@ def run_ours(args, rank, world, device):
         else:
             phases["plan"] = mean_ms(lambda e: e["attn0"], lambda e: e["pod"][0])
         phases["pod_attn"] = t_attn * 1e3
-        phases["merge_oproj"] = mean_ms(lambda e: e["pod"][1], lambda e: e["attn1"])
+        # split merge + gate (k_pod_merge), then the o_proj GEMM (with tensor parallelism:
+        # the GEMM storing fp32 tiles into the owners' memory, the owners' reduction and
+        # the gather of the other ranks' rows)
+        phases["merge"] = mean_ms(lambda e: e["pod"][1], lambda e: e["pod"][2])
+        phases["oproj"] = mean_ms(lambda e: e["pod"][2], lambda e: e["pod"][3])
         phases["attention_layer"] = mean_ms(lambda e: e["attn0"], lambda e: e["attn1"])
         if layer:
             g, pr = layer_proj_work(attn.num_tokens, Hq=Hq_l, Hkv=Hkv_l)
@@ -547,7 +550,15 @@ def run_ours(args, rank, world, device):
                            "prologue_gbs": pr["bytes"] / phases["prologue"] / 1e6}
     if moe:
         phases["moe_layer"] = mean_ms(lambda e: e["moe0"], lambda e: e["moe1"])
-        if not sharded:
+        if sharded:
+            # expert parallel: router + top-k + routing table + row dispatch over NVLink;
+            # the wait for every source's rows + permutation + gather; the grouped GEMMs;
+            # the per-row sums sent back + the wait for them + the combine
+            phases["moe_dispatch"] = mean_ms(lambda e: e["moe0"], lambda e: e["moe"][1])
+            phases["moe_wait_permute"] = mean_ms(lambda e: e["moe"][1], lambda e: e["moe"][2])
+            phases["moe_experts"] = mean_ms(lambda e: e["moe"][2], lambda e: e["moe"][3])
+            phases["moe_return_combine"] = mean_ms(lambda e: e["moe"][3], lambda e: e["moe1"])
+        else:
             t_g1 = mean_ms(lambda e: e["moe"][0], lambda e: e["moe"][1]) * 1e-3
             t_g2 = mean_ms(lambda e: e["moe"][2], lambda e: e["moe"][3]) * 1e-3
             phases["moe_gate_up"] = t_g1 * 1e3

@@ -7,8 +7,9 @@ them.
 
 Every check compares the CUDA path with ``oracle/``:
 
-* routing: router logits within one bf16 ulp of the CPU oracle's, top-k ids bit-exact
-  given the kernel's logits, and the expert permutation bit-exact, over all T tokens;
+* routing: router logits within one bf16 ulp of the exactly rounded product, top-k ids
+  bit-exact against the oracle given the kernel's logits, and the expert permutation
+  bit-exact against the oracle, over all T tokens;
 * outputs: ``max|y - y32| / max|y32| <= 2e-2`` against the fp32 oracle, on EVERY row with
   the oracle's torch code evaluated in fp32 on the GPU (TF32 off), and on a seeded sample
   of rows with the oracle on the CPU: prefill rows spread over the whole chunk (first and
@@ -66,12 +67,19 @@ def _check_moe_full(dev, T, p, x, out, logits, ids):
     k, E = 10, 512
     ids_c = ids.cpu().long()
     logits_c = logits.cpu()
-    # router logits within one bf16 ulp of the CPU oracle (fp32 summation order differs)
-    ref = OM.router_logits(x.cpu(), p.router.cpu())
+    # router logits (F.linear in bf16 with fp32 accumulation, qwen3_5.py:769) against the
+    # exact product (fp64 on the GPU): within one bf16 ulp plus the fp32 summation error
+    # allowed for K = 2048 terms (2^-17 of sum |x w|; it only matters where the Zipf bias
+    # column cancels the rest of the sum and the logit is near zero)
+    exact = x.double() @ p.router.double().t()
+    absum = x.double().abs() @ p.router.double().abs().t()
+    ref = exact.to(torch.bfloat16).cpu()
     d = (logits_c.float() - ref.float()).abs()
     ulp = torch.maximum(ref.float().abs(), logits_c.float().abs()) * 2 ** -7
-    assert bool((d <= ulp + 1e-6).all())
-    assert float((d == 0).float().mean()) > 0.9
+    slack = (absum * 2.0 ** -17).float().cpu()
+    assert bool((d <= ulp + slack + 1e-6).all()), float((d / (ulp + slack)).max())
+    assert float((d == 0).float().mean()) > 0.99
+    del exact, absum
     # routing bit-exact given the kernel's logits, every token
     w32, ids_ref = OM.topk_route(logits_c, k)
     assert torch.equal(ids_c, ids_ref)

@@ -1,7 +1,9 @@
 """Tensor / expert parallel on 2 GPUs (skipped with fewer than 2 GPUs).
 
 Each rank compares the sharded result with the single-GPU library call on the same
-inputs: attention TP by KV head with the fp32 o_proj all-reduce, the MoE block with
+inputs: attention TP by KV head with the fp32 o_proj all-reduce and with the reduction
+over peer memory, the whole gated attention layer (projections, prologue and K/V store of
+each rank's heads, attention, o_proj reduced over peer memory), the MoE block with
 experts split over the ranks and the NCCL all-to-all exchange, and the MoE block with the
 NVLink peer-memory exchange (``lb_ep_moe_forward``).  NVLS is off (plain NCCL transport,
 no multicast objects) and the process group has a short timeout.
@@ -61,7 +63,41 @@ def _worker(rank, world, port, q):
                                        b.cu_seqlens_q, wo, b.scale, max_q_len=300, exchange=tpx)
         torch.cuda.synchronize()
         errs["tp_peer"] = OM.rel_err(tp2.float(), full.float())
+        # ---- the whole gated attention layer, TP by KV head (the bench's sharded step):
+        # each rank projects its own heads (its rows of the merged q/k/v weight), stores
+        # its KV head's new rows into its cache slice and reduces o_proj over peer memory
+        lp = W.make_attn_layer_params(seed=5, device=dev)
+        pos, slots = W.layer_positions_slots(b)
+        pos, slots = pos.to(dev), slots.to(dev)
+        x_attn = W.make_layer_input(b.num_tokens, 2048, seed=6, device=dev)
+        kc_full, vc_full = b.k_cache.clone(), b.v_cache.clone()
+        full_l = ops.gated_attention_layer(
+            x_attn, lp.w_qkv, 16, 2, lp.q_norm_w, lp.k_norm_w, lp.cos_sin_cache, lp.eps, pos,
+            slots, kc_full, vc_full, b.block_tables, b.context_lens, b.cu_seqlens_q, b.w_o,
+            b.scale, max_q_len=300, ws_tag="full_layer")
+        D = 256
+        hs, ks = shard.q_heads, shard.kv_heads
+        w_loc = torch.cat([lp.w_qkv[hs.start * 2 * D:hs.stop * 2 * D],
+                           lp.w_qkv[16 * 2 * D + ks.start * D:16 * 2 * D + ks.stop * D],
+                           lp.w_qkv[16 * 2 * D + 2 * D + ks.start * D:
+                                    16 * 2 * D + 2 * D + ks.stop * D]]).contiguous()
+        kc_l = b.k_cache[:, :, ks].contiguous()
+        vc_l = b.v_cache[:, :, ks].contiguous()
+        tpx2 = TPExchange(1024, 2048, device=dev)
+        for _ in range(2):
+            tp_l = ops.gated_attention_layer(
+                x_attn, w_loc, hs.stop - hs.start, ks.stop - ks.start, lp.q_norm_w,
+                lp.k_norm_w, lp.cos_sin_cache, lp.eps, pos, slots, kc_l, vc_l, b.block_tables,
+                b.context_lens, b.cu_seqlens_q, wo, b.scale, max_q_len=300,
+                ws_tag=f"tp_layer{rank}", tp=tpx2)
+        torch.cuda.synchronize()
+        errs["tp_layer"] = OM.rel_err(tp_l.float(), full_l.float())
+        # the K/V rows this rank stored equal the single-GPU layer's rows of its head
+        errs["tp_layer_cache"] = float(not (torch.equal(kc_l, kc_full[:, :, ks]) and
+                                            torch.equal(vc_l, vc_full[:, :, ks])))
+        errs["tp_layer_status"] = float(ops.device_status(ops._WS[(rank, f"tp_layer{rank}")]))
         dist.barrier()
+        tpx2.close()
         tpx.close()
         # ---- MoE, expert parallel with all-to-all
         H, E, I, k, T = 2048, 64, 512, 8, 96 + 32 * rank
@@ -176,3 +212,5 @@ def test_tp_attention_and_ep_moe_on_two_gpus():
     assert all(r[1] == "ok" for r in res), res
     for _, _, errs in res:
         assert errs["tp"] <= 2e-2 and errs["ep"] <= 2e-2 and errs["tp_peer"] <= 2e-2, errs
+        assert errs["tp_layer"] <= 2e-2, errs
+        assert errs["tp_layer_cache"] == 0 and errs["tp_layer_status"] == 0, errs
