@@ -295,17 +295,34 @@ __global__ void k_pod_merge(const int32_t* __restrict__ ctx_lens, const int32_t*
   }
 }
 
-__global__ void k_f32_to_bf16(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst,
-                              long long rows, int cols, long long ld_dst) {
+// out[r, c] = sum over s = 0..splits-1 (in that order) of parts[s][r, c]: the split-K
+// partial slices of the o_proj GEMM (EPI_F32_SPLIT) added in a fixed order, so the result
+// does not depend on which split finished first; written as bf16 or fp32.
+__global__ void k_splitk_reduce(const float* __restrict__ parts, int splits, long long rows,
+                                int cols, __nv_bfloat16* __restrict__ out_bf16,
+                                float* __restrict__ out_f32, long long ld_out) {
   pdl_entry();
+  const long long slice = rows * cols;
   // one block per row (grid-stride), the block's threads across the row's 4-float groups
   for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
     for (int c = threadIdx.x * 4; c < cols; c += blockDim.x * 4) {
-      const float4 v = *reinterpret_cast<const float4*>(src + r * cols + c);
-      uint2 o;
-      o.x = pack_bf16x2(v.x, v.y);
-      o.y = pack_bf16x2(v.z, v.w);
-      *reinterpret_cast<uint2*>(dst + r * ld_dst + c) = o;
+      const float* src = parts + r * cols + c;
+      float4 acc = *reinterpret_cast<const float4*>(src);
+      for (int s = 1; s < splits; ++s) {
+        const float4 v = *reinterpret_cast<const float4*>(src + s * slice);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      if (out_f32) {
+        *reinterpret_cast<float4*>(out_f32 + r * ld_out + c) = acc;
+      } else {
+        uint2 o;
+        o.x = pack_bf16x2(acc.x, acc.y);
+        o.y = pack_bf16x2(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(out_bf16 + r * ld_out + c) = o;
+      }
     }
   }
 }
@@ -390,6 +407,9 @@ __global__ void __launch_bounds__(256) k_tp_gather(int* hdr, const __nv_bfloat16
 // ------------------------------------------------------------------------------ host
 struct PodPlan {
   int split_tokens, max_splits, max_ctx, pf_cap, dec_cap, gqa, grid, n_pf_ctas;
+  // o_proj: one bf16 GEMM when its output tiles fill the SMs (oproj_direct), else K split
+  // oproj_splits ways into fp32 slices that k_splitk_reduce adds in split order
+  int oproj_direct, oproj_splits;
 };
 
 struct PodWs {
@@ -494,6 +514,20 @@ static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
     const int n = (int)(1.1 * w_pf / std::max(t_end, 1e-9) + 0.5);
     pl.n_pf_ctas = std::max(1, std::min(nsm, n));
   }
+  pl.oproj_direct = 1;
+  pl.oproj_splits = 1;
+  if (a->w_o && a->tp_size <= 1) {
+    const long long K = a->num_q_heads * POD_D, Hd = a->hidden;
+    const long long mt = (a->num_tokens + GEMM_BM - 1) / GEMM_BM;
+    const long long tiles = mt * (Hd / ((Hd % 128 == 0) ? 128 : 32));
+    if (a->out_fp32 || tiles * 2 < nsm) {
+      pl.oproj_direct = 0;
+      const int kb = (int)(K / 64);
+      while (pl.oproj_splits * 2 <= kb && kb % (pl.oproj_splits * 2) == 0 &&
+             tiles * pl.oproj_splits * 2 <= nsm)
+        pl.oproj_splits *= 2;
+    }
+  }
   return LB_OK;
 }
 
@@ -506,7 +540,8 @@ static size_t carve_pod(const LbPodArgs& a, const PodPlan& pl, void* base, PodWs
   w.part_o = c.take<float>((size_t)a.num_seqs * pl.max_splits * a.num_q_heads * POD_D);
   w.part_lse = c.take<float>((size_t)a.num_seqs * pl.max_splits * a.num_q_heads);
   w.ogated = c.take<__nv_bfloat16>((size_t)a.num_tokens * a.num_q_heads * POD_D);
-  w.o32 = c.take<float>(a.w_o ? (size_t)a.num_tokens * a.hidden : 0);
+  w.o32 = c.take<float>(a.w_o && !pl.oproj_direct
+                            ? (size_t)a.num_tokens * a.hidden * pl.oproj_splits : 0);
   return c.off + 256;
 }
 
@@ -681,28 +716,22 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
   // o_proj: out[N, hidden] = ogated[N, Hq*D] . W_o^T
   const int K = (int)(a.num_q_heads * POD_D), Hd = (int)a.hidden;
   const int nsm = num_sms();
-  const int mt = (N + GEMM_BM - 1) / GEMM_BM;
-  const int BN = (Hd % 128 == 0) ? 128 : 32;
-  const long long tiles = (long long)mt * (Hd / BN);
   record_event(a.timing_events[2], st);
-  if (!a.out_fp32 && tiles * 2 >= nsm) {
-    rc = lb_gemm_bf16(w.ogated, K, a.w_o, K, a.out, Hd, N, Hd, K, 0, 1, w.status, st);
+  if (pl.oproj_direct) {
+    rc = gemm_run(w.ogated, K, a.w_o, K, a.out, Hd, N, Hd, K, EPI_BF16, 1, w.status, st);
     record_event(a.timing_events[3], st);
     return rc;
   }
-  int splits = 1;
-  const int kb = K / 64;
-  while (splits * 2 <= kb && kb % (splits * 2) == 0 && tiles * splits * 2 <= nsm) splits *= 2;
-  float* acc = a.out_fp32 ? static_cast<float*>(a.out) : w.o32;
-  LB_CUDA_CHECK(cudaMemsetAsync(acc, 0, sizeof(float) * (size_t)N * Hd, st));
-  rc = lb_gemm_bf16(w.ogated, K, a.w_o, K, acc, Hd, N, Hd, K, 1, splits, w.status, st);
-  if (rc || a.out_fp32) {
-    record_event(a.timing_events[3], st);
-    return rc;
-  }
+  // few output tiles: K split over the SMs, each split's fp32 partial in its own slice,
+  // the slices added in split order (no atomics, no zeroing: a deterministic result)
+  const int splits = pl.oproj_splits;
+  rc = gemm_run(w.ogated, K, a.w_o, K, w.o32, Hd, N, Hd, K, EPI_F32_SPLIT, splits, w.status, st);
+  if (rc) return rc;
   const int g = (int)std::max<long long>(1, std::min<long long>(nsm * 4, N));
-  launch_k(k_f32_to_bf16, g, 256, 0, st, w.o32, static_cast<__nv_bfloat16*>(a.out), N, Hd, Hd);
-  { int _rc = launched("k_f32_to_bf16"); if (_rc) return _rc; }
+  launch_k(k_splitk_reduce, g, 256, 0, st, static_cast<const float*>(w.o32), splits, (long long)N,
+           Hd, a.out_fp32 ? nullptr : static_cast<__nv_bfloat16*>(a.out),
+           a.out_fp32 ? static_cast<float*>(a.out) : nullptr, (long long)Hd);
+  { int _rc = launched("k_splitk_reduce"); if (_rc) return _rc; }
   record_event(a.timing_events[3], st);
   return LB_OK;
 }

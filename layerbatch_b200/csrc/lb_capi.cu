@@ -145,6 +145,68 @@ int max_smem_optin() {
   return n > 0 ? n : 232448;
 }
 
+
+// The dense GEMM behind lb_gemm_bf16 and the library's own projections: checks, tile
+// width choice, tensor maps and the launch of the epilogue `epi` (EPI_BF16, EPI_F32_RED or
+// EPI_F32_SPLIT; the last writes split ks into out32 + ks * M * ldc).
+int gemm_run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+             int64_t M, int64_t N, int64_t K, int epi, int splits, int* status, cudaStream_t st) {
+  LB_REQUIRE(A && B && C, "lb_gemm_bf16: null pointer");
+  LB_REQUIRE(M >= 0 && N > 0 && K > 0, "lb_gemm_bf16: bad shape M=%lld N=%lld K=%lld",
+             (long long)M, (long long)N, (long long)K);
+  LB_REQUIRE(K % 64 == 0, "lb_gemm_bf16: K=%lld must be a multiple of 64", (long long)K);
+  LB_REQUIRE(N % 32 == 0, "lb_gemm_bf16: N=%lld must be a multiple of 32", (long long)N);
+  LB_REQUIRE(lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0 && lda >= K && ldb >= K && ldc >= N,
+             "lb_gemm_bf16: leading dimensions must be >= the row length and multiples of 8");
+  LB_REQUIRE(aligned16(A) && aligned16(B) && aligned16(C), "lb_gemm_bf16: unaligned pointer");
+  LB_REQUIRE(M <= (1ll << 30) && N <= (1ll << 30), "lb_gemm_bf16: shape too large");
+  if (splits < 1) splits = 1;
+  LB_REQUIRE(epi != EPI_BF16 || splits == 1, "lb_gemm_bf16: split-K needs an fp32 accumulator");
+  LB_REQUIRE((K / 64) % splits == 0, "lb_gemm_bf16: K/64 must divide by splits");
+  if (M == 0) return LB_OK;
+
+  int BN = N % 128 == 0 ? 128 : (N % 64 == 0 ? 64 : 32);
+  if (N % 256 == 0 && M > 512) {
+    // 256-wide tiles unless 128-wide ones finish sooner: a tile's time taken as
+    // proportional to the rows it loads (128 of A + BN of B), times the waves of tiles
+    // over the SMs (the router logits, M 4608 x N 512: 72 tiles of 256 leave half the
+    // SMs idle, 144 tiles of 128 fill them in one wave)
+    const long long mt = (M + GEMM_BM - 1) / GEMM_BM;
+    auto cost = [&](int bn) {
+      const long long tiles = mt * (N / bn) * splits;
+      return ((tiles + num_sms() - 1) / num_sms()) * (GEMM_BM + bn);
+    };
+    BN = cost(256) <= cost(128) ? 256 : 128;
+  }
+  CUtensorMap tA, tB;
+  int rc = make_tmap_bf16_2d(&tA, A, M, K, lda, GEMM_BM, 64);
+  if (rc) return rc;
+  rc = make_tmap_bf16_3d(&tB, B, 1, N, K, ldb, ldb * N, BN, 64);
+  if (rc) return rc;
+  GemmArgs a = gemm_args_default(status);
+  a.m = (int)M;
+  a.n_tiles = (int)(N / BN);
+  a.splits = splits;
+  a.k_blocks = (int)(K / 64) / splits;
+  a.out = C;
+  a.ldo = ldc;
+  a.out_rows = (int)M;
+  a.out_cols = (int)N;
+  const long long tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (long long)a.n_tiles * splits;
+  const int grid = (int)std::min<long long>(tiles, num_sms());
+#define LB_GEMM_CASES(E)                                                          \
+  switch (BN) {                                                                   \
+    case 256: return launch_gemm<256, 4, E>(tA, tB, a, grid, st);                 \
+    case 128: return launch_gemm<128, 6, E>(tA, tB, a, grid, st);                 \
+    case 64: return launch_gemm<64, 8, E>(tA, tB, a, grid, st);                   \
+    default: return launch_gemm<32, 8, E>(tA, tB, a, grid, st);                   \
+  }
+  if (epi == EPI_F32_RED) LB_GEMM_CASES(EPI_F32_RED)
+  if (epi == EPI_F32_SPLIT) LB_GEMM_CASES(EPI_F32_SPLIT)
+  LB_GEMM_CASES(EPI_BF16)
+#undef LB_GEMM_CASES
+}
+
 }  // namespace lb
 
 using namespace lb;
@@ -185,63 +247,10 @@ int lb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
                  int64_t M, int64_t N, int64_t K, int c_is_fp32, int splits, void* workspace,
                  void* stream) {
   LB_REQUIRE(A && B && C && workspace, "lb_gemm_bf16: null pointer");
-  LB_REQUIRE(M >= 0 && N > 0 && K > 0, "lb_gemm_bf16: bad shape M=%lld N=%lld K=%lld",
-             (long long)M, (long long)N, (long long)K);
-  LB_REQUIRE(K % 64 == 0, "lb_gemm_bf16: K=%lld must be a multiple of 64", (long long)K);
-  LB_REQUIRE(N % 32 == 0, "lb_gemm_bf16: N=%lld must be a multiple of 32", (long long)N);
-  LB_REQUIRE(lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0 && lda >= K && ldb >= K && ldc >= N,
-             "lb_gemm_bf16: leading dimensions must be >= the row length and multiples of 8");
-  LB_REQUIRE(aligned16(A) && aligned16(B) && aligned16(C), "lb_gemm_bf16: unaligned pointer");
-  LB_REQUIRE(M <= (1ll << 30) && N <= (1ll << 30), "lb_gemm_bf16: shape too large");
   if (splits < 1) splits = 1;
   LB_REQUIRE(c_is_fp32 || splits == 1, "lb_gemm_bf16: split-K needs an fp32 accumulator");
-  LB_REQUIRE((K / 64) % splits == 0, "lb_gemm_bf16: K/64 must divide by splits");
-  if (M == 0) return LB_OK;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-
-  int BN = N % 128 == 0 ? 128 : (N % 64 == 0 ? 64 : 32);
-  if (N % 256 == 0 && M > 512) {
-    // 256-wide tiles unless 128-wide ones finish sooner: a tile's time taken as
-    // proportional to the rows it loads (128 of A + BN of B), times the waves of tiles
-    // over the SMs (the router logits, M 4608 x N 512: 72 tiles of 256 leave half the
-    // SMs idle, 144 tiles of 128 fill them in one wave)
-    const long long mt = (M + GEMM_BM - 1) / GEMM_BM;
-    auto cost = [&](int bn) {
-      const long long tiles = mt * (N / bn) * splits;
-      return ((tiles + num_sms() - 1) / num_sms()) * (GEMM_BM + bn);
-    };
-    BN = cost(256) <= cost(128) ? 256 : 128;
-  }
-  CUtensorMap tA, tB;
-  int rc = make_tmap_bf16_2d(&tA, A, M, K, lda, GEMM_BM, 64);
-  if (rc) return rc;
-  rc = make_tmap_bf16_3d(&tB, B, 1, N, K, ldb, ldb * N, BN, 64);
-  if (rc) return rc;
-  GemmArgs a = gemm_args_default(static_cast<int*>(workspace));
-  a.m = (int)M;
-  a.n_tiles = (int)(N / BN);
-  a.splits = splits;
-  a.k_blocks = (int)(K / 64) / splits;
-  a.out = C;
-  a.ldo = ldc;
-  a.out_rows = (int)M;
-  a.out_cols = (int)N;
-  const long long tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (long long)a.n_tiles * splits;
-  const int grid = (int)std::min<long long>(tiles, num_sms());
-  if (c_is_fp32) {
-    switch (BN) {
-      case 256: return launch_gemm<256, 4, EPI_F32_RED>(tA, tB, a, grid, st);
-      case 128: return launch_gemm<128, 6, EPI_F32_RED>(tA, tB, a, grid, st);
-      case 64: return launch_gemm<64, 8, EPI_F32_RED>(tA, tB, a, grid, st);
-      default: return launch_gemm<32, 8, EPI_F32_RED>(tA, tB, a, grid, st);
-    }
-  }
-  switch (BN) {
-    case 256: return launch_gemm<256, 4, EPI_BF16>(tA, tB, a, grid, st);
-    case 128: return launch_gemm<128, 6, EPI_BF16>(tA, tB, a, grid, st);
-    case 64: return launch_gemm<64, 8, EPI_BF16>(tA, tB, a, grid, st);
-    default: return launch_gemm<32, 8, EPI_BF16>(tA, tB, a, grid, st);
-  }
+  return gemm_run(A, lda, B, ldb, C, ldc, M, N, K, c_is_fp32 ? EPI_F32_RED : EPI_BF16, splits,
+                  static_cast<int*>(workspace), static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

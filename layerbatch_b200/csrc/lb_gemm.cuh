@@ -26,6 +26,8 @@ enum EpiKind : int {
   EPI_F32_RED = 4,     // out32 += acc (split-K partials, vector reductions)
   EPI_F32_PEER = 5,    // fp32 tile -> inbox of the rank owning its m-tile (tensor parallel);
                        // the last CTA publishes the call's epoch to every rank
+  EPI_F32_SPLIT = 6,   // split-K partial ks -> its own fp32 slice out32[ks] (plain stores;
+                       // k_splitk_reduce sums the slices in split order: deterministic)
 };
 
 struct GemmArgs {
@@ -239,6 +241,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         if (!row_ok || col + 32 > p.out_cols) {
           // nothing to store for this row / chunk
+        } else if constexpr (EPI == EPI_F32_SPLIT) {
+          float* out = reinterpret_cast<float*>(p.out) +
+                       ((long long)c.ks * p.out_rows + out_row) * p.ldo + col;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4*>(out + 4 * i) =
+                make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                            __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
         } else if constexpr (EPI == EPI_F32_RED) {
           float* out = reinterpret_cast<float*>(p.out) + (long long)out_row * p.ldo + col;
 #pragma unroll

@@ -76,6 +76,11 @@ void record_event(void* ev, cudaStream_t st);
 int num_sms();
 int max_smem_optin();
 
+// Dense bf16 GEMM C = A . B^T with epilogue `epi` (an EpiKind of lb_gemm.cuh); the body of
+// lb_gemm_bf16, also used for the library's internal split-K projections.
+int gemm_run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+             int64_t M, int64_t N, int64_t K, int epi, int splits, int* status, cudaStream_t st);
+
 // Raise a kernel's dynamic shared-memory limit on the current device to at least `bytes`.
 // The attribute is set once per (kernel, device) and cached, so steady-state calls (and
 // calls made while a stream is being captured into a CUDA graph) make no runtime call.
