@@ -124,7 +124,8 @@ typedef struct LbMoeArgs {
   const void* w_shared_gate; /* [Is, H] bf16          mlp.shared_expert.gate_proj.weight */
   const void* w_shared_up;   /* [Is, H] bf16          mlp.shared_expert.up_proj.weight */
   const void* w_shared_down; /* [H, Is] bf16          mlp.shared_expert.down_proj.weight */
-  const void* w_shared_expert_gate; /* [1, H] bf16    mlp.shared_expert_gate.weight */
+  const void* w_shared_expert_gate; /* [1, H] bf16    mlp.shared_expert_gate.weight
+                              * (NULL: the shared expert's rows are not gated, scale 1) */
   void* out;                 /* [T, H] bf16 output */
   void* router_logits;       /* optional out [T, E] bf16 */
   int32_t* topk_ids;         /* optional out [T, k] int32 */
@@ -319,6 +320,14 @@ typedef struct LbPodArgs {
   void* tp_bufs[LB_EP_MAX_RANKS];  /* every rank's TP buffer (lb_tp_buffer_size bytes,
                                     * from lb_ep_buffer_alloc / lb_ep_buffer_open) */
   int32_t tp_phases;               /* 0 = all; else a mask of LB_TP_PHASE_* (tests) */
+  /* ---- fused attention prologue (optional; NULL = q is final).  The call then runs the
+   * prologue of lb_attn_prologue for its num_tokens tokens inside the attention kernel:
+   * the CTAs first normalise and rotate every query row into q (which must be the
+   * prologue's q_out, same strides) and store every new K/V row into the paged cache (the
+   * prologue's k_cache / v_cache, num_slots = num_pages * page_size); each attention item
+   * waits (bounded) for its sequence's rows before it loads them.  Replaces the separate
+   * lb_attn_prologue launch in front of this call. */
+  const LbPrologueArgs* prologue;
 } LbPodArgs;
 
 #define LB_TP_PHASE_ATTN 1    /* attention, merge, o_proj GEMM to the owners + signal */

@@ -93,6 +93,7 @@ class LbPodArgs(C.Structure):
         ("timing_events", vp * 4), ("prefill_pairs_hint", i64), ("decode_tokens_hint", i64),
         ("tp_rank", i32), ("tp_size", i32), ("tp_capacity", i64),
         ("tp_bufs", vp * LB_EP_MAX_RANKS), ("tp_phases", i32),
+        ("prologue", C.POINTER(LbPrologueArgs)),
     ]
 
 

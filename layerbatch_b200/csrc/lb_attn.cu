@@ -5,6 +5,7 @@
 #include "lb_gemm_launch.cuh"
 #include "lb_host.h"
 #include "lb_pod.cuh"
+#include "lb_prologue.cuh"
 
 namespace lb {
 
@@ -33,84 +34,18 @@ __global__ void k_store_kvcache(const __nv_bfloat16* __restrict__ k, long long k
 
 
 // ------------------------------------------------------------------------------ prologue
-// One warp per (token, head): heads [0, Hq) are query heads, [Hq, Hq + Hkv) KV heads.
-// A lane holds 8 consecutive dims (D = 256).  The RMSNorm and RoPE follow the reference's
-// fp32 operation order with explicit rounding (no contraction), so the bf16 results match
-// it up to the order of the sum of squares.
+// The standalone prologue (lb_attn_prologue): one block per task of PRO_TASK_TOKENS
+// tokens (grid-stride), 8 warps on its rows (lb_prologue.cuh).
 __global__ void __launch_bounds__(256) k_attn_prologue(const LbPrologueArgs a) {
   pdl_entry();
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
-  const int lane = threadIdx.x % 32;
-  const int Hq = (int)a.num_q_heads, Hkv = (int)a.num_kv_heads;
-  const int nh = Hq + Hkv;
-  if (warp >= a.num_tokens * nh) return;
-  const long long n = warp / nh;
-  const int h = warp - (int)(n * nh);
-  const bool is_q = h < Hq;
-  const int g = h - Hq;
-  constexpr int D = POD_D;
-  const long long slot = is_q ? 0 : (long long)a.slot_mapping[n];
-  if (!is_q && slot >= a.num_slots) {
-    if (a.status) report(a.status, LB_DEV_BAD_INDEX);
-    return;
-  }
-  if (!is_q && slot < 0) return;   // padding token: nothing to store
-  const __nv_bfloat16* src = is_q
-      ? static_cast<const __nv_bfloat16*>(a.q_in) + n * a.q_in_stride_tok + (long long)h * a.q_in_stride_head
-      : static_cast<const __nv_bfloat16*>(a.k_in) + n * a.k_in_stride_tok + (long long)g * D;
-  const uint4 raw = reinterpret_cast<const uint4*>(src)[lane];
-  float x[8] = {bf16_lo(raw.x), bf16_hi(raw.x), bf16_lo(raw.y), bf16_hi(raw.y),
-                bf16_lo(raw.z), bf16_hi(raw.z), bf16_lo(raw.w), bf16_hi(raw.w)};
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-  const float rstd = 1.0f / sqrtf(__fadd_rn(ss / (float)D, a.eps));
-  const uint4 wr = reinterpret_cast<const uint4*>(is_q ? a.q_norm_w : a.k_norm_w)[lane];
-  const float w[8] = {bf16_lo(wr.x), bf16_hi(wr.x), bf16_lo(wr.y), bf16_hi(wr.y),
-                      bf16_lo(wr.z), bf16_hi(wr.z), bf16_lo(wr.w), bf16_hi(wr.w)};
-  float y[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    y[i] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[i], rstd), __fadd_rn(1.0f, w[i]))));
-  // partial RoPE: dims [0, rot/2) pair with [rot/2, rot); lanes < rot/16 hold the first
-  // half, the next rot/16 lanes the second
-  const int rot = (int)a.rotary_dim;
-  const int hl = rot / 16;
-  const bool first = lane < hl, second = lane >= hl && lane < 2 * hl;
-  const int partner = first ? lane + hl : (second ? lane - hl : lane);
-  float pv[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) pv[i] = __shfl_sync(0xffffffffu, y[i], partner);
-  if (first || second) {
-    long long pos = a.positions[n];
-    if (pos < 0 || pos >= a.max_position) {
-      if (a.status) report(a.status, LB_DEV_BAD_INDEX);
-      pos = pos < 0 ? 0 : a.max_position - 1;
-    }
-    const float* cs = a.cos_sin_cache + pos * rot;
-    const int f0 = (first ? lane : lane - hl) * 8;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float c = cs[f0 + i], sn = cs[rot / 2 + f0 + i];
-      const float r = first ? __fsub_rn(__fmul_rn(y[i], c), __fmul_rn(pv[i], sn))   // x1 c - x2 s
-                            : __fadd_rn(__fmul_rn(y[i], c), __fmul_rn(pv[i], sn));  // x2 c + x1 s
-      y[i] = __bfloat162float(__float2bfloat16_rn(r));
-    }
-  }
-  const uint4 outv = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
-                                pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
-  if (is_q) {
-    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.q_out) + n * a.q_out_stride_tok +
-                         (long long)h * a.q_out_stride_head;
-    reinterpret_cast<uint4*>(dst)[lane] = outv;
-  } else {
-    const long long row = slot * (long long)Hkv * D + (long long)g * D;
-    reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.k_cache) + row)[lane] = outv;
-    const __nv_bfloat16* vs = static_cast<const __nv_bfloat16*>(a.v_in) + n * a.v_in_stride_tok + (long long)g * D;
-    reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.v_cache) + row)[lane] =
-        reinterpret_cast<const uint4*>(vs)[lane];
+  __shared__ ProStage st;
+  const int tasks = (int)((a.num_tokens + PRO_TASK_TOKENS - 1) / PRO_TASK_TOKENS);
+  for (int t = blockIdx.x; t < tasks; t += gridDim.x) {
+    const int tok0 = t * PRO_TASK_TOKENS;
+    const int ntok = (int)(a.num_tokens - tok0) < PRO_TASK_TOKENS ? (int)(a.num_tokens - tok0)
+                                                                    : PRO_TASK_TOKENS;
+    prologue_task(a, tok0, ntok, &st, threadIdx.x / 32, 8, threadIdx.x % 32, a.status);
+    __syncthreads();
   }
 }
 
@@ -125,7 +60,7 @@ __global__ void k_pod_plan(const int32_t* __restrict__ ctx_lens, const int32_t* 
                            int B, int Hq, int Hkv, int split_tokens, int max_splits,
                            int max_ctx, int pf_cap, int dec_cap, int4* __restrict__ pf_items,
                            int* __restrict__ counters, int4* __restrict__ dec_items,
-                           int* __restrict__ status) {
+                           int* __restrict__ seq_ready, int* __restrict__ status) {
   pdl_entry();
   __shared__ int s_pf[1024], s_full[1024], s_rem[1024];
   extern __shared__ int s_off[];  // [3 * B]: first prefill / full-split / last-split item
@@ -225,7 +160,12 @@ __global__ void k_pod_plan(const int32_t* __restrict__ ctx_lens, const int32_t* 
     counters[1] = 0;
     counters[2] = min(td, dec_cap);
     counters[3] = 0;
+    counters[4] = 0;   // fused prologue: next task
+    counters[5] = 0;   // fused prologue: tasks finished
   }
+  // fused prologue: no new token of any sequence is stored yet
+  if (seq_ready)
+    for (int b = tid; b < B; b += 1024) seq_ready[b] = 0;
 }
 
 // ------------------------------------------------------------------------------ merge
@@ -414,7 +354,8 @@ struct PodPlan {
 
 struct PodWs {
   int* status;
-  int* counters;
+  int* counters;        // [8]: prefill count / next, decode count / next, prologue next / done
+  int* seq_ready;       // [B] fused prologue: new tokens stored per sequence
   int4* pf_items;
   int4* dec_items;
   float* part_o;
@@ -422,6 +363,31 @@ struct PodWs {
   __nv_bfloat16* ogated;
   float* o32;
 };
+
+// Argument checks of the prologue (standalone lb_attn_prologue or fused into the POD call).
+static int check_prologue(const LbPrologueArgs* a) {
+  LB_REQUIRE(a != nullptr, "lb_attn_prologue: null args");
+  LB_REQUIRE(a->head_dim == POD_D, "lb_attn_prologue: head_dim must be 256");
+  LB_REQUIRE(a->num_tokens >= 0 && a->num_q_heads > 0 && a->num_kv_heads > 0 &&
+                 a->num_tokens * (a->num_q_heads + a->num_kv_heads) < (1ll << 31),
+             "lb_attn_prologue: bad sizes");
+  LB_REQUIRE(a->rotary_dim >= 0 && a->rotary_dim <= a->head_dim && a->rotary_dim % 16 == 0,
+             "lb_attn_prologue: rotary_dim must be a multiple of 16 and <= head_dim");
+  LB_REQUIRE(a->q_in && a->k_in && a->v_in && a->q_norm_w && a->k_norm_w && a->positions &&
+                 a->slot_mapping && a->k_cache && a->v_cache && a->q_out &&
+                 (a->rotary_dim == 0 || a->cos_sin_cache),
+             "lb_attn_prologue: null pointer");
+  LB_REQUIRE(a->max_position > 0 && a->num_slots >= 0, "lb_attn_prologue: bad cache sizes");
+  LB_REQUIRE(aligned16(a->q_in) && aligned16(a->k_in) && aligned16(a->v_in) &&
+                 aligned16(a->q_norm_w) && aligned16(a->k_norm_w) && aligned16(a->k_cache) &&
+                 aligned16(a->v_cache) && aligned16(a->q_out),
+             "lb_attn_prologue: tensors must be 16-byte aligned");
+  LB_REQUIRE(a->q_in_stride_tok % 8 == 0 && a->q_in_stride_head % 8 == 0 &&
+                 a->k_in_stride_tok % 8 == 0 && a->v_in_stride_tok % 8 == 0 &&
+                 a->q_out_stride_tok % 8 == 0 && a->q_out_stride_head % 8 == 0,
+             "lb_attn_prologue: strides must be multiples of 8 elements");
+  return LB_OK;
+}
 
 static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
   LB_REQUIRE(a != nullptr, "lb_pod: null args");
@@ -463,6 +429,19 @@ static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
     for (int r = 0; r < a->tp_size; ++r)
       LB_REQUIRE(a->tp_bufs[r] && (reinterpret_cast<uintptr_t>(a->tp_bufs[r]) & 255) == 0,
                  "lb_pod: tp buffer %d missing or not 256-byte aligned", r);
+  }
+  if (a->prologue) {
+    const LbPrologueArgs* r = a->prologue;
+    if (int rc = check_prologue(r)) return rc;
+    LB_REQUIRE(r->num_tokens == a->num_tokens && r->num_q_heads == a->num_q_heads &&
+                   r->num_kv_heads == a->num_kv_heads,
+               "lb_pod: the fused prologue must cover the call's tokens and heads");
+    LB_REQUIRE(r->q_out == a->q && r->q_out_stride_tok == a->q_stride_tok &&
+                   r->q_out_stride_head == a->q_stride_head,
+               "lb_pod: the fused prologue's q_out must be the attention's q");
+    LB_REQUIRE(r->k_cache == a->k_cache && r->v_cache == a->v_cache &&
+                   r->num_slots == a->num_pages * a->page_size,
+               "lb_pod: the fused prologue must store into the attention's paged cache");
   }
   const long long HD = a->num_q_heads * POD_D;
   LB_REQUIRE(HD % 64 == 0, "lb_pod: Hq*D must be a multiple of 64");
@@ -534,7 +513,8 @@ static int pod_plan_host(const LbPodArgs* a, PodPlan& pl) {
 static size_t carve_pod(const LbPodArgs& a, const PodPlan& pl, void* base, PodWs& w) {
   Carve c(base, ~size_t(0));
   w.status = c.take<int>(64);
-  w.counters = c.take<int>(4);
+  w.counters = c.take<int>(8);
+  w.seq_ready = c.take<int>(a.prologue ? (size_t)a.num_seqs : 0);
   w.pf_items = c.take<int4>(pl.pf_cap);
   w.dec_items = c.take<int4>(pl.dec_cap);
   w.part_o = c.take<float>((size_t)a.num_seqs * pl.max_splits * a.num_q_heads * POD_D);
@@ -579,7 +559,8 @@ static int pod_attention(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, 
     return rc;
   launch_k(k_pod_plan, 1, 1024, 3 * sizeof(int) * B, st, a.context_lens, a.cu_seqlens_q, B, (int)a.num_q_heads,
                                  (int)a.num_kv_heads, pl.split_tokens, pl.max_splits, pl.max_ctx,
-                                 pl.pf_cap, pl.dec_cap, w.pf_items, w.counters, w.dec_items, w.status);
+                                 pl.pf_cap, pl.dec_cap, w.pf_items, w.counters, w.dec_items,
+                                 a.prologue ? w.seq_ready : nullptr, w.status);
   { int _rc = launched("k_pod_plan"); if (_rc) return _rc; }
 
   PodParams p{};
@@ -611,6 +592,15 @@ static int pod_attention(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, 
   p.n_prefill_ctas = pl.n_pf_ctas;
   p.scale_log2 = a.sm_scale * 1.4426950408889634f;
   p.qd_bytes = 4 * qd_rows * 128;
+  p.num_tokens = N;
+  p.num_seqs = B;
+  if (a.prologue) {
+    p.pro = *a.prologue;
+    p.pro_tasks = (N + PRO_TASK_TOKENS - 1) / PRO_TASK_TOKENS;
+    p.pro_next = w.counters + 4;
+    p.pro_done = w.counters + 5;
+    p.seq_ready = w.seq_ready;
+  }
   if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(k_pod_attn), POD_SMEM))) return rc;
   record_event(a.timing_events[0], st);
   launch_k(k_pod_attn, pl.grid, POD_THREADS, POD_SMEM, st, tmK, tmV, tmK64, tmV64, tmQd, tmQp, p);
@@ -762,29 +752,10 @@ int lb_store_kvcache(const void* k, int64_t k_stride, const void* v, int64_t v_s
 }
 
 int lb_attn_prologue(const LbPrologueArgs* a, void* stream) {
-  LB_REQUIRE(a != nullptr, "lb_attn_prologue: null args");
-  LB_REQUIRE(a->head_dim == POD_D, "lb_attn_prologue: head_dim must be 256");
-  LB_REQUIRE(a->num_tokens >= 0 && a->num_q_heads > 0 && a->num_kv_heads > 0 &&
-                 a->num_tokens * (a->num_q_heads + a->num_kv_heads) < (1ll << 31),
-             "lb_attn_prologue: bad sizes");
-  LB_REQUIRE(a->rotary_dim >= 0 && a->rotary_dim <= a->head_dim && a->rotary_dim % 16 == 0,
-             "lb_attn_prologue: rotary_dim must be a multiple of 16 and <= head_dim");
-  LB_REQUIRE(a->q_in && a->k_in && a->v_in && a->q_norm_w && a->k_norm_w && a->positions &&
-                 a->slot_mapping && a->k_cache && a->v_cache && a->q_out &&
-                 (a->rotary_dim == 0 || a->cos_sin_cache),
-             "lb_attn_prologue: null pointer");
-  LB_REQUIRE(a->max_position > 0 && a->num_slots >= 0, "lb_attn_prologue: bad cache sizes");
-  LB_REQUIRE(aligned16(a->q_in) && aligned16(a->k_in) && aligned16(a->v_in) &&
-                 aligned16(a->q_norm_w) && aligned16(a->k_norm_w) && aligned16(a->k_cache) &&
-                 aligned16(a->v_cache) && aligned16(a->q_out),
-             "lb_attn_prologue: tensors must be 16-byte aligned");
-  LB_REQUIRE(a->q_in_stride_tok % 8 == 0 && a->q_in_stride_head % 8 == 0 &&
-                 a->k_in_stride_tok % 8 == 0 && a->v_in_stride_tok % 8 == 0 &&
-                 a->q_out_stride_tok % 8 == 0 && a->q_out_stride_head % 8 == 0,
-             "lb_attn_prologue: strides must be multiples of 8 elements");
+  if (int rc = check_prologue(a)) return rc;
   if (a->num_tokens == 0) return LB_OK;
-  const long long warps = a->num_tokens * (a->num_q_heads + a->num_kv_heads);
-  const long long blocks = (warps * 32 + 255) / 256;
+  const long long tasks = (a->num_tokens + PRO_TASK_TOKENS - 1) / PRO_TASK_TOKENS;
+  const long long blocks = std::max<long long>(1, std::min<long long>(tasks, num_sms() * 8));
   launch_k(k_attn_prologue, (unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream), *a);
   { int _rc = launched("k_attn_prologue"); if (_rc) return _rc; }
   return LB_OK;

@@ -368,6 +368,24 @@ __device__ __forceinline__ bool peer_wait(const int* flag, int epoch, int* statu
   return true;
 }
 
+// GPU-scope flag accesses between CTAs of one device.
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders this thread's generic-proxy global accesses with async-proxy (TMA) accesses:
+// a writer runs it after stores that TMA loads will read, a reader after it has seen
+// the writer's flag and before it issues those loads.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 __device__ __forceinline__ void red_add_v4_f32(float* p, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b),
                "f"(c), "f"(d)

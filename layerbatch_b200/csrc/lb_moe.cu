@@ -112,13 +112,18 @@ __global__ void k_router_topk(const __nv_bfloat16* __restrict__ logits, long lon
 }
 
 // sg[t] = sigmoid(x[t] . w_sg) in fp32, one warp per token (qwen3_5.py:903); used when the
-// routing is given and the top-k kernel (which also computes it) does not run.
+// routing is given and the top-k kernel (which also computes it) does not run.  Without
+// w_sg (a shared expert called on its own, qwen3_5.py:916-917) the scale is 1.
 __global__ void k_shared_gate(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wsg,
                               int T, int H, float* __restrict__ sg) {
   pdl_entry();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (t >= T) return;
+  if (wsg == nullptr) {
+    if (lane == 0) sg[t] = 1.0f;
+    return;
+  }
   const __nv_bfloat16* xr = x + (long long)t * H;
   float acc = 0.f;
   for (int h = lane * 8; h < H; h += 256) {
@@ -314,8 +319,7 @@ static int check_moe(const LbMoeArgs* a) {
   LB_REQUIRE(a->routing_given ? (a->topk_ids && a->topk_weights_f32) : (a->w_router != nullptr),
              "lb_moe: need w_router, or topk_ids + topk_weights_f32 with routing_given");
   LB_REQUIRE(a->num_local_experts == 0 || (a->w_gate_up && a->w_down), "lb_moe: null expert weights");
-  LB_REQUIRE(a->no_shared || (a->w_shared_gate && a->w_shared_up && a->w_shared_down &&
-                              a->w_shared_expert_gate),
+  LB_REQUIRE(a->no_shared || (a->w_shared_gate && a->w_shared_up && a->w_shared_down),
              "lb_moe: null shared-expert weights");
   LB_REQUIRE(!a->pair_rows == !a->pair_index, "lb_moe: pair_rows and pair_index go together");
   const void* ptrs[] = {a->x, a->out, a->w_router, a->w_gate_up, a->w_down, a->w_shared_gate,
@@ -812,10 +816,16 @@ int lb_moe_forward(const LbMoeArgs* a, void* stream) {
     // 2. top-k + shared-expert gate.  The gate lands in perm_w[0:T): rows [0,T) of every
     //    packed buffer are the shared expert's, so the down GEMM scales them by it exactly
     //    as it scales routed rows by their routing weight.
+    const bool gated = shared && a->w_shared_expert_gate != nullptr;
     rc = launch_topk(logits, E, T, E, k, ids_out, w.wf, wb, x,
                      static_cast<const __nv_bfloat16*>(a->w_shared_expert_gate), H,
-                     shared ? w.perm_w : nullptr, st);
+                     gated ? w.perm_w : nullptr, st);
     if (rc) return rc;
+    if (shared && !gated) {   // an ungated shared expert: scale 1
+      launch_k(k_shared_gate, (T * 32 + 255) / 256, 256, 0, st, x,
+               static_cast<const __nv_bfloat16*>(nullptr), T, H, w.perm_w);
+      { int _rc = launched("k_shared_gate"); if (_rc) return _rc; }
+    }
     ids = ids_out;
     wf = w.wf;
   }

@@ -29,6 +29,7 @@
 
 #include <cuda.h>
 #include "lb_common.cuh"
+#include "lb_prologue.cuh"
 
 namespace lb {
 
@@ -91,7 +92,22 @@ struct PodParams {
   int n_prefill_ctas;
   int qd_bytes;                // bytes of one decode Q tile (4 chunks x rows x 128 B)
   float scale_log2;
+  // Fused prologue (optional, pro_tasks = 0: off).  Before attention, the CTAs take tasks
+  // of PRO_TASK_TOKENS tokens from pro_next and run the prologue of their rows (query to
+  // `q`, key / value into the cache); seq_ready[b] then counts sequence b's new tokens
+  // done (release).  An item's producer waits for its sequence's count to reach what the
+  // item reads before it loads Q / K / V.  Every CTA finishes claiming tasks before it
+  // starts any item, so a wait only ever waits for tasks running on resident CTAs.
+  LbPrologueArgs pro;
+  int pro_tasks;
+  int* pro_next;
+  int* pro_done;        // tasks finished (release); == pro_tasks: every row is stored
+  int* seq_ready;
+  int num_tokens;
+  int num_seqs;
 };
+
+
 
 struct PodBars {
   uint64_t kv_full[5], kv_empty[5];
@@ -106,6 +122,7 @@ struct PodBars {
   float red[2][4][16];
   float lred[4][16];
   float psum[2][128];      // prefill: per-warpgroup partial row sums at the end of an item
+  int pro_task;            // fused prologue: the task the CTA works on
 };
 
 static_assert(sizeof(PodBars) <= POD_MISC, "PodBars exceeds the reserved shared memory");
@@ -113,6 +130,67 @@ static_assert(sizeof(PodBars) <= POD_MISC, "PodBars exceeds the reserved shared 
 struct PodCounters {  // per-role running positions, kept across items and modes
   uint32_t kv, item, s, o, qp, kv2;  // kv2: prefill V tiles (K tiles use kv)
 };
+
+// Sequence of packed token `tok`: the last b with cu_seqlens_q[b] <= tok.
+__device__ __forceinline__ int seq_of_token(const PodParams& p, int tok) {
+  int lo = 0, hi = p.num_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.cu_seqlens_q[mid] <= tok) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Bounded wait until sequence b has `need` new tokens through the fused prologue; then
+// its query rows and stored K/V rows may be loaded by TMA by this thread.  `all_ready` is
+// the thread's own note that every task was seen finished (after which there is nothing
+// to wait for and the fences below have been run once).  No-op without the prologue.
+__device__ __forceinline__ bool wait_seq_ready(const PodParams& p, int b, int need,
+                                               bool& all_ready) {
+  if (p.pro_tasks == 0 || all_ready) return true;
+  if (ld_acquire_gpu(p.pro_done) >= p.pro_tasks) {
+    fence_proxy_async_global();
+    all_ready = true;
+    return true;
+  }
+  if (ld_acquire_gpu(p.seq_ready + b) < need) {
+    const long long t0 = clock64();
+    while (ld_acquire_gpu(p.seq_ready + b) < need) {
+      if (clock64() - t0 > (long long)LB_SPIN_LIMIT_CYCLES) {
+        report(p.status, LB_DEV_TIMEOUT);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+  fence_proxy_async_global();
+  return true;
+}
+
+// The fused prologue phase: every thread of the CTA takes part; the data region of shared
+// memory (free until the attention pipelines start) holds the tasks' staging area.
+__device__ __forceinline__ void pod_prologue_phase(const PodParams& p, PodBars* bars,
+                                                   uint8_t* smem) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  ProStage* st = reinterpret_cast<ProStage*>(smem);
+  while (true) {
+    if (threadIdx.x == 0) bars->pro_task = atomicAdd(p.pro_next, 1);
+    __syncthreads();
+    const int t = bars->pro_task;
+    if (t >= p.pro_tasks) break;
+    const int tok0 = t * PRO_TASK_TOKENS;
+    const int ntok = min(PRO_TASK_TOKENS, p.num_tokens - tok0);
+    prologue_task(p.pro, tok0, ntok, st, warp, POD_THREADS / 32, lane, p.status);
+    // the rows are read back by TMA (async proxy) on other SMs
+    fence_proxy_async_global();
+    __threadfence();
+    __syncthreads();
+    if ((int)threadIdx.x < ntok) red_release_gpu_add(p.seq_ready + seq_of_token(p, tok0 + threadIdx.x), 1);
+    if (threadIdx.x == 0) red_release_gpu_add(p.pro_done, 1);
+  }
+  // the staging area becomes TMA destination memory
+  fence_proxy_async_smem();
+}
 
 __device__ __forceinline__ int kv_page_row(const PodParams& p, int b, int tok) {
   const int pi = tok / p.page_size;
@@ -190,6 +268,8 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
   }
   if (threadIdx.x == 0) bars->abort = 0;
   PodCounters cnt = {0, 0, 0, 0, 0, 0};
+  if (p.pro_tasks > 0) pod_prologue_phase(p, bars, smem);
+  bool pro_all_ready = false;   // producer lanes: every prologue task seen finished
 
   const bool pf_first = (int)blockIdx.x < p.n_prefill_ctas;
   for (int pass = 0; pass < 2; ++pass) {
@@ -238,6 +318,18 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
             break;
           }
           const int4 it = items[idx];
+          {
+            // fused prologue: the item's query rows and new K/V rows must be stored
+            const int bq = it.x;
+            const int need = prefill ? p.cu_seqlens_q[bq + 1] - p.cu_seqlens_q[bq] : 1;
+            if (!wait_seq_ready(p, bq, need, pro_all_ready)) {
+              *abortp = 1;
+              bars->items[islot] = make_int4(-1, 0, 0, 0);
+              mbar_arrive(&bars->item_full[islot]);
+              ++cnt.item;
+              break;
+            }
+          }
           bars->items[islot] = it;
           const int b = it.x;
           const int ctx = p.context_lens[b];
@@ -317,6 +409,9 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           const int b = it.x;
           const int ctx = p.context_lens[b];
           const int qlen = p.cu_seqlens_q[b + 1] - p.cu_seqlens_q[b];
+          // lane 0 saw the count before publishing the item; this lane's own acquire
+          // orders its V loads after the prologue's stores
+          if (!wait_seq_ready(p, b, qlen, pro_all_ready)) { *abortp = 1; break; }
           const int kvh = it.y / p.gqa;
           const int kv_end = min(ctx, ctx - qlen + (it.z + 1) * POD_KV);
           const int ntiles = (kv_end + PF_KV - 1) / PF_KV;

@@ -45,6 +45,11 @@ class Qwen3_5TopKRouter(nn.Module):
 
 
 class Qwen3_5Experts(nn.Module):
+    """The routed experts (qwen3_5.py:776-874).  ``forward(hidden_states, top_k_indices,
+    top_k_weights)`` returns ``sum_j w[t,j] * expert_{id[t,j]}(x[t])`` for the experts this
+    module holds (global ids ``[expert_base, expert_base + num_experts)``; others add
+    nothing) with one grouped GEMM pair; the reference's prefill (sparse) and decode
+    (dense) dispatches (:808-813) are the same call here."""
 
     def __init__(self, num_experts: int, hidden_size: int, moe_intermediate_size: int):
         super().__init__()
@@ -54,15 +59,42 @@ class Qwen3_5Experts(nn.Module):
         self.gate_up_proj = nn.Parameter(
             torch.empty(num_experts, 2 * moe_intermediate_size, hidden_size))
         self.down_proj = nn.Parameter(torch.empty(num_experts, hidden_size, moe_intermediate_size))
+        self.expert_base = 0                 # first global id held (expert parallel)
+        self.total_experts = num_experts     # router width
+
+    def forward(self, hidden_states, top_k_indices, top_k_weights):
+        x = hidden_states.reshape(-1, self.hidden_size).contiguous()
+        k = top_k_indices.shape[-1]
+        y = ops.moe_forward(x, None, self.gate_up_proj, self.down_proj, None, None, None, None,
+                            k, expert_base=self.expert_base,
+                            topk_ids=top_k_indices.reshape(-1, k).to(torch.int32),
+                            topk_weights=top_k_weights.reshape(-1, k).float(),
+                            num_experts=self.total_experts, ws_tag="experts")
+        return y.view_as(hidden_states)
 
 
 class Qwen3_5SharedExpertMLP(nn.Module):
+    """The shared expert (qwen3_5.py:910-917): ``down(silu(gate(x)) * up(x))``, as the
+    shared group of the library's grouped GEMM pair, ungated (the block's sigmoid gate is
+    applied by the block)."""
 
     def __init__(self, hidden_size: int, intermediate_size: int):
         super().__init__()
         self.gate_proj = nn.Linear(hidden_size, intermediate_size, bias=False)
         self.up_proj = nn.Linear(hidden_size, intermediate_size, bias=False)
         self.down_proj = nn.Linear(intermediate_size, hidden_size, bias=False)
+
+    def forward(self, x):
+        H = self.gate_proj.weight.shape[1]
+        x2 = x.reshape(-1, H).contiguous()
+        T = x2.shape[0]
+        # no routed experts: every (token, slot) pair is dropped
+        ids = torch.zeros(T, 1, dtype=torch.int32, device=x.device)
+        w = torch.zeros(T, 1, dtype=torch.float32, device=x.device)
+        y = ops.moe_forward(x2, None, None, None, self.gate_proj.weight, self.up_proj.weight,
+                            self.down_proj.weight, None, 1, topk_ids=ids, topk_weights=w,
+                            num_experts=1, ws_tag="shared_expert")
+        return y.view_as(x)
 
 
 class Qwen3_5SparseMoeBlock(nn.Module):
@@ -80,6 +112,8 @@ class Qwen3_5SparseMoeBlock(nn.Module):
         self.expert_base = ep_rank * self.local_experts
         self.gate = Qwen3_5TopKRouter(num_experts, hidden_size, num_experts_per_tok)
         self.experts = Qwen3_5Experts(self.local_experts, hidden_size, moe_intermediate_size)
+        self.experts.expert_base = self.expert_base
+        self.experts.total_experts = num_experts
         self.shared_expert = Qwen3_5SharedExpertMLP(hidden_size, shared_expert_intermediate_size)
         self.shared_expert_gate = nn.Linear(hidden_size, 1, bias=False)
         self.ep_exchange = None

@@ -1,4 +1,6 @@
-"""Drop-in tensor-parallel linears (nanovllm/layers/linear.py:12-159) on the sm_100a GEMM.
+"""Drop-in tensor-parallel linears (nanovllm/layers/linear.py:12-159) on the sm_100a GEMM:
+``ReplicatedLinear``, ``ColumnParallelLinear``, ``MergedColumnParallelLinear``,
+``QKVParallelLinear`` and ``RowParallelLinear``.
 
 Same constructor signatures, parameter names and ``weight_loader`` sharding hooks as the
 reference.  Forward passes run ``lb_gemm_bf16`` (tcgen05 tensor cores, fp32 accumulate).
@@ -74,6 +76,46 @@ class ColumnParallelLinear(LinearBase):
 
     def forward(self, x):
         return _linear(x, self.weight, self.bias)
+
+
+class MergedColumnParallelLinear(ColumnParallelLinear):
+    """Several column-parallel outputs in one weight (linear.py:76-95): the loader writes
+    shard ``loaded_shard_id`` of ``output_sizes`` into its rows; one GEMM computes all."""
+
+    def __init__(self, input_size, output_sizes, bias=False):
+        self.output_sizes = list(output_sizes)
+        super().__init__(input_size, sum(self.output_sizes), bias)
+
+    def weight_loader(self, param, loaded_weight, loaded_shard_id: int):
+        off = sum(self.output_sizes[:loaded_shard_id]) // self.tp_size
+        size = self.output_sizes[loaded_shard_id] // self.tp_size
+        dst = param.data.narrow(self.tp_dim, off, size)
+        dst.copy_(loaded_weight.chunk(self.tp_size, self.tp_dim)[self.tp_rank])
+
+
+class QKVParallelLinear(ColumnParallelLinear):
+    """Query, key and value projections in one weight (linear.py:98-130): rows
+    ``[q | k | v]`` of this rank's heads, written by the loader per shard id "q" / "k" /
+    "v"; one GEMM computes all three (the merged projection ``ops.gated_attention_layer``
+    takes)."""
+
+    def __init__(self, hidden_size, head_size, total_num_heads, total_num_kv_heads=None,
+                 bias=False):
+        _, tp_size = _tp()
+        total_num_kv_heads = total_num_kv_heads or total_num_heads
+        self.head_size = head_size
+        self.num_heads = divide(total_num_heads, tp_size)
+        self.num_kv_heads = divide(total_num_kv_heads, tp_size)
+        super().__init__(hidden_size, (total_num_heads + 2 * total_num_kv_heads) * head_size,
+                         bias)
+
+    def weight_loader(self, param, loaded_weight, loaded_shard_id: str):
+        assert loaded_shard_id in ("q", "k", "v")
+        q = self.num_heads * self.head_size
+        kv = self.num_kv_heads * self.head_size
+        off, size = {"q": (0, q), "k": (q, kv), "v": (q + kv, kv)}[loaded_shard_id]
+        dst = param.data.narrow(self.tp_dim, off, size)
+        dst.copy_(loaded_weight.chunk(self.tp_size, self.tp_dim)[self.tp_rank])
 
 
 class RowParallelLinear(LinearBase):

@@ -175,16 +175,10 @@ def store_kvcache(k, v, k_cache, v_cache, slot_mapping):
                                  row, stream_ptr()), "lb_store_kvcache")
 
 
-def attn_prologue(q_in, k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions, slot_mapping,
-                  k_cache, v_cache, eps, q_out=None, status=None):
-    """Fused (1+w) RMSNorm + partial RoPE of query and key, and the K/V cache store
-    (reference qwen3_5.py:730-736 and attention.py:50-80).
-
-    ``q_in [N, Hq, D]`` may be a strided view (the query half of q_proj's output);
-    ``k_in``/``v_in`` are ``[N, Hkv, D]`` with packed heads; ``cos_sin_cache`` is the
-    rotary module's fp32 ``[max_position, (1,) rotary_dim]`` buffer.  Returns ``q_out``
-    ``[N, Hq, D]`` (allocated when not given).
-    """
+def prologue_args(q_in, k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions,
+                  slot_mapping, k_cache, v_cache, eps, q_out, status=None):
+    """``LbPrologueArgs`` of one prologue call, and the tensors it points to (keep them
+    alive until the call is enqueued)."""
     N, Hq, D = q_in.shape
     Hkv = k_in.shape[1]
     for t, name in ((k_in, "k_in"), (v_in, "v_in")):
@@ -192,8 +186,6 @@ def attn_prologue(q_in, k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions
             raise ValueError(f"{name} must be [N, Hkv, D] with packed heads")
     if q_in.stride(-1) != 1:
         raise ValueError("q_in must have a contiguous last dim")
-    if q_out is None:
-        q_out = torch.empty(N, Hq, D, dtype=q_in.dtype, device=q_in.device)
     cs = cos_sin_cache.reshape(cos_sin_cache.shape[0], -1)
     if cs.dtype != torch.float32 or not cs.is_contiguous():
         raise ValueError("cos_sin_cache must be a contiguous fp32 [max_position, rotary_dim]")
@@ -210,7 +202,26 @@ def attn_prologue(q_in, k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions
         v_cache=v_cache.data_ptr(), num_slots=k_cache.numel() // row, q_out=q_out.data_ptr(),
         q_out_stride_tok=q_out.stride(0), q_out_stride_head=q_out.stride(1),
         status=ptr(status))
+    return a, (cs, pos, sm)
+
+
+def attn_prologue(q_in, k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions, slot_mapping,
+                  k_cache, v_cache, eps, q_out=None, status=None):
+    """Fused (1+w) RMSNorm + partial RoPE of query and key, and the K/V cache store
+    (reference qwen3_5.py:730-736 and attention.py:50-80).
+
+    ``q_in [N, Hq, D]`` may be a strided view (the query half of q_proj's output);
+    ``k_in``/``v_in`` are ``[N, Hkv, D]`` with packed heads; ``cos_sin_cache`` is the
+    rotary module's fp32 ``[max_position, (1,) rotary_dim]`` buffer.  Returns ``q_out``
+    ``[N, Hq, D]`` (allocated when not given).
+    """
+    N, Hq, D = q_in.shape
+    if q_out is None:
+        q_out = torch.empty(N, Hq, D, dtype=q_in.dtype, device=q_in.device)
+    a, keep = prologue_args(q_in, k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions,
+                            slot_mapping, k_cache, v_cache, eps, q_out, status)
     check(lib().lb_attn_prologue(C.byref(a), stream_ptr()), "lb_attn_prologue")
+    del keep
     return q_out
 
 
@@ -219,17 +230,21 @@ def gated_attention_layer(x, w_qkv, num_heads, num_kv_heads, q_norm_w, k_norm_w,
                           block_tables, context_lens, cu_seqlens_q, w_o, scale, out=None,
                           max_q_len=None, work_hint=None, events=None, qkv=None, q=None,
                           attn_out=None, ws_tag="pod", tp=None, tp_phases=0,
-                          stage_events=None):
+                          stage_events=None, fuse_prologue=True):
     """The whole gated full-attention layer from its hidden states
     (``Qwen3_5FullAttention.forward``, nanovllm/models/qwen3_5.py:705-746), three library
     calls:
 
     1. one GEMM for the three projections: ``qkv = x @ w_qkv.T`` with ``w_qkv`` =
        ``[q_proj.weight; k_proj.weight; v_proj.weight]`` (``[Hq*2D + 2*Hkv*D, H]``);
-    2. ``lb_attn_prologue``: (1+w) RMSNorm and partial RoPE of query and key, the K/V of the
-       new tokens stored into the paged cache at ``slot_mapping``;
+    2. the prologue: (1+w) RMSNorm and partial RoPE of query and key, the K/V of the new
+       tokens stored into the paged cache at ``slot_mapping``;
     3. ``lb_pod_attn_oproj``: attention over the cache for every sequence of the batch,
        ``* sigmoid(gate)`` (the gate read in place from q_proj's output) and o_proj.
+
+    With ``fuse_prologue`` (the default) step 2 runs inside the attention kernel of step 3
+    (``LbPodArgs.prologue``): its CTAs first do the prologue rows, and each attention item
+    waits for its own sequence's rows; else step 2 is its own ``lb_attn_prologue`` launch.
 
     ``qkv`` ``[N, Hq*2D + 2*Hkv*D]`` and ``q`` ``[N, Hq, D]`` may be given as preallocated
     buffers (CUDA-graph capture); ``attn_out`` ``[N, Hq*D]`` optionally receives the
@@ -250,14 +265,21 @@ def gated_attention_layer(x, w_qkv, num_heads, num_kv_heads, q_norm_w, k_norm_w,
     k_in = qkv[:, Hq * 2 * D:Hq * 2 * D + Hkv * D].view(N, Hkv, D)
     v_in = qkv[:, Hq * 2 * D + Hkv * D:].view(N, Hkv, D)
     status = workspace(256, x.device, ws_tag + "_prologue").view(torch.int32)[:1]
-    q = attn_prologue(q3[..., :D], k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions,
+    if q is None:
+        q = torch.empty(N, Hq, D, dtype=x.dtype, device=x.device)
+    pro = None
+    if fuse_prologue:
+        pro, keep = prologue_args(q3[..., :D], k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache,
+                                  positions, slot_mapping, k_cache, v_cache, eps, q, status)
+    else:
+        attn_prologue(q3[..., :D], k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions,
                       slot_mapping, k_cache, v_cache, eps, q_out=q, status=status)
     if stage_events[1] is not None:
         stage_events[1].record()
     return pod_attn_oproj(q, q3[..., D:], k_cache, v_cache, block_tables, context_lens,
                           cu_seqlens_q, w_o, scale, out=out, attn_out=attn_out,
                           max_q_len=max_q_len, ws_tag=ws_tag, events=events,
-                          work_hint=work_hint, tp=tp, tp_phases=tp_phases)
+                          work_hint=work_hint, tp=tp, tp_phases=tp_phases, prologue=pro)
 
 
 def pod_args(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o, scale,
@@ -290,7 +312,8 @@ def pod_work_hint(ctx_list, qlen_list):
 
 def pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, w_o,
                    scale, out=None, attn_out=None, max_q_len=None, kv_split_pages=0,
-                   ws_tag="pod", events=None, work_hint=None, tp=None, tp_phases=0):
+                   ws_tag="pod", events=None, work_hint=None, tp=None, tp_phases=0,
+                   prologue=None):
     """Fused paged attention (prefill + decode mixed) -> sigmoid gate -> o_proj.
 
     ``gate`` may be None (no output gate).  With ``w_o=None`` only the attention runs and
@@ -299,6 +322,8 @@ def pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seq
     ``tp`` (an ``engine.peer.TPExchange``): this rank holds a head slice and W_o's matching
     columns; the o_proj partials are reduced over the group through peer memory inside
     the call and ``out`` (bf16) receives the all-reduced result.
+    ``prologue`` (an ``LbPrologueArgs`` from ``prologue_args`` whose ``q_out`` is ``q``): the
+    prologue of the call's tokens runs inside the attention kernel.
     """
     N, Hq, D = q.shape
     for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache)):
@@ -322,6 +347,8 @@ def pod_attn_oproj(q, gate, k_cache, v_cache, block_tables, context_lens, cu_seq
             a.tp_bufs[r] = p
         a.tp_phases = tp_phases
     _events(a, events)
+    if prologue is not None:
+        a.prologue = C.pointer(prologue)
     need = C.c_size_t(0)
     check(lib().lb_pod_workspace_size(C.byref(a), C.byref(need)), "lb_pod_workspace_size")
     ws = workspace(need.value, q.device, ws_tag)

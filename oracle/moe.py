@@ -152,6 +152,31 @@ def moe_block_bf16(x, p, path="sparse", ids=None, w=None):
 
 
 # ---------------------------------------------------------------- fp32 oracle
+def experts_fp32(x, gate_up, down, ids, w, expert_base=0):
+    """The routed experts alone in fp32 (``Qwen3_5Experts.forward``, qwen3_5.py:815-841):
+    ``sum_j w[t,j] * down_e(silu(gate_e x) * up_e x)`` over the slots whose expert id lies
+    in ``[expert_base, expert_base + len(gate_up))``."""
+    xf = x.float()
+    T = ids.shape[0]
+    out = torch.zeros(T, down.shape[1], dtype=torch.float32, device=xf.device)
+    ids = ids.long()
+    for e in torch.unique(ids).tolist():
+        le = e - expert_base
+        if le < 0 or le >= gate_up.shape[0]:
+            continue
+        tok, pos = torch.where(ids == e)
+        g, u = (xf[tok] @ gate_up[le].float().t()).chunk(2, dim=-1)
+        y = (F.silu(g) * u) @ down[le].float().t()
+        out.index_add_(0, tok, y * w[tok, pos, None].float())
+    return out
+
+
+def shared_expert_fp32(x, sh_gate, sh_up, sh_down):
+    """``Qwen3_5SharedExpertMLP.forward`` (qwen3_5.py:916-917) in fp32, ungated."""
+    xf = x.float()
+    return (F.silu(xf @ sh_gate.float().t()) * (xf @ sh_up.float().t())) @ sh_down.float().t()
+
+
 def moe_block_fp32(x, p, ids, w):
     """The block in fp32 for a fixed routing (ids [T,k], w [T,k] fp32).  Returns fp32.
 

@@ -7,8 +7,10 @@ import torch
 
 from layerbatch_b200 import workloads as W
 from layerbatch_b200.layers import attention as LA
-from layerbatch_b200.layers.fused_moe import Qwen3_5SparseMoeBlock, Qwen3_5TopKRouter
-from layerbatch_b200.layers.linear import ReplicatedLinear
+from layerbatch_b200.layers.fused_moe import (Qwen3_5Experts, Qwen3_5SharedExpertMLP,
+                                               Qwen3_5SparseMoeBlock, Qwen3_5TopKRouter)
+from layerbatch_b200.layers.linear import (MergedColumnParallelLinear, QKVParallelLinear,
+                                           ReplicatedLinear)
 from layerbatch_b200.utils.context import reset_context, set_context
 from oracle import attention as OA
 from oracle import moe as OM
@@ -120,3 +122,60 @@ def test_replicated_linear(cuda):
     torch.cuda.synchronize()
     assert y.shape == (3, 7, 256)
     assert OM.rel_err(y, x.float() @ lin.weight.float().t()) <= 1e-2
+
+
+def test_experts_and_shared_expert_modules(cuda):
+    """``Qwen3_5Experts.forward(x, ids, w)`` and ``Qwen3_5SharedExpertMLP.forward(x)``, the
+    block's two halves called on their own as the reference's block calls them
+    (qwen3_5.py:899-905), against the fp32 oracle; their sum with the sigmoid gate is the
+    block's output."""
+    H, E, I, k, T = 2048, 64, 512, 8, 37
+    p = W.make_moe_params(H, E, I, I, k, seed=15)
+    x = W.make_moe_input(T, H, seed=16)
+    w32, ids = OM.topk_route(OM.router_logits(x, p.router), k)
+    ex = Qwen3_5Experts(E, H, I).to(torch.bfloat16)
+    se = Qwen3_5SharedExpertMLP(H, I).to(torch.bfloat16)
+    with torch.no_grad():
+        ex.gate_up_proj.copy_(p.gate_up)
+        ex.down_proj.copy_(p.down)
+        se.gate_proj.weight.copy_(p.sh_gate)
+        se.up_proj.weight.copy_(p.sh_up)
+        se.down_proj.weight.copy_(p.sh_down)
+    ex, se = ex.to(cuda), se.to(cuda)
+    xd = x.to(cuda)
+    y_e = ex(xd, ids.to(cuda), w32.to(torch.bfloat16).to(cuda))
+    y_s = se(xd)
+    torch.cuda.synchronize()
+    assert OM.rel_err(y_e.cpu(), OM.experts_fp32(x, p.gate_up, p.down, ids, w32.to(torch.bfloat16))) <= TOL
+    assert OM.rel_err(y_s.cpu(), OM.shared_expert_fp32(x, p.sh_gate, p.sh_up, p.sh_down)) <= TOL
+    # an expert-parallel shard: only ids in [16, 48) contribute
+    part = Qwen3_5Experts(32, H, I).to(torch.bfloat16)
+    with torch.no_grad():
+        part.gate_up_proj.copy_(p.gate_up[16:48])
+        part.down_proj.copy_(p.down[16:48])
+    part = part.to(cuda)
+    part.expert_base, part.total_experts = 16, E
+    y_p = part(xd, ids.to(cuda), w32.to(cuda))
+    torch.cuda.synchronize()
+    ref_p = OM.experts_fp32(x, p.gate_up[16:48], p.down[16:48], ids, w32, expert_base=16)
+    assert OM.rel_err(y_p.cpu(), ref_p) <= TOL
+
+
+def test_merged_and_qkv_linears_load_shards_and_compute_one_gemm(cuda):
+    H = 512
+    qkv = QKVParallelLinear(H, 64, 4, 2).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(3)
+    wq, wk, wv = (0.02 * torch.randn(n, H, generator=g) for n in (4 * 64, 2 * 64, 2 * 64))
+    for wt, sid in ((wq, "q"), (wk, "k"), (wv, "v")):
+        qkv.weight.weight_loader(qkv.weight, wt.to(torch.bfloat16), sid)
+    mc = MergedColumnParallelLinear(H, [256, 256]).to(torch.bfloat16)
+    wa, wb = (0.02 * torch.randn(256, H, generator=g) for _ in range(2))
+    mc.weight.weight_loader(mc.weight, wa.to(torch.bfloat16), 0)
+    mc.weight.weight_loader(mc.weight, wb.to(torch.bfloat16), 1)
+    qkv, mc = qkv.to(cuda), mc.to(cuda)
+    x = torch.randn(9, H, generator=g).to(torch.bfloat16)
+    y, z = qkv(x.to(cuda)), mc(x.to(cuda))
+    torch.cuda.synchronize()
+    ref_y = x.float() @ torch.cat([wq, wk, wv]).to(torch.bfloat16).float().t()
+    ref_z = x.float() @ torch.cat([wa, wb]).to(torch.bfloat16).float().t()
+    assert OM.rel_err(y.cpu(), ref_y) <= 1e-2 and OM.rel_err(z.cpu(), ref_z) <= 1e-2

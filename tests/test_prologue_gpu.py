@@ -193,3 +193,37 @@ def test_full_attention_layer_mixed_step_from_scheduler(cuda):
     finally:
         reset_context()
     assert OM.rel_err(y.cpu(), ref) <= TOL
+
+
+def test_fused_prologue_equals_the_separate_launch(cuda):
+    """The prologue fused into the attention kernel (its CTAs normalise, rotate and store
+    the batch's rows first; each item waits for its sequence) gives bit for bit what the
+    separate lb_attn_prologue launch gives: the query rows, the stored K/V rows, the layer
+    output.  Two prefill chunks (one on a prefix) and decode steps, one token a padding
+    token (slot -1: its K/V are not stored)."""
+    b = W.make_attn_batch([700, 33, 1900, 256, 2], [(300, 200), (0, 129)], seed=41)
+    N = b.num_tokens
+    lp = W.make_attn_layer_params(seed=42, device=cuda)
+    pos, slots = W.layer_positions_slots(b)
+    slots[N - 1] = -1
+    x = W.make_layer_input(N, 2048, seed=43, device=cuda)
+    g = b.to(cuda)
+    outs = {}
+    for fuse in (False, True):
+        kc, vc = g.k_cache.clone(), g.v_cache.clone()
+        q = torch.empty(N, 16, 256, dtype=torch.bfloat16, device=cuda)
+        attn = torch.empty(N, 16 * 256, dtype=torch.bfloat16, device=cuda)
+        y = ops.gated_attention_layer(
+            x, lp.w_qkv, 16, 2, lp.q_norm_w, lp.k_norm_w, lp.cos_sin_cache, lp.eps,
+            pos.to(cuda), slots.to(cuda), kc, vc, g.block_tables, g.context_lens,
+            g.cu_seqlens_q, g.w_o, g.scale, max_q_len=200, q=q, attn_out=attn,
+            ws_tag=f"fused{int(fuse)}", fuse_prologue=fuse)
+        torch.cuda.synchronize()
+        assert ops.device_status(ops.workspace(0, cuda, f"fused{int(fuse)}")) == 0
+        assert ops.device_status(ops.workspace(0, cuda, f"fused{int(fuse)}_prologue")) == 0
+        outs[fuse] = (y, q, attn, kc, vc)
+    for a, r in zip(outs[True], outs[False]):
+        assert torch.equal(a, r)
+    # and the padding token's slot was left alone
+    last = int(b.block_tables[b.num_seqs - 1, 0]) * 256 + 1
+    assert torch.equal(outs[True][3].view(-1, 2, 256)[last], g.k_cache.view(-1, 2, 256)[last])
