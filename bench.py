@@ -25,8 +25,10 @@ path.  Each GPU keeps one c4 batch of work, so scaling is weak.  Rank 0 prints o
 line; the time is the max over ranks of CUDA-event time.
 
 ``value`` is device throughput with inputs resident in HBM, timed over K steps with no
-events inside them; a second pass over K steps records CUDA events between the stages for
-the per-phase times and the roofline kernel's duration.  ``e2e`` is the same step through
+events inside them (on one GPU the step is captured once as a CUDA graph and replayed, so
+short steps are not bounded by the host's launch rate); a second pass over K eager steps
+records CUDA events between the stages for the per-phase times and the roofline kernel's
+duration.  ``e2e`` is the same step through
 the same public calls in a serving loop: each step uploads its inputs (hidden states and
 batch metadata) from pinned host memory and downloads its outputs, on copy streams that
 overlap the previous and next steps' kernels (double-buffered device inputs and outputs).
@@ -493,6 +495,19 @@ def run_ours(args, rank, world, device):
     for _ in range(Wu):
         step()
     torch.cuda.synchronize()
+    # On one GPU the step is captured once as a CUDA graph and the timed loop replays it,
+    # as the reference replays its decode steps (nanovllm/engine/model_runner.py:862-891):
+    # the device time is then not bounded by the host's launch rate (which matters for the
+    # 0.1 ms steps of c1).  The library's launch counter sees the launches at capture.
+    graph, per_step = None, None
+    if world == 1 and not args.no_graph:
+        n0 = ops.launch_count()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        per_step = ops.launch_count() - n0
+        graph.replay()
+        torch.cuda.synchronize()
     # ---------------- the timed region: K steps, no events inside them
     st, en = mk(), mk()
     n0 = ops.launch_count()
@@ -501,11 +516,14 @@ def run_ours(args, rank, world, device):
     with ClockSampler(torch.cuda.current_device()) as clk:
         st.record()
         for _ in range(K):
-            step()
+            if graph is not None:
+                graph.replay()
+            else:
+                step()
         en.record()
         torch.cuda.synchronize()
     barrier()
-    launches = ops.launch_count() - n0
+    launches = per_step * K if graph is not None else ops.launch_count() - n0
     ms = st.elapsed_time(en) / K
     ms_t = torch.tensor([ms], dtype=torch.float64, device=device)
     if world > 1:
@@ -527,17 +545,20 @@ def run_ours(args, rank, world, device):
         return statistics.mean(a(e).elapsed_time(b(e)) for e in evs)
 
     res = {"ms": ms, "tokens": tokens, "launches": launches, "launches_per_step": launches / K,
-           "clocks": clk.summary()}
+           "clocks": clk.summary(),
+           "timed_loop": "CUDA graph replay of the captured step" if graph is not None
+           else "eager launches"}
+    del graph
     peaks = load_peaks()
     phases = {}
     if attn is not None:
         t_attn = mean_ms(lambda e: e["pod"][0], lambda e: e["pod"][1]) * 1e-3
-        flops, byts = attn_work(attn, fused_prologue=layer)
+        flops, byts = attn_work(attn)
         res["attn"] = {"ms": t_attn * 1e3, "flops": flops, "bytes": byts,
                        "gbs": byts / t_attn / 1e9, "tflops": flops / t_attn / 1e12}
         if layer:
-            # the prologue runs inside the attention kernel (pod_attn)
             phases["qkv_gemm"] = mean_ms(lambda e: e["attn0"], lambda e: e["stages"][0])
+            phases["prologue"] = mean_ms(lambda e: e["stages"][0], lambda e: e["stages"][1])
             phases["plan"] = mean_ms(lambda e: e["stages"][1], lambda e: e["pod"][0])
         else:
             phases["plan"] = mean_ms(lambda e: e["attn0"], lambda e: e["pod"][0])
@@ -549,10 +570,10 @@ def run_ours(args, rank, world, device):
         phases["oproj"] = mean_ms(lambda e: e["pod"][2], lambda e: e["pod"][3])
         phases["attention_layer"] = mean_ms(lambda e: e["attn0"], lambda e: e["attn1"])
         if layer:
-            g, _ = layer_proj_work(attn.num_tokens, Hq=Hq_l, Hkv=Hkv_l)
+            g, pr = layer_proj_work(attn.num_tokens, Hq=Hq_l, Hkv=Hkv_l)
             res["proj"] = {"gemm_gbs": g["bytes"] / phases["qkv_gemm"] / 1e6,
                            "gemm_tflops": g["flops"] / phases["qkv_gemm"] / 1e9,
-                           "prologue": "fused into k_pod_attn"}
+                           "prologue_gbs": pr["bytes"] / phases["prologue"] / 1e6}
     if moe:
         phases["moe_layer"] = mean_ms(lambda e: e["moe0"], lambda e: e["moe1"])
         if sharded:
@@ -704,6 +725,8 @@ def main():
     ap.add_argument("--config", choices=list(CONFIGS), default="c4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time eager launches instead of replaying a captured step")
     ap.add_argument("--ref-budget-s", type=float, default=240.0,
                     help="wall-clock bound of the reference arm's CPU run")
     args = ap.parse_args()
@@ -797,6 +820,7 @@ def main():
             "config": cfg_desc, "parallelism": res["parallelism"],
             "roofline": roof, "cpu_baseline": cpu, "clocks": res["clocks"],
             "gpu_launches": res["launches"], "phases_ms": res["phases_ms"],
+            "timed_loop": res["timed_loop"],
         }
         for key in ("moe_layer", "proj"):
             if key in res:

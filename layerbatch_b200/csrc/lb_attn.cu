@@ -44,7 +44,7 @@ __global__ void __launch_bounds__(256) k_attn_prologue(const LbPrologueArgs a) {
     const int tok0 = t * PRO_TASK_TOKENS;
     const int ntok = (int)(a.num_tokens - tok0) < PRO_TASK_TOKENS ? (int)(a.num_tokens - tok0)
                                                                     : PRO_TASK_TOKENS;
-    prologue_task(a, tok0, ntok, &st, threadIdx.x / 32, 8, threadIdx.x % 32, a.status);
+    prologue_task(a, nullptr, tok0, ntok, &st, threadIdx.x / 32, 8, threadIdx.x % 32, a.status);
     __syncthreads();
   }
 }

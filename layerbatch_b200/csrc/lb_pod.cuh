@@ -167,29 +167,29 @@ __device__ __forceinline__ bool wait_seq_ready(const PodParams& p, int b, int ne
   return true;
 }
 
-// The fused prologue phase: every thread of the CTA takes part; the data region of shared
-// memory (free until the attention pipelines start) holds the tasks' staging area.
-__device__ __forceinline__ void pod_prologue_phase(const PodParams& p, PodBars* bars,
-                                                   uint8_t* smem) {
+// The fused prologue phase, run by every CTA before its first attention item: the CTA's
+// warps take tasks of PRO_TASK_TOKENS consecutive tokens from the counter until every task
+// is claimed (rows straight from global memory, prologue_rows_direct).  A CTA thus starts
+// items only once every task has been claimed by a running CTA, and an item's wait for its
+// sequence's rows only ever waits for tasks in progress.
+__device__ __forceinline__ void pod_prologue_phase(const PodParams& p, PodBars* bars) {
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  ProStage* st = reinterpret_cast<ProStage*>(smem);
+  const ProNorm nw = prologue_norm(p.pro, lane);
   while (true) {
     if (threadIdx.x == 0) bars->pro_task = atomicAdd(p.pro_next, 1);
     __syncthreads();
     const int t = bars->pro_task;
     if (t >= p.pro_tasks) break;
-    const int tok0 = t * PRO_TASK_TOKENS;
-    const int ntok = min(PRO_TASK_TOKENS, p.num_tokens - tok0);
-    prologue_task(p.pro, tok0, ntok, st, warp, POD_THREADS / 32, lane, p.status);
+    const int t0 = t * PRO_TASK_TOKENS;
+    const int ntok = min(PRO_TASK_TOKENS, p.num_tokens - t0);
+    prologue_rows_direct(p.pro, t0, ntok, warp, POD_THREADS / 32, lane, nw, p.status);
     // the rows are read back by TMA (async proxy) on other SMs
     fence_proxy_async_global();
     __threadfence();
     __syncthreads();
-    if ((int)threadIdx.x < ntok) red_release_gpu_add(p.seq_ready + seq_of_token(p, tok0 + threadIdx.x), 1);
+    if ((int)threadIdx.x < ntok) red_release_gpu_add(p.seq_ready + seq_of_token(p, t0 + threadIdx.x), 1);
     if (threadIdx.x == 0) red_release_gpu_add(p.pro_done, 1);
   }
-  // the staging area becomes TMA destination memory
-  fence_proxy_async_smem();
 }
 
 __device__ __forceinline__ int kv_page_row(const PodParams& p, int b, int tok) {
@@ -268,13 +268,14 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
   }
   if (threadIdx.x == 0) bars->abort = 0;
   PodCounters cnt = {0, 0, 0, 0, 0, 0};
-  if (p.pro_tasks > 0) pod_prologue_phase(p, bars, smem);
+  if (p.pro_tasks > 0) pod_prologue_phase(p, bars);
   bool pro_all_ready = false;   // producer lanes: every prologue task seen finished
 
   const bool pf_first = (int)blockIdx.x < p.n_prefill_ctas;
   for (int pass = 0; pass < 2; ++pass) {
     const bool prefill = (pass == 0) ? pf_first : !pf_first;
     const int nslots = DEC_SLOTS;   // decode ring (prefill: the PF_KSLOTS / PF_VSLOTS rings)
+
     if (threadIdx.x == 0) {
       for (int i = 0; i < 5; ++i) {
         mbar_init(&bars->kv_full[i], 1);

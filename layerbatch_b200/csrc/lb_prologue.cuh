@@ -29,6 +29,7 @@ constexpr int PRO_BATCH = 8;          // rows a warp loads before it uses any
 
 // Per-task staging area in shared memory.
 struct ProStage {
+  int tok[PRO_TASK_TOKENS];               // the task's tokens, -1: none (invalid entry)
   int slot[PRO_TASK_TOKENS];              // cache slot of each token, -1: nothing to store
   float cs[PRO_TASK_TOKENS][PRO_D];       // cos | sin row of each token's position
 };
@@ -41,13 +42,17 @@ struct ProRow {
 };
 
 __device__ __forceinline__ ProRow prologue_load(const LbPrologueArgs& a, const ProStage* st,
-                                                int tok0, int n, int h, int lane) {
+                                                int n, int h, int lane) {
   ProRow r;
   r.n = n;
   r.h = h;
   r.x = make_uint4(0, 0, 0, 0);
   const int Hq = (int)a.num_q_heads, Hkv = (int)a.num_kv_heads;
-  const long long t = (long long)tok0 + n;
+  const long long t = st->tok[n];
+  if (t < 0) {
+    r.h = -1;
+    return r;
+  }
   const __nv_bfloat16* src;
   if (h < Hq) {
     src = static_cast<const __nv_bfloat16*>(a.q_in) + t * a.q_in_stride_tok +
@@ -67,83 +72,137 @@ __device__ __forceinline__ ProRow prologue_load(const LbPrologueArgs& a, const P
   return r;
 }
 
-// Normalise, rotate and store one loaded row (value rows are stored as they are).  All 32
-// lanes of the warp call it together (warp shuffles), also for rows with h = -1.
-__device__ __forceinline__ void prologue_store(const LbPrologueArgs& a, const ProStage* st,
-                                               int tok0, const ProRow& r, int lane,
-                                               const uint4& qw, const uint4& kw) {
-  const int Hq = (int)a.num_q_heads, Hkv = (int)a.num_kv_heads;
-  if (r.h >= Hq + Hkv) {   // value row (a warp-uniform branch: the row is the warp's)
-    const long long row = (long long)st->slot[r.n] * Hkv * PRO_D + (long long)(r.h - Hq - Hkv) * PRO_D;
-    reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.v_cache) + row)[lane] = r.x;
-    return;
+// The (1 + w) factors of the two norms for this lane's 8 dims, once per task.
+struct ProNorm {
+  float q[8], k[8];
+};
+
+__device__ __forceinline__ ProNorm prologue_norm(const LbPrologueArgs& a, int lane) {
+  ProNorm w;
+  const uint4 qw = reinterpret_cast<const uint4*>(a.q_norm_w)[lane];
+  const uint4 kw = reinterpret_cast<const uint4*>(a.k_norm_w)[lane];
+  const uint32_t qv[4] = {qw.x, qw.y, qw.z, qw.w}, kv[4] = {kw.x, kw.y, kw.z, kw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    w.q[2 * i] = __fadd_rn(1.0f, bf16_lo(qv[i]));
+    w.q[2 * i + 1] = __fadd_rn(1.0f, bf16_hi(qv[i]));
+    w.k[2 * i] = __fadd_rn(1.0f, bf16_lo(kv[i]));
+    w.k[2 * i + 1] = __fadd_rn(1.0f, bf16_hi(kv[i]));
   }
-  const bool is_q = r.h < Hq;
-  float x[8] = {bf16_lo(r.x.x), bf16_hi(r.x.x), bf16_lo(r.x.y), bf16_hi(r.x.y),
-                bf16_lo(r.x.z), bf16_hi(r.x.z), bf16_lo(r.x.w), bf16_hi(r.x.w)};
+  return w;
+}
+
+// The normalised (and, for the first rotary_dim dims, rotated) bf16 row of a loaded query
+// or key row, this lane's 8 dims packed.  All 32 lanes of the warp call it together (warp
+// shuffles).  `cs` is the row's cos|sin table row; only the lanes holding rotated dims read
+// it.  The normalised row is rounded to bf16 before the rotation, as the reference rounds
+// the norm's output.
+__device__ __forceinline__ uint4 prologue_row_math(const LbPrologueArgs& a, const uint4& xr,
+                                                   bool is_q, const float* cs, int lane,
+                                                   const ProNorm& nw) {
+  const uint32_t xv[4] = {xr.x, xr.y, xr.z, xr.w};
+  float x[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = bf16_lo(xv[i]);
+    x[2 * i + 1] = bf16_hi(xv[i]);
+  }
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-  const float rstd = 1.0f / sqrtf(__fadd_rn(ss / (float)PRO_D, a.eps));
-  const uint4 wr = is_q ? qw : kw;
-  const float w[8] = {bf16_lo(wr.x), bf16_hi(wr.x), bf16_lo(wr.y), bf16_hi(wr.y),
-                      bf16_lo(wr.z), bf16_hi(wr.z), bf16_lo(wr.w), bf16_hi(wr.w)};
-  float y[8];
+  const float rstd = rsqrtf(__fadd_rn(ss / (float)PRO_D, a.eps));
+  uint32_t yb[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
-    y[i] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[i], rstd), __fadd_rn(1.0f, w[i]))));
+  for (int i = 0; i < 4; ++i) {
+    const float w0 = is_q ? nw.q[2 * i] : nw.k[2 * i];
+    const float w1 = is_q ? nw.q[2 * i + 1] : nw.k[2 * i + 1];
+    yb[i] = pack_bf16x2(__fmul_rn(__fmul_rn(x[2 * i], rstd), w0),
+                        __fmul_rn(__fmul_rn(x[2 * i + 1], rstd), w1));
+  }
   // partial RoPE: dims [0, rot/2) pair with [rot/2, rot); lanes < rot/16 hold the first
   // half, the next rot/16 lanes the second
   const int rot = (int)a.rotary_dim;
   const int hl = rot / 16;
   const bool first = lane < hl, second = lane >= hl && lane < 2 * hl;
   const int partner = first ? lane + hl : (second ? lane - hl : lane);
-  float pv[8];
+  uint32_t pb[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) pv[i] = __shfl_sync(0xffffffffu, y[i], partner);
-  if (r.h < 0) return;
+  for (int i = 0; i < 4; ++i) pb[i] = __shfl_sync(0xffffffffu, yb[i], partner);
   if (first || second) {
-    const float* cs = st->cs[r.n];
     const int f0 = (first ? lane : lane - hl) * 8;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float c = cs[f0 + i], sn = cs[rot / 2 + f0 + i];
-      const float t = first ? __fsub_rn(__fmul_rn(y[i], c), __fmul_rn(pv[i], sn))   // x1 c - x2 s
-                            : __fadd_rn(__fmul_rn(y[i], c), __fmul_rn(pv[i], sn));  // x2 c + x1 s
-      y[i] = __bfloat162float(__float2bfloat16_rn(t));
+    for (int i = 0; i < 4; ++i) {
+      float y2[2] = {bf16_lo(yb[i]), bf16_hi(yb[i])};
+      const float p2[2] = {bf16_lo(pb[i]), bf16_hi(pb[i])};
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const float c = cs[f0 + 2 * i + u], sn = cs[rot / 2 + f0 + 2 * i + u];
+        y2[u] = first ? __fsub_rn(__fmul_rn(y2[u], c), __fmul_rn(p2[u], sn))   // x1 c - x2 s
+                      : __fadd_rn(__fmul_rn(y2[u], c), __fmul_rn(p2[u], sn));  // x2 c + x1 s
+      }
+      yb[i] = pack_bf16x2(y2[0], y2[1]);
     }
   }
-  const uint4 outv = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
-                                pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
-  const long long t = (long long)tok0 + r.n;
-  if (is_q) {
+  return make_uint4(yb[0], yb[1], yb[2], yb[3]);
+}
+
+// Store one row: the query row to q_out, the key row (normalised, rotated) or the value row
+// (as loaded) into the cache at `slot`.  h: [0, Hq) query, [Hq, Hq+Hkv) key, then value.
+__device__ __forceinline__ void prologue_put(const LbPrologueArgs& a, long long t, int h,
+                                             long long slot, const uint4& v, int lane) {
+  const int Hq = (int)a.num_q_heads, Hkv = (int)a.num_kv_heads;
+  if (h < Hq) {
     __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.q_out) + t * a.q_out_stride_tok +
-                         (long long)r.h * a.q_out_stride_head;
-    reinterpret_cast<uint4*>(dst)[lane] = outv;
+                         (long long)h * a.q_out_stride_head;
+    reinterpret_cast<uint4*>(dst)[lane] = v;
+  } else if (h < Hq + Hkv) {
+    const long long row = slot * Hkv * PRO_D + (long long)(h - Hq) * PRO_D;
+    reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.k_cache) + row)[lane] = v;
   } else {
-    const long long row = (long long)st->slot[r.n] * Hkv * PRO_D + (long long)(r.h - Hq) * PRO_D;
-    reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.k_cache) + row)[lane] = outv;
+    const long long row = slot * Hkv * PRO_D + (long long)(h - Hq - Hkv) * PRO_D;
+    reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.v_cache) + row)[lane] = v;
   }
 }
 
-// One task: tokens [tok0, tok0 + ntok), ntok <= PRO_TASK_TOKENS.  Every thread of the block
-// calls it (it stages with the whole block and meets at __syncthreads); `nwarps` warps
-// (warp ids [0, nwarps)) take the rows.  The caller separates consecutive tasks with a
-// __syncthreads, as the staging area is reused.
-__device__ __forceinline__ void prologue_task(const LbPrologueArgs& a, int tok0, int ntok,
-                                              ProStage* st, int warp, int nwarps, int lane,
-                                              int* status) {
+// A staged row (prologue_task): normalise / rotate query and key rows, store every row.
+__device__ __forceinline__ void prologue_store(const LbPrologueArgs& a, const ProStage* st,
+                                               const ProRow& r, int lane, const ProNorm& nw) {
+  const int Hq = (int)a.num_q_heads, Hkv = (int)a.num_kv_heads;
+  if (r.h >= Hq + Hkv) {   // value row (a warp-uniform branch: the row is the warp's)
+    prologue_put(a, st->tok[r.n], r.h, st->slot[r.n], r.x, lane);
+    return;
+  }
+  const uint4 y = prologue_row_math(a, r.x, r.h < Hq, st->cs[r.n], lane, nw);
+  if (r.h >= 0) prologue_put(a, st->tok[r.n], r.h, st->slot[r.n], y, lane);
+}
+
+// One task: entries [e0, e0 + ntok) of the token list `toks` (NULL: tokens e0, e0 + 1, ...),
+// ntok <= PRO_TASK_TOKENS.  Every thread of the block calls it (it stages with the whole
+// block and meets at __syncthreads); `nwarps` warps (warp ids [0, nwarps)) take the rows.
+// The caller separates consecutive tasks with a __syncthreads, as the staging area is
+// reused.  Tokens outside [0, num_tokens) are reported and skipped.
+__device__ __forceinline__ void prologue_task(const LbPrologueArgs& a, const int* toks, int e0,
+                                              int ntok, ProStage* st, int warp, int nwarps,
+                                              int lane, int* status) {
   const int rot = (int)a.rotary_dim;
   for (int i = threadIdx.x; i < ntok; i += blockDim.x) {
-    const long long s = (long long)a.slot_mapping[tok0 + i];
+    int t = toks ? toks[e0 + i] : e0 + i;
+    if (t < 0 || t >= a.num_tokens) {
+      report(status, LB_DEV_BAD_INDEX);
+      t = -1;
+    }
+    st->tok[i] = t;
+    const long long s = t < 0 ? -1 : (long long)a.slot_mapping[t];
     if (s >= a.num_slots) report(status, LB_DEV_BAD_INDEX);
     st->slot[i] = (s < 0 || s >= a.num_slots) ? -1 : (int)s;
   }
+  __syncthreads();
   for (int e = threadIdx.x; e < ntok * rot; e += blockDim.x) {
     const int i = e / rot, c = e - (e / rot) * rot;
-    long long pos = a.positions[tok0 + i];
+    const int t = st->tok[i];
+    long long pos = t < 0 ? 0 : a.positions[t];
     if (pos < 0 || pos >= a.max_position) {
       if (c == 0) report(status, LB_DEV_BAD_INDEX);
       pos = pos < 0 ? 0 : a.max_position - 1;
@@ -152,25 +211,91 @@ __device__ __forceinline__ void prologue_task(const LbPrologueArgs& a, int tok0,
   }
   __syncthreads();
   if (warp >= nwarps) return;
-  const uint4 qw = reinterpret_cast<const uint4*>(a.q_norm_w)[lane];
-  const uint4 kw = reinterpret_cast<const uint4*>(a.k_norm_w)[lane];
+  const ProNorm nw = prologue_norm(a, lane);
   const int nh = (int)(a.num_q_heads + 2 * a.num_kv_heads);
   const int rows = ntok * nh;
   for (int j0 = warp * PRO_BATCH; j0 < rows; j0 += nwarps * PRO_BATCH) {
     ProRow r[PRO_BATCH];
+    int n = j0 / nh, h = j0 - (j0 / nh) * nh;   // row j0; the next rows step the head
 #pragma unroll
     for (int i = 0; i < PRO_BATCH; ++i) {
-      const int j = j0 + i;
-      if (j < rows) {
-        r[i] = prologue_load(a, st, tok0, j / nh, j - (j / nh) * nh, lane);
+      if (j0 + i < rows) {
+        r[i] = prologue_load(a, st, n, h, lane);
       } else {
         r[i].h = -1;
         r[i].n = 0;
         r[i].x = make_uint4(0, 0, 0, 0);
       }
+      if (++h == nh) {
+        h = 0;
+        ++n;
+      }
     }
 #pragma unroll
-    for (int i = 0; i < PRO_BATCH; ++i) prologue_store(a, st, tok0, r[i], lane, qw, kw);
+    for (int i = 0; i < PRO_BATCH; ++i) prologue_store(a, st, r[i], lane, nw);
+  }
+}
+
+// Rows of the contiguous tokens [t0, t0 + ntok) loaded straight from global memory (no
+// staging: each row reads its token's slot and, on the rotated lanes, its cos/sin row),
+// `nwarps` warps from `warp` on, PRO_BATCH rows in flight per warp.  Whole warps call it.
+__device__ __forceinline__ void prologue_rows_direct(const LbPrologueArgs& a, int t0, int ntok,
+                                                     int warp, int nwarps, int lane,
+                                                     const ProNorm& nw, int* status) {
+  const int Hq = (int)a.num_q_heads, Hkv = (int)a.num_kv_heads;
+  const int nh = Hq + 2 * Hkv;
+  const int rows = ntok * nh;
+  const int rot = (int)a.rotary_dim;
+  for (int j0 = warp * PRO_BATCH; j0 < rows; j0 += nwarps * PRO_BATCH) {
+    uint4 x[PRO_BATCH];
+    int tt[PRO_BATCH], hh[PRO_BATCH], sl[PRO_BATCH];
+    int n = j0 / nh, h = j0 - (j0 / nh) * nh;
+#pragma unroll
+    for (int i = 0; i < PRO_BATCH; ++i) {
+      const int t = t0 + n;
+      tt[i] = t;
+      hh[i] = (j0 + i < rows) ? h : -1;
+      sl[i] = 0;
+      x[i] = make_uint4(0, 0, 0, 0);
+      if (hh[i] >= Hq) {
+        const long long s = (long long)a.slot_mapping[t];
+        if (s >= a.num_slots) report(status, LB_DEV_BAD_INDEX);
+        if (s < 0 || s >= a.num_slots) hh[i] = -1;
+        sl[i] = (int)s;
+      }
+      if (hh[i] >= 0) {
+        const __nv_bfloat16* src =
+            hh[i] < Hq ? static_cast<const __nv_bfloat16*>(a.q_in) + (long long)t * a.q_in_stride_tok +
+                             (long long)hh[i] * a.q_in_stride_head
+            : hh[i] < Hq + Hkv ? static_cast<const __nv_bfloat16*>(a.k_in) + (long long)t * a.k_in_stride_tok +
+                                     (long long)(hh[i] - Hq) * PRO_D
+                               : static_cast<const __nv_bfloat16*>(a.v_in) + (long long)t * a.v_in_stride_tok +
+                                     (long long)(hh[i] - Hq - Hkv) * PRO_D;
+        x[i] = reinterpret_cast<const uint4*>(src)[lane];
+      }
+      if (++h == nh) {
+        h = 0;
+        ++n;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PRO_BATCH; ++i) {
+      if (hh[i] >= Hq + Hkv) {   // value row
+        prologue_put(a, tt[i], hh[i], sl[i], x[i], lane);
+        continue;
+      }
+      const float* cs = a.cos_sin_cache;
+      if (hh[i] >= 0 && rot > 0 && lane < rot / 8) {
+        long long pos = a.positions[tt[i]];
+        if (pos < 0 || pos >= a.max_position) {
+          report(status, LB_DEV_BAD_INDEX);
+          pos = pos < 0 ? 0 : a.max_position - 1;
+        }
+        cs += pos * rot;
+      }
+      const uint4 y = prologue_row_math(a, x[i], hh[i] < Hq, cs, lane, nw);
+      if (hh[i] >= 0) prologue_put(a, tt[i], hh[i], sl[i], y, lane);
+    }
   }
 }
 

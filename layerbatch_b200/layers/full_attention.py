@@ -6,11 +6,12 @@ Same constructor arguments and parameter names (``q_proj``, ``k_proj``, ``v_proj
 ``forward(positions, hidden_states)``.  One call runs:
 
 1. the q / k / v projections (``lb_gemm_bf16``: tcgen05, fp32 accumulate, bf16 out);
-2. ``lb_pod_attn_oproj`` with the prologue fused: its attention kernel first does the
-   (1+w) RMSNorm of query and key, their partial RoPE and the K/V store into the paged
-   cache, then POD attention over the cache for any mix of prefill and decode sequences,
-   the sigmoid gate (read in place as the second half of each head of q_proj's output,
-   qwen3_5.py:710-713) and o_proj.
+2. ``lb_attn_prologue``: (1+w) RMSNorm of query and key, partial RoPE of both, and the
+   K/V store into the paged cache, in one launch; the gate stays in place as the second
+   half of each head of q_proj's output (qwen3_5.py:710-713) and is read strided;
+3. ``lb_pod_attn_oproj``: POD attention over the paged cache for any mix of prefill and
+   decode sequences, sigmoid gate and o_proj.  (The prologue can also run inside this
+   call's attention kernel, ``ops.gated_attention_layer(fuse_prologue=True)``.)
 
 The rotary cache is built with the same torch operations as the reference
 (rotary_embedding.py:26-33), so the kernel reads bit-identical cos/sin values.  Tensor
@@ -93,12 +94,10 @@ class Qwen3_5FullAttention(nn.Module):
         q_out = ops.gemm(x, self.q_proj.weight).view(N, Hq, 2 * D)
         k = ops.gemm(x, self.k_proj.weight).view(N, Hkv, D)
         v = ops.gemm(x, self.v_proj.weight).view(N, Hkv, D)
-        query = torch.empty(N, Hq, D, dtype=x.dtype, device=x.device)
-        # the prologue (norms, RoPE, K/V store) runs inside the attention kernel
-        pro, keep = ops.prologue_args(q_out[..., :D], k, v, self.q_norm.weight,
-                                      self.k_norm.weight, self.rotary_emb.cos_sin_cache,
-                                      positions, context.slot_mapping, attn.k_cache,
-                                      attn.v_cache, self.q_norm.eps, query)
+        query = ops.attn_prologue(q_out[..., :D], k, v, self.q_norm.weight, self.k_norm.weight,
+                                  self.rotary_emb.cos_sin_cache, positions,
+                                  context.slot_mapping, attn.k_cache, attn.v_cache,
+                                  self.q_norm.eps)
         gate = q_out[..., D:]
         decode = not context.is_prefill
         bt, lens, cu, max_q = _batch_meta(query, context, decode)
@@ -106,4 +105,4 @@ class Qwen3_5FullAttention(nn.Module):
             bt, lens = _tables_from_slots(context.slot_mapping, cu, max_q, attn.k_cache.shape[1])
         return ops.pod_attn_oproj(query, gate, attn.k_cache, attn.v_cache, bt, lens, cu,
                                   self.o_proj.weight, self.scaling, out=out, max_q_len=max_q,
-                                  kv_split_pages=_split_pages(bt), prologue=pro)
+                                  kv_split_pages=_split_pages(bt))

@@ -230,7 +230,7 @@ def gated_attention_layer(x, w_qkv, num_heads, num_kv_heads, q_norm_w, k_norm_w,
                           block_tables, context_lens, cu_seqlens_q, w_o, scale, out=None,
                           max_q_len=None, work_hint=None, events=None, qkv=None, q=None,
                           attn_out=None, ws_tag="pod", tp=None, tp_phases=0,
-                          stage_events=None, fuse_prologue=True):
+                          stage_events=None, fuse_prologue=False):
     """The whole gated full-attention layer from its hidden states
     (``Qwen3_5FullAttention.forward``, nanovllm/models/qwen3_5.py:705-746), three library
     calls:
@@ -242,9 +242,11 @@ def gated_attention_layer(x, w_qkv, num_heads, num_kv_heads, q_norm_w, k_norm_w,
     3. ``lb_pod_attn_oproj``: attention over the cache for every sequence of the batch,
        ``* sigmoid(gate)`` (the gate read in place from q_proj's output) and o_proj.
 
-    With ``fuse_prologue`` (the default) step 2 runs inside the attention kernel of step 3
-    (``LbPodArgs.prologue``): its CTAs first do the prologue rows, and each attention item
-    waits for its own sequence's rows; else step 2 is its own ``lb_attn_prologue`` launch.
+    Step 2 is its own ``lb_attn_prologue`` launch; with ``fuse_prologue`` it runs inside
+    the attention kernel of step 3 instead (``LbPodArgs.prologue``: the kernel's CTAs first
+    do the prologue rows, each attention item waits for its own sequence's rows).  Both
+    give the same bits; on B200 the separate launch is the faster one at the benchmark
+    sizes (its many small blocks hide the row latency better than the persistent CTAs).
 
     ``qkv`` ``[N, Hq*2D + 2*Hkv*D]`` and ``q`` ``[N, Hq, D]`` may be given as preallocated
     buffers (CUDA-graph capture); ``attn_out`` ``[N, Hq*D]`` optionally receives the

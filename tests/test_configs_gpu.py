@@ -220,10 +220,12 @@ def test_c2_pod_full_size(cuda):
     _check_attention_sample(b, b.q, b.gate, b.k_cache, b.v_cache, out, attn, b.w_o, samples)
 
 
-def test_c4_step_full_size(cuda):
+@pytest.mark.parametrize("fuse", [False, True])
+def test_c4_step_full_size(cuda, fuse):
     """The C4 step as bench.py runs it: the gated attention layer from hidden states
     (merged q/k/v GEMM, prologue with the K/V store, POD attention, gate, o_proj) over
-    512 decode sequences and a 4096-token chunk, then the MoE at T = 4608."""
+    512 decode sequences and a 4096-token chunk, then the MoE at T = 4608; with the
+    prologue as its own launch (bench.py's form) and fused into the attention kernel."""
     b = W.c4_attn_batch(seed=1, device=cuda)
     N, Hq, D = b.q.shape
     Hkv = b.k_cache.shape[2]
@@ -241,7 +243,7 @@ def test_c4_step_full_size(cuda):
         pos.to(cuda), slots.to(cuda), b.k_cache, b.v_cache, b.block_tables, b.context_lens,
         b.cu_seqlens_q, b.w_o, b.scale, max_q_len=max(b.qlen_list),
         work_hint=ops.pod_work_hint(b.ctx_list, b.qlen_list), qkv=qkv, q=qbuf,
-        attn_out=attn, ws_tag="cfg_c4")
+        attn_out=attn, ws_tag="cfg_c4", fuse_prologue=fuse)
     torch.cuda.synchronize()
     _status_ok(cuda, "cfg_c4")
     _status_ok(cuda, "cfg_c4_prologue")
@@ -271,6 +273,8 @@ def test_c4_step_full_size(cuda):
     samples = _sample_rows(b, [0], 256, 32, seed=3)
     _check_attention_sample(b, qbuf, gate, b.k_cache, b.v_cache, out, attn, b.w_o, samples)
     del ref_qkv, x_attn, qkv
+    if fuse:
+        return
     # 4. the MoE layer on the step's 4608 tokens
     p, x = _moe_inputs(cuda, N)
     mo, logits, ids, _ = ops.moe_forward(x, p.router, p.gate_up, p.down, p.sh_gate, p.sh_up,
