@@ -148,8 +148,10 @@ struct EpDispatch {
 
 // One warp per token: its row is read once (all of a lane's 16-byte pieces in flight
 // together) and stored to every destination rank's recv region (NVLink stores for other
-// ranks), with the k ids and weights.  The last CTA to finish publishes the row counts and
-// this call's epoch to every destination.
+// ranks), with the k ids and weights.  Token t visits its destinations starting at rank
+// (t + rank) % P, so at any moment the warps of every GPU spread their stores over all
+// destinations instead of all GPUs writing into the same one.  The last CTA to finish
+// publishes the row counts and this call's epoch to every destination.
 template <int MAXS>  // H <= MAXS * 256
 __global__ void __launch_bounds__(256) k_ep_dispatch(const EpDispatch d) {
   pdl_entry();
@@ -167,15 +169,20 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(const EpDispatch d) {
 #pragma unroll
     for (int u = 0; u < MAXS; ++u)
       if (u < stripes) v[u] = src[u * 32];
+    // destinations in the order r0, r0 + 1, ..., P - 1, 0, ..., r0 - 1 (compile-time rank
+    // indices keep sl[] and the peer pointers in registers)
+    const int r0 = (t + d.rank) % d.P;
 #pragma unroll
-    for (int r = 0; r < LB_EP_MAX_RANKS; ++r)
-      if (sl[r] >= 0) {
-        uint4* dst = reinterpret_cast<uint4*>(d.peers.p[r] + d.off_x) +
-                     ((long long)d.rank * d.C + sl[r]) * nvec + lane;
+    for (int pass = 0; pass < 2; ++pass)
 #pragma unroll
-        for (int u = 0; u < MAXS; ++u)
-          if (u < stripes) dst[u * 32] = v[u];
-      }
+      for (int r = 0; r < LB_EP_MAX_RANKS; ++r)
+        if ((pass == 0) == (r >= r0) && sl[r] >= 0) {
+          uint4* dst = reinterpret_cast<uint4*>(d.peers.p[r] + d.off_x) +
+                       ((long long)d.rank * d.C + sl[r]) * nvec + lane;
+#pragma unroll
+          for (int u = 0; u < MAXS; ++u)
+            if (u < stripes) dst[u * 32] = v[u];
+        }
     if (lane < d.k) {
       const int32_t id = d.ids[(long long)t * d.k + lane];
       const float w = d.wf[(long long)t * d.k + lane];
@@ -254,7 +261,9 @@ struct EpReturn {
 
 // One warp per received row: the sum of its local experts' weighted rows (fp32, one bf16
 // rounding) is written to the source's ret region, slot = the row's position in the
-// source's region.  The last CTA publishes the epoch to every source.
+// source's region.  Warp q takes row q / P of source (q + rank) % P, so consecutive warps
+// write to different GPUs (a source-major walk would have every GPU storing into the same
+// source at the same time).  The last CTA publishes the epoch to every source.
 template <int MAXS>  // H <= MAXS * 256
 __global__ void __launch_bounds__(256) k_ep_return(const EpReturn d) {
   pdl_entry();
@@ -264,9 +273,10 @@ __global__ void __launch_bounds__(256) k_ep_return(const EpReturn d) {
   const int stripes = d.H / 256;
   const int nrows = d.P * d.C;
   for (int q = blockIdx.x * wpb + (int)(threadIdx.x >> 5); q < nrows; q += gridDim.x * wpb) {
-    const int s = q / d.C, i = q - s * d.C;
+    const int s = (q + d.rank) % d.P, i = q / d.P;
     if (i >= min(*(volatile int*)(hdr + EPH_COUNT + s), d.C)) continue;
-    const int my_row = lane < d.k ? d.row_of[(long long)q * d.k + lane] : -1;
+    const long long rr = (long long)s * d.C + i;   // the row in this rank's recv regions
+    const int my_row = lane < d.k ? d.row_of[rr * d.k + lane] : -1;
     float acc[MAXS][8];
 #pragma unroll
     for (int u = 0; u < MAXS; ++u)
@@ -289,7 +299,11 @@ __global__ void __launch_bounds__(256) k_ep_return(const EpReturn d) {
           acc[u][6] += bf16_lo(v[u].w); acc[u][7] += bf16_hi(v[u].w);
         }
     }
-    uint4* dst = reinterpret_cast<uint4*>(d.peers.p[s] + d.off_ret) +
+    uint8_t* peer = nullptr;
+#pragma unroll
+    for (int q = 0; q < LB_EP_MAX_RANKS; ++q)
+      if (q == s) peer = d.peers.p[q];
+    uint4* dst = reinterpret_cast<uint4*>(peer + d.off_ret) +
                  ((long long)d.rank * d.C + i) * (d.H / 8) + lane;
 #pragma unroll
     for (int u = 0; u < MAXS; ++u)
