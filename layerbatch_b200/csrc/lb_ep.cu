@@ -57,32 +57,36 @@ struct EpPeers {
   uint8_t* p[LB_EP_MAX_RANKS];
 };
 
-// Ranks owning at least one of a token's k experts (bit r): expert e sits in slot
-// slot[e] (identity when slot is null), rank = slot / epr.
-__device__ __forceinline__ unsigned ep_dest_mask(const int32_t* ids, int k, int epr, int P,
-                                                 const int32_t* slot, int* status) {
-  unsigned m = 0;
-  for (int j = 0; j < k; ++j) {
-    int e = ids[j];
-    if (slot && e >= 0 && e < epr * P) e = slot[e];
+// ------------------------------------------------------------------------------ route
+// Destination mask of every token (bit r: rank r owns >= 1 of its k experts), one warp per
+// token: lane j maps id j through the placement table, the warp ORs the ranks.
+__global__ void __launch_bounds__(256) k_ep_mask(const int32_t* __restrict__ ids, int T, int k,
+                                                 int epr, int P, const int32_t* __restrict__ expert_slot,
+                                                 uint8_t* __restrict__ mask, int* status) {
+  pdl_entry();
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  unsigned bit = 0;
+  for (int j = lane; j < k; j += 32) {
+    int e = ids[(long long)t * k + j];
+    if (expert_slot && e >= 0 && e < epr * P) e = expert_slot[e];
     const int r = e >= 0 ? e / epr : -1;
     if (r < 0 || r >= P) {
       report(status, LB_DEV_BAD_INDEX);
       continue;
     }
-    m |= 1u << r;
+    bit |= 1u << r;
   }
-  return m;
+  const unsigned m = __reduce_or_sync(0xffffffffu, bit);
+  if (lane == 0) mask[t] = (uint8_t)m;
 }
 
-// ------------------------------------------------------------------------------ route
-// One block of 1024 threads.  slot[t][r] = rank of token t among the tokens that send a
-// row to rank r (token order), -1 if none; send_count[r] = rows sent to r.
-__global__ void __launch_bounds__(1024) k_ep_route(const int32_t* __restrict__ ids, int T, int k,
-                                                   int epr, int P, int32_t* __restrict__ slot,
-                                                   int* __restrict__ send_count,
-                                                   const int32_t* __restrict__ expert_slot,
-                                                   int* status) {
+// One block of 1024 threads over the masks.  slot[t][r] = rank of token t among the tokens
+// that send a row to rank r (token order), -1 if none; send_count[r] = rows sent to r.
+__global__ void __launch_bounds__(1024) k_ep_route(const uint8_t* __restrict__ mask, int T, int P,
+                                                   int32_t* __restrict__ slot,
+                                                   int* __restrict__ send_count) {
   pdl_entry();
   __shared__ int s_w[32][LB_EP_MAX_RANKS];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -92,7 +96,7 @@ __global__ void __launch_bounds__(1024) k_ep_route(const int32_t* __restrict__ i
 #pragma unroll
   for (int r = 0; r < LB_EP_MAX_RANKS; ++r) cnt[r] = 0;
   for (int t = t0; t < t1; ++t) {
-    const unsigned m = ep_dest_mask(ids + (long long)t * k, k, epr, P, expert_slot, status);
+    const unsigned m = mask[t];
 #pragma unroll
     for (int r = 0; r < LB_EP_MAX_RANKS; ++r) cnt[r] += (m >> r) & 1u;
   }
@@ -128,7 +132,7 @@ __global__ void __launch_bounds__(1024) k_ep_route(const int32_t* __restrict__ i
 #pragma unroll
   for (int r = 0; r < LB_EP_MAX_RANKS; ++r) base[r] = s_w[wid][r] + incl[r] - cnt[r];
   for (int t = t0; t < t1; ++t) {
-    const unsigned m = ep_dest_mask(ids + (long long)t * k, k, epr, P, expert_slot, nullptr);
+    const unsigned m = mask[t];
     for (int r = 0; r < P; ++r) slot[(long long)t * P + r] = ((m >> r) & 1u) ? base[r]++ : -1;
   }
 }
@@ -382,6 +386,7 @@ struct EpWs {
   MoeWs m;
   int32_t* slot;
   int* send_count;
+  uint8_t* mask;      // [C] destination ranks of every token (bit r)
 };
 
 static size_t carve_ep(const LbEpArgs& a, void* base, EpWs& w) {
@@ -394,6 +399,7 @@ static size_t carve_ep(const LbEpArgs& a, void* base, EpWs& w) {
   w.m.wb = c.take<__nv_bfloat16>(C * k);
   w.slot = c.take<int32_t>(C * P);
   w.send_count = c.take<int>(LB_EP_MAX_RANKS);
+  w.mask = c.take<uint8_t>(C);
   carve_core(c, C, P * C, k, H, E / P, a.inter, w.m);
   return c.off + 256;
 }
@@ -518,8 +524,12 @@ int lb_ep_moe_forward(const LbEpArgs* a, void* stream) {
                        static_cast<const __nv_bfloat16*>(a->w_shared_expert_gate), H, w.m.perm_w, st);
       if (rc) return rc;
     }
-    launch_k(k_ep_route, 1, 1024, 0, st, w.m.ids, T, k, epr, P, w.slot, w.send_count,
-             a->expert_slot, w.m.status);
+    if (T > 0) {
+      launch_k(k_ep_mask, (T * 32 + 255) / 256, 256, 0, st, w.m.ids, T, k, epr, P,
+               a->expert_slot, w.mask, w.m.status);
+      if ((rc = launched("k_ep_mask"))) return rc;
+    }
+    launch_k(k_ep_route, 1, 1024, 0, st, w.mask, T, P, w.slot, w.send_count);
     if ((rc = launched("k_ep_route"))) return rc;
     EpDispatch d;
     d.x = x;
