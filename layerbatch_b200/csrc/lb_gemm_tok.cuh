@@ -65,13 +65,16 @@ struct TokSmem {
   static constexpr int W_BYTES = 2 * TOK_FB * 64 * 2;  // two 128 x 64 weight tiles
   static constexpr int X_BYTES = TN * 64 * 2;          // TN x 64 token tile
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
+  // down epilogue: per epilogue warp a 32-token x 32-feature bf16 block (token rows)
+  static constexpr int STG_WARP_BYTES = 32 * 32 * 2;
+  static constexpr int STG_BYTES = 8 * STG_WARP_BYTES;
   static constexpr int BAR_BYTES = 256;
   // TMEM columns per accumulator: TN rounded up to a power of two, so that every
   // accumulator starts on a power-of-two column
   static constexpr int ACC_COLS = TN <= 32 ? 32 : TN <= 64 ? 64 : TN <= 128 ? 128 : 256;
   static constexpr int TMEM_COLS = 2 * ACC_COLS * NBUF;
   static size_t bytes(int num_groups) {
-    return 1024 + (size_t)STAGES * STAGE_BYTES + BAR_BYTES +
+    return 1024 + (size_t)STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES +
            4 * (2 * (size_t)num_groups + 4) + 4 * TOK_MAX_THREADS;
   }
 };
@@ -107,7 +110,8 @@ __global__ void __launch_bounds__(64 + 32 * EPW, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sW = smem;
   uint8_t* sX = smem + STAGES * S::W_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sX + STAGES * S::X_BYTES);
+  uint8_t* sStg = sX + STAGES * S::X_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStg + S::STG_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
@@ -298,14 +302,20 @@ __global__ void __launch_bounds__(64 + 32 * EPW, 1)
           }
         }
       } else {
+        // The warp's 32 features x 32 tokens of a chunk become token rows through its own
+        // 2 KB shared block: 2-byte shared stores (one token per instruction, 64 contiguous
+        // bytes), then per lane 16-byte loads and 16-byte global stores (four lanes per
+        // token's 64 bytes), an eighth of the store instructions of per-feature stores.
+        __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(sStg + (warp - 2) * S::STG_WARP_BYTES);
+        const int f8 = (lane & 3) * 8;   // this lane's 8 features of a token row
 #pragma unroll 1
         for (int a = 0; a < 2; ++a) {
-          const int col = c.fb * p.fb_stride + (a ? (sh ? p.acc1_off_sh : p.acc1_off) : 0) + f_in;
-          const bool col_ok = col < p.out_cols;
+          const int col0 = c.fb * p.fb_stride + (a ? (sh ? p.acc1_off_sh : p.acc1_off) : 0) + quad * 32;
+          const bool col_ok = col0 + f8 + 8 <= p.out_cols;
 #pragma unroll 1
           for (int ch = part; ch < nch; ch += NPART) {
             uint32_t v[32];
-            __syncwarp();
+            __syncwarp();   // the previous chunk's shared reads are done
             tmem_ld32(tb + a * S::ACC_COLS + ch * 32, v);
             tmem_wait_ld();
             const int nj = min(32, nv - ch * 32);
@@ -315,8 +325,15 @@ __global__ void __launch_bounds__(64 + 32 * EPW, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float s = __shfl_sync(0xffffffffu, s_mine, j);
+              stg[j * 32 + lane] = __float2bfloat16_rn(__uint_as_float(v[j]) * s);
+            }
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int j = 8 * i + (lane >> 2);
+              const uint4 val = *reinterpret_cast<const uint4*>(stg + j * 32 + f8);
               if (j < nj && col_ok && r0 + j < p.out_rows)
-                out[(r0 + j) * p.ldo + col] = __float2bfloat16_rn(__uint_as_float(v[j]) * s);
+                *reinterpret_cast<uint4*>(out + (r0 + j) * p.ldo + col0 + f8) = val;
             }
           }
         }

@@ -628,7 +628,7 @@ int moe_core(const MoeCore& c, const MoeWs& w, cudaStream_t st) {
   //    routing weight (shared rows: sigmoid gate): yw[rows, H].  Accumulators 0 / 1 hold
   //    output features fb*256 + [0, 128) / [128, 256).
   if (any_gemm) {
-    constexpr int TN = 128, NBUF = 2, STAGES = 4, EPW = 4;
+    constexpr int TN = 128, NBUF = 2, STAGES = 4, EPW = 8;
     CUtensorMap tX, tW, tWs;
     if ((rc = make_tmap_bf16_2d(&tX, w.act, rows, I, I, TOK_BOX, 64))) return rc;
     if (nl > 0 && (rc = make_tmap_bf16_3d(&tW, c.w_down, nl, H, I, I, (uint64_t)H * I, TOK_FB, 64)))
