@@ -221,25 +221,34 @@ __device__ __forceinline__ int dec_pos_v(int j, int n) { return min(2 * j + 2, 2
 constexpr int DEC_S_COL = 0;
 constexpr int DEC_O_COL = 128;
 
-// Sum of the four token-quarter partials of each dim half of a decode O^T buffer.
-__device__ __forceinline__ void dec_load_o(uint32_t taddr, uint32_t (&o0)[16], uint32_t (&o1)[16]) {
-  uint32_t a[16], b[16], c[16];
-  tmem_ld16(taddr, o0);
-  tmem_ld16(taddr + 16, a);
-  tmem_ld16(taddr + 32, b);
-  tmem_ld16(taddr + 48, c);
+// 32 lanes x 32 bit, N (8 or 16) consecutive TMEM columns per thread.
+template <int N>
+__device__ __forceinline__ void tmem_ldn(uint32_t taddr, uint32_t (&r)[N]) {
+  static_assert(N == 8 || N == 16, "8 or 16 columns");
+  if constexpr (N == 8) tmem_ld8(taddr, r); else tmem_ld16(taddr, r);
+}
+
+// Sum of the four token-quarter partials of each dim half of a decode O^T buffer (the
+// first NH of the 16 head columns of each partial).
+template <int NH>
+__device__ __forceinline__ void dec_load_o(uint32_t taddr, uint32_t (&o0)[NH], uint32_t (&o1)[NH]) {
+  uint32_t a[NH], b[NH], c[NH];
+  tmem_ldn<NH>(taddr, o0);
+  tmem_ldn<NH>(taddr + 16, a);
+  tmem_ldn<NH>(taddr + 32, b);
+  tmem_ldn<NH>(taddr + 48, c);
   tmem_wait_ld();
 #pragma unroll
-  for (int h = 0; h < 16; ++h)
+  for (int h = 0; h < NH; ++h)
     o0[h] = __float_as_uint((__uint_as_float(o0[h]) + __uint_as_float(a[h])) +
                             (__uint_as_float(b[h]) + __uint_as_float(c[h])));
-  tmem_ld16(taddr + 64, o1);
-  tmem_ld16(taddr + 80, a);
-  tmem_ld16(taddr + 96, b);
-  tmem_ld16(taddr + 112, c);
+  tmem_ldn<NH>(taddr + 64, o1);
+  tmem_ldn<NH>(taddr + 80, a);
+  tmem_ldn<NH>(taddr + 96, b);
+  tmem_ldn<NH>(taddr + 112, c);
   tmem_wait_ld();
 #pragma unroll
-  for (int h = 0; h < 16; ++h)
+  for (int h = 0; h < NH; ++h)
     o1[h] = __float_as_uint((__uint_as_float(o1[h]) + __uint_as_float(a[h])) +
                             (__uint_as_float(b[h]) + __uint_as_float(c[h])));
 }
@@ -247,6 +256,166 @@ __device__ __forceinline__ void dec_load_o(uint32_t taddr, uint32_t (&o0)[16], u
 // Byte offset of element (r, c) in a K-major SW128 tile of 64-element (128 B) rows.
 __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
   return (uint32_t)(r * 128 + ((((c >> 3) ^ (r & 7)) & 7) << 4) + ((c & 7) << 1));
+}
+
+// One decode item of the softmax warpgroup (128 threads, thread = token row of each
+// 128-token tile): online softmax over the item's tiles for the NH head columns of the
+// S / O^T accumulators, P^T to shared memory for the PV MMA, and the split's partial O and
+// log2-sum-exp.  NH = 8 serves GQA groups of up to 8 heads with half the registers,
+// TMEM loads and instructions of NH = 16; the MMAs still compute 16 head columns, and
+// columns NH..15 of S and O^T (whatever their contents) are never read, since a column of
+// an MMA result depends only on the same column of its B operand.  Returns false when the
+// item must be abandoned (a wait gave up); `ok` is false then.
+template <int NH>
+__device__ __forceinline__ bool dec_softmax_item(const PodParams& p, PodBars* bars, PodCounters& cnt,
+                                                 uint8_t* smem, uint8_t* kv_base, int nslots,
+                                                 uint32_t tl, int quad, int lane, int row, int tid,
+                                                 int b, int ctx, int kvh, int split, bool& ok) {
+  const int t_begin = split * p.split_tokens;
+  const int t_end = min(ctx, t_begin + p.split_tokens);
+  const int ntiles = (t_end - t_begin + POD_KV - 1) / POD_KV;
+  const uint32_t kvbase = cnt.kv;
+  cnt.kv += 2 * ntiles;
+  float m[NH], l[NH], a0[NH], a1[NH], ap[NH];
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+    a0[h] = 0.f;
+    a1[h] = 0.f;
+    ap[h] = 1.f;
+  }
+  for (int j = 0; j <= ntiles; ++j) {
+    if (j < ntiles) {
+      const int sb = cnt.s & 1;
+      // a failed wait (here or earlier in the item) is agreed on at this tile's
+      // barrier below, where all 128 threads leave the item together
+      if (ok) ok = mbar_wait_warp(&bars->s_full[sb], (cnt.s >> 1) & 1, p.status);
+      tc_fence_after();
+      uint32_t r[NH];
+      {
+        uint32_t r1[NH], r2[NH], r3[NH];
+        tmem_ldn<NH>(tl + DEC_S_COL + sb * 64, r);
+        tmem_ldn<NH>(tl + DEC_S_COL + sb * 64 + 16, r1);
+        tmem_ldn<NH>(tl + DEC_S_COL + sb * 64 + 32, r2);
+        tmem_ldn<NH>(tl + DEC_S_COL + sb * 64 + 48, r3);
+        tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < NH; ++h)
+          r[h] = __float_as_uint((__uint_as_float(r[h]) + __uint_as_float(r1[h])) +
+                                 (__uint_as_float(r2[h]) + __uint_as_float(r3[h])));
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->s_empty[sb]);
+      ++cnt.s;
+      const bool valid = t_begin + j * POD_KV + row < t_end;
+      float s[NH];
+#pragma unroll
+      for (int h = 0; h < NH; ++h)
+        s[h] = (valid && h < p.gqa) ? __uint_as_float(r[h]) * p.scale_log2 : -INFINITY;
+      // tile max per head across the 128 token rows
+      const int par = j & 1;
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        float v = s[h];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) bars->red[par][quad][h] = v;
+      }
+      if (named_bar_any(1, 128, !ok)) { ok = false; break; }
+      const int ob = cnt.o & 1;
+      const uint32_t pt = smem_u32(smem + DEC_SLOTS * POD_TILE + 2 * POD_QD_BYTES +
+                                   ob * POD_PD_BYTES);
+      float al[NH];
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        const float mt = fmaxf(fmaxf(bars->red[par][0][h], bars->red[par][1][h]),
+                               fmaxf(bars->red[par][2][h], bars->red[par][3][h]));
+        const float mn = fmaxf(m[h], mt);
+        al[h] = (m[h] == -INFINITY) ? 1.f : exp2_approx(m[h] - mn);
+        const float e = (mn == -INFINITY) ? 0.f : exp2_approx(s[h] - mn);
+        l[h] = l[h] * al[h] + e;
+        m[h] = mn;
+        // P^T[h][token]: K-major rows of 128 tokens, two 64-token chunks
+        st_shared_u16(pt + (row >> 6) * 2048 + sw128_off(h, row & 63),
+                      __bfloat16_as_ushort(__float2bfloat16_rn(e)));
+      }
+      // tokens past the end of the last tile: zero their V rows (stale cache bytes
+      // could be NaN, and 0 * NaN would poison O^T)
+      if (t_begin + (j + 1) * POD_KV > t_end) {
+        const uint32_t vp = kvbase + dec_pos_v(j, ntiles);
+        if (!mbar_wait_warp(&bars->kv_full[vp % nslots], (vp / nslots) & 1, p.status)) {
+          ok = false;
+        } else if (!valid) {
+          const uint32_t v = smem_u32(kv_base + (vp % nslots) * POD_TILE) + row * 128;
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int u = 0; u < 8; ++u) st_shared_v4(v + c * POD_CHUNK + u * 16, 0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->p_full[ob]);
+      if (j > 0 && ok) {
+        // accumulate O_{j-1} (scale of tile j-1), deferred behind P_j
+        const int pb = ob ^ 1;
+        ok = mbar_wait_warp(&bars->o_full[pb], ((cnt.o - 1) >> 1) & 1, p.status);
+        if (ok) {
+          tc_fence_after();
+          uint32_t o0[NH], o1[NH];
+          dec_load_o<NH>(tl + DEC_O_COL + pb * 128, o0, o1);
+#pragma unroll
+          for (int h = 0; h < NH; ++h) {
+            a0[h] = a0[h] * ap[h] + __uint_as_float(o0[h]);
+            a1[h] = a1[h] * ap[h] + __uint_as_float(o1[h]);
+          }
+          tc_fence_before();
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < NH; ++h) ap[h] = al[h];
+      ++cnt.o;
+    } else {
+      // final O
+      const int pb = (cnt.o - 1) & 1;
+      if (ok) ok = mbar_wait_warp(&bars->o_full[pb], ((cnt.o - 1) >> 1) & 1, p.status);
+      if (ok) {
+        tc_fence_after();
+        uint32_t o0[NH], o1[NH];
+        dec_load_o<NH>(tl + DEC_O_COL + pb * 128, o0, o1);
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          a0[h] = a0[h] * ap[h] + __uint_as_float(o0[h]);
+          a1[h] = a1[h] * ap[h] + __uint_as_float(o1[h]);
+        }
+        tc_fence_before();
+      }
+    }
+  }
+  // row sums across the 128 threads
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    float v = l[h];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) bars->lred[quad][h] = v;
+  }
+  if (named_bar_any(1, 128, !ok)) return false;
+  const long long pbase = ((long long)b * p.max_splits + split) * p.Hq;
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    if (h < p.gqa) {
+      const float ls = bars->lred[0][h] + bars->lred[1][h] + bars->lred[2][h] + bars->lred[3][h];
+      const float inv = ls > 0.f ? 1.f / ls : 0.f;
+      const int hq = kvh * p.gqa + h;
+      float* dst = p.part_o + (pbase + hq) * POD_D;
+      dst[row] = a0[h] * inv;
+      dst[row + 128] = a1[h] * inv;
+      if (tid == h) p.part_lse[pbase + hq] = m[h] + log2f(ls);
+    }
+  }
+  return true;
 }
 
 __global__ void __launch_bounds__(POD_THREADS, 1)
@@ -769,151 +938,10 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           tc_fence_before();
         } else {
           // ---------------------------------------------------- decode item
-          const int kvh = it.y, split = it.z;
-          const int t_begin = split * p.split_tokens;
-          const int t_end = min(ctx, t_begin + p.split_tokens);
-          const int ntiles = (t_end - t_begin + POD_KV - 1) / POD_KV;
-          const uint32_t kvbase = cnt.kv;
-          cnt.kv += 2 * ntiles;
-          float m[16], l[16], a0[16], a1[16], ap[16];
-#pragma unroll
-          for (int h = 0; h < 16; ++h) {
-            m[h] = -INFINITY;
-            l[h] = 0.f;
-            a0[h] = 0.f;
-            a1[h] = 0.f;
-            ap[h] = 1.f;
-          }
-          for (int j = 0; j <= ntiles; ++j) {
-            if (j < ntiles) {
-              const int sb = cnt.s & 1;
-              // a failed wait (here or earlier in the item) is agreed on at this tile's
-              // barrier below, where all 128 threads leave the item together
-              if (ok) ok = mbar_wait_warp(&bars->s_full[sb], (cnt.s >> 1) & 1, p.status);
-              tc_fence_after();
-              uint32_t r[16];
-              {
-                uint32_t r1[16], r2[16], r3[16];
-                tmem_ld16(tl + DEC_S_COL + sb * 64, r);
-                tmem_ld16(tl + DEC_S_COL + sb * 64 + 16, r1);
-                tmem_ld16(tl + DEC_S_COL + sb * 64 + 32, r2);
-                tmem_ld16(tl + DEC_S_COL + sb * 64 + 48, r3);
-                tmem_wait_ld();
-#pragma unroll
-                for (int h = 0; h < 16; ++h)
-                  r[h] = __float_as_uint((__uint_as_float(r[h]) + __uint_as_float(r1[h])) +
-                                         (__uint_as_float(r2[h]) + __uint_as_float(r3[h])));
-              }
-              tc_fence_before();
-              mbar_arrive(&bars->s_empty[sb]);
-              ++cnt.s;
-              const bool valid = t_begin + j * POD_KV + row < t_end;
-              float s[16];
-#pragma unroll
-              for (int h = 0; h < 16; ++h)
-                s[h] = (valid && h < p.gqa) ? __uint_as_float(r[h]) * p.scale_log2 : -INFINITY;
-              // tile max per head across the 128 token rows
-              const int par = j & 1;
-#pragma unroll
-              for (int h = 0; h < 16; ++h) {
-                float v = s[h];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-                if (lane == 0) bars->red[par][quad][h] = v;
-              }
-              if (named_bar_any(1, 128, !ok)) { ok = false; break; }
-              const int ob = cnt.o & 1;
-              const uint32_t pt = smem_u32(smem + DEC_SLOTS * POD_TILE + 2 * POD_QD_BYTES +
-                                           ob * POD_PD_BYTES);
-              float al[16];
-#pragma unroll
-              for (int h = 0; h < 16; ++h) {
-                const float mt = fmaxf(fmaxf(bars->red[par][0][h], bars->red[par][1][h]),
-                                       fmaxf(bars->red[par][2][h], bars->red[par][3][h]));
-                const float mn = fmaxf(m[h], mt);
-                al[h] = (m[h] == -INFINITY) ? 1.f : exp2_approx(m[h] - mn);
-                const float e = (mn == -INFINITY) ? 0.f : exp2_approx(s[h] - mn);
-                l[h] = l[h] * al[h] + e;
-                m[h] = mn;
-                // P^T[h][token]: K-major rows of 128 tokens, two 64-token chunks
-                st_shared_u16(pt + (row >> 6) * 2048 + sw128_off(h, row & 63),
-                              __bfloat16_as_ushort(__float2bfloat16_rn(e)));
-              }
-              // tokens past the end of the last tile: zero their V rows (stale cache bytes
-              // could be NaN, and 0 * NaN would poison O^T)
-              if (t_begin + (j + 1) * POD_KV > t_end) {
-                const uint32_t vp = kvbase + dec_pos_v(j, ntiles);
-                if (!mbar_wait_warp(&bars->kv_full[vp % nslots], (vp / nslots) & 1, p.status)) {
-                  ok = false;
-                } else if (!valid) {
-                  const uint32_t v = smem_u32(kv_base + (vp % nslots) * POD_TILE) + row * 128;
-#pragma unroll
-                  for (int c = 0; c < 4; ++c)
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) st_shared_v4(v + c * POD_CHUNK + u * 16, 0, 0, 0, 0);
-                }
-              }
-              fence_proxy_async_smem();
-              tc_fence_before();
-              mbar_arrive(&bars->p_full[ob]);
-              if (j > 0 && ok) {
-                // accumulate O_{j-1} (scale of tile j-1), deferred behind P_j
-                const int pb = ob ^ 1;
-                ok = mbar_wait_warp(&bars->o_full[pb], ((cnt.o - 1) >> 1) & 1, p.status);
-                if (ok) {
-                  tc_fence_after();
-                  uint32_t o0[16], o1[16];
-                  dec_load_o(tl + DEC_O_COL + pb * 128, o0, o1);
-#pragma unroll
-                  for (int h = 0; h < 16; ++h) {
-                    a0[h] = a0[h] * ap[h] + __uint_as_float(o0[h]);
-                    a1[h] = a1[h] * ap[h] + __uint_as_float(o1[h]);
-                  }
-                  tc_fence_before();
-                }
-              }
-#pragma unroll
-              for (int h = 0; h < 16; ++h) ap[h] = al[h];
-              ++cnt.o;
-            } else {
-              // final O
-              const int pb = (cnt.o - 1) & 1;
-              if (ok) ok = mbar_wait_warp(&bars->o_full[pb], ((cnt.o - 1) >> 1) & 1, p.status);
-              if (ok) {
-                tc_fence_after();
-                uint32_t o0[16], o1[16];
-                dec_load_o(tl + DEC_O_COL + pb * 128, o0, o1);
-#pragma unroll
-                for (int h = 0; h < 16; ++h) {
-                  a0[h] = a0[h] * ap[h] + __uint_as_float(o0[h]);
-                  a1[h] = a1[h] * ap[h] + __uint_as_float(o1[h]);
-                }
-                tc_fence_before();
-              }
-            }
-          }
-          // row sums across the 128 threads
-#pragma unroll
-          for (int h = 0; h < 16; ++h) {
-            float v = l[h];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) bars->lred[quad][h] = v;
-          }
-          if (named_bar_any(1, 128, !ok)) { *abortp = 1; break; }
-          const long long pbase = ((long long)b * p.max_splits + split) * p.Hq;
-#pragma unroll
-          for (int h = 0; h < 16; ++h) {
-            if (h < p.gqa) {
-              const float ls = bars->lred[0][h] + bars->lred[1][h] + bars->lred[2][h] + bars->lred[3][h];
-              const float inv = ls > 0.f ? 1.f / ls : 0.f;
-              const int hq = kvh * p.gqa + h;
-              float* dst = p.part_o + (pbase + hq) * POD_D;
-              dst[row] = a0[h] * inv;
-              dst[row + 128] = a1[h] * inv;
-              if (tid == h) p.part_lse[pbase + hq] = m[h] + log2f(ls);
-            }
-          }
+          const bool fine = p.gqa <= 8
+              ? dec_softmax_item<8>(p, bars, cnt, smem, kv_base, nslots, tl, quad, lane, row, tid, b, ctx, it.y, it.z, ok)
+              : dec_softmax_item<16>(p, bars, cnt, smem, kv_base, nslots, tl, quad, lane, row, tid, b, ctx, it.y, it.z, ok);
+          if (!fine) { *abortp = 1; break; }
         }
         // item done: release its descriptor / Q slot (all softmax threads are past it)
         named_bar_sync(3, nthr);
