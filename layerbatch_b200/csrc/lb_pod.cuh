@@ -628,6 +628,76 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
           const uint32_t qaddr = prefill ? smem_u32(smem + PF_Q_OFF)
                                          : smem_u32(smem + DEC_SLOTS * POD_TILE + islot * POD_QD_BYTES);
           bool ok = true;
+          if (prefill) {
+            // S and PV MMAs are issued each as soon as its own inputs are ready (polled, not
+            // waited on in a fixed order): S_{j+2} needs only the softmax to have read S_j
+            // (and K_{j+2}), PV_j needs P_j (and V_j).  A fixed S, PV, S, PV order would hold
+            // the next scores behind the softmax -> PV hand-off of an earlier tile.  Bounded:
+            // the spin limit counts from the last MMA issued.
+            int ns = 0, npv = 0;
+            unsigned long long t_last = clock64();
+            while (npv < ntiles) {
+              bool moved = false;
+              if (ns < ntiles) {
+                const uint32_t kp = base + ns;
+                const int ks = kp % PF_KSLOTS;
+                const int sb = cnt.s & 1;
+                if (mbar_try_wait(&bars->s_empty[sb], ((cnt.s >> 1) & 1) ^ 1) &&
+                    mbar_try_wait(&bars->kv_full[ks], (kp / PF_KSLOTS) & 1)) {
+                  tc_fence_after();
+                  const uint32_t kaddr = smem_u32(smem + PF_K_OFF + ks * PF_TILE);
+                  const uint32_t d = tmem + sb * PF_KV;
+#pragma unroll
+                  for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                      umma_bf16(d, umma_desc_sw128(qaddr + c * POD_CHUNK + kk * 32, 16, 1024),
+                                umma_desc_sw128(kaddr + c * PF_CHUNK + kk * 32, 16, 1024), idesc_s,
+                                (c | kk) != 0);
+                  umma_commit(&bars->s_full[sb]);
+                  umma_commit(&bars->kv_empty[ks]);
+                  if (ns == ntiles - 1) umma_commit(&bars->q_empty);
+                  ++cnt.s;
+                  ++ns;
+                  moved = true;
+                }
+              }
+              if (npv < ns) {
+                const uint32_t vp = vbase + npv;
+                const int vs = PF_KSLOTS + (int)(vp % PF_VSLOTS);
+                const int ob = cnt.o & 1;
+                if (mbar_try_wait(&bars->p_full[ob], (cnt.o >> 1) & 1) &&
+                    mbar_try_wait(&bars->kv_full[vs], (vp / PF_VSLOTS) & 1)) {
+                  tc_fence_after();
+                  const uint32_t vaddr = smem_u32(smem + PF_V_OFF + (vp % PF_VSLOTS) * PF_TILE);
+                  // A = P from TMEM: 16 keys (8 columns) per MMA
+                  const uint32_t pcol = tmem + PF_P_COL + ob * (PF_KV / 2);
+                  const uint32_t d = tmem + 256;
+#pragma unroll
+                  for (int kk = 0; kk < PF_KV / 16; ++kk)
+                    umma_bf16_ts(d, pcol + kk * 8,
+                                 umma_desc_sw128(vaddr + kk * 2048, PF_CHUNK, 1024), idesc_o,
+                                 (npv | kk) != 0);
+                  umma_commit(&bars->o_full[ob]);
+                  umma_commit(&bars->kv_empty[vs]);
+                  ++cnt.o;
+                  ++npv;
+                  moved = true;
+                }
+              }
+              if (moved) {
+                t_last = clock64();
+              } else if (*abortp || clock64() - t_last > LB_SPIN_LIMIT_CYCLES) {
+                if (!*abortp) report(p.status, LB_DEV_TIMEOUT);
+                ok = false;
+                break;
+              }
+            }
+            cnt.kv = base + ntiles;
+            cnt.kv2 = vbase + ntiles;
+            if (!ok) { *abortp = 1; break; }
+            continue;
+          }
           for (int j = 0; j <= ntiles && ok; ++j) {
             if (j < ntiles) {
               // ---- S_j  (prefill: K ring; decode: unified ring)
