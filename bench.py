@@ -458,7 +458,7 @@ def run_ours(args, rank, world, device):
                     inp.get("slots", slots), attn.k_cache, attn.v_cache, bt, cl, cu, attn.w_o,
                     attn.scale, out=oa, max_q_len=max_q, work_hint=hint, events=ev.get("pod"),
                     qkv=qkv_buf, q=q_buf, ws_tag=pod_tag, tp=tp_ex,
-                    stage_events=ev.get("stages"))
+                    stage_events=ev.get("stages"), prologue=args.prologue)
             else:
                 if "attn0" in ev:
                     ev["attn0"].record()
@@ -556,7 +556,10 @@ def run_ours(args, rank, world, device):
         flops, byts = attn_work(attn)
         res["attn"] = {"ms": t_attn * 1e3, "flops": flops, "bytes": byts,
                        "gbs": byts / t_attn / 1e9, "tflops": flops / t_attn / 1e12}
-        if layer:
+        if layer and args.prologue == "gemm":
+            phases["qkv_gemm_prologue"] = mean_ms(lambda e: e["attn0"], lambda e: e["stages"][1])
+            phases["plan"] = mean_ms(lambda e: e["stages"][1], lambda e: e["pod"][0])
+        elif layer:
             phases["qkv_gemm"] = mean_ms(lambda e: e["attn0"], lambda e: e["stages"][0])
             phases["prologue"] = mean_ms(lambda e: e["stages"][0], lambda e: e["stages"][1])
             phases["plan"] = mean_ms(lambda e: e["stages"][1], lambda e: e["pod"][0])
@@ -569,7 +572,11 @@ def run_ours(args, rank, world, device):
         phases["merge"] = mean_ms(lambda e: e["pod"][1], lambda e: e["pod"][2])
         phases["oproj"] = mean_ms(lambda e: e["pod"][2], lambda e: e["pod"][3])
         phases["attention_layer"] = mean_ms(lambda e: e["attn0"], lambda e: e["attn1"])
-        if layer:
+        if layer and args.prologue == "gemm":
+            g, pr = layer_proj_work(attn.num_tokens, Hq=Hq_l, Hkv=Hkv_l)
+            res["proj"] = {"gemm_tflops": g["flops"] / phases["qkv_gemm_prologue"] / 1e9,
+                           "prologue": "in the q/k/v GEMM's epilogue (lb_qkv_prologue_gemm)"}
+        elif layer:
             g, pr = layer_proj_work(attn.num_tokens, Hq=Hq_l, Hkv=Hkv_l)
             res["proj"] = {"gemm_gbs": g["bytes"] / phases["qkv_gemm"] / 1e6,
                            "gemm_tflops": g["flops"] / phases["qkv_gemm"] / 1e9,
@@ -725,6 +732,9 @@ def main():
     ap.add_argument("--config", choices=list(CONFIGS), default="c4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--prologue", choices=["gemm", "kernel", "pod"], default="gemm",
+                    help="where the c4 layer's attention prologue runs: in the q/k/v GEMM's "
+                         "epilogue (default), its own kernel, or inside the attention kernel")
     ap.add_argument("--no-graph", action="store_true",
                     help="time eager launches instead of replaying a captured step")
     ap.add_argument("--ref-budget-s", type=float, default=240.0,

@@ -15,6 +15,8 @@
  *   lb_moe_permute          <- expert dispatch of _forward_sparse nanovllm/models/qwen3_5.py:821-831
  *   lb_gemm_bf16            <- F.linear / RowParallelLinear.forward nanovllm/layers/linear.py:149-159
  *   lb_store_kvcache        <- store_kvcache                    nanovllm/layers/attention.py:71-80
+ *   lb_attn_prologue        <- q/k norms, rotary, store_kvcache nanovllm/models/qwen3_5.py:707-736
+ *   lb_qkv_prologue_gemm    <- q/k/v projections + the above   nanovllm/models/qwen3_5.py:705-736
  *   lb_pod_attn_oproj       <- pod_fused_attn_gemm / pod_attn_only nanovllm/layers/pod_kernels.py:237-354
  *                              + Attention.forward decode/prefill nanovllm/layers/attention.py:99-226
  *                              + output gate and o_proj         nanovllm/models/qwen3_5.py:739-746
@@ -265,6 +267,23 @@ typedef struct LbPrologueArgs {
 } LbPrologueArgs;
 
 int lb_attn_prologue(const LbPrologueArgs* args, void* stream);
+
+/* The q/k/v projections with the prologue in the GEMM's epilogue (the projections of
+ * Qwen3_5FullAttention.forward, nanovllm/models/qwen3_5.py:705-713, then the prologue
+ * above): one GEMM x[N, K] . w_qkv^T with w_qkv = [q_proj.weight (per head: query D rows,
+ * gate D rows); k_proj.weight; v_proj.weight], [(2*Hq + 2*Hkv)*D, K].  Each 256-column
+ * tile of the product is one head row: query rows are normalised, rotated and written to
+ * q_out, key rows normalised, rotated and stored into k_cache at slot_mapping, value rows
+ * stored into v_cache, and only the gate rows are written to qkv_out ([N, ldo], at the
+ * columns the plain GEMM would give them, where lb_pod_attn_oproj reads the gate).  The
+ * results are bit-identical to lb_gemm_bf16 followed by lb_attn_prologue.  args supplies
+ * N (num_tokens), the heads, eps, the norm weights, positions, slots, caches, q_out and
+ * status; its q_in / k_in / v_in are not used.  Requires head_dim 256 and rotary_dim 64
+ * (else LB_ERR_UNSUPPORTED), K a multiple of 64, 16-byte aligned rows.  workspace: at
+ * least lb_gemm_workspace_size() bytes (status word). */
+int lb_qkv_prologue_gemm(const void* x, int64_t ldx, const void* w_qkv, int64_t ldw,
+                         void* qkv_out, int64_t ldo, int64_t K, const LbPrologueArgs* args,
+                         void* workspace, void* stream);
 
 /* ---------------------------------------------------------------- POD attention + o_proj
  * One batch of sequences, prefill chunks and decode steps mixed in any order.

@@ -25,7 +25,8 @@ EXPORTS = [
     "lb_moe_workspace_size",
     "lb_moe_forward", "lb_ep_buffer_size", "lb_ep_buffer_alloc", "lb_ep_buffer_open",
     "lb_ep_buffer_close", "lb_ep_buffer_free", "lb_ep_workspace_size", "lb_ep_moe_forward",
-    "lb_store_kvcache", "lb_attn_prologue", "lb_tp_buffer_size", "lb_pod_workspace_size",
+    "lb_store_kvcache", "lb_attn_prologue", "lb_qkv_prologue_gemm", "lb_tp_buffer_size",
+    "lb_pod_workspace_size",
     "lb_pod_attn_oproj",
 ]
 
@@ -129,6 +130,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.lb_tp_buffer_size.restype = C.c_size_t
     L.lb_tp_buffer_size.argtypes = [i64, i64, i64]
     L.lb_attn_prologue.argtypes = [C.POINTER(LbPrologueArgs), vp]
+    L.lb_qkv_prologue_gemm.argtypes = [vp, i64, vp, i64, vp, i64, i64, C.POINTER(LbPrologueArgs),
+                                       vp, vp]
     L.lb_store_kvcache.argtypes = [vp, i64, vp, i64, vp, vp, vp, i64, i64, i64, vp]
     L.lb_pod_workspace_size.argtypes = [C.POINTER(LbPodArgs), C.POINTER(C.c_size_t)]
     L.lb_pod_attn_oproj.argtypes = [C.POINTER(LbPodArgs), vp]

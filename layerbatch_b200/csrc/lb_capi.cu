@@ -243,6 +243,53 @@ int lb_read_device_status(const void* workspace, int clear, int* status_out) {
 
 size_t lb_gemm_workspace_size(void) { return 256; }
 
+int lb_qkv_prologue_gemm(const void* x, int64_t ldx, const void* w_qkv, int64_t ldw,
+                         void* qkv_out, int64_t ldo, int64_t K, const LbPrologueArgs* a,
+                         void* workspace, void* stream) {
+  LB_REQUIRE(a != nullptr && x && w_qkv && qkv_out && workspace, "lb_qkv_prologue_gemm: null pointer");
+  if (a->head_dim != PRO_D || a->rotary_dim != PRO_GEMM_ROT)
+    return fail(LB_ERR_UNSUPPORTED, "lb_qkv_prologue_gemm: needs head_dim 256 and rotary_dim 64 "
+                "(got %lld, %lld): use lb_gemm_bf16 + lb_attn_prologue",
+                (long long)a->head_dim, (long long)a->rotary_dim);
+  const int64_t M = a->num_tokens, Hq = a->num_q_heads, Hkv = a->num_kv_heads;
+  LB_REQUIRE(M >= 0 && M <= (1ll << 30) && Hq > 0 && Hkv > 0 && Hq <= 4096 && Hkv <= 4096,
+             "lb_qkv_prologue_gemm: bad token / head counts");
+  const int64_t N = (2 * Hq + 2 * Hkv) * PRO_D;
+  LB_REQUIRE(K > 0 && K % 64 == 0, "lb_qkv_prologue_gemm: K=%lld must be a multiple of 64", (long long)K);
+  LB_REQUIRE(ldx % 8 == 0 && ldw % 8 == 0 && ldo % 8 == 0 && ldx >= K && ldw >= K && ldo >= N,
+             "lb_qkv_prologue_gemm: leading dimensions must cover the rows and be multiples of 8");
+  LB_REQUIRE(a->q_norm_w && a->k_norm_w && a->positions && a->slot_mapping && a->cos_sin_cache &&
+                 a->k_cache && a->v_cache && a->q_out,
+             "lb_qkv_prologue_gemm: null pointer in args");
+  LB_REQUIRE(aligned16(x) && aligned16(w_qkv) && aligned16(qkv_out) && aligned16(a->q_out) &&
+                 aligned16(a->k_cache) && aligned16(a->v_cache) && aligned16(a->q_norm_w) &&
+                 aligned16(a->k_norm_w) && aligned16(a->cos_sin_cache),
+             "lb_qkv_prologue_gemm: unaligned pointer");
+  LB_REQUIRE(a->q_out_stride_tok % 8 == 0 && a->q_out_stride_head % 8 == 0 &&
+                 a->q_out_stride_head >= PRO_D,
+             "lb_qkv_prologue_gemm: q_out strides must be multiples of 8 elements");
+  LB_REQUIRE(a->max_position > 0 && a->num_slots >= 0, "lb_qkv_prologue_gemm: bad cache sizes");
+  if (M == 0) return LB_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUtensorMap tA, tB;
+  int rc = make_tmap_bf16_2d(&tA, x, M, K, ldx, GEMM_BM, 64);
+  if (rc) return rc;
+  rc = make_tmap_bf16_3d(&tB, w_qkv, 1, N, K, ldw, ldw * N, PRO_D, 64);
+  if (rc) return rc;
+  GemmArgs g = gemm_args_default(static_cast<int*>(workspace));
+  g.m = (int)M;
+  g.n_tiles = (int)(N / PRO_D);
+  g.k_blocks = (int)(K / 64);
+  g.out = qkv_out;
+  g.ldo = ldo;
+  g.out_rows = (int)M;
+  g.out_cols = (int)N;
+  g.pro = *a;
+  const long long tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (long long)g.n_tiles;
+  const int grid = (int)std::min<long long>(tiles, num_sms());
+  return launch_gemm<PRO_D, 4, EPI_QKV>(tA, tB, g, grid, st);
+}
+
 int lb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
                  int64_t M, int64_t N, int64_t K, int c_is_fp32, int splits, void* workspace,
                  void* stream) {

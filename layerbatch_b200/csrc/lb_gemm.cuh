@@ -14,6 +14,7 @@
 #include <cuda.h>
 #include "lb_common.cuh"
 #include "lb_peer.h"
+#include "lb_prologue.cuh"
 
 namespace lb {
 
@@ -28,6 +29,8 @@ enum EpiKind : int {
                        // the last CTA publishes the call's epoch to every rank
   EPI_F32_SPLIT = 6,   // split-K partial ks -> its own fp32 slice out32[ks] (plain stores;
                        // k_splitk_reduce sums the slices in split order: deterministic)
+  EPI_QKV = 7,         // q/k/v projection with the attention prologue (qkv_prologue_tile;
+                       // BN = 256 = one head row per tile)
 };
 
 struct GemmArgs {
@@ -41,6 +44,7 @@ struct GemmArgs {
   int out_rows;            // rows of `out` (bounds check)
   int out_cols;            // columns of `out` (bounds check)
   TpPeers tp;              // EPI_F32_PEER
+  LbPrologueArgs pro;      // EPI_QKV
 };
 
 constexpr int EPI_STAGE_LD = 36;  // floats per row of the peer-store transpose buffer
@@ -201,8 +205,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int out_row = c.m * GEMM_BM + row_in_tile;
       const bool row_ok = row_in_tile < valid_rows && out_row < p.out_rows;
 
+      if constexpr (EPI == EPI_QKV) {
+        static_assert(EPI != EPI_QKV || BN == PRO_D, "EPI_QKV: one 256-dim head row per tile");
+        qkv_prologue_tile(p.pro, c.n, tbase, row_ok, out_row, p.out, p.ldo, p.status);
+      }
 #pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
+      for (int ch = 0; ch < (EPI == EPI_QKV ? 0 : BN / 32); ++ch) {
         uint32_t v[32];
         __syncwarp();
         tmem_ld32(tbase + ch * 32, v);

@@ -47,14 +47,15 @@ constexpr int POD_MISC = 2048;
 constexpr int POD_SMEM = 1024 + POD_DATA + POD_MISC;
 constexpr int POD_TMEM_COLS = 512;
 constexpr int DEC_SLOTS = 3;
-// prefill: 64-key K/V tiles (32 KB) in separate K and V rings, K three tiles deep (the
-// next S MMA waits on K), V two; P goes to TMEM, not shared memory
+// prefill: 64-key K/V tiles (32 KB) in separate K and V rings, K two tiles deep, V three
+// (with the MMAs issued as their inputs arrive, the scores run ahead and PV_j, which also
+// waits for the softmax, holds its V slot longest); P goes to TMEM, not shared memory
 constexpr int PF_KV = 64;
 constexpr int PF_CHUNK = PF_KV * 128;            // 8 KB: one 64-dim chunk of a prefill tile
 constexpr int PF_TILE = 4 * PF_CHUNK;            // 32 KB
-constexpr int PF_KSLOTS = 3;                     // K ring: barriers kv_*[0, 3)
-constexpr int PF_VSLOTS = 2;                     // V ring: barriers kv_*[3, 5)
-// prefill shared-memory map: [K ring 3 x 32 KB][V ring 2 x 32 KB][Q 64 KB]
+constexpr int PF_KSLOTS = 2;                     // K ring: barriers kv_*[0, 2)
+constexpr int PF_VSLOTS = 3;                     // V ring: barriers kv_*[2, 5)
+// prefill shared-memory map: [K ring 2 x 32 KB][V ring 3 x 32 KB][Q 64 KB]
 constexpr int PF_K_OFF = 0;
 constexpr int PF_V_OFF = PF_KSLOTS * PF_TILE;
 constexpr int PF_Q_OFF = PF_V_OFF + PF_VSLOTS * PF_TILE;

@@ -299,4 +299,156 @@ __device__ __forceinline__ void prologue_rows_direct(const LbPrologueArgs& a, in
   }
 }
 
+// ------------------------------------------------------------------------------ in the GEMM
+// The prologue as the epilogue of the q/k/v projection GEMM (EPI_QKV): the GEMM's
+// 256-column output tile `ntile` of the stacked weight [q_proj (query | gate per head);
+// k_proj; v_proj] is one head row of kind query, gate, key or value for each of the
+// tile's 128 tokens; the epilogue thread of a row holds all 256 of its accumulators in
+// TMEM.  Query and key rows: rounded to bf16 (the projection's output), (1+w) RMSNorm with
+// the sum of squares taken in exactly the order of prologue_row_math (8-dim partial sums,
+// then the 32 partials pairwise at distances 16, 8, 4, 2, 1, as the warp's butterfly
+// does), the same rounding points, RoPE on the first 64 dims; then the query row goes to
+// q_out and the key row into the cache.  Value rows go into the cache as bf16, gate rows
+// into the GEMM's own output (where the attention kernel reads the gate).  The stores are
+// those of the separate prologue kernel, bit for bit.  rotary_dim must be 64 (the callers
+// check it).  All lanes of the warp call this (TMEM loads are warp-collective); `row_ok`
+// false: no loads of the token's metadata, no stores.
+constexpr int PRO_GEMM_ROT = 64;
+
+__device__ __forceinline__ void pro_ld_row32(uint32_t taddr, float (&x)[32]) {
+  uint32_t v[32];
+  __syncwarp();
+  tmem_ld32(taddr, v);
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) x[i] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[i])));
+}
+
+__device__ __forceinline__ void pro_store32(__nv_bfloat16* dst, const float (&y)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    d[q] = make_uint4(pack_bf16x2(y[8 * q], y[8 * q + 1]), pack_bf16x2(y[8 * q + 2], y[8 * q + 3]),
+                      pack_bf16x2(y[8 * q + 4], y[8 * q + 5]), pack_bf16x2(y[8 * q + 6], y[8 * q + 7]));
+}
+
+// y = bf16(x * rstd * (1 + w)) for 32 dims starting at d0 of a norm weight row
+__device__ __forceinline__ void pro_norm32(float (&x)[32], float rstd, const __nv_bfloat16* nw, int d0) {
+  const uint4* wp = reinterpret_cast<const uint4*>(nw + d0);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 w4 = wp[q];
+    const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float w0 = __fadd_rn(1.0f, bf16_lo(wv[i]));
+      const float w1 = __fadd_rn(1.0f, bf16_hi(wv[i]));
+      const int e = 8 * q + 2 * i;
+      x[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], rstd), w0)));
+      x[e + 1] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e + 1], rstd), w1)));
+    }
+  }
+}
+
+__device__ __forceinline__ void qkv_prologue_tile(const LbPrologueArgs& a, int ntile, uint32_t tbase,
+                                                  bool row_ok, long long t, void* qkv_out,
+                                                  long long ldo, int* gemm_status) {
+  int* status = a.status ? a.status : gemm_status;
+  const int Hq = (int)a.num_q_heads, Hkv = (int)a.num_kv_heads;
+  int kind, hh;  // 0 query, 1 gate, 2 key, 3 value
+  if (ntile < 2 * Hq) {
+    hh = ntile >> 1;
+    kind = (ntile & 1) ? 1 : 0;
+  } else if (ntile < 2 * Hq + Hkv) {
+    hh = ntile - 2 * Hq;
+    kind = 2;
+  } else {
+    hh = ntile - 2 * Hq - Hkv;
+    kind = 3;
+  }
+  __nv_bfloat16* dst = nullptr;
+  long long pos = 0;
+  if (row_ok) {
+    if (kind == 1) {
+      dst = static_cast<__nv_bfloat16*>(qkv_out) + t * ldo + (long long)ntile * PRO_D;
+    } else if (kind == 0) {
+      dst = static_cast<__nv_bfloat16*>(a.q_out) + t * a.q_out_stride_tok + (long long)hh * a.q_out_stride_head;
+    } else {
+      const long long s = (long long)a.slot_mapping[t];
+      if (s >= a.num_slots) report(status, LB_DEV_BAD_INDEX);
+      if (s >= 0 && s < a.num_slots)
+        dst = static_cast<__nv_bfloat16*>(kind == 2 ? a.k_cache : a.v_cache) +
+              (s * Hkv + hh) * (long long)PRO_D;
+    }
+    if (kind == 0 || kind == 2) {
+      pos = a.positions[t];
+      if (pos < 0 || pos >= a.max_position) {
+        if (kind == 0 && hh == 0) report(status, LB_DEV_BAD_INDEX);
+        pos = pos < 0 ? 0 : a.max_position - 1;
+      }
+    }
+  }
+  if (kind == 1 || kind == 3) {
+#pragma unroll 1
+    for (int ch = 0; ch < PRO_D / 32; ++ch) {
+      float x[32];
+      pro_ld_row32(tbase + ch * 32, x);
+      if (dst) pro_store32(dst + ch * 32, x);
+    }
+    return;
+  }
+  // sum of squares: 32 partials of 8 dims, then the butterfly's pairing
+  float part[32];
+#pragma unroll
+  for (int ch = 0; ch < PRO_D / 32; ++ch) {
+    float x[32];
+    pro_ld_row32(tbase + ch * 32, x);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(x[8 * g + i], x[8 * g + i]));
+      part[4 * ch + g] = ss;
+    }
+  }
+#pragma unroll
+  for (int w = 16; w > 0; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) part[i] = __fadd_rn(part[i], part[i + w]);
+  const float rstd = rsqrtf(__fadd_rn(part[0] / (float)PRO_D, a.eps));
+  const __nv_bfloat16* nw = static_cast<const __nv_bfloat16*>(kind == 0 ? a.q_norm_w : a.k_norm_w);
+  {
+    // dims [0, 64): norm, then RoPE pairs (i, i + 32)
+    float x0[32], x1[32];
+    pro_ld_row32(tbase, x0);
+    pro_ld_row32(tbase + 32, x1);
+    pro_norm32(x0, rstd, nw, 0);
+    pro_norm32(x1, rstd, nw, 32);
+    const float4* cs = reinterpret_cast<const float4*>(a.cos_sin_cache + pos * PRO_GEMM_ROT);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 c4 = cs[q], s4 = cs[8 + q];
+      const float c[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = 4 * q + u;
+        const float y1 = x0[i], y2 = x1[i];
+        x0[i] = __fsub_rn(__fmul_rn(y1, c[u]), __fmul_rn(y2, sn[u]));
+        x1[i] = __fadd_rn(__fmul_rn(y2, c[u]), __fmul_rn(y1, sn[u]));
+      }
+    }
+    if (dst) {
+      pro_store32(dst, x0);
+      pro_store32(dst + 32, x1);
+    }
+  }
+#pragma unroll 1
+  for (int ch = 2; ch < PRO_D / 32; ++ch) {
+    float x[32];
+    pro_ld_row32(tbase + ch * 32, x);
+    pro_norm32(x, rstd, nw, ch * 32);
+    if (dst) pro_store32(dst + ch * 32, x);
+  }
+}
+
 }  // namespace lb

@@ -230,10 +230,9 @@ def gated_attention_layer(x, w_qkv, num_heads, num_kv_heads, q_norm_w, k_norm_w,
                           block_tables, context_lens, cu_seqlens_q, w_o, scale, out=None,
                           max_q_len=None, work_hint=None, events=None, qkv=None, q=None,
                           attn_out=None, ws_tag="pod", tp=None, tp_phases=0,
-                          stage_events=None, fuse_prologue=False):
+                          stage_events=None, fuse_prologue=False, prologue="gemm"):
     """The whole gated full-attention layer from its hidden states
-    (``Qwen3_5FullAttention.forward``, nanovllm/models/qwen3_5.py:705-746), three library
-    calls:
+    (``Qwen3_5FullAttention.forward``, nanovllm/models/qwen3_5.py:705-746):
 
     1. one GEMM for the three projections: ``qkv = x @ w_qkv.T`` with ``w_qkv`` =
        ``[q_proj.weight; k_proj.weight; v_proj.weight]`` (``[Hq*2D + 2*Hkv*D, H]``);
@@ -242,11 +241,13 @@ def gated_attention_layer(x, w_qkv, num_heads, num_kv_heads, q_norm_w, k_norm_w,
     3. ``lb_pod_attn_oproj``: attention over the cache for every sequence of the batch,
        ``* sigmoid(gate)`` (the gate read in place from q_proj's output) and o_proj.
 
-    Step 2 is its own ``lb_attn_prologue`` launch; with ``fuse_prologue`` it runs inside
-    the attention kernel of step 3 instead (``LbPodArgs.prologue``: the kernel's CTAs first
-    do the prologue rows, each attention item waits for its own sequence's rows).  Both
-    give the same bits; on B200 the separate launch is the faster one at the benchmark
-    sizes (its many small blocks hide the row latency better than the persistent CTAs).
+    Where step 2 runs (``prologue``), all giving the same bits:
+    ``"gemm"`` (default; head_dim 256 with rotary_dim 64, else "kernel"): in the epilogue
+    of the projection GEMM (``lb_qkv_prologue_gemm``), so only the gate columns of
+    ``qkv`` are written; ``"kernel"``: its own ``lb_attn_prologue`` launch after the
+    GEMM; ``"pod"`` (or ``fuse_prologue=True``): inside the attention kernel of step 3
+    (``LbPodArgs.prologue``: the kernel's CTAs first do the prologue rows, each attention
+    item waits for its own sequence's rows).
 
     ``qkv`` ``[N, Hq*2D + 2*Hkv*D]`` and ``q`` ``[N, Hq, D]`` may be given as preallocated
     buffers (CUDA-graph capture); ``attn_out`` ``[N, Hq*D]`` optionally receives the
@@ -260,9 +261,17 @@ def gated_attention_layer(x, w_qkv, num_heads, num_kv_heads, q_norm_w, k_norm_w,
     if w_qkv.shape[0] != Hq * 2 * D + 2 * Hkv * D:
         raise ValueError("w_qkv must stack q_proj [Hq*2D], k_proj [Hkv*D] and v_proj [Hkv*D] rows")
     stage_events = list(stage_events or []) + [None, None]
-    qkv = gemm(x, w_qkv, out=qkv)
-    if stage_events[0] is not None:
-        stage_events[0].record()
+    if fuse_prologue:
+        prologue = "pod"
+    if prologue not in ("gemm", "kernel", "pod"):
+        raise ValueError("prologue must be 'gemm', 'kernel' or 'pod'")
+    rot = cos_sin_cache.reshape(cos_sin_cache.shape[0], -1).shape[1]
+    if prologue == "gemm" and (D != 256 or rot != 64):
+        prologue = "kernel"
+    _bf16_2d(x, "x")
+    _bf16_2d(w_qkv, "w_qkv")
+    if qkv is None:
+        qkv = torch.empty(N, w_qkv.shape[0], dtype=torch.bfloat16, device=x.device)
     q3 = qkv[:, :Hq * 2 * D].view(N, Hq, 2 * D)
     k_in = qkv[:, Hq * 2 * D:Hq * 2 * D + Hkv * D].view(N, Hkv, D)
     v_in = qkv[:, Hq * 2 * D + Hkv * D:].view(N, Hkv, D)
@@ -270,14 +279,31 @@ def gated_attention_layer(x, w_qkv, num_heads, num_kv_heads, q_norm_w, k_norm_w,
     if q is None:
         q = torch.empty(N, Hq, D, dtype=x.dtype, device=x.device)
     pro = None
-    if fuse_prologue:
-        pro, keep = prologue_args(q3[..., :D], k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache,
-                                  positions, slot_mapping, k_cache, v_cache, eps, q, status)
+    if prologue == "gemm":
+        a, keep = prologue_args(q3[..., :D], k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache,
+                                positions, slot_mapping, k_cache, v_cache, eps, q, status)
+        ws = workspace(256, x.device, "gemm")
+        check(lib().lb_qkv_prologue_gemm(x.data_ptr(), x.stride(0), w_qkv.data_ptr(),
+                                         w_qkv.stride(0), qkv.data_ptr(), qkv.stride(0),
+                                         x.shape[1], C.byref(a), ws.data_ptr(), stream_ptr()),
+              "lb_qkv_prologue_gemm")
+        del keep
+        for e in stage_events[:2]:
+            if e is not None:
+                e.record()
     else:
-        attn_prologue(q3[..., :D], k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions,
-                      slot_mapping, k_cache, v_cache, eps, q_out=q, status=status)
-    if stage_events[1] is not None:
-        stage_events[1].record()
+        gemm(x, w_qkv, out=qkv)
+        if stage_events[0] is not None:
+            stage_events[0].record()
+        if prologue == "pod":
+            pro, keep = prologue_args(q3[..., :D], k_in, v_in, q_norm_w, k_norm_w,
+                                      cos_sin_cache, positions, slot_mapping, k_cache, v_cache,
+                                      eps, q, status)
+        else:
+            attn_prologue(q3[..., :D], k_in, v_in, q_norm_w, k_norm_w, cos_sin_cache, positions,
+                          slot_mapping, k_cache, v_cache, eps, q_out=q, status=status)
+        if stage_events[1] is not None:
+            stage_events[1].record()
     return pod_attn_oproj(q, q3[..., D:], k_cache, v_cache, block_tables, context_lens,
                           cu_seqlens_q, w_o, scale, out=out, attn_out=attn_out,
                           max_q_len=max_q_len, ws_tag=ws_tag, events=events,

@@ -220,12 +220,13 @@ def test_c2_pod_full_size(cuda):
     _check_attention_sample(b, b.q, b.gate, b.k_cache, b.v_cache, out, attn, b.w_o, samples)
 
 
-@pytest.mark.parametrize("fuse", [False, True])
-def test_c4_step_full_size(cuda, fuse):
+@pytest.mark.parametrize("mode", ["gemm", "kernel", "pod"])
+def test_c4_step_full_size(cuda, mode):
     """The C4 step as bench.py runs it: the gated attention layer from hidden states
     (merged q/k/v GEMM, prologue with the K/V store, POD attention, gate, o_proj) over
     512 decode sequences and a 4096-token chunk, then the MoE at T = 4608; with the
-    prologue as its own launch (bench.py's form) and fused into the attention kernel."""
+    prologue in the projection GEMM's epilogue (bench.py's form), as its own launch and
+    fused into the attention kernel."""
     b = W.c4_attn_batch(seed=1, device=cuda)
     N, Hq, D = b.q.shape
     Hkv = b.k_cache.shape[2]
@@ -243,19 +244,29 @@ def test_c4_step_full_size(cuda, fuse):
         pos.to(cuda), slots.to(cuda), b.k_cache, b.v_cache, b.block_tables, b.context_lens,
         b.cu_seqlens_q, b.w_o, b.scale, max_q_len=max(b.qlen_list),
         work_hint=ops.pod_work_hint(b.ctx_list, b.qlen_list), qkv=qkv, q=qbuf,
-        attn_out=attn, ws_tag="cfg_c4", fuse_prologue=fuse)
+        attn_out=attn, ws_tag="cfg_c4", prologue=mode)
     torch.cuda.synchronize()
     _status_ok(cuda, "cfg_c4")
     _status_ok(cuda, "cfg_c4_prologue")
-    # 1. merged projection GEMM, every row, against fp32 torch on the GPU
+    # 1. merged projection GEMM, every row, against fp32 torch on the GPU (with the
+    #    prologue in the GEMM's epilogue only the gate columns reach qkv; the projection
+    #    the epilogue normalised is the plain GEMM's, same tiles and accumulation order)
     ref_qkv = x_attn.float() @ lp.w_qkv.float().t()
-    assert OM.rel_err(qkv, ref_qkv) <= 1e-2
+    if mode == "gemm":
+        gate_of = lambda t: t[:, :Hq * 2 * D].reshape(N, Hq, 2, D)[:, :, 1]
+        assert OM.rel_err(gate_of(qkv), gate_of(ref_qkv)) <= 1e-2
+        proj = ops.gemm(x_attn, lp.w_qkv)
+        assert OM.rel_err(proj, ref_qkv) <= 1e-2
+        assert torch.equal(gate_of(proj), gate_of(qkv))
+    else:
+        assert OM.rel_err(qkv, ref_qkv) <= 1e-2
+        proj = qkv
     # 2. prologue on a sample of tokens (chunk rows and decode tokens), from the kernel's
     #    own projection output: query rows and the K/V rows stored at the tokens' slots
     g = torch.Generator().manual_seed(11)
     sub = torch.cat([torch.tensor([0, 1, 4095, 4096, N - 1]),
                      torch.randperm(N, generator=g)[:384]]).unique()
-    qkv_s = qkv[sub.to(cuda)].cpu()
+    qkv_s = proj[sub.to(cuda)].cpu()
     q_in = qkv_s[:, :Hq * 2 * D]
     k_raw = qkv_s[:, Hq * 2 * D:Hq * 2 * D + Hkv * D]
     v_raw = qkv_s[:, Hq * 2 * D + Hkv * D:]
@@ -272,8 +283,8 @@ def test_c4_step_full_size(cuda, fuse):
     _check_attention_every_row(b, qbuf, gate, b.k_cache, b.v_cache, out, attn, b.w_o)
     samples = _sample_rows(b, [0], 256, 32, seed=3)
     _check_attention_sample(b, qbuf, gate, b.k_cache, b.v_cache, out, attn, b.w_o, samples)
-    del ref_qkv, x_attn, qkv
-    if fuse:
+    del ref_qkv, x_attn, qkv, proj
+    if mode != "gemm":
         return
     # 4. the MoE layer on the step's 4608 tokens
     p, x = _moe_inputs(cuda, N)

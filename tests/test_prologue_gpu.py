@@ -197,10 +197,11 @@ def test_full_attention_layer_mixed_step_from_scheduler(cuda):
 
 def test_fused_prologue_equals_the_separate_launch(cuda):
     """The prologue fused into the attention kernel (its CTAs normalise, rotate and store
-    the batch's rows first; each item waits for its sequence) gives bit for bit what the
-    separate lb_attn_prologue launch gives: the query rows, the stored K/V rows, the layer
-    output.  Two prefill chunks (one on a prefix) and decode steps, one token a padding
-    token (slot -1: its K/V are not stored)."""
+    the batch's rows first; each item waits for its sequence) and fused into the q/k/v
+    projection GEMM's epilogue (lb_qkv_prologue_gemm) give bit for bit what the separate
+    lb_attn_prologue launch gives: the query rows, the stored K/V rows, the layer output.
+    Two prefill chunks (one on a prefix) and decode steps, one token a padding token
+    (slot -1: its K/V are not stored)."""
     b = W.make_attn_batch([700, 33, 1900, 256, 2], [(300, 200), (0, 129)], seed=41)
     N = b.num_tokens
     lp = W.make_attn_layer_params(seed=42, device=cuda)
@@ -209,7 +210,7 @@ def test_fused_prologue_equals_the_separate_launch(cuda):
     x = W.make_layer_input(N, 2048, seed=43, device=cuda)
     g = b.to(cuda)
     outs = {}
-    for fuse in (False, True):
+    for mode in ("kernel", "pod", "gemm"):
         kc, vc = g.k_cache.clone(), g.v_cache.clone()
         q = torch.empty(N, 16, 256, dtype=torch.bfloat16, device=cuda)
         attn = torch.empty(N, 16 * 256, dtype=torch.bfloat16, device=cuda)
@@ -217,13 +218,42 @@ def test_fused_prologue_equals_the_separate_launch(cuda):
             x, lp.w_qkv, 16, 2, lp.q_norm_w, lp.k_norm_w, lp.cos_sin_cache, lp.eps,
             pos.to(cuda), slots.to(cuda), kc, vc, g.block_tables, g.context_lens,
             g.cu_seqlens_q, g.w_o, g.scale, max_q_len=200, q=q, attn_out=attn,
-            ws_tag=f"fused{int(fuse)}", fuse_prologue=fuse)
+            ws_tag=f"fused_{mode}", prologue=mode)
         torch.cuda.synchronize()
-        assert ops.device_status(ops.workspace(0, cuda, f"fused{int(fuse)}")) == 0
-        assert ops.device_status(ops.workspace(0, cuda, f"fused{int(fuse)}_prologue")) == 0
-        outs[fuse] = (y, q, attn, kc, vc)
-    for a, r in zip(outs[True], outs[False]):
-        assert torch.equal(a, r)
+        assert ops.device_status(ops.workspace(0, cuda, f"fused_{mode}")) == 0
+        assert ops.device_status(ops.workspace(0, cuda, f"fused_{mode}_prologue")) == 0
+        assert ops.device_status(ops.workspace(0, cuda, "gemm")) == 0
+        outs[mode] = (y, q, attn, kc, vc)
+    for mode in ("pod", "gemm"):
+        for a, r in zip(outs[mode], outs["kernel"]):
+            assert torch.equal(a, r), mode
     # and the padding token's slot was left alone
     last = int(b.block_tables[b.num_seqs - 1, 0]) * 256 + 1
-    assert torch.equal(outs[True][3].view(-1, 2, 256)[last], g.k_cache.view(-1, 2, 256)[last])
+    for mode in outs:
+        assert torch.equal(outs[mode][3].view(-1, 2, 256)[last], g.k_cache.view(-1, 2, 256)[last])
+
+
+def test_qkv_prologue_gemm_reports_bad_positions_and_slots(cuda):
+    """lb_qkv_prologue_gemm checks each token's position and slot like lb_attn_prologue:
+    a position outside the rotary table and a slot past the cache are reported in the
+    status word (and skipped or clamped), never read or written out of bounds."""
+    b = W.make_attn_batch([300, 40], [(0, 64)], seed=51)
+    N = b.num_tokens
+    lp = W.make_attn_layer_params(seed=52, device=cuda)
+    pos, slots = W.layer_positions_slots(b)
+    g = b.to(cuda)
+    x = W.make_layer_input(N, 2048, seed=53, device=cuda)
+    for bad_pos, bad_slot in ((True, False), (False, True)):
+        p2, s2 = pos.clone(), slots.clone()
+        if bad_pos:
+            p2[3] = lp.cos_sin_cache.shape[0] + 5
+        if bad_slot:
+            s2[5] = g.k_cache.shape[0] * 256 + 7
+        kc, vc = g.k_cache.clone(), g.v_cache.clone()
+        tag = f"qkvbad{int(bad_pos)}{int(bad_slot)}"
+        ops.gated_attention_layer(
+            x, lp.w_qkv, 16, 2, lp.q_norm_w, lp.k_norm_w, lp.cos_sin_cache, lp.eps,
+            p2.to(cuda), s2.to(cuda), kc, vc, g.block_tables, g.context_lens, g.cu_seqlens_q,
+            g.w_o, g.scale, max_q_len=64, ws_tag=tag, prologue="gemm")
+        torch.cuda.synchronize()
+        assert ops.device_status(ops.workspace(0, cuda, tag + "_prologue")) == 2   # LB_DEV_BAD_INDEX
