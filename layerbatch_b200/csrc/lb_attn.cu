@@ -171,42 +171,67 @@ __global__ void k_pod_plan(const int32_t* __restrict__ ctx_lens, const int32_t* 
 // ------------------------------------------------------------------------------ merge
 // Decode sequences: combine the split partials by their log2-sum-exp, apply
 // sigmoid(gate) and write the bf16 o_proj input row (and optionally the raw output).
+// One CTA per (sequence, group of `hpc` heads), 32 threads per head (8 dims each).  The
+// partials' loads are issued eight splits at a time before any is used, so a CTA waits
+// for about one memory latency per eight splits, not one per split.  The sums run over
+// the splits in order, as before the loads were batched.
+constexpr int MERGE_SPLIT_BATCH = 8;
 __global__ void k_pod_merge(const int32_t* __restrict__ ctx_lens, const int32_t* __restrict__ cu,
-                            int Hq, int split_tokens, int max_splits, int max_ctx,
+                            int Hq, int hpc, int split_tokens, int max_splits, int max_ctx,
                             const float* __restrict__ part_o, const float* __restrict__ part_lse,
                             const __nv_bfloat16* __restrict__ gate, long long gst, long long gsh,
                             __nv_bfloat16* __restrict__ ogated, __nv_bfloat16* __restrict__ attn_out) {
   pdl_entry();
-  extern __shared__ float wts[];  // [max_splits][Hq]
-  const int b = blockIdx.x;
+  extern __shared__ float wts[];  // [max_splits][hpc]
+  const int groups = Hq / hpc;
+  const int b = blockIdx.x / groups;
+  const int h0 = (blockIdx.x - b * groups) * hpc;
   const int q0 = cu[b];
   if (cu[b + 1] - q0 != 1) return;
   const int ctx = ctx_lens[b];
   const int ns = (ctx >= 1 && ctx <= max_ctx) ? min(max_splits, (ctx + split_tokens - 1) / split_tokens) : 0;
   const long long pb = (long long)b * max_splits;
-  for (int h = threadIdx.x; h < Hq; h += blockDim.x) {
+  for (int e = threadIdx.x; e < ns * hpc; e += blockDim.x) {
+    const int sp = e / hpc, hl = e - (e / hpc) * hpc;
+    wts[sp * hpc + hl] = part_lse[(pb + sp) * Hq + h0 + hl];
+  }
+  __syncthreads();
+  for (int hl = threadIdx.x; hl < hpc; hl += blockDim.x) {
     float m = -INFINITY;
-    for (int s = 0; s < ns; ++s) m = fmaxf(m, part_lse[(pb + s) * Hq + h]);
+    for (int sp = 0; sp < ns; ++sp) m = fmaxf(m, wts[sp * hpc + hl]);
     float sum = 0.f;
-    for (int s = 0; s < ns; ++s) {
-      const float w = exp2f(part_lse[(pb + s) * Hq + h] - m);
-      wts[s * Hq + h] = w;
+    for (int sp = 0; sp < ns; ++sp) {
+      const float w = exp2f(wts[sp * hpc + hl] - m);
+      wts[sp * hpc + hl] = w;
       sum += w;
     }
     const float inv = sum > 0.f ? 1.f / sum : 0.f;
-    for (int s = 0; s < ns; ++s) wts[s * Hq + h] *= inv;
+    for (int sp = 0; sp < ns; ++sp) wts[sp * hpc + hl] *= inv;
   }
   __syncthreads();
   const int HD = Hq * POD_D;
-  for (int i = threadIdx.x * 8; i < HD; i += blockDim.x * 8) {
-    const int h = i / POD_D, d = i % POD_D;
+  for (int i = h0 * POD_D + threadIdx.x * 8; i < (h0 + hpc) * POD_D; i += blockDim.x * 8) {
+    const int h = i / POD_D, d = i % POD_D, hl = h - h0;
     float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int s = 0; s < ns; ++s) {
-      const float w = wts[s * Hq + h];
-      const float4* src = reinterpret_cast<const float4*>(part_o + ((pb + s) * Hq + h) * POD_D + d);
-      const float4 x0 = src[0], x1 = src[1];
-      o[0] += w * x0.x; o[1] += w * x0.y; o[2] += w * x0.z; o[3] += w * x0.w;
-      o[4] += w * x1.x; o[5] += w * x1.y; o[6] += w * x1.z; o[7] += w * x1.w;
+    for (int s0 = 0; s0 < ns; s0 += MERGE_SPLIT_BATCH) {
+      float4 xa[MERGE_SPLIT_BATCH], xb[MERGE_SPLIT_BATCH];
+#pragma unroll
+      for (int u = 0; u < MERGE_SPLIT_BATCH; ++u) {
+        if (s0 + u < ns) {
+          const float4* src = reinterpret_cast<const float4*>(part_o + ((pb + s0 + u) * Hq + h) * POD_D + d);
+          xa[u] = src[0];
+          xb[u] = src[1];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < MERGE_SPLIT_BATCH; ++u) {
+        if (s0 + u < ns) {
+          const float w = wts[(s0 + u) * hpc + hl];
+          const float4 x0 = xa[u], x1 = xb[u];
+          o[0] += w * x0.x; o[1] += w * x0.y; o[2] += w * x0.z; o[3] += w * x0.w;
+          o[4] += w * x1.x; o[5] += w * x1.y; o[6] += w * x1.z; o[7] += w * x1.w;
+        }
+      }
     }
     if (ogated) {
       float gv[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
@@ -607,9 +632,14 @@ static int pod_attention(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, 
   { int _rc = launched("k_pod_attn"); if (_rc) return _rc; }
   record_event(a.timing_events[1], st);
 
-  const size_t merge_smem = sizeof(float) * (size_t)pl.max_splits * a.num_q_heads;
+  // heads per merge CTA: 4 (128 threads, 8 dims each) when Hq allows, else all of them
+  const int hpc = a.num_q_heads % 4 == 0 ? 4 : (int)a.num_q_heads;
+  const size_t merge_smem = sizeof(float) * (size_t)pl.max_splits * hpc;
   LB_REQUIRE(merge_smem <= 48 * 1024, "lb_pod: too many decode splits (%d)", pl.max_splits);
-  launch_k(k_pod_merge, B, 256, merge_smem, st, a.context_lens, a.cu_seqlens_q, (int)a.num_q_heads,
+  const long long merge_grid = B * (a.num_q_heads / hpc);
+  LB_REQUIRE(merge_grid < (1ll << 31), "lb_pod: too many sequences x heads");
+  launch_k(k_pod_merge, (int)merge_grid, std::min(256, 32 * hpc), merge_smem, st, a.context_lens,
+                                          a.cu_seqlens_q, (int)a.num_q_heads, hpc,
                                           pl.split_tokens, pl.max_splits, pl.max_ctx, w.part_o,
                                           w.part_lse, p.gate, a.gate_stride_tok, a.gate_stride_head,
                                           p.ogated, p.attn_out);
