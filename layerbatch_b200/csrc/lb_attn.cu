@@ -632,8 +632,9 @@ static int pod_attention(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, 
   { int _rc = launched("k_pod_attn"); if (_rc) return _rc; }
   record_event(a.timing_events[1], st);
 
-  // heads per merge CTA: 4 (128 threads, 8 dims each) when Hq allows, else all of them
-  const int hpc = a.num_q_heads % 4 == 0 ? 4 : (int)a.num_q_heads;
+  // heads per merge CTA: all of them when the sequences alone give every SM two CTAs,
+  // else 4 (128 threads, 8 dims each) when Hq allows, for more CTAs in flight
+  const int hpc = (B >= 2ll * num_sms() || a.num_q_heads % 4 != 0) ? (int)a.num_q_heads : 4;
   const size_t merge_smem = sizeof(float) * (size_t)pl.max_splits * hpc;
   LB_REQUIRE(merge_smem <= 48 * 1024, "lb_pod: too many decode splits (%d)", pl.max_splits);
   const long long merge_grid = B * (a.num_q_heads / hpc);
