@@ -349,6 +349,146 @@ def cpu_reference_run(cfg, warmup, steps, budget_s):
 
 
 # ---------------------------------------------------------------------------- GPU side
+def _time_cuda(fn, warmup=3, iters=10):
+    """Median of ``iters`` CUDA-event timings (ms) of ``fn`` on the current stream."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        ts.append(s.elapsed_time(e))
+    return statistics.median(ts)
+
+
+def _rel_err(a, b):
+    a, b = a.float(), b.float()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def gpu_library_baselines(device):
+    """GPU implementations of the c4 step's two halves other than this library's, timed
+    on the same inputs: flashinfer's paged prefill/decode attention (then the gate and
+    o_proj as torch ops), vLLM's fused-MoE Triton kernels for the routed experts (router,
+    top-k and shared expert as torch ops), and the reference's own algorithm as plain
+    torch on the GPU (the expert loop of its sparse path).  Each is checked against this
+    library's output.  Libraries that are missing or fail to build report why."""
+    import torch.nn.functional as F
+    from layerbatch_b200 import ops
+    from layerbatch_b200 import workloads as W
+    out = {}
+    b = W.c4_attn_batch(seed=1, device=device)
+    N, Hq, D = b.q.shape
+    Hkv = b.k_cache.shape[2]
+    hint = ops.pod_work_hint(b.ctx_list, b.qlen_list)
+    o_ours = torch.empty(N, 2048, dtype=torch.bfloat16, device=device)
+    att = {"workload": "c4 attention + gate + o_proj (given q, gate; 512 decode + 4096 chunk)"}
+    att["ours_ms"] = _time_cuda(lambda: ops.pod_attn_oproj(
+        b.q, b.gate, b.k_cache, b.v_cache, b.block_tables, b.context_lens, b.cu_seqlens_q,
+        b.w_o, b.scale, out=o_ours, max_q_len=max(b.qlen_list), work_hint=hint, ws_tag="gb"))
+    try:
+        import flashinfer
+        ps = b.k_cache.shape[1]
+        lens = b.context_lens.long().cpu()
+        npg = (lens + ps - 1) // ps
+        kv_indptr = torch.zeros(len(lens) + 1, dtype=torch.int32)
+        kv_indptr[1:] = torch.cumsum(npg, 0).to(torch.int32)
+        bt = b.block_tables.cpu()
+        kv_idx = torch.cat([bt[i, :int(npg[i])] for i in range(len(lens))]).to(torch.int32)
+        last = (lens - (npg - 1) * ps).to(torch.int32)
+        wsb = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+        o_fi = torch.empty(N, Hq, D, dtype=torch.bfloat16, device=device)
+        att["flashinfer"] = flashinfer.__version__
+        for backend in ("auto", "fa2", "trtllm-gen", "cudnn"):
+            try:
+                w = flashinfer.BatchPrefillWithPagedKVCacheWrapper(wsb, kv_layout="NHD",
+                                                                   backend=backend)
+                extra = {}
+                qo = b.cu_seqlens_q.to(device)
+                if backend == "cudnn":   # element offsets, lengths and tables
+                    qo = (b.cu_seqlens_q.long() * Hq * D).to(device)
+                    qlens = (b.cu_seqlens_q[1:] - b.cu_seqlens_q[:-1]).to(device)
+                    extra = dict(seq_lens=b.context_lens.to(device), seq_lens_q=qlens,
+                                 block_tables=b.block_tables.to(device),
+                                 max_token_per_sequence=max(b.qlen_list),
+                                 max_sequence_kv=max(b.ctx_list))
+                w.plan(qo, kv_indptr.to(device), kv_idx.to(device),
+                       last.to(device), Hq, Hkv, D, ps, causal=True,
+                       q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16,
+                       sm_scale=b.scale, **extra)
+
+                def fi_attn():
+                    w.run(b.q, (b.k_cache, b.v_cache), out=o_fi)
+
+                def fi_layer():
+                    fi_attn()
+                    og = (o_fi.float() * torch.sigmoid(b.gate.float())).to(torch.bfloat16)
+                    return F.linear(og.reshape(N, Hq * D), b.w_o)
+
+                att[f"flashinfer_{backend}"] = {
+                    "attention_ms": _time_cuda(fi_attn),
+                    "plus_torch_gate_oproj_ms": _time_cuda(fi_layer),
+                    "rel_err_vs_ours": _rel_err(fi_layer(), o_ours)}
+            except Exception as e:
+                att[f"flashinfer_{backend}"] = f"unavailable: {type(e).__name__}: {str(e)[:160]}"
+    except Exception as e:  # a missing or failing library is reported, not fatal
+        att["flashinfer"] = f"unavailable: {type(e).__name__}: {str(e)[:200]}"
+    out["attention"] = att
+    del b
+    torch.cuda.empty_cache()
+
+    T, k = 4608, 10
+    p = W.make_moe_params(2048, 512, 512, 512, k, seed=0, device=device)
+    x = W.make_moe_input(T, 2048, seed=1, device=device)
+    W.apply_zipf_bias(p, x)
+    moe = {"workload": "c4 MoE layer, T=4608, E=512 top-10, I=512, shared expert, Zipf(1.1)"}
+    m_ours = torch.empty_like(x)
+    moe["ours_ms"] = _time_cuda(lambda: ops.moe_forward(
+        x, p.router, p.gate_up, p.down, p.sh_gate, p.sh_up, p.sh_down, p.sh_gate_w, k,
+        out=m_ours, ws_tag="gb_moe"))
+
+    def routing():
+        logits = F.linear(x, p.router)
+        probs = torch.softmax(logits.float(), dim=-1)
+        wts, ids = torch.topk(probs, k, dim=-1)
+        return wts / wts.sum(-1, keepdim=True), ids
+
+    def shared():
+        h = F.silu(F.linear(x, p.sh_gate)) * F.linear(x, p.sh_up)
+        return F.linear(h, p.sh_down) * torch.sigmoid(F.linear(x, p.sh_gate_w))
+
+    try:
+        from vllm.model_executor.layers.fused_moe.fused_moe import fused_experts
+
+        def vllm_moe():
+            wts, ids = routing()
+            return fused_experts(x, p.gate_up, p.down, wts, ids.to(torch.int32)) + shared()
+
+        moe["vllm_fused_experts_plus_torch_ms"] = _time_cuda(vllm_moe)
+        moe["rel_err_vllm_vs_ours"] = _rel_err(vllm_moe(), m_ours)
+    except Exception as e:
+        moe["vllm"] = f"unavailable: {type(e).__name__}: {str(e)[:200]}"
+
+    def torch_loop():
+        wts, ids = routing()
+        y = torch.zeros_like(x)
+        for e in torch.unique(ids).tolist():
+            tok, slot = torch.nonzero(ids == e, as_tuple=True)
+            g, u = F.linear(x[tok], p.gate_up[e]).chunk(2, dim=-1)
+            r = F.linear(F.silu(g) * u, p.down[e]) * wts[tok, slot, None].to(x.dtype)
+            y.index_add_(0, tok, r)
+        return y + shared()
+
+    moe["torch_expert_loop_ms"] = _time_cuda(torch_loop, warmup=1, iters=3)
+    moe["rel_err_torch_vs_ours"] = _rel_err(torch_loop(), m_ours)
+    out["moe"] = moe
+    return out
+
+
 def run_ours(args, rank, world, device):
     from layerbatch_b200 import ops
     from layerbatch_b200 import workloads as W
@@ -739,6 +879,9 @@ def main():
                     help="time eager launches instead of replaying a captured step")
     ap.add_argument("--ref-budget-s", type=float, default=240.0,
                     help="wall-clock bound of the reference arm's CPU run")
+    ap.add_argument("--gpu-baselines", action="store_true",
+                    help="also time flashinfer / vLLM / plain-torch GPU versions of the c4 "
+                         "attention and MoE on the same inputs (1 GPU, after the timed run)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -839,6 +982,8 @@ def main():
             e = res["e2e"]
             line["e2e"] = {"value": res["tokens"] * world / (e["ms"] * 1e-3), "unit": "tokens/s",
                            "h2d_bytes_per_step": e["h2d"], "d2h_bytes_per_step": e["d2h"]}
+        if args.gpu_baselines and world == 1:
+            line["gpu_baselines"] = gpu_library_baselines(device)
         if errors:
             line["errors"] = errors
         print(json.dumps(line), flush=True)
