@@ -82,21 +82,53 @@ __global__ void k_pod_plan(const int32_t* __restrict__ ctx_lens, const int32_t* 
       npf += Hq * ((qlen + POD_KV - 1) / POD_KV);
     }
   }
-  s_pf[tid] = npf;
-  s_full[tid] = nfull;
-  s_rem[tid] = nrem;
-  __syncthreads();
-  for (int off = 1; off < 1024; off <<= 1) {
-    int a = 0, c = 0, d = 0;
-    if (tid >= off) {
-      a = s_pf[tid - off];
-      c = s_full[tid - off];
-      d = s_rem[tid - off];
+  // inclusive block scans of the three counts: within each warp by shuffles, then the
+  // 32 warp totals by one warp (two block barriers instead of one pair per step)
+  {
+    const int lane = tid & 31, wid = tid >> 5;
+    int a = npf, c = nfull, d = nrem;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int xa = __shfl_up_sync(0xffffffffu, a, o);
+      const int xc = __shfl_up_sync(0xffffffffu, c, o);
+      const int xd = __shfl_up_sync(0xffffffffu, d, o);
+      if (lane >= o) {
+        a += xa;
+        c += xc;
+        d += xd;
+      }
+    }
+    if (lane == 31) {
+      s_pf[wid] = a;
+      s_full[wid] = c;
+      s_rem[wid] = d;
     }
     __syncthreads();
-    s_pf[tid] += a;
-    s_full[tid] += c;
-    s_rem[tid] += d;
+    if (wid == 0) {
+      int wa = s_pf[lane], wc = s_full[lane], wd = s_rem[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int xa = __shfl_up_sync(0xffffffffu, wa, o);
+        const int xc = __shfl_up_sync(0xffffffffu, wc, o);
+        const int xd = __shfl_up_sync(0xffffffffu, wd, o);
+        if (lane >= o) {
+          wa += xa;
+          wc += xc;
+          wd += xd;
+        }
+      }
+      s_pf[32 + lane] = wa;   // inclusive prefix of the warp totals
+      s_full[32 + lane] = wc;
+      s_rem[32 + lane] = wd;
+    }
+    __syncthreads();
+    const int pa = wid ? s_pf[32 + wid - 1] : 0;
+    const int pc = wid ? s_full[32 + wid - 1] : 0;
+    const int pd = wid ? s_rem[32 + wid - 1] : 0;
+    __syncthreads();   // every thread has read the warp prefixes before they are overwritten
+    s_pf[tid] = a + pa;
+    s_full[tid] = c + pc;
+    s_rem[tid] = d + pd;
     __syncthreads();
   }
   const int total_full = s_full[1023];

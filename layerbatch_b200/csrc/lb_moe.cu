@@ -97,7 +97,8 @@ __global__ void k_router_topk(const __nv_bfloat16* __restrict__ logits, long lon
   if (sg != nullptr) {
     const __nv_bfloat16* xr = x + (long long)t * H;
     float acc = 0.f;
-    for (int h = lane * 8; h < H; h += 256) {
+#pragma unroll 8
+    for (int h = lane * 8; h < H; h += 256) {   // unrolled: a lane's loads all in flight
       const uint4 a = *reinterpret_cast<const uint4*>(xr + h);
       const uint4 b = *reinterpret_cast<const uint4*>(wsg + h);
       acc += bf16_lo(a.x) * bf16_lo(b.x) + bf16_hi(a.x) * bf16_hi(b.x);
@@ -126,7 +127,8 @@ __global__ void k_shared_gate(const __nv_bfloat16* __restrict__ x, const __nv_bf
   }
   const __nv_bfloat16* xr = x + (long long)t * H;
   float acc = 0.f;
-  for (int h = lane * 8; h < H; h += 256) {
+#pragma unroll 8
+  for (int h = lane * 8; h < H; h += 256) {   // unrolled: a lane's loads all in flight
     const uint4 a = *reinterpret_cast<const uint4*>(xr + h);
     const uint4 b = *reinterpret_cast<const uint4*>(wsg + h);
     acc += bf16_lo(a.x) * bf16_lo(b.x) + bf16_hi(a.x) * bf16_hi(b.x);
