@@ -204,10 +204,10 @@ __global__ void k_pod_plan(const int32_t* __restrict__ ctx_lens, const int32_t* 
 // Decode sequences: combine the split partials by their log2-sum-exp, apply
 // sigmoid(gate) and write the bf16 o_proj input row (and optionally the raw output).
 // One CTA per (sequence, group of `hpc` heads), 32 threads per head (8 dims each).  The
-// partials' loads are issued eight splits at a time before any is used, so a CTA waits
-// for about one memory latency per eight splits, not one per split.  The sums run over
+// partials' loads are issued four splits at a time before any is used, so a CTA waits
+// for about one memory latency per four splits, not one per split.  The sums run over
 // the splits in order, as before the loads were batched.
-constexpr int MERGE_SPLIT_BATCH = 8;
+constexpr int MERGE_SPLIT_BATCH = 4;
 __global__ void k_pod_merge(const int32_t* __restrict__ ctx_lens, const int32_t* __restrict__ cu,
                             int Hq, int hpc, int split_tokens, int max_splits, int max_ctx,
                             const float* __restrict__ part_o, const float* __restrict__ part_lse,
@@ -300,26 +300,37 @@ __global__ void k_splitk_reduce(const float* __restrict__ parts, int splits, lon
                                 float* __restrict__ out_f32, long long ld_out) {
   pdl_entry();
   const long long slice = rows * cols;
-  // one block per row (grid-stride), the block's threads across the row's 4-float groups
-  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
-    for (int c = threadIdx.x * 4; c < cols; c += blockDim.x * 4) {
-      const float* src = parts + r * cols + c;
-      float4 acc = *reinterpret_cast<const float4*>(src);
-      for (int s = 1; s < splits; ++s) {
-        const float4 v = *reinterpret_cast<const float4*>(src + s * slice);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+  const int groups = cols / 4;   // 4-float groups per row
+  // one thread per 4-float group of the output (grid-stride); a thread's slice loads are
+  // issued eight at a time before they are added, in split order
+  for (long long gi = (long long)blockIdx.x * blockDim.x + threadIdx.x; gi < rows * groups;
+       gi += (long long)gridDim.x * blockDim.x) {
+    const long long r = gi / groups;
+    const int c = (int)(gi - r * groups) * 4;
+    const float* src = parts + r * cols + c;
+    float4 acc = *reinterpret_cast<const float4*>(src);
+    for (int s0 = 1; s0 < splits; s0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (s0 + u < splits) v[u] = *reinterpret_cast<const float4*>(src + (s0 + u) * slice);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (s0 + u < splits) {
+          acc.x += v[u].x;
+          acc.y += v[u].y;
+          acc.z += v[u].z;
+          acc.w += v[u].w;
+        }
       }
-      if (out_f32) {
-        *reinterpret_cast<float4*>(out_f32 + r * ld_out + c) = acc;
-      } else {
-        uint2 o;
-        o.x = pack_bf16x2(acc.x, acc.y);
-        o.y = pack_bf16x2(acc.z, acc.w);
-        *reinterpret_cast<uint2*>(out_bf16 + r * ld_out + c) = o;
-      }
+    }
+    if (out_f32) {
+      *reinterpret_cast<float4*>(out_f32 + r * ld_out + c) = acc;
+    } else {
+      uint2 o;
+      o.x = pack_bf16x2(acc.x, acc.y);
+      o.y = pack_bf16x2(acc.z, acc.w);
+      *reinterpret_cast<uint2*>(out_bf16 + r * ld_out + c) = o;
     }
   }
 }
@@ -780,7 +791,7 @@ static int pod_run(const LbPodArgs& a, const PodPlan& pl, const PodWs& w, cudaSt
   const int splits = pl.oproj_splits;
   rc = gemm_run(w.ogated, K, a.w_o, K, w.o32, Hd, N, Hd, K, EPI_F32_SPLIT, splits, w.status, st);
   if (rc) return rc;
-  const int g = (int)std::max<long long>(1, std::min<long long>(nsm * 4, N));
+  const int g = (int)std::max<long long>(1, std::min<long long>(nsm * 8, (N * (Hd / 4) + 255) / 256));
   launch_k(k_splitk_reduce, g, 256, 0, st, static_cast<const float*>(w.o32), splits, (long long)N,
            Hd, a.out_fp32 ? nullptr : static_cast<__nv_bfloat16*>(a.out),
            a.out_fp32 ? static_cast<float*>(a.out) : nullptr, (long long)Hd);
