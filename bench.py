@@ -750,6 +750,26 @@ def run_ours(args, rank, world, device):
                                 "bytes_counted": "weights hit + shared + router, x, out "
                                                  "(no scratch rows)"}
     res["phases_ms"] = {k: round(v, 4) for k, v in phases.items()}
+    if layer and moe and not sharded:
+        # The whole step against its floor: each stage at the slower of its algorithmic
+        # bytes over the measured HBM bandwidth and its FLOPs over the measured bf16 peak
+        # (attention and the MoE layer are byte-bound, the projections FLOP-bound).
+        bw, pf = peaks["hbm_gbs"] * 1e9, peaks["bf16_tflops"] * 1e12
+        fa, ba = attn_work(attn)
+        g, _ = layer_proj_work(attn.num_tokens, Hq=Hq_l, Hkv=Hkv_l)
+        n_t, kd = attn.num_tokens, Hq_l * attn.q.shape[2]
+        o_fl = 2.0 * n_t * kd * 2048
+        o_by = kd * 2048 * 2 + n_t * kd * 2 + n_t * 2048 * 2
+        _, _, ly = moe_work(T_moe, moe_hit)
+        stages = {"attention": max(ba / bw, fa / pf),
+                  "qkv_projection": max(g["bytes"] / bw, g["flops"] / pf),
+                  "o_proj": max(o_by / bw, o_fl / pf),
+                  "moe_layer": max(ly["bytes"] / bw, ly["flops"] / pf)}
+        floor = sum(stages.values())
+        res["step_roofline"] = {"floor_ms": floor * 1e3, "frac": floor * 1e3 / res["ms"],
+                                "stage_floor_ms": {k: round(v * 1e3, 4) for k, v in stages.items()},
+                                "basis": "per stage max(algorithmic bytes / measured HBM GB/s, "
+                                         "FLOPs / measured bf16 TFLOP/s), summed"}
     res["parallelism"] = (f"tp{tp} x dp{world // tp} attention (KV-head shards, o_proj GEMM "
                           f"reducing over NVLink peer memory), ep{world} MoE (NVLink "
                           f"peer-memory dispatch/return, experts placed by popularity)"
@@ -999,7 +1019,7 @@ def main():
             "gpu_launches": res["launches"], "phases_ms": res["phases_ms"],
             "timed_loop": res["timed_loop"],
         }
-        for key in ("moe_layer", "proj"):
+        for key in ("moe_layer", "proj", "step_roofline"):
             if key in res:
                 line[key] = res[key]
         if "e2e" in res:
