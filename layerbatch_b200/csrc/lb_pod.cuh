@@ -210,12 +210,42 @@ __device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* ma
   for (int c = 0; c < 4; ++c) tma_load_3d(dst + c * POD_CHUNK, map, bar, c * 64, kvh, row);
 }
 
-// Decode ring order of one item of n tiles: K0, K1, V0, K2, V1, ..., K(n-1), V(n-2), V(n-1).
-// K runs one tile ahead of V, so the K tile of the next S MMA is never queued behind a V
-// tile that waits for the current softmax, and each V tile streams in while its scores are
-// being turned into P.
-__device__ __forceinline__ int dec_pos_k(int j) { return j ? 2 * j - 1 : 0; }
-__device__ __forceinline__ int dec_pos_v(int j, int n) { return min(2 * j + 2, 2 * n - 1); }
+// Decode ring order of one item of n tiles: the first DEC_KAHEAD K tiles, then V0, K(A),
+// V1, K(A+1), ..., then the remaining V tiles (A = DEC_KAHEAD; with A = 2: K0, K1, V0, K2,
+// V1, ..., K(n-1), V(n-2), V(n-1)).  K runs ahead of V, so the K tile of the next S MMA is
+// never queued behind a V tile that waits for the current softmax, and each V tile streams
+// in while its scores are being turned into P.
+#ifndef LB_DEC_KAHEAD
+#define LB_DEC_KAHEAD 2
+#endif
+constexpr int DEC_KAHEAD = LB_DEC_KAHEAD;
+// With DEC_SLOTS = 3 and the MMA order S_j, PV_{j-1}: V_j takes the slot of the load three
+// positions earlier, which for DEC_KAHEAD = 4 is K_{j+2}, freed only by S_{j+2}, issued
+// after PV_j: a deadlock.  1 to 3 are safe (2 measured fastest).
+static_assert(DEC_KAHEAD >= 1 && DEC_KAHEAD <= 3, "decode ring order");
+__device__ __forceinline__ int dec_pos_k(int j) {
+  return j < DEC_KAHEAD ? j : DEC_KAHEAD + 2 * (j - DEC_KAHEAD) + 1;
+}
+__device__ __forceinline__ int dec_pos_v(int j, int n) {
+  const int a = min(n, DEC_KAHEAD), m = max(0, n - DEC_KAHEAD);
+  return j < m ? DEC_KAHEAD + 2 * j : a + 2 * m + (j - m);
+}
+// Ring position q of an item of n tiles -> its tile, and whether it is the V tile (the
+// inverse of dec_pos_k / dec_pos_v).
+__device__ __forceinline__ int dec_ring_tile(int q, int n, bool& is_v) {
+  const int a = min(n, DEC_KAHEAD), m = max(0, n - DEC_KAHEAD);
+  if (q < a) {
+    is_v = false;
+    return q;
+  }
+  if (q < a + 2 * m) {
+    const int r = q - a;
+    is_v = !(r & 1);
+    return is_v ? (r >> 1) : (r >> 1) + DEC_KAHEAD;
+  }
+  is_v = true;
+  return m + (q - a - 2 * m);
+}
 
 // Decode TMEM columns: S^T [2 buffers][4 chunk partials][16 heads], O^T [2 buffers][2 dim
 // halves][4 token-quarter partials][16 heads].
@@ -553,14 +583,8 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
               const int slot = cnt.kv % nslots;
               const uint32_t ph = (cnt.kv / nslots) & 1;
               if (!mbar_wait(&bars->kv_empty[slot], ph ^ 1, p.status)) { *abortp = 1; break; }
-              // ring position j -> (tile, K or V), the inverse of dec_pos_k / dec_pos_v
-              int tile = 0;
-              bool is_v = false;
-              if (j > 0) {
-                tile = (j - 1) >> 1;
-                is_v = ((j - 1) & 1) || tile + 1 >= ntiles;
-                if (!is_v) ++tile;
-              }
+              bool is_v;
+              const int tile = dec_ring_tile(j, ntiles, is_v);
               const int row = kv_page_row(p, b, t_begin + tile * POD_KV);
               mbar_arrive_expect_tx(&bars->kv_full[slot], POD_TILE);
               load_kv_tile(kv_base + slot * POD_TILE, is_v ? &tmV : &tmK, &bars->kv_full[slot],
