@@ -443,19 +443,37 @@ __global__ void k_perm_chunk_scatter(const int32_t* __restrict__ ids, const floa
   extern __shared__ int cnt[];
   const int lane = threadIdx.x;
   const int nc = gridDim.x;
-  // cnt[e] starts at the first packed row of expert e's pairs in this chunk
+  // cnt[e] starts at the first packed row of expert e's pairs in this chunk (unrolled, so
+  // that a lane's loads are all in flight before the first shared store)
+#pragma unroll 16
   for (int i = lane; i < nl; i += 32)
     cnt[i] = row_start[1 + i] + chunk_prefix[(long long)i * nc + blockIdx.x];
   __syncwarp();
   const int n = T * k;
   const int f0 = blockIdx.x * PERM_CHUNK;
-  for (int s = 0; s < PERM_CHUNK; s += 32) {
-    const int f = f0 + s + lane;
+  // the chunk's expert ids, every step's load issued before any is ranked
+  constexpr int STEPS = PERM_CHUNK / 32;
+  int es[STEPS];
+  float ws[STEPS];
+#pragma unroll
+  for (int u = 0; u < STEPS; ++u) {
+    const int f = f0 + 32 * u + lane;
+    es[u] = -1;
+    ws[u] = 0.f;
+    if (f < n) {
+      const int j = f / T, t = f - (f / T) * T;
+      es[u] = ids[(long long)t * k + j] - expert_base;
+      if (perm_w) ws[u] = w[(long long)t * k + j];
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < STEPS; ++u) {
+    const int f = f0 + 32 * u + lane;
     int e = -1, t = 0, j = 0;
     if (f < n) {
       j = f / T;
       t = f - j * T;
-      e = ids[(long long)t * k + j] - expert_base;
+      e = es[u];
       if (e < 0 || e >= nl) e = -1;
     }
     const unsigned peers = __match_any_sync(0xffffffffu, e);
@@ -467,7 +485,7 @@ __global__ void k_perm_chunk_scatter(const int32_t* __restrict__ ids, const floa
     __syncwarp();
     if (e >= 0) {
       perm_token[r] = t;
-      if (perm_w) perm_w[r] = w[(long long)t * k + j];
+      if (perm_w) perm_w[r] = ws[u];
       row_of[(long long)t * k + j] = r;
     }
   }

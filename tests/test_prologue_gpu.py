@@ -257,3 +257,40 @@ def test_qkv_prologue_gemm_reports_bad_positions_and_slots(cuda):
             g.w_o, g.scale, max_q_len=64, ws_tag=tag, prologue="gemm")
         torch.cuda.synchronize()
         assert ops.device_status(ops.workspace(0, cuda, tag + "_prologue")) == 2   # LB_DEV_BAD_INDEX
+
+
+def test_qkv_prologue_gemm_rejects_other_rotary_dims(cuda):
+    """The GEMM-epilogue prologue handles head_dim 256 with 64 rotated dims; another
+    rotary_dim is refused with LB_ERR_UNSUPPORTED before anything is launched, and the layer
+    call falls back to the separate prologue launch (same results as prologue="kernel")."""
+    import ctypes as C
+    from layerbatch_b200._lib import lib
+    b = W.make_attn_batch([300, 40], [(0, 64)], seed=61)
+    N = b.num_tokens
+    lp = W.make_attn_layer_params(seed=62, device=cuda)
+    cs32 = lp.cos_sin_cache[:, :32].contiguous()   # a 32-dim rotary table
+    pos, slots = W.layer_positions_slots(b)
+    g = b.to(cuda)
+    x = W.make_layer_input(N, 2048, seed=63, device=cuda)
+    qkv = torch.empty(N, lp.w_qkv.shape[0], dtype=torch.bfloat16, device=cuda)
+    q = torch.empty(N, 16, 256, dtype=torch.bfloat16, device=cuda)
+    q3 = qkv[:, :16 * 512].view(N, 16, 512)
+    k_in = qkv[:, 16 * 512:16 * 512 + 512].view(N, 2, 256)
+    v_in = qkv[:, 16 * 512 + 512:].view(N, 2, 256)
+    a, keep = ops.prologue_args(q3[..., :256], k_in, v_in, lp.q_norm_w, lp.k_norm_w, cs32,
+                                pos.to(cuda), slots.to(cuda), g.k_cache, g.v_cache, lp.eps, q)
+    ws = ops.workspace(256, cuda, "gemm")
+    n0 = ops.launch_count()
+    rc = lib().lb_qkv_prologue_gemm(x.data_ptr(), x.stride(0), lp.w_qkv.data_ptr(),
+                                    lp.w_qkv.stride(0), qkv.data_ptr(), qkv.stride(0),
+                                    x.shape[1], C.byref(a), ws.data_ptr(), None)
+    assert rc == 2 and ops.launch_count() == n0
+    outs = {}
+    for mode in ("gemm", "kernel"):
+        kc, vc = g.k_cache.clone(), g.v_cache.clone()
+        outs[mode] = ops.gated_attention_layer(
+            x, lp.w_qkv, 16, 2, lp.q_norm_w, lp.k_norm_w, cs32, lp.eps, pos.to(cuda),
+            slots.to(cuda), kc, vc, g.block_tables, g.context_lens, g.cu_seqlens_q, g.w_o,
+            g.scale, max_q_len=64, ws_tag=f"rot32_{mode}", prologue=mode)
+    torch.cuda.synchronize()
+    assert torch.equal(outs["gemm"], outs["kernel"])
