@@ -160,6 +160,23 @@ def layer_proj_work(N, H=2048, Hq=16, Hkv=2, D=256):
     return gemm, pro
 
 
+def step_floor(attn, T_moe, moe_hit, Hq, Hkv, peaks, H=2048):
+    """The c4 layer step's floor per stage (seconds): the slower of its algorithmic bytes
+    over the measured HBM bandwidth and its FLOPs over the measured bf16 peak (attention
+    and the MoE layer are byte-bound, the projections FLOP-bound)."""
+    bw, pf = peaks["hbm_gbs"] * 1e9, peaks["bf16_tflops"] * 1e12
+    fa, ba = attn_work(attn)
+    g, _ = layer_proj_work(attn.num_tokens, H=H, Hq=Hq, Hkv=Hkv)
+    n_t, kd = attn.num_tokens, Hq * attn.q.shape[2]
+    o_fl = 2.0 * n_t * kd * H
+    o_by = kd * H * 2 + n_t * kd * 2 + n_t * H * 2
+    _, _, ly = moe_work(T_moe, moe_hit, H=H)
+    return {"attention": max(ba / bw, fa / pf),
+            "qkv_projection": max(g["bytes"] / bw, g["flops"] / pf),
+            "o_proj": max(o_by / bw, o_fl / pf),
+            "moe_layer": max(ly["bytes"] / bw, ly["flops"] / pf)}
+
+
 # ---------------------------------------------------------------------------- clocks
 def nvml_handle(device_index: int):
     """NVML handle of a CUDA device, matched by PCI bus id (CUDA and NVML may order
@@ -751,20 +768,7 @@ def run_ours(args, rank, world, device):
                                                  "(no scratch rows)"}
     res["phases_ms"] = {k: round(v, 4) for k, v in phases.items()}
     if layer and moe and not sharded:
-        # The whole step against its floor: each stage at the slower of its algorithmic
-        # bytes over the measured HBM bandwidth and its FLOPs over the measured bf16 peak
-        # (attention and the MoE layer are byte-bound, the projections FLOP-bound).
-        bw, pf = peaks["hbm_gbs"] * 1e9, peaks["bf16_tflops"] * 1e12
-        fa, ba = attn_work(attn)
-        g, _ = layer_proj_work(attn.num_tokens, Hq=Hq_l, Hkv=Hkv_l)
-        n_t, kd = attn.num_tokens, Hq_l * attn.q.shape[2]
-        o_fl = 2.0 * n_t * kd * 2048
-        o_by = kd * 2048 * 2 + n_t * kd * 2 + n_t * 2048 * 2
-        _, _, ly = moe_work(T_moe, moe_hit)
-        stages = {"attention": max(ba / bw, fa / pf),
-                  "qkv_projection": max(g["bytes"] / bw, g["flops"] / pf),
-                  "o_proj": max(o_by / bw, o_fl / pf),
-                  "moe_layer": max(ly["bytes"] / bw, ly["flops"] / pf)}
+        stages = step_floor(attn, T_moe, moe_hit, Hq_l, Hkv_l, peaks)
         floor = sum(stages.values())
         res["step_roofline"] = {"floor_ms": floor * 1e3, "frac": floor * 1e3 / res["ms"],
                                 "stage_floor_ms": {k: round(v * 1e3, 4) for k, v in stages.items()},

@@ -70,3 +70,18 @@ def test_reference_arm_prints_the_contract_line():
     # full steps of the workload, the same config object as the GPU arm's line
     assert "full c1 step" in cb["sample"] and 1 <= line["steps"] <= 2
     assert line["config"] == bench.config_dict("c1", 64)
+
+
+def test_step_floor_is_the_slower_of_bytes_and_flops_per_stage():
+    """The whole-step roofline of the c4 line: attention and the MoE layer bound by their
+    bytes, the projections by their FLOPs, at the measured peaks."""
+    b = W.make_attn_batch([4000] * 8, [(0, 512)], seed=3)
+    peaks = {"hbm_gbs": 6546.6, "bf16_tflops": 1619.4}
+    st = bench.step_floor(b, b.num_tokens, 500, 16, 2, peaks)
+    fa, ba = bench.attn_work(b)
+    assert st["attention"] == max(ba / 6546.6e9, fa / 1619.4e12) == ba / 6546.6e9
+    g, _ = bench.layer_proj_work(b.num_tokens)
+    assert st["qkv_projection"] == g["flops"] / 1619.4e12 > g["bytes"] / 6546.6e9
+    assert st["o_proj"] == 2.0 * b.num_tokens * 4096 * 2048 / 1619.4e12
+    _, _, ly = bench.moe_work(b.num_tokens, 500)
+    assert st["moe_layer"] == ly["bytes"] / 6546.6e9
