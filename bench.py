@@ -74,8 +74,8 @@ def load_peaks():
 # (summaries under profiles/); re-captured whenever the kernel changes.  k_pod_attn for
 # the attention workloads, the grouped gate/up GEMM (k_gemm_tok, SwiGLU) for c3.
 NCU_GATE_UP_TRAFFIC = {"c3s": 1556182016 + 6260480, "c3l": 2548653056 + 86476800}
-NCU_POD_TRAFFIC = {"c1": 293260800 + 5938432, "c2": 1220505088 + 22828800,
-                   "c4": 9129531904 + 59853824}
+NCU_POD_TRAFFIC = {"c1": 293298688 + 4990976, "c2": 1225966080 + 24515328,
+                   "c4": 9144729344 + 47202048}
 
 # ---------------------------------------------------------------------------- workloads
 CONFIGS = {
