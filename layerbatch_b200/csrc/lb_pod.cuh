@@ -124,6 +124,7 @@ struct PodBars {
   float lred[4][16];
   float psum[2][128];      // prefill: per-warpgroup partial row sums at the end of an item
   int pro_task;            // fused prologue: the task the CTA works on
+  int skip_pass;           // the second pass's queue was already empty
 };
 
 static_assert(sizeof(PodBars) <= POD_MISC, "PodBars exceeds the reserved shared memory");
@@ -1059,9 +1060,12 @@ __global__ void __launch_bounds__(POD_THREADS, 1)
       }
       mbar_inval(&bars->q_empty);
       mbar_inval(&bars->drain);
+      // the other queue already handed out every item (or never had any): no second pass
+      bars->skip_pass = pf_first ? *(volatile const int*)p.dec_next >= *p.dec_count
+                                 : *(volatile const int*)p.pf_next >= *p.pf_count;
     }
     __syncthreads();
-    if (*abortp) break;
+    if (*abortp || (pass == 0 && bars->skip_pass)) break;
   }
   if (warp == 1) {
     tc_fence_after();
