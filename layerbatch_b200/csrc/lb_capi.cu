@@ -146,6 +146,25 @@ int max_smem_optin() {
 }
 
 
+// 256 x 256 tiles of the CTA-pair GEMM for an M x N product.
+static long long pair_tiles(long long M, long long N) {
+  return ((M + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * (N / PAIR_BN);
+}
+
+// Whether the CTA-pair GEMM beats the single-CTA one of tile width `bn`: a wave's time
+// taken as proportional to the rows each SM loads per k-block (128 + 128 for a pair,
+// 128 + bn alone), times the waves of tiles over the SMs.  The q/k/v projection (M 4608,
+// N 9216) and o_proj (N 2048) go to pairs; the router logits (N 512: 36 pair tiles for 74
+// SM pairs) stay on 128-wide single tiles.
+static bool pair_gemm_pays(long long M, long long N, int bn) {
+  if (N % PAIR_BN != 0 || M <= 0) return false;
+  const long long sms = num_sms();
+  const long long waves2 = (pair_tiles(M, N) + sms / 2 - 1) / (sms / 2);
+  const long long tiles1 = ((M + GEMM_BM - 1) / GEMM_BM) * (N / bn);
+  const long long waves1 = (tiles1 + sms - 1) / sms;
+  return waves2 * (GEMM_BM + PAIR_BN / 2) < waves1 * (GEMM_BM + bn);
+}
+
 // The dense GEMM behind lb_gemm_bf16 and the library's own projections: checks, tile
 // width choice, tensor maps and the launch of the epilogue `epi` (EPI_BF16, EPI_F32_RED or
 // EPI_F32_SPLIT; the last writes split ks into out32 + ks * M * ldc).
@@ -181,6 +200,19 @@ int gemm_run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, in
   CUtensorMap tA, tB;
   int rc = make_tmap_bf16_2d(&tA, A, M, K, lda, GEMM_BM, 64);
   if (rc) return rc;
+  if (epi == EPI_BF16 && pair_gemm_pays(M, N, BN)) {
+    // CTA pairs: 256 x 256 tiles, each CTA loading 128 rows of A and 128 of B
+    if ((rc = make_tmap_bf16_2d(&tB, B, N, K, ldb, PAIR_BN / 2, 64))) return rc;
+    GemmArgs a = gemm_args_default(status);
+    a.m = (int)M;
+    a.n_tiles = (int)(N / PAIR_BN);
+    a.k_blocks = (int)(K / 64);
+    a.out = C;
+    a.ldo = ldc;
+    a.out_rows = (int)M;
+    a.out_cols = (int)N;
+    return launch_gemm_pair<6, EPI_BF16>(tA, tB, a, pair_tiles(M, N), st);
+  }
   rc = make_tmap_bf16_3d(&tB, B, 1, N, K, ldb, ldb * N, BN, 64);
   if (rc) return rc;
   GemmArgs a = gemm_args_default(status);
@@ -274,7 +306,9 @@ int lb_qkv_prologue_gemm(const void* x, int64_t ldx, const void* w_qkv, int64_t 
   CUtensorMap tA, tB;
   int rc = make_tmap_bf16_2d(&tA, x, M, K, ldx, GEMM_BM, 64);
   if (rc) return rc;
-  rc = make_tmap_bf16_3d(&tB, w_qkv, 1, N, K, ldw, ldw * N, PRO_D, 64);
+  const bool pair = pair_gemm_pays(M, N, PRO_D);
+  rc = pair ? make_tmap_bf16_2d(&tB, w_qkv, N, K, ldw, PAIR_BN / 2, 64)
+            : make_tmap_bf16_3d(&tB, w_qkv, 1, N, K, ldw, ldw * N, PRO_D, 64);
   if (rc) return rc;
   GemmArgs g = gemm_args_default(static_cast<int*>(workspace));
   g.m = (int)M;
@@ -285,6 +319,7 @@ int lb_qkv_prologue_gemm(const void* x, int64_t ldx, const void* w_qkv, int64_t 
   g.out_rows = (int)M;
   g.out_cols = (int)N;
   g.pro = *a;
+  if (pair) return launch_gemm_pair<6, EPI_QKV>(tA, tB, g, pair_tiles(M, N), st);
   const long long tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (long long)g.n_tiles;
   const int grid = (int)std::min<long long>(tiles, num_sms());
   return launch_gemm<PRO_D, 4, EPI_QKV>(tA, tB, g, grid, st);

@@ -307,4 +307,207 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 }
 
+
+// ------------------------------------------------------------------------------ CTA pair
+// The same C = A . B^T on a cluster of two CTAs (cta_group::2): the pair computes a
+// 256 x 256 tile with one M = 256 MMA per K step.  Each CTA loads its own 128 rows of A and
+// 128 of the 256 B rows (32 KB per k-block instead of the 48 KB a 128 x 256 tile needs
+// alone, so each SM reads a third less from L2 per FLOP and six stages fit), and its TMEM
+// receives its 128 accumulator rows, which its own epilogue stores.
+//   warp 0 (both CTAs) : TMA producer; the loads of both CTAs complete on the first CTA's
+//                        `full` barrier, which expects the pair's bytes
+//   warp 1             : pair TMEM allocation (both CTAs); MMA issue (first CTA only), with
+//                        each commit sent to the barrier of both CTAs
+//   warps 2..5         : epilogue of this CTA's rows; one arrival per warp on the first
+//                        CTA's `tempty` barrier (eight per tile)
+// Every wait is bounded; the CTAs meet in cluster barriers after the barrier set-up and
+// before the TMEM release, so neither leaves while the other may still signal it.
+constexpr int PAIR_BN = 256;
+
+template <int STAGES>
+struct PairSmem {
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;          // this CTA's 128 A rows
+  static constexpr int B_BYTES = (PAIR_BN / 2) * GEMM_BK * 2;    // this CTA's 128 B rows
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int TMEM_COLS = 2 * PAIR_BN;                  // two accumulators
+  static size_t bytes() { return 1024 + (size_t)STAGES * (A_BYTES + B_BYTES) + BAR_BYTES; }
+};
+
+template <int STAGES, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const GemmArgs p) {
+  static_assert(EPI == EPI_BF16 || EPI == EPI_QKV, "pair GEMM epilogues: bf16 and q/k/v");
+  static_assert(EPI != EPI_QKV || PAIR_BN == PRO_D, "EPI_QKV: one 256-dim head row per tile");
+  using S = PairSmem<STAGES>;
+  constexpr uint32_t PAIR_TX = 2u * (S::A_BYTES + S::B_BYTES);
+  pdl_entry();
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * S::B_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();   // 0: issues the MMAs, 1: its peer
+  const int cid = blockIdx.x >> 1;           // cluster (2 consecutive CTAs of the 1-D grid)
+  const int ncl = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);
+    }
+    mbar_init(drain, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  __syncthreads();
+  cluster_sync();   // both CTAs' barriers exist before either signals the other
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int mt2 = (p.m + 2 * GEMM_BM - 1) / (2 * GEMM_BM);
+  const int total = p.m > 0 ? mt2 * p.n_tiles : 0;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (elect_one_sync()) {
+      prefetch_tmap(&tmA);
+      prefetch_tmap(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = cid; t < total && !*s_abort; t += ncl) {
+        const int arow = (t % mt2) * 2 * GEMM_BM + (int)rank * GEMM_BM;
+        const int brow = (t / mt2) * PAIR_BN + (int)rank * (PAIR_BN / 2);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.status)) { *s_abort = 1; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], PAIR_TX);
+          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+          const int kc = kb * GEMM_BK;
+          tma_load_2d_pair(sA + stage * S::A_BYTES, &tmA, fb, kc, arow);
+          tma_load_2d_pair(sB + stage * S::B_BYTES, &tmB, fb, kc, brow);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Tail: every stage this CTA filled has been released by the pair's MMAs, i.e. their
+      // commits' arrivals on this CTA's `empty` barriers have landed (stages never filled
+      // pass at once).  After an abort the waits still end at their time limit.
+      for (int i = 0; i < STAGES; ++i) {
+        mbar_wait(&empty[stage], phase ^ 1, nullptr);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t IDESC = umma_idesc_bf16(2 * GEMM_BM, PAIR_BN, false, false);
+    if (rank == 0 && elect_one_sync()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int buf = 0;
+      uint32_t aphase = 0;
+      bool issued_any = false;
+      for (int t = cid; t < total && !*s_abort; t += ncl) {
+        if (!mbar_wait(&tempty[buf], aphase ^ 1, p.status)) { *s_abort = 1; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * PAIR_BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status)) { *s_abort = 1; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * S::A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * S::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 16; ++k) {
+            const uint64_t ad = umma_desc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = umma_desc_sw128(b0 + k * 32, 16, 1024);
+            umma_bf16_pair(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          const uint32_t e = smem_u32(&empty[stage]);
+          umma_commit_pair(mapa_shared(e, 0));
+          umma_commit_pair(mapa_shared(e, 1));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (*s_abort) break;
+        const uint32_t f = smem_u32(&tfull[buf]);
+        umma_commit_pair(mapa_shared(f, 0));
+        umma_commit_pair(mapa_shared(f, 1));
+        buf ^= 1;
+        if (buf == 0) aphase ^= 1;
+      }
+      if (*s_abort && issued_any) {
+        umma_commit_pair(mapa_shared(smem_u32(drain), 0));
+        mbar_wait(drain, 0, nullptr);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int quad = warp & 3;             // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    int buf = 0;
+    uint32_t aphase = 0;
+    for (int t = cid; t < total && !*s_abort; t += ncl) {
+      if (!mbar_wait(&tfull[buf], aphase, p.status)) { *s_abort = 1; break; }
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * PAIR_BN;
+      const int n = t / mt2;
+      const int row0 = (t % mt2) * 2 * GEMM_BM + (int)rank * GEMM_BM;
+      const int out_row = row0 + row_in_tile;
+      const bool row_ok = out_row < p.m && out_row < p.out_rows;
+      if constexpr (EPI == EPI_QKV) {
+        qkv_prologue_tile(p.pro, n, tbase, row_ok, out_row, p.out, p.ldo, p.status);
+      } else {
+#pragma unroll 1
+        for (int ch = 0; ch < PAIR_BN / 32; ++ch) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld32(tbase + ch * 32, v);
+          tmem_wait_ld();
+          const int col = n * PAIR_BN + ch * 32;
+          if (row_ok && col + 32 <= p.out_cols) {
+            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+            uint4* dst = reinterpret_cast<uint4*>(out + (long long)out_row * p.ldo + col);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(
+                  pack_bf16x2(__uint_as_float(v[8 * i]), __uint_as_float(v[8 * i + 1])),
+                  pack_bf16x2(__uint_as_float(v[8 * i + 2]), __uint_as_float(v[8 * i + 3])),
+                  pack_bf16x2(__uint_as_float(v[8 * i + 4]), __uint_as_float(v[8 * i + 5])),
+                  pack_bf16x2(__uint_as_float(v[8 * i + 6]), __uint_as_float(v[8 * i + 7])));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
+      buf ^= 1;
+      if (buf == 0) aphase ^= 1;
+    }
+  }
+
+  __syncthreads();
+  cluster_sync();   // no CTA releases TMEM or exits while its peer may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, S::TMEM_COLS);
+  }
+}
+
 }  // namespace lb

@@ -5,6 +5,9 @@
 #include "lb_gemm_tok.cuh"
 #include "lb_host.h"
 
+#include <algorithm>
+#include <atomic>
+
 namespace lb {
 
 template <int BN, int STAGES, int EPI>
@@ -33,6 +36,50 @@ int launch_gemm_tok(const CUtensorMap& tW, const CUtensorMap& tWsh0, const CUten
   if (grid <= 0) return LB_OK;
   launch_k(kern, grid, 64 + 32 * EPW, smem, st, tW, tWsh0, tWsh1, tX, tXsh, a);
   { int _rc = launched("k_gemm_tok"); if (_rc) return _rc; }
+  return LB_OK;
+}
+
+// CTA-pair GEMM (k_gemm_pair): clusters of two CTAs, the persistent grid as many
+// clusters as fit the GPU at once (cudaOccupancyMaxActiveClusters, looked up once per
+// device), at most one per 256 x 256 tile.
+template <int STAGES, int EPI>
+int launch_gemm_pair(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& a,
+                     long long tiles, cudaStream_t st) {
+  auto kern = k_gemm_pair<STAGES, EPI>;
+  const size_t smem = PairSmem<STAGES>::bytes();
+  if ((int)smem > max_smem_optin())
+    return fail(LB_ERR_UNSUPPORTED, "gemm pair: %zu bytes of shared memory exceed the limit", smem);
+  if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)smem)) return rc;
+  if (tiles <= 0) return LB_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static std::atomic<int> s_clusters[64];
+  int dev = 0;
+  LB_CUDA_CHECK(cudaGetDevice(&dev));
+  int ncl = (dev >= 0 && dev < 64) ? s_clusters[dev].load() : 0;
+  if (ncl <= 0) {
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    if (cudaOccupancyMaxActiveClusters(&ncl, kern, &cfg) != cudaSuccess || ncl <= 0) {
+      (void)cudaGetLastError();
+      ncl = num_sms() / 2;
+    }
+    if (dev >= 0 && dev < 64) s_clusters[dev].store(ncl);
+  }
+  cfg.gridDim = dim3(2 * (unsigned)std::min<long long>(tiles, ncl));
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  (void)cudaLaunchKernelEx(&cfg, kern, tA, tB, a);
+  { int _rc = launched("k_gemm_pair"); if (_rc) return _rc; }
   return LB_OK;
 }
 
