@@ -211,7 +211,7 @@ int gemm_run(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, in
     a.ldo = ldc;
     a.out_rows = (int)M;
     a.out_cols = (int)N;
-    return launch_gemm_pair<6, EPI_BF16>(tA, tB, a, pair_tiles(M, N), st);
+    return launch_gemm_pair<6, EPI_BF16, 4>(tA, tB, a, pair_tiles(M, N), st);
   }
   rc = make_tmap_bf16_3d(&tB, B, 1, N, K, ldb, ldb * N, BN, 64);
   if (rc) return rc;
@@ -319,7 +319,7 @@ int lb_qkv_prologue_gemm(const void* x, int64_t ldx, const void* w_qkv, int64_t 
   g.out_rows = (int)M;
   g.out_cols = (int)N;
   g.pro = *a;
-  if (pair) return launch_gemm_pair<6, EPI_QKV>(tA, tB, g, pair_tiles(M, N), st);
+  if (pair) return launch_gemm_pair<6, EPI_QKV, 8>(tA, tB, g, pair_tiles(M, N), st);
   const long long tiles = ((M + GEMM_BM - 1) / GEMM_BM) * (long long)g.n_tiles;
   const int grid = (int)std::min<long long>(tiles, num_sms());
   return launch_gemm<PRO_D, 4, EPI_QKV>(tA, tB, g, grid, st);

@@ -318,8 +318,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 //                        `full` barrier, which expects the pair's bytes
 //   warp 1             : pair TMEM allocation (both CTAs); MMA issue (first CTA only), with
 //                        each commit sent to the barrier of both CTAs
-//   warps 2..5         : epilogue of this CTA's rows; one arrival per warp on the first
-//                        CTA's `tempty` barrier (eight per tile)
+//   warps 2..          : epilogue of this CTA's rows, EPW warps: with 4 one warp per TMEM
+//                        lane quadrant drains both accumulators in turn; with 8 (the q/k/v
+//                        prologue epilogue, longer than a tile's mainloop) warps 2-5 drain
+//                        accumulator 0 and warps 6-9 accumulator 1, so each group has two
+//                        mainloops' time per tile; one arrival per warp on the first CTA's
+//                        `tempty` barrier (eight per tile)
 // Every wait is bounded; the CTAs meet in cluster barriers after the barrier set-up and
 // before the TMEM release, so neither leaves while the other may still signal it.
 constexpr int PAIR_BN = 256;
@@ -333,12 +337,13 @@ struct PairSmem {
   static size_t bytes() { return 1024 + (size_t)STAGES * (A_BYTES + B_BYTES) + BAR_BYTES; }
 };
 
-template <int STAGES, int EPI>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+template <int STAGES, int EPI, int EPW>
+__global__ void __launch_bounds__(64 + 32 * EPW, 1)
     k_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const GemmArgs p) {
   static_assert(EPI == EPI_BF16 || EPI == EPI_QKV, "pair GEMM epilogues: bf16 and q/k/v");
   static_assert(EPI != EPI_QKV || PAIR_BN == PRO_D, "EPI_QKV: one 256-dim head row per tile");
+  static_assert(EPW == 4 || EPW == 8, "one or two epilogue warps per TMEM lane quadrant");
   using S = PairSmem<STAGES>;
   constexpr uint32_t PAIR_TX = 2u * (S::A_BYTES + S::B_BYTES);
   pdl_entry();
@@ -461,9 +466,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ------------------------------------------------------------------ epilogue
     const int quad = warp & 3;             // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
-    int buf = 0;
-    uint32_t aphase = 0;
-    for (int t = cid; t < total && !*s_abort; t += ncl) {
+    constexpr int NG = EPW / 4;            // epilogue groups; group g takes local tiles g, g+NG..
+    const int grp = (warp - 2) / 4;
+    for (int i = grp;; i += NG) {
+      const int t = cid + i * ncl;
+      if (t >= total || *s_abort) break;
+      const int buf = i & 1;                        // accumulator of the pair's i-th tile
+      const uint32_t aphase = (uint32_t)(i >> 1) & 1u;
       if (!mbar_wait(&tfull[buf], aphase, p.status)) { *s_abort = 1; break; }
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + buf * PAIR_BN;
@@ -497,8 +506,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
-      buf ^= 1;
-      if (buf == 0) aphase ^= 1;
     }
   }
 

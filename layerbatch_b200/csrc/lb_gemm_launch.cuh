@@ -42,17 +42,17 @@ int launch_gemm_tok(const CUtensorMap& tW, const CUtensorMap& tWsh0, const CUten
 // CTA-pair GEMM (k_gemm_pair): clusters of two CTAs, the persistent grid as many
 // clusters as fit the GPU at once (cudaOccupancyMaxActiveClusters, looked up once per
 // device), at most one per 256 x 256 tile.
-template <int STAGES, int EPI>
+template <int STAGES, int EPI, int EPW>
 int launch_gemm_pair(const CUtensorMap& tA, const CUtensorMap& tB, const GemmArgs& a,
                      long long tiles, cudaStream_t st) {
-  auto kern = k_gemm_pair<STAGES, EPI>;
+  auto kern = k_gemm_pair<STAGES, EPI, EPW>;
   const size_t smem = PairSmem<STAGES>::bytes();
   if ((int)smem > max_smem_optin())
     return fail(LB_ERR_UNSUPPORTED, "gemm pair: %zu bytes of shared memory exceed the limit", smem);
   if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)smem)) return rc;
   if (tiles <= 0) return LB_OK;
   cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.blockDim = dim3(64 + 32 * EPW);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
