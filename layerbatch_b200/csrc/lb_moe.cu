@@ -27,6 +27,26 @@ static int perm_chunks(int T, int k) { return (T * k + PERM_CHUNK - 1) / PERM_CH
 // One warp per token.  Softmax in fp32 over E logits, top-k by (value desc, index asc),
 // renormalisation over the selected k (qwen3_5.py:770-773).  Optionally the shared-expert
 // gate sigmoid(x . w_sg) (qwen3_5.py:903) in fp32.
+//
+// Selection: the logits are bf16, so each one gets a 32-bit key whose high half orders
+// the bf16 values as unsigned integers (-0 taken as +0, NaN below every number) and whose
+// low half is 0xFFFF - e: the largest key is the largest value with the lowest expert
+// index, and each of the k rounds is one redux.sync max over the warp's untaken keys.
+__device__ __forceinline__ uint32_t topk_key(float v, int e) {
+  uint32_t b = __float_as_uint(v) >> 16;          // the bf16 bits (v is a bf16 value)
+  if ((b & 0x7FFFu) == 0) b = 0;                  // -0 -> +0
+  uint32_t ord;
+  if ((b & 0x7FFFu) > 0x7F80u) ord = 0;           // NaN
+  else ord = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+  return (ord << 16) | (0xFFFFu - (uint32_t)e);
+}
+
+__device__ __forceinline__ float topk_key_value(uint32_t key) {
+  const uint32_t ord = key >> 16;
+  const uint32_t b = (ord & 0x8000u) ? (ord & 0x7FFFu) : (~ord & 0xFFFFu);
+  return __uint_as_float(b << 16);
+}
+
 template <int VPL>
 __global__ void k_router_topk(const __nv_bfloat16* __restrict__ logits, long long ld, int T,
                               int E, int k, int32_t* __restrict__ ids, float* __restrict__ wf,
@@ -40,13 +60,28 @@ __global__ void k_router_topk(const __nv_bfloat16* __restrict__ logits, long lon
   if (t >= T) return;
   const __nv_bfloat16* row = logits + (long long)t * ld;
   float v[VPL];
-  float m = -FLT_MAX;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int e = lane + 32 * i;
     v[i] = e < E ? __bfloat162float(row[e]) : -FLT_MAX;
-    m = fmaxf(m, v[i]);
   }
+  // shared-expert gate inputs: the first 8 stripes of x[t] and w_sg in flight with the logits
+  constexpr int SG_PRE = 8;
+  uint4 xa[SG_PRE], xb[SG_PRE];
+  const __nv_bfloat16* xr = sg != nullptr ? x + (long long)t * H : nullptr;
+  if (sg != nullptr) {
+#pragma unroll
+    for (int u = 0; u < SG_PRE; ++u) {
+      const int h = lane * 8 + 256 * u;
+      if (h < H) {
+        xa[u] = *reinterpret_cast<const uint4*>(xr + h);
+        xb[u] = *reinterpret_cast<const uint4*>(wsg + h);
+      }
+    }
+  }
+  float m = -FLT_MAX;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) m = fmaxf(m, v[i]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   float z = 0.f;
@@ -56,31 +91,24 @@ __global__ void k_router_topk(const __nv_bfloat16* __restrict__ logits, long lon
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
 
+  uint32_t key[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int e = lane + 32 * i;
+    key[i] = e < E ? topk_key(v[i], e) : 0u;
+  }
   unsigned taken = 0;
   float my_p = 0.f, psum = 0.f;
   int my_id = 0;
   for (int j = 0; j < k; ++j) {
-    float best = -FLT_MAX;
-    int bi = 0x7fffffff;
+    uint32_t best = 0;
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E && !((taken >> i) & 1u) && v[i] > best) {  // ascending e within a lane
-        best = v[i];
-        bi = e;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ob > best || (ob == best && oi < bi)) {
-        best = ob;
-        bi = oi;
-      }
-    }
+    for (int i = 0; i < VPL; ++i)
+      if (!((taken >> i) & 1u)) best = max(best, key[i]);
+    best = __reduce_max_sync(0xffffffffu, best);
+    const int bi = (int)(0xFFFFu - (best & 0xFFFFu));
     if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-    const float p = expf(best - m) / z;
+    const float p = expf(topk_key_value(best) - m) / z;
     psum += p;
     if (lane == j) {
       my_p = p;
@@ -95,10 +123,18 @@ __global__ void k_router_topk(const __nv_bfloat16* __restrict__ logits, long lon
     if (wb) wb[o] = __float2bfloat16_rn(w);
   }
   if (sg != nullptr) {
-    const __nv_bfloat16* xr = x + (long long)t * H;
     float acc = 0.f;
-#pragma unroll 8
-    for (int h = lane * 8; h < H; h += 256) {   // unrolled: a lane's loads all in flight
+#pragma unroll
+    for (int u = 0; u < SG_PRE; ++u) {
+      if (lane * 8 + 256 * u < H) {
+        const uint4 a = xa[u], b = xb[u];
+        acc += bf16_lo(a.x) * bf16_lo(b.x) + bf16_hi(a.x) * bf16_hi(b.x);
+        acc += bf16_lo(a.y) * bf16_lo(b.y) + bf16_hi(a.y) * bf16_hi(b.y);
+        acc += bf16_lo(a.z) * bf16_lo(b.z) + bf16_hi(a.z) * bf16_hi(b.z);
+        acc += bf16_lo(a.w) * bf16_lo(b.w) + bf16_hi(a.w) * bf16_hi(b.w);
+      }
+    }
+    for (int h = lane * 8 + 256 * SG_PRE; h < H; h += 256) {
       const uint4 a = *reinterpret_cast<const uint4*>(xr + h);
       const uint4 b = *reinterpret_cast<const uint4*>(wsg + h);
       acc += bf16_lo(a.x) * bf16_lo(b.x) + bf16_hi(a.x) * bf16_hi(b.x);
