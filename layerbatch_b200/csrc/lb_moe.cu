@@ -195,9 +195,12 @@ __global__ void k_moe_count(const int32_t* __restrict__ ids, int n, int expert_b
 }
 
 // Exclusive scans: row_start[g] and mtile_start[g] (128-row tiles) over G groups, with
-// group 0 (shared expert) holding T rows.  One block of 1024 threads, G <= 2047.
+// group 0 (shared expert) holding T rows.  One block of 1024 threads, G <= 2047.  With
+// `iota` it also writes the identity map of the shared-expert rows, iota[i] = i for
+// i < iota_n.
 __global__ void k_moe_scan(const int* __restrict__ counts, int G, int T,
-                           int* __restrict__ row_start, int* __restrict__ mtile_start) {
+                           int* __restrict__ row_start, int* __restrict__ mtile_start,
+                           int32_t* __restrict__ iota, int iota_n) {
   pdl_entry();
   __shared__ int s_rows[1024], s_tiles[1024];
   const int tid = threadIdx.x;
@@ -233,7 +236,8 @@ __global__ void k_moe_scan(const int* __restrict__ counts, int G, int T,
   if (2 * tid + 1 <= G) {
     row_start[2 * tid + 1] = ex_r + r[0];
     mtile_start[2 * tid + 1] = ex_t + tl[0];
-  }
+  }  if (iota != nullptr)
+    for (int i = tid; i < iota_n; i += blockDim.x) iota[i] = i;
 }
 
 // One block per local expert: scan all pairs in (slot, token) order and assign packed
@@ -402,7 +406,7 @@ static int run_permute(const int32_t* ids, const float* wf, int T, int k, int ex
     launch_k(k_moe_count, std::max(grid, 1), 1024, sizeof(int) * nl, st, ids, n, expert_base, nl, counts);
     { int _rc = launched("k_moe_count"); if (_rc) return _rc; }
   }
-  launch_k(k_moe_scan, 1, 1024, 0, st, counts, G, T, row_start, mtile_start);
+  launch_k(k_moe_scan, 1, 1024, 0, st, counts, G, T, row_start, mtile_start, nullptr, 0);
   { int _rc = launched("k_moe_scan"); if (_rc) return _rc; }
   if (T > 0) {
     launch_k(k_iota, std::min(1024, (T + 255) / 256), 256, 0, st, perm_token, T);
@@ -423,7 +427,8 @@ static int run_permute(const int32_t* ids, const float* wf, int T, int k, int ex
 // k_perm_chunk_scatter walks each chunk in order with one warp and assigns rows, so the
 // result equals the sequential definition bit for bit.
 __global__ void k_perm_chunk_hist(const int32_t* __restrict__ ids, int T, int k, int expert_base,
-                                  int nl, int* __restrict__ chunk_hist) {
+                                  int nl, int* __restrict__ chunk_hist,
+                                  int32_t* __restrict__ row_of) {
   pdl_entry();
   extern __shared__ int hist[];
   for (int i = threadIdx.x; i < nl; i += blockDim.x) hist[i] = 0;
@@ -434,6 +439,7 @@ __global__ void k_perm_chunk_hist(const int32_t* __restrict__ ids, int T, int k,
     const int j = f / T, t = f - (f / T) * T;
     const int e = ids[(long long)t * k + j] - expert_base;
     if (e >= 0 && e < nl) atomicAdd(&hist[e], 1);
+    row_of[(long long)t * k + j] = -1;   // routed nowhere until the scatter assigns a row
   }
   __syncthreads();
   // expert-major layout [nl][n_chunks]: each expert's chunk counts are contiguous
@@ -589,21 +595,22 @@ static int run_permute_chunked(const int32_t* ids, const float* wf, int T, int k
                                int32_t* row_of, cudaStream_t st, int T0) {
   const int n = T * k;
   const int nc = perm_chunks(T, k);
-  if (n > 0) LB_CUDA_CHECK(cudaMemsetAsync(row_of, 0xff, sizeof(int32_t) * (size_t)n, st));
+  // k_perm_chunk_hist marks every pair as routed nowhere (row_of = -1) before the scatter
+  // fills in the local ones; without it the marking is a memset
+  if (n > 0 && !(nc > 0 && nl > 0))
+    LB_CUDA_CHECK(cudaMemsetAsync(row_of, 0xff, sizeof(int32_t) * (size_t)n, st));
   if (nc > 0 && nl > 0) {
-    launch_k(k_perm_chunk_hist, nc, PERM_CHUNK, sizeof(int) * nl, st, ids, T, k, expert_base, nl, chunk_hist);
+    launch_k(k_perm_chunk_hist, nc, PERM_CHUNK, sizeof(int) * nl, st, ids, T, k, expert_base, nl, chunk_hist,
+             row_of);
     { int _rc = launched("k_perm_chunk_hist"); if (_rc) return _rc; }
     launch_k(k_perm_expert_scan, (nl + 7) / 8, 256, 0, st, chunk_hist, nc, nl, counts);
     { int _rc = launched("k_perm_expert_scan"); if (_rc) return _rc; }
   } else if (nl > 0) {
     LB_CUDA_CHECK(cudaMemsetAsync(counts, 0, sizeof(int) * (nl + 2), st));
   }
-  launch_k(k_moe_scan, 1, 1024, 0, st, counts, nl + 1, T0, row_start, mtile_start);
+  launch_k(k_moe_scan, 1, 1024, 0, st, counts, nl + 1, T0, row_start, mtile_start,
+           T0 > 0 ? perm_token : nullptr, T0);
   { int _rc = launched("k_moe_scan"); if (_rc) return _rc; }
-  if (T0 > 0) {
-    launch_k(k_iota, std::min(1024, (T0 + 255) / 256), 256, 0, st, perm_token, T0);
-    { int _rc = launched("k_iota"); if (_rc) return _rc; }
-  }
   if (nc > 0 && nl > 0) {
     launch_k(k_perm_chunk_scatter, nc, 32, sizeof(int) * nl, st, ids, wf, T, k, expert_base, nl, chunk_hist,
                                                            row_start, perm_token, perm_w, row_of);
